@@ -1,0 +1,168 @@
+/*
+ * piton_b200.h - C ABI of libpiton_b200.so, the B200 (sm_100a) backend of the
+ * PIton `kernel[grid](..., device="b200")` launch.
+ *
+ * Every operator entry point takes one argument struct (device pointers as
+ * uint64_t, sizes and strides in ELEMENTS as int64_t, the launch's grid and
+ * constexprs) and a CUDA stream (`void*`, NULL = the legacy default stream),
+ * enqueues its kernels and returns without synchronising.  The shape follows
+ * the reference's AOT launcher `<sym>_launch(const <sym>_args_t*, gx, gy, gz)`
+ * (piton/tools/compile.py:71-90, pi/runtime/piton_rt.h:37) except that the
+ * grid travels inside the struct and the return value is a status code
+ * instead of elapsed microseconds (time with CUDA events around the call).
+ *
+ * Status codes are 0 (ok) or one of the negative PITON_B200_E* values; the
+ * calling thread's last error message is available from
+ * piton_b200_last_error().  Pointer arguments follow the reference's launch
+ * semantics (piton/runtime/launcher.py:66-95): a pointer is the address the
+ * kernel indexes from, so a negative row stride addresses memory below it.
+ *
+ * Threading: the library keeps no per-call global state except the calling
+ * thread's error message and per-device caches (SM count, kernel attributes),
+ * so one host thread per device may call it concurrently.
+ */
+#ifndef PITON_B200_H
+#define PITON_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PITON_B200_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define PITON_B200_API __attribute__((visibility("default")))
+#else
+#define PITON_B200_API
+#endif
+
+/* status codes */
+#define PITON_B200_OK 0
+#define PITON_B200_EINVAL (-1)     /* bad argument: shape, stride, pointer, flag */
+#define PITON_B200_ECUDA (-2)      /* a CUDA runtime call failed */
+#define PITON_B200_ETIMEOUT (-3)   /* a bounded wait ran out */
+#define PITON_B200_ENOTSUP (-4)    /* no B200 implementation for this constexpr combination */
+#define PITON_B200_ENOMEM (-5)     /* allocation failed */
+#define PITON_B200_EWORKSPACE (-6) /* workspace missing or smaller than *_workspace_size() */
+
+/* flags (bitwise or) */
+#define PITON_B200_QPU_ROUNDING 0x1u /* reproduce the QPU's float semantics bit for bit: round-toward-zero
+                                        adds and multiplies, no FMA, sequential-k dots, denormals read and
+                                        written as +0 (piton/qpu/emulator.py:137-212). add, matmul, dense. */
+#define PITON_B200_FORCE_SIMT 0x2u   /* matmul/dense: take the CUDA-core path even where tensor cores apply */
+
+/* ---- runtime (replaces pi/runtime/piton_rt.h:37-107: allocation, launch, sync, timers) ---- */
+
+PITON_B200_API int piton_b200_abi_version(void);
+PITON_B200_API const char *piton_b200_last_error(void);
+/* Make `device` current for the calling thread and create its context. */
+PITON_B200_API int piton_b200_init(int device);
+PITON_B200_API int piton_b200_device_count(int *count);
+PITON_B200_API int piton_b200_malloc(uint64_t *ptr, size_t bytes);
+PITON_B200_API int piton_b200_free(uint64_t ptr);
+PITON_B200_API int piton_b200_memcpy_h2d(uint64_t dst, const void *src, size_t bytes, void *stream);
+PITON_B200_API int piton_b200_memcpy_d2h(void *dst, uint64_t src, size_t bytes, void *stream);
+PITON_B200_API int piton_b200_memset(uint64_t dst, int value, size_t bytes, void *stream);
+/* Wait for `stream` with a deadline: polls cudaStreamQuery, returns PITON_B200_ETIMEOUT
+   after `timeout_s` seconds instead of blocking for ever
+   (the counterpart of piton_rt.c:150-189's 20 s launch timeout). */
+PITON_B200_API int piton_b200_stream_wait(void *stream, double timeout_s);
+
+/* ---- vector add: examples/kernels.py:6-15 add_kernel ---- */
+typedef struct {
+    uint64_t x, y, out;   /* float* */
+    int64_t n_elements;
+    int64_t block_size;   /* BLOCK_SIZE constexpr */
+    int64_t grid_x;       /* programs launched: elements [0, min(n, grid_x*BLOCK_SIZE)) are written */
+    uint32_t flags;       /* PITON_B200_QPU_ROUNDING */
+    uint32_t _pad;
+} piton_add_args;
+PITON_B200_API int piton_b200_add_f32(const piton_add_args *args, void *stream);
+
+/* ---- fused row softmax: examples/kernels.py:60-76 softmax_kernel ---- */
+typedef struct {
+    uint64_t out, in;     /* float* */
+    int64_t in_row_stride, out_row_stride, n_cols;
+    int64_t block_size;   /* BLOCK_SIZE constexpr: columns >= BLOCK_SIZE are neither read nor written */
+    int64_t grid_x;       /* rows = programs launched */
+    uint32_t flags;
+    uint32_t _pad;
+} piton_softmax_args;
+PITON_B200_API int piton_b200_softmax_f32(const piton_softmax_args *args, void *stream);
+
+/* ---- grouped tutorial matmul: examples/kernels.py:18-57 matmul_kernel ---- */
+typedef struct {
+    uint64_t a, b, c;     /* float* */
+    int64_t M, N, K;
+    int64_t stride_am, stride_ak, stride_bk, stride_bn, stride_cm, stride_cn;
+    int64_t block_m, block_n, block_k, group_m;   /* constexprs */
+    int64_t grid_x;       /* programs launched (grouped pid order decides which C tiles exist) */
+    uint64_t workspace;   /* device scratch for the tensor-core path, >= piton_b200_matmul_workspace_size() */
+    uint64_t workspace_bytes;
+    uint32_t flags;       /* PITON_B200_QPU_ROUNDING, PITON_B200_FORCE_SIMT */
+    uint32_t _pad;
+} piton_matmul_args;
+/* Bytes of workspace the call needs (0 when it takes the CUDA-core path). */
+PITON_B200_API size_t piton_b200_matmul_workspace_size(const piton_matmul_args *args);
+PITON_B200_API int piton_b200_matmul_f32(const piton_matmul_args *args, void *stream);
+
+/* ---- dense layer Y = X W (+b) (ReLU): examples/nn_kernels.py:23-74 dense_layer_kernel ---- */
+typedef struct {
+    uint64_t x, w, bias, y;  /* float*: X[M,K], W[K,N], bias[N], Y[M,N], contiguous row-major */
+    int64_t M, N, K;
+    int64_t block_m, block_n, block_k, group_m;
+    int64_t grid_x;
+    int32_t add_bias, relu;
+    uint32_t flags;
+    uint32_t _pad;
+} piton_dense_args;
+PITON_B200_API int piton_b200_dense_f32(const piton_dense_args *args, void *stream);
+
+/* ---- digits MLP 64->128->64->16 in one launch: examples/digits_model.py:120-139 ----
+   images: uint8 intensities 0..16 (x = v/16) when `images_u8` is set, else float 0..1.
+   logits[M,16] always written; argmax of the first `n_classes` logits into pred[M] when pred != 0. */
+typedef struct {
+    uint64_t images;      /* uint8_t* or float* [M,64] */
+    uint64_t w1, b1, w2, b2, w3, b3;   /* float*: [64,128],[128],[128,64],[64],[64,16],[16] */
+    uint64_t logits;      /* float* [M,16] */
+    uint64_t pred;        /* int32_t* [M] or 0 */
+    int64_t M;
+    int32_t images_u8, n_classes;
+    uint32_t flags;
+    uint32_t _pad;
+} piton_mlp_args;
+PITON_B200_API int piton_b200_mlp_f32(const piton_mlp_args *args, void *stream);
+
+/* ---- causal / full attention: examples/attention.py:75-113 attn_fwd_kernel ----
+   Q, V, Out rows [n_ctx, head_dim] with row strides; K through stride_kn (key) and
+   stride_kk (dim), so K may be [n_ctx, D] or pre-transposed [D, n_ctx].  Heads advance by
+   stride_*h.  Rows >= min(n_ctx, grid_x*block_m) and heads >= grid_y are not written. */
+typedef struct {
+    uint64_t q, k, v, out;  /* float* */
+    double sm_scale;
+    int64_t stride_qh, stride_qm, stride_kh, stride_kn, stride_kk, stride_vh, stride_vn, stride_oh, stride_om;
+    int64_t n_ctx, head_dim, block_m, block_n;
+    int64_t grid_x, grid_y;
+    int32_t causal, even_n;
+    uint32_t flags;
+    uint32_t _pad;
+} piton_attention_args;
+PITON_B200_API int piton_b200_attention_f32(const piton_attention_args *args, void *stream);
+
+/* ---- row LayerNorm without affine: tests/test_reroll_reduce.py:199-208 layernorm_kernel ---- */
+typedef struct {
+    uint64_t x, y;        /* float* */
+    int64_t rows, n_cols, x_row_stride, y_row_stride;
+    double eps;
+    uint32_t flags;
+    uint32_t _pad;
+} piton_layernorm_args;
+PITON_B200_API int piton_b200_layernorm_f32(const piton_layernorm_args *args, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* PITON_B200_H */

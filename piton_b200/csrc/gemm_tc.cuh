@@ -1,0 +1,22 @@
+// Interface of the tcgen05 3xTF32 GEMM (gemm_tc.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace piton {
+
+struct TcGemmShape {
+    const float *a, *b;
+    float *c;
+    int64_t M, N, K;
+    int64_t sam, sak, sbk, sbn, scm, scn;
+};
+
+// True when the tensor-core path can run this problem (layout and alignment).
+bool tc_gemm_supported(const TcGemmShape &s);
+// Scratch bytes the path needs for the split operands.
+size_t tc_gemm_workspace_bytes(const TcGemmShape &s);
+int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream);
+
+}  // namespace piton

@@ -1,0 +1,91 @@
+// Entry points of the tutorial matmul (examples/kernels.py:18-57) and the dense
+// layer (examples/nn_kernels.py:23-74): argument checks and the choice between
+// the tcgen05 3xTF32 path (gemm_tc.cu) and the CUDA-core path (gemm_simt.cu).
+#include "common.cuh"
+#include "gemm_simt.cuh"
+#include "gemm_tc.cuh"
+
+using namespace piton;
+
+static int check_matmul(const piton_matmul_args *a) {
+    PITON_REQUIRE(a != nullptr, "args is NULL");
+    PITON_REQUIRE(a->M >= 0 && a->N >= 0 && a->K >= 0, "negative shape %lld x %lld x %lld", (long long)a->M,
+                  (long long)a->N, (long long)a->K);
+    PITON_REQUIRE(a->block_m > 0 && a->block_n > 0 && a->block_k > 0 && a->group_m > 0 && a->grid_x >= 0,
+                  "bad tile/group/grid");
+    PITON_REQUIRE((a->flags & ~(PITON_B200_QPU_ROUNDING | PITON_B200_FORCE_SIMT)) == 0, "unknown flags 0x%x",
+                  a->flags);
+    return PITON_B200_OK;
+}
+
+static TcGemmShape tc_shape(const piton_matmul_args *a) {
+    TcGemmShape t;
+    t.a = reinterpret_cast<const float *>(a->a);
+    t.b = reinterpret_cast<const float *>(a->b);
+    t.c = reinterpret_cast<float *>(a->c);
+    t.M = a->M; t.N = a->N; t.K = a->K;
+    t.sam = a->stride_am; t.sak = a->stride_ak; t.sbk = a->stride_bk; t.sbn = a->stride_bn;
+    t.scm = a->stride_cm; t.scn = a->stride_cn;
+    return t;
+}
+
+// The tensor-core path computes every element of C, so it needs a grid that
+// covers every reference tile and a non-degenerate problem.
+static bool use_tc(const piton_matmul_args *a) {
+    if (a->flags & (PITON_B200_QPU_ROUNDING | PITON_B200_FORCE_SIMT)) return false;
+    if (a->grid_x < grouped_tiles(a->M, a->N, a->block_m, a->block_n)) return false;
+    return tc_gemm_supported(tc_shape(a));
+}
+
+extern "C" size_t piton_b200_matmul_workspace_size(const piton_matmul_args *a) {
+    if (check_matmul(a) != PITON_B200_OK || !use_tc(a)) return 0;
+    return tc_gemm_workspace_bytes(tc_shape(a));
+}
+
+extern "C" int piton_b200_matmul_f32(const piton_matmul_args *a, void *stream) {
+    int rc = check_matmul(a);
+    if (rc) return rc;
+    if (a->M == 0 || a->N == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->a && a->b && a->c, "NULL pointer");
+    cudaStream_t s = as_stream(stream);
+    if (use_tc(a)) {
+        size_t need = tc_gemm_workspace_bytes(tc_shape(a));
+        if (a->workspace_bytes < need || (need && !a->workspace))
+            return set_error(PITON_B200_EWORKSPACE, "matmul needs %zu bytes of workspace, got %llu", need,
+                             (unsigned long long)a->workspace_bytes);
+        return tc_gemm(tc_shape(a), reinterpret_cast<void *>(a->workspace), s);
+    }
+    GemmSimtParams p{};
+    p.a = reinterpret_cast<const float *>(a->a);
+    p.b = reinterpret_cast<const float *>(a->b);
+    p.c = reinterpret_cast<float *>(a->c);
+    p.M = a->M; p.N = a->N; p.K = a->K;
+    p.sam = a->stride_am; p.sak = a->stride_ak; p.sbk = a->stride_bk; p.sbn = a->stride_bn;
+    p.scm = a->stride_cm; p.scn = a->stride_cn;
+    p.ref_bm = a->block_m; p.ref_bn = a->block_n; p.ref_group = a->group_m; p.grid_x = a->grid_x;
+    p.check_grid = a->grid_x < grouped_tiles(a->M, a->N, a->block_m, a->block_n);
+    return gemm_simt(p, (a->flags & PITON_B200_QPU_ROUNDING) != 0, s);
+}
+
+extern "C" int piton_b200_dense_f32(const piton_dense_args *a, void *stream) {
+    PITON_REQUIRE(a != nullptr, "args is NULL");
+    PITON_REQUIRE(a->M >= 0 && a->N > 0 && a->K > 0, "bad shape %lld x %lld x %lld", (long long)a->M,
+                  (long long)a->N, (long long)a->K);
+    PITON_REQUIRE(a->block_m > 0 && a->block_n > 0 && a->block_k > 0 && a->group_m > 0 && a->grid_x >= 0,
+                  "bad tile/group/grid");
+    PITON_REQUIRE((a->flags & ~(PITON_B200_QPU_ROUNDING | PITON_B200_FORCE_SIMT)) == 0, "unknown flags 0x%x",
+                  a->flags);
+    if (a->M == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->x && a->w && a->y && (!a->add_bias || a->bias), "NULL pointer");
+    GemmSimtParams p{};
+    p.a = reinterpret_cast<const float *>(a->x);
+    p.b = reinterpret_cast<const float *>(a->w);
+    p.c = reinterpret_cast<float *>(a->y);
+    p.bias = a->add_bias ? reinterpret_cast<const float *>(a->bias) : nullptr;
+    p.relu = a->relu != 0;
+    p.M = a->M; p.N = a->N; p.K = a->K;
+    p.sam = a->K; p.sak = 1; p.sbk = a->N; p.sbn = 1; p.scm = a->N; p.scn = 1;
+    p.ref_bm = a->block_m; p.ref_bn = a->block_n; p.ref_group = a->group_m; p.grid_x = a->grid_x;
+    p.check_grid = a->grid_x < grouped_tiles(a->M, a->N, a->block_m, a->block_n);
+    return gemm_simt(p, (a->flags & PITON_B200_QPU_ROUNDING) != 0, as_stream(stream));
+}

@@ -1,0 +1,314 @@
+"""The ``device="b200"`` backend: operator registry and argument marshalling.
+
+``run_on_b200`` is what ``Launcher.__call__`` calls for a B200 launch (the
+counterpart of the reference's ``run_emulator``, piton/runtime/launcher.py:168-214):
+
+1. the launched kernel is looked up in the registry by its name and parameter
+   list (the reference's ``JITFunction`` objects match too);
+2. pointer arguments become device pointers: CUDA torch tensors are used in
+   place; numpy arrays are copied to device buffers and, after the launch,
+   **every array is copied back**, as the emulator path does
+   (launcher.py:209-211), so in-place outputs behave the same;
+3. the accessed extent of every buffer is checked against its size before
+   anything launches (the kernels trust their pointers);
+4. one ``extern "C"`` entry point of libpiton_b200.so runs on the current
+   torch stream; its status code becomes a Python exception.
+
+A kernel (or constexpr combination) without a B200 implementation raises
+``NotImplementedError``; there is no CPU fallback.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from ..launcher import offset_ptr, _is_torch_tensor
+from . import _lib
+from ._lib import check, lib
+
+_REGISTRY = {}
+_WORKSPACE = {}
+
+
+def register(name: str, params: tuple):
+    def deco(fn):
+        _REGISTRY[(name, tuple(params))] = fn
+        return fn
+    return deco
+
+
+def registered():
+    return sorted(_REGISTRY)
+
+
+def _torch():
+    import torch
+    return torch
+
+
+class Buffer:
+    """A pointer argument resolved to a device address.
+
+    ``addr`` is the address the kernel indexes from; ``lo``/``hi`` bound the
+    element indices (relative to ``addr``) that lie inside the allocation."""
+
+    def __init__(self, name, value, device):
+        torch = _torch()
+        self.name = name
+        off = 0
+        base = value
+        if isinstance(value, offset_ptr):
+            base, off = value.base, value.elements
+        self.host = None
+        if isinstance(base, np.ndarray):
+            self.host = base
+            host_t = torch.from_numpy(np.ascontiguousarray(base).reshape(-1))
+            self.tensor = host_t.to(device, non_blocking=host_t.is_pinned())
+        elif _is_torch_tensor(base):
+            if base.device.type != "cuda":
+                raise TypeError(f"argument {name}: tensor on {base.device}, expected a CUDA tensor or numpy array")
+            self.tensor = base
+        else:
+            raise TypeError(f"argument {name}: expected an array, got {type(base).__name__}")
+        t = self.tensor
+        self.itemsize = t.element_size()
+        storage_elems = t.untyped_storage().nbytes() // self.itemsize
+        start = t.storage_offset() if self.host is None else 0
+        self.addr = t.data_ptr() + off * self.itemsize
+        self.lo = -(start + off)
+        self.hi = storage_elems - start - off - 1
+
+    def require(self, lo: int, hi: int):
+        """Every index in [lo, hi] (relative to addr) must be inside the buffer."""
+        if hi < lo:
+            return
+        if lo < self.lo or hi > self.hi:
+            raise ValueError(f"argument {self.name}: the launch reads/writes elements [{lo}, {hi}] "
+                             f"but the buffer holds [{self.lo}, {self.hi}]")
+
+    def copy_back(self):
+        if self.host is not None:
+            self.host[...] = self.tensor.cpu().numpy().reshape(self.host.shape)
+
+
+def extent(*dims):
+    """(min, max) of sum(i_k * stride_k) over 0 <= i_k < n_k; dims = (n, stride) pairs."""
+    lo = hi = 0
+    for n, s in dims:
+        if n <= 0:
+            return 0, -1
+        lo += min(0, (n - 1) * s)
+        hi += max(0, (n - 1) * s)
+    return lo, hi
+
+
+class Launch:
+    """State of one B200 launch: marshalled buffers, the stream, the flags."""
+
+    def __init__(self, values, constants, device, qpu):
+        self.args = dict(constants)
+        self.args.update(values)
+        self.device = device
+        self.qpu = qpu
+        self.buffers = {}
+        torch = _torch()
+        self.stream = torch.cuda.current_stream(device)
+        self.stream_ptr = C.c_void_p(self.stream.cuda_stream)
+        self.ev0 = torch.cuda.Event(enable_timing=True)
+        self.ev1 = torch.cuda.Event(enable_timing=True)
+        self.called = False
+
+    def call(self, fname: str, args, what: str):
+        """Run one C-ABI entry point on the launch's stream, timed with CUDA events."""
+        f = getattr(lib(), fname)
+        self.ev0.record(self.stream)
+        rc = f(C.byref(args), self.stream_ptr)
+        self.ev1.record(self.stream)
+        self.called = True
+        check(rc, what)
+
+    def ptr(self, name) -> Buffer:
+        if name not in self.buffers:
+            v = self.args[name]
+            self.buffers[name] = Buffer(name, v, self.device)
+        return self.buffers[name]
+
+    def int(self, name) -> int:
+        v = self.args[name]
+        if isinstance(v, (bool, np.bool_)):
+            return int(v)
+        if not isinstance(v, (int, np.integer)):
+            raise TypeError(f"argument {name}: expected an integer, got {type(v).__name__}")
+        return int(v)
+
+    def float(self, name) -> float:
+        return float(self.args[name])
+
+    def workspace(self, nbytes: int) -> int:
+        torch = _torch()
+        if nbytes == 0:
+            return 0
+        key = torch.cuda.current_device() if self.device is None else self.device
+        buf = _WORKSPACE.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device or "cuda")
+            _WORKSPACE[key] = buf
+        return buf.data_ptr()
+
+    def finish(self):
+        for b in self.buffers.values():
+            b.copy_back()
+
+
+def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
+    """Run one launch; returns its stats dict."""
+    fn = getattr(jitfn, "fn", jitfn)
+    name = getattr(fn, "__name__", str(fn))
+    params = tuple(getattr(jitfn, "arg_names", None) or fn.__code__.co_varnames[:fn.__code__.co_argcount])
+    handler = _REGISTRY.get((name, params))
+    if handler is None:
+        raise NotImplementedError(f"{name}{params} has no B200 implementation "
+                                  f"(registered: {[k[0] for k in registered()]})")
+    torch = _torch()
+    if not torch.cuda.is_available():
+        raise RuntimeError("device='b200' needs a CUDA device; none is visible")
+    lib()      # fail loudly before touching any buffer if the library is missing
+    dev = torch.device("cuda", device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(dev):
+        launch = Launch(values, constants, dev, qpu)
+        stats = dict(handler(launch, tuple(grid) + (1,) * (3 - len(grid))) or {})
+        if launch.called:
+            launch.ev1.synchronize()
+            stats["time_us"] = launch.ev0.elapsed_time(launch.ev1) * 1e3
+        launch.finish()
+    return stats
+
+
+def _flags(launch, allowed_qpu=True):
+    if launch.qpu and not allowed_qpu:
+        raise NotImplementedError("qpu_rounding is implemented for add, matmul and dense only")
+    return _lib.QPU_ROUNDING if launch.qpu else 0
+
+
+# ---------------------------------------------------------------------------------------
+# operators
+# ---------------------------------------------------------------------------------------
+
+@register("add_kernel", ("x_ptr", "y_ptr", "output_ptr", "n_elements", "BLOCK_SIZE"))
+def _add(L: Launch, grid):
+    n, blk = L.int("n_elements"), L.int("BLOCK_SIZE")
+    n_eff = max(0, min(n, grid[0] * blk))
+    x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr")
+    for b in (x, y, out):
+        b.require(0, n_eff - 1)
+    a = _lib.AddArgs(x.addr, y.addr, out.addr, n, blk, grid[0], _flags(L), 0)
+    L.call("piton_b200_add_f32", a, "add_kernel")
+    return {"bytes": 12 * n_eff, "flops": n_eff, "path": "add_vec4"}
+
+
+@register("softmax_kernel", ("output_ptr", "input_ptr", "input_row_stride", "output_row_stride", "n_cols",
+                             "BLOCK_SIZE"))
+def _softmax(L: Launch, grid):
+    rows, ncols, blk = grid[0], L.int("n_cols"), L.int("BLOCK_SIZE")
+    sin, sout = L.int("input_row_stride"), L.int("output_row_stride")
+    n = max(0, min(ncols, blk))
+    out, inp = L.ptr("output_ptr"), L.ptr("input_ptr")
+    inp.require(*extent((rows, sin), (n, 1)))
+    out.require(*extent((rows, sout), (n, 1)))
+    a = _lib.SoftmaxArgs(out.addr, inp.addr, sin, sout, ncols, blk, rows, _flags(L, False), 0)
+    L.call("piton_b200_softmax_f32", a, "softmax_kernel")
+    return {"bytes": 8 * rows * n, "flops": 4 * rows * n, "path": "softmax"}
+
+
+@register("matmul_kernel", ("a_ptr", "b_ptr", "c_ptr", "M", "N", "K", "stride_am", "stride_ak", "stride_bk",
+                            "stride_bn", "stride_cm", "stride_cn", "BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K",
+                            "GROUP_SIZE_M"))
+def _matmul(L: Launch, grid):
+    M, N, K = L.int("M"), L.int("N"), L.int("K")
+    s = {k: L.int(k) for k in ("stride_am", "stride_ak", "stride_bk", "stride_bn", "stride_cm", "stride_cn")}
+    bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
+    A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr")
+    if M > 0 and N > 0 and grid[0] > 0:
+        A.require(*extent((M, s["stride_am"]), (K, s["stride_ak"])))
+        B.require(*extent((K, s["stride_bk"]), (N, s["stride_bn"])))
+        Cb.require(*extent((M, s["stride_cm"]), (N, s["stride_cn"])))
+    a = _lib.MatmulArgs(A.addr, B.addr, Cb.addr, M, N, K, s["stride_am"], s["stride_ak"], s["stride_bk"],
+                        s["stride_bn"], s["stride_cm"], s["stride_cn"], bm, bn, bk, g, grid[0], 0, 0,
+                        _flags(L), 0)
+    ws = lib().piton_b200_matmul_workspace_size(C.byref(a))
+    a.workspace, a.workspace_bytes = L.workspace(ws), ws
+    L.call("piton_b200_matmul_f32", a, "matmul_kernel")
+    return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K,
+            "path": "tcgen05_3xtf32" if ws else "cuda_core"}
+
+
+@register("dense_layer_kernel", ("x_ptr", "w_ptr", "bias_ptr", "y_ptr", "M", "N", "K", "BLOCK_SIZE_M",
+                                 "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M", "ADD_BIAS", "RELU"))
+def _dense(L: Launch, grid):
+    M, N, K = L.int("M"), L.int("N"), L.int("K")
+    bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
+    add_bias, relu = bool(L.args["ADD_BIAS"]), bool(L.args["RELU"])
+    X, Wt, Y = L.ptr("x_ptr"), L.ptr("w_ptr"), L.ptr("y_ptr")
+    bias = L.ptr("bias_ptr") if add_bias else None
+    if M > 0 and grid[0] > 0:
+        X.require(0, M * K - 1)
+        Wt.require(0, K * N - 1)
+        Y.require(0, M * N - 1)
+        if bias is not None:
+            bias.require(0, N - 1)
+    a = _lib.DenseArgs(X.addr, Wt.addr, bias.addr if bias else 0, Y.addr, M, N, K, bm, bn, bk, g, grid[0],
+                       int(add_bias), int(relu), _flags(L), 0)
+    L.call("piton_b200_dense_f32", a, "dense_layer_kernel")
+    return {"bytes": 4 * (M * K + K * N + M * N + N), "flops": 2 * M * N * K, "path": "cuda_core"}
+
+
+@register("attn_fwd_kernel", ("Q", "K", "V", "Out", "sm_scale", "stride_qh", "stride_qm", "stride_kh", "stride_kn",
+                              "stride_kk", "stride_vh", "stride_vn", "stride_oh", "stride_om", "N_CTX", "HEAD_DIM",
+                              "BLOCK_M", "BLOCK_N", "CAUSAL", "EVEN_N"))
+def _attention(L: Launch, grid):
+    n_ctx, d = L.int("N_CTX"), L.int("HEAD_DIM")
+    bm, bn = L.int("BLOCK_M"), L.int("BLOCK_N")
+    causal, even = bool(L.args["CAUSAL"]), bool(L.args["EVEN_N"])
+    st = {k: L.int(k) for k in ("stride_qh", "stride_qm", "stride_kh", "stride_kn", "stride_kk", "stride_vh",
+                                "stride_vn", "stride_oh", "stride_om")}
+    heads = grid[1]
+    rows = max(0, min(n_ctx, grid[0] * bm))
+    keys = n_ctx if (causal or not even) else (n_ctx // bn) * bn
+    Q, K, V, O = L.ptr("Q"), L.ptr("K"), L.ptr("V"), L.ptr("Out")
+    if rows > 0 and heads > 0:
+        Q.require(*extent((heads, st["stride_qh"]), (rows, st["stride_qm"]), (d, 1)))
+        O.require(*extent((heads, st["stride_oh"]), (rows, st["stride_om"]), (d, 1)))
+        kmax = min(keys, rows) if causal else keys
+        K.require(*extent((heads, st["stride_kh"]), (kmax, st["stride_kn"]), (d, st["stride_kk"])))
+        V.require(*extent((heads, st["stride_vh"]), (kmax, st["stride_vn"]), (d, 1)))
+    a = _lib.AttentionArgs(Q.addr, K.addr, V.addr, O.addr, L.float("sm_scale"), st["stride_qh"], st["stride_qm"],
+                           st["stride_kh"], st["stride_kn"], st["stride_kk"], st["stride_vh"], st["stride_vn"],
+                           st["stride_oh"], st["stride_om"], n_ctx, d, bm, bn, grid[0], heads, int(causal),
+                           int(even), _flags(L, False), 0)
+    L.call("piton_b200_attention_f32", a, "attn_fwd_kernel")
+    flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
+    return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops, "path": "attention"}
+
+
+@register("layernorm_kernel", ("x_ptr", "out_ptr", "n", "eps", "BLOCK"))
+def _layernorm(L: Launch, grid):
+    rows, n, blk = grid[0], L.int("n"), L.int("BLOCK")
+    n_eff = max(0, min(n, blk))
+    X, Y = L.ptr("x_ptr"), L.ptr("out_ptr")
+    X.require(*extent((rows, blk), (n_eff, 1)))
+    Y.require(*extent((rows, blk), (n_eff, 1)))
+    a = _lib.LayernormArgs(X.addr, Y.addr, rows, n_eff, blk, blk, L.float("eps"), _flags(L, False), 0)
+    L.call("piton_b200_layernorm_f32", a, "layernorm_kernel")
+    return {"bytes": 8 * rows * n_eff, "flops": 5 * rows * n_eff, "path": "layernorm"}
+
+
+def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
+    """A numpy array in page-locked host memory (fast, asynchronous H2D/D2H)."""
+    torch = _torch()
+    t = torch.empty(int(np.prod(shape)), dtype=getattr(torch, np.dtype(dtype).name), pin_memory=True)
+    return t.numpy().reshape(shape)
+
+
+__all__ = ["run_on_b200", "register", "registered", "Buffer", "Launch", "extent", "pinned_empty", "lib", "check"]
