@@ -58,6 +58,8 @@ extern "C" {
 
 PITON_B200_API int piton_b200_abi_version(void);
 PITON_B200_API const char *piton_b200_last_error(void);
+/* Kernels this library has launched since it was loaded (all threads). */
+PITON_B200_API uint64_t piton_b200_launch_count(void);
 /* Make `device` current for the calling thread and create its context. */
 PITON_B200_API int piton_b200_init(int device);
 PITON_B200_API int piton_b200_device_count(int *count);

@@ -1,6 +1,7 @@
 // Runtime half of the C ABI: error state, device set-up, memory helpers and a
 // bounded stream wait.  The B200 counterpart of pi/runtime/piton_rt.c (mailbox
 // allocation, launch with a 20 s timeout, perf counters).
+#include <atomic>
 #include <chrono>
 #include <string>
 #include <thread>
@@ -23,7 +24,12 @@ int set_error(int code, const char *fmt, ...) {
 
 void clear_error() { g_last_error.clear(); }
 
-int check_launch(const char *what) {
+static std::atomic<uint64_t> g_launches{0};
+
+void count_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int check_launch(const char *what, int launches) {
+    count_launches(launches);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return set_error(PITON_B200_ECUDA, "%s: %s", what, cudaGetErrorString(err));
     return PITON_B200_OK;
@@ -49,6 +55,8 @@ using namespace piton;
 extern "C" {
 
 int piton_b200_abi_version(void) { return PITON_B200_ABI_VERSION; }
+
+uint64_t piton_b200_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char *piton_b200_last_error(void) { return g_last_error.c_str(); }
 

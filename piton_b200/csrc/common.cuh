@@ -17,10 +17,14 @@ int set_error(int code, const char *fmt, ...);
 void clear_error();
 
 // Maps the last CUDA error (launch configuration or a sticky fault) to a status.
-int check_launch(const char *what);
+int check_launch(const char *what, int launches = 1);
 
 // SM count of the current device (cached per device).
 int num_sms();
+
+// Counts this library's kernel launches (all threads); read with
+// piton_b200_launch_count().  check_launch() adds `n` per operator call.
+void count_launches(int n);
 
 inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 

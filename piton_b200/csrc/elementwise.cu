@@ -71,7 +71,7 @@ static int launch_add(const piton_add_args *a, cudaStream_t s, int64_t n) {
         if (blocks > 4 * num_sms()) blocks = 4 * num_sms();
         add_scalar_kernel<QPU><<<(unsigned)blocks, 256, 0, s>>>(x, y, out, 4 * n4, n);
     }
-    return check_launch("add");
+    return check_launch("add", (n4 > 0) + (rest > 0));
 }
 
 }  // namespace piton

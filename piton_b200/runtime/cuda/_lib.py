@@ -67,6 +67,7 @@ class LayernormArgs(C.Structure):
 PROTOTYPES = {
     "piton_b200_abi_version": (C.c_int, []),
     "piton_b200_last_error": (C.c_char_p, []),
+    "piton_b200_launch_count": (C.c_uint64, []),
     "piton_b200_init": (C.c_int, [C.c_int]),
     "piton_b200_device_count": (C.c_int, [C.POINTER(C.c_int)]),
     "piton_b200_malloc": (C.c_int, [C.POINTER(u64), C.c_size_t]),

@@ -1,0 +1,140 @@
+"""Causal / full attention on the B200 (examples/attention.py:33-113).
+
+Mirrors tests/test_attention.py of the reference: ATOL 2e-5 against float64
+and against the oracle (bit-exact with the emulator goldens), ragged N_CTX
+with sentinel rows past the end, multi-head runtime strides through the
+launcher, transposed K, hard attention, causal rows independent of future keys.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import golden_ids, goldens
+from oracle import oracle as O
+from piton_b200 import workloads as W
+from piton_b200.kernels import attn_fwd_kernel
+
+pytestmark = pytest.mark.gpu
+ATTN = goldens("attn_")
+ATOL = 2e-5
+
+
+def qkv(n, d, seed=0, gain=1.0, heads=None):
+    rng = np.random.default_rng(seed)
+    shape = (n, d) if heads is None else (heads, n, d)
+    q, k, v = (rng.standard_normal(shape).astype(np.float32) for _ in range(3))
+    return (q * np.float32(gain)).astype(np.float32), k, v
+
+
+def run(q, k, v, causal, block_m=2, block_n=16, k_layout="nd", out=None, even_n=None):
+    squeeze = q.ndim == 2
+    if squeeze:
+        q, k, v = q[None], k[None], v[None]
+    h, n, d = q.shape
+    kk = np.ascontiguousarray(k.transpose(0, 2, 1)) if k_layout == "dn" else k
+    s_kn, s_kk = (1, n) if k_layout == "dn" else (d, 1)
+    o = np.zeros_like(q) if out is None else out
+    even = (n % block_n == 0) if even_n is None else even_n
+    grid = (-(-n // block_m), h)
+    attn_fwd_kernel[grid](q, kk, v, o, float(1 / np.sqrt(d)), n * d, d, n * d, s_kn, s_kk, n * d, d,
+                          o.shape[-2] * d if o.ndim == 3 else 0, d, n, HEAD_DIM=d, BLOCK_M=block_m,
+                          BLOCK_N=block_n, CAUSAL=bool(causal), EVEN_N=bool(even), device="b200")
+    return o[0] if squeeze else o
+
+
+@pytest.mark.parametrize("n,d,block_m,block_n,causal", [
+    (64, 16, 2, 16, False), (64, 16, 2, 16, True), (64, 32, 2, 32, False), (64, 32, 2, 32, True),
+    (64, 32, 4, 16, False), (32, 64, 2, 16, True), (256, 128, 2, 16, True)])
+def test_matches_float64(cuda, n, d, block_m, block_n, causal):
+    q, k, v = qkv(n, d, seed=n + d + block_m)
+    out = run(q, k, v, causal, block_m, block_n)
+    assert np.isfinite(out).all()
+    np.testing.assert_allclose(out, O.attention_f64(q, k, v, causal), rtol=0, atol=ATOL)
+
+
+@pytest.mark.parametrize("g", ATTN, ids=golden_ids(ATTN))
+def test_matches_emulator_golden(cuda, g):
+    m = g.meta
+    q, k, v = W.attention_inputs(m["heads"], m["n"], m["d"], m["seed"])
+    out = run(q, k, v, m["causal"], m["block"][0], m["block"][1])
+    ref = O.qpu_attention(q, k, v, m["causal"], m["block"][0], m["block"][1])
+    np.testing.assert_allclose(out, ref, rtol=0, atol=ATOL)
+
+
+def test_config_b4_h4_s256_d64(cuda):
+    q, k, v = W.attention_inputs(16, 256, 64, 0)
+    out = run(q, k, v, True)
+    np.testing.assert_allclose(out, O.qpu_attention(q, k, v, True), rtol=0, atol=ATOL)
+    np.testing.assert_allclose(out, O.attention_f64(q, k, v, True), rtol=0, atol=ATOL)
+
+
+@pytest.mark.parametrize("n,causal", [(37, False), (37, True), (1, False), (17, True), (200, True)])
+def test_ragged_sequence_lengths(cuda, n, causal):
+    q, k, v = qkv(n, 16, seed=n)
+    sentinel = np.float32(-1234.5)
+    out = np.full((1, n + 3, 16), sentinel, np.float32)
+    run(q[None], k[None], v[None], causal, 2, 16, out=out)
+    np.testing.assert_array_equal(out[0, n:], sentinel)
+    np.testing.assert_allclose(out[0, :n], O.attention_f64(q, k, v, causal), rtol=0, atol=ATOL)
+    if n == 1:
+        np.testing.assert_array_max_ulp(out[0, :1], v, maxulp=2)
+
+
+def test_multi_head_runtime_strides_through_the_launcher(cuda):
+    heads, n, d, pad = 2, 48, 16, 8
+    rng = np.random.default_rng(5)
+    q_store = rng.standard_normal((heads, n, d + pad)).astype(np.float32)
+    k, v = (rng.standard_normal((heads, n, d)).astype(np.float32) for _ in range(2))
+    out = np.zeros((heads, n, d), np.float32)
+    attn_fwd_kernel[(n // 2, heads)](q_store, k, v, out, float(1 / np.sqrt(d)), n * (d + pad), d + pad, n * d, d, 1,
+                                     n * d, d, n * d, d, n, HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16, CAUSAL=True,
+                                     EVEN_N=True, device="b200")
+    ref = O.attention_f64(q_store[:, :, :d], k, v, causal=True)
+    np.testing.assert_allclose(out, ref, rtol=0, atol=ATOL)
+
+
+def test_transposed_k_layout_is_bit_identical(cuda):
+    q, k, v = qkv(32, 32, seed=11)
+    nd = run(q, k, v, False, 2, 16, k_layout="nd")
+    dn = run(q, k, v, False, 2, 16, k_layout="dn")
+    np.testing.assert_array_equal(nd.view(np.uint32), dn.view(np.uint32))
+
+
+def test_hard_attention_retrieves_values(cuda):
+    n = d = 32
+    rng = np.random.default_rng(3)
+    perm = rng.permutation(n)
+    k = np.eye(n, dtype=np.float32)
+    q = (1000.0 * np.eye(n, dtype=np.float32)[perm]).astype(np.float32)
+    v = rng.standard_normal((n, d)).astype(np.float32)
+    out = run(q, k, v, False, 2, 16)
+    np.testing.assert_array_max_ulp(out, v[perm], maxulp=2)
+
+
+def test_causal_rows_ignore_future_keys(cuda):
+    n, d = 48, 16
+    q, k, v = qkv(n, d, seed=8)
+    a = run(q, k, v, True)
+    k2, v2 = k.copy(), v.copy()
+    rng = np.random.default_rng(9)
+    k2[32:] = rng.standard_normal((n - 32, d)) * 10
+    v2[32:] = rng.standard_normal((n - 32, d)) * 10
+    b = run(q, k2, v2, True)
+    np.testing.assert_array_equal(a[:32].view(np.uint32), b[:32].view(np.uint32))
+    np.testing.assert_array_max_ulp(a[0], v[0], maxulp=2)
+    assert not np.array_equal(a[32:], b[32:])
+
+
+def test_large_scores_stay_finite(cuda):
+    q, k, v = qkv(48, 16, seed=4, gain=25.0)
+    out = run(q, k, v, False)
+    assert np.isfinite(out).all()
+    np.testing.assert_allclose(out, O.attention_f64(q, k, v, False), rtol=0, atol=ATOL)
+
+
+def test_even_n_promise_skips_ragged_tail_like_the_reference(cuda):
+    # EVEN_N=True on a non-causal launch with N_CTX % BLOCK_N != 0: the reference
+    # skips the last partial key block (examples/attention.py:104-111)
+    q, k, v = qkv(40, 16, seed=2)
+    out = run(q, k, v, False, 2, 16, even_n=True)
+    np.testing.assert_allclose(out, O.qpu_attention(q, k, v, False, 2, 16, even_n=True), rtol=0, atol=ATOL)

@@ -1,0 +1,119 @@
+"""Grouped tutorial matmul on the B200 (examples/kernels.py:18-57).
+
+* QPU rounding mode (CUDA cores, sequential k, round-toward-zero): bit-exact
+  with the oracle and the emulator goldens, negative C row stride included.
+* Default mode (tcgen05 3xTF32 where the layout allows, CUDA cores else):
+  normalised error max|C - C_oracle| / max|C_oracle| <= 2e-5 * sqrt(K), the
+  hot-path tolerance; the float64 product is also checked at fp32 level,
+  <= 1e-7 * sqrt(K) normalised (200x tighter), which plain TF32 would miss.
+"""
+
+import math
+
+import numpy as np
+import pytest
+
+import piton_b200 as triton
+from conftest import dot_error, golden_ids, goldens
+from oracle import oracle as O
+from piton_b200 import workloads as W
+from piton_b200.kernels import matmul_kernel
+from piton_b200.runtime.launcher import Launcher, offset_ptr
+
+pytestmark = pytest.mark.gpu
+MATMUL = goldens("matmul_")
+FP32_LEVEL = 1e-7      # normalised error per sqrt(K) against float64
+
+
+def launch(a, b, c, M, N, K, bm=8, bn=64, bk=8, g=8, grid=None, neg=False, qpu=False, c_arg=None):
+    grid = grid or (triton.cdiv(M, bm) * triton.cdiv(N, bn),)
+    scm = -N if neg else N
+    c_arg = c_arg if c_arg is not None else (offset_ptr(c, (M - 1) * N) if neg else c)
+    return Launcher(matmul_kernel, grid)(a, b, c_arg, M, N, K, K, 1, N, 1, scm, 1, BLOCK_SIZE_M=bm, BLOCK_SIZE_N=bn,
+                                          BLOCK_SIZE_K=bk, GROUP_SIZE_M=g, device="b200", qpu_rounding=qpu)
+
+
+@pytest.mark.parametrize("M,N,Kd", [(64, 64, 64), (72, 100, 64), (40, 70, 36), (16, 128, 32)])
+def test_reference_shapes(cuda, M, N, Kd):
+    rng = np.random.default_rng(42)
+    a = rng.standard_normal((M, Kd)).astype(np.float32)
+    b = rng.standard_normal((Kd, N)).astype(np.float32)
+    c = np.full((M, N), -1.0, np.float32)
+    launch(a, b, c, M, N, Kd, bk=4, g=4)
+    np.testing.assert_allclose(c, a @ b, rtol=1e-4, atol=1e-4)      # tests/test_kernels.py:50
+
+
+@pytest.mark.parametrize("g", MATMUL, ids=golden_ids(MATMUL))
+def test_qpu_mode_bit_exact_vs_emulator(cuda, g):
+    m = g.meta
+    M, N, K = m["M"], m["N"], m["K"]
+    a, b = W.matmul_inputs(M, N, K, m["seed"])
+    store = np.zeros((M, N), np.float32)
+    bm, bn, bk = m["block"]
+    launch(a, b, store, M, N, K, bm, bn, bk, m["group"], neg=m["negative_stride_cm"], qpu=True)
+    c = store[::-1] if m["negative_stride_cm"] else store
+    ref = O.qpu_matmul(a, b, threads=8)
+    np.testing.assert_array_equal(np.ascontiguousarray(c).view(np.uint32), ref.view(np.uint32))
+    if "c" in g:
+        np.testing.assert_array_equal(np.ascontiguousarray(c).view(np.uint32), g["c"].view(np.uint32))
+
+
+@pytest.mark.parametrize("M,N,K,neg", [(128, 128, 128, False), (512, 512, 512, False), (1024, 1024, 1024, False),
+                                       (1000, 777, 513, True)])
+def test_config_shapes_within_dot_tolerance(cuda, M, N, K, neg):
+    a, b = W.matmul_inputs(M, N, K, 0)
+    store = np.zeros((M, N), np.float32)
+    stats = launch(a, b, store, M, N, K, bk=4 if K % 8 else 8, neg=neg).last_stats
+    c = store[::-1] if neg else store
+    ref = O.qpu_matmul(a, b, threads=8)
+    assert dot_error(c, ref) <= 2e-5 * math.sqrt(K), stats
+    exact = a.astype(np.float64) @ b.astype(np.float64)
+    assert dot_error(c, exact) <= FP32_LEVEL * math.sqrt(K), stats
+
+
+def test_partial_grid_only_writes_its_tiles(cuda):
+    M, N, K = 40, 200, 24
+    a, b = W.matmul_inputs(M, N, K, 3)
+    c = np.full((M, N), 9.0, np.float32)
+    bm, bn, g = 8, 64, 2
+    grid = 7                                   # of 5 * 4 = 20 programs
+    launch(a, b, c, M, N, K, bm, bn, 8, g, grid=(grid,))
+    num_pid_m, num_pid_n = 5, 4
+    expect = np.full((M, N), 9.0, np.float32)
+    full = a @ b
+    for pid in range(grid):                    # the grouped order of examples/kernels.py:26-35
+        group_id = pid // (g * num_pid_n)
+        first = group_id * g
+        gsize = min(num_pid_m - first, g)
+        pm = first + (pid % (g * num_pid_n)) % gsize
+        pn = (pid % (g * num_pid_n)) // gsize
+        expect[pm * bm:(pm + 1) * bm, pn * bn:(pn + 1) * bn] = full[pm * bm:(pm + 1) * bm, pn * bn:(pn + 1) * bn]
+    np.testing.assert_allclose(c, expect, rtol=1e-5, atol=1e-5)
+    assert np.all(c[expect == 9.0] == 9.0)
+
+
+def test_strided_and_transposed_operands(cuda):
+    torch = cuda
+    M, N, K = 96, 80, 72
+    A = torch.randn(K, M, device="cuda").t()            # stride_am = 1, stride_ak = M
+    B = torch.randn(N, K, device="cuda").t()            # stride_bk = 1, stride_bn = K
+    C = torch.zeros(N, M, device="cuda").t()            # stride_cm = 1, stride_cn = M
+    Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, A.stride(0), A.stride(1), B.stride(0), B.stride(1), C.stride(0), C.stride(1),
+        BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200")
+    torch.testing.assert_close(C, (A.double() @ B.double()).float(), rtol=1e-5, atol=1e-4)
+
+
+@pytest.mark.parametrize("M,N,K", [(2048, 2048, 2048), (256, 384, 1000), (4096, 256, 512)])
+def test_tensor_core_path_large(cuda, M, N, K):
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(M + N + K)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    C = torch.empty(M, N, device="cuda")
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
+        device="b200").last_stats
+    ref = A.double() @ B.double()
+    err = float((C.double() - ref).abs().max() / ref.abs().max())
+    assert err <= FP32_LEVEL * math.sqrt(K), (err, st)
