@@ -403,8 +403,12 @@ def main():
     ap.add_argument("--ops", default="matmul,softmax,attention,add")
     ap.add_argument("--cpu-rows", type=int, default=48, help="rows of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--mm-size", type=int, default=MM, help="matmul M=N=K (profiling runs use a smaller case)")
+    ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    global MM
+    MM = args.mm_size
     if args.impl == "reference":
         return run_reference(args)
 
@@ -428,7 +432,7 @@ def main():
             res["add"] = bench_add(torch, D, args, lib_calls)
     finally:
         sampler.stop()
-    e2e = e2e_matmul(torch, D, max(2, args.steps // 5)) if "matmul" in ops else None
+    e2e = e2e_matmul(torch, D, max(2, args.steps // 5)) if "matmul" in ops and not args.no_e2e else None
     tf32 = tf32_peak(torch) if "matmul" in ops else None
     D.close()
     if D.rank != 0:

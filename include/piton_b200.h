@@ -72,6 +72,10 @@ PITON_B200_API int piton_b200_memset(uint64_t dst, int value, size_t bytes, void
    after `timeout_s` seconds instead of blocking for ever
    (the counterpart of piton_rt.c:150-189's 20 s launch timeout). */
 PITON_B200_API int piton_b200_stream_wait(void *stream, double timeout_s);
+/* Device-side status of the current device's tensor-core kernels, then reset to 0:
+   0 = ok, else the bounded wait that ran out (1 producer, 2 MMA, 3 epilogue, 4 drain).
+   Those kernels never trap or spin for ever: they record this, drain and return. */
+PITON_B200_API int piton_b200_device_status(int *status);
 
 /* ---- vector add: examples/kernels.py:6-15 add_kernel ---- */
 typedef struct {

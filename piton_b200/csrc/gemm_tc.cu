@@ -1,9 +1,396 @@
-// tcgen05 3xTF32 GEMM: placeholder until the tensor-core path lands.
+// fp32 GEMM on the 5th-generation tensor cores with the 3xTF32 split
+// (tutorial matmul, examples/kernels.py:18-57, default rounding mode).
+//
+// fp32 accuracy from TF32 tensor cores: each operand x is split into
+// x_hi = x with the low 13 mantissa bits cleared (exactly representable in
+// TF32) and x_lo = tf32(x - x_hi), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi,
+// accumulated in fp32 in tensor memory.  The dropped A_lo B_lo term and the
+// truncation of x_lo are below 2^-21 relative to each product.
+//
+// Two kernels per call:
+//  1. split: reads A and B with their (arbitrary) element strides and writes
+//     A_hi, A_lo as [M, ld] and B_hi, B_lo transposed as [N, ld] (K-major,
+//     ld = K rounded up to 4) into the caller's workspace.  HBM-bound.
+//  2. gemm: persistent, one CTA per SM (320 threads): warp 0 issues TMA tile
+//     loads (128x16 A tiles, 256x16 B tiles, 64-byte swizzle, 4-stage
+//     mbarrier ring), warp 1 owns 512 TMEM columns (two 128x256 fp32
+//     accumulators) and issues tcgen05.mma kind::tf32 128x256x8 from one
+//     thread, warps 2-9 drain finished accumulators with tcgen05.ld.
+//
+// The tensor cores add into the TMEM accumulator with truncation, and that
+// bias grows with the number of accumulation steps (at K = 8192 it is ~30x
+// the error of an fp32 FFMA loop).  So an accumulator only ever holds a chunk
+// of KC = 256 k-values: the MMA warp alternates between the two TMEM
+// buffers per chunk, and the epilogue warps add every finished chunk into an
+// fp32 register sum (round to nearest), then store the tile with C's element
+// strides.  The error is then at the level of an fp32 FFMA loop.
+// Every mbarrier wait is bounded (2 s of global time): on expiry the kernel
+// records a status word, drains its own TMA copies and MMAs, frees TMEM and
+// returns.
+#include <vector>
+
 #include "common.cuh"
 #include "gemm_tc.cuh"
+#include "sm100.cuh"
 
 namespace piton {
-bool tc_gemm_supported(const TcGemmShape &) { return false; }
-size_t tc_gemm_workspace_bytes(const TcGemmShape &) { return 0; }
-int tc_gemm(const TcGemmShape &, void *, cudaStream_t) { return set_error(PITON_B200_ENOTSUP, "tensor-core GEMM not built"); }
+
+using namespace sm100;
+
+__device__ int g_tc_status = 0;
+
+namespace {
+
+constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int THREADS = 320;
+constexpr int EPI_WARPS = 8;
+constexpr int KC_BLOCKS = 16;   // k-blocks of BK per accumulation chunk (KC = 256)
+constexpr uint32_t A_TILE_BYTES = BM * BK * 4;   // 8 KB
+constexpr uint32_t B_TILE_BYTES = BN * BK * 4;   // 16 KB
+constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;   // 48 KB
+constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+constexpr int TMEM_COLS = 512;
+constexpr int GROUP_M = 16;
+
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+
+// dst_hi/lo[r * ld + c] from src[r * s_row + c * s_col], r < rows, c < cols, through
+// 32 x 32 shared-memory tiles so that both the strided read and the write coalesce.
+__global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                    int64_t s_row, int64_t s_col, float *__restrict__ hi,
+                                                    float *__restrict__ lo, int64_t ld, int lanes_along_rows) {
+    __shared__ float tile[32][33];
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;    // 32 x 8
+    for (int j = ty; j < 32; j += 8) {
+        int64_t r = lanes_along_rows ? r0 + tx : r0 + j;
+        int64_t c = lanes_along_rows ? c0 + j : c0 + tx;
+        float v = (r < rows && c < cols) ? src[r * s_row + c * s_col] : 0.0f;
+        if (lanes_along_rows) tile[tx][j] = v;
+        else tile[j][tx] = v;
+    }
+    __syncthreads();
+    for (int j = ty; j < 32; j += 8) {
+        int64_t r = r0 + j, c = c0 + tx;
+        if (r < rows && c < cols) {
+            float v = tile[j][tx];
+            float h = tf32_trunc(v);
+            float l = isfinite(v) ? tf32_trunc(v - h) : 0.0f;
+            hi[r * ld + c] = h;
+            lo[r * ld + c] = l;
+        }
+    }
+}
+
+struct GemmArgs {
+    float *c;
+    int64_t M, N, K, scm, scn;
+    int tiles_m, tiles_n, num_tiles, k_blocks;
+};
+
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
+    int per_group = GROUP_M * tiles_n;
+    int group = t / per_group;
+    int first = group * GROUP_M;
+    int gsize = min(tiles_m - first, GROUP_M);
+    int in = t % per_group;
+    tm = first + in % gsize;
+    tn = in / gsize;
+}
+
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
+
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                       const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                       GemmArgs args) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *empty = full + STAGES;
+    uint64_t *tfull = empty + STAGES;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], EPI_WARPS);
+        }
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        prefetch_tmap(&tm_ahi);
+        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_bhi);
+        prefetch_tmap(&tm_blo);
+    }
+    if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_holder);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+
+    const int kb_total = args.k_blocks;
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+                int tm, tn;
+                tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+                for (int kb = 0; kb < kb_total; ++kb, ++it) {
+                    uint32_t s = it % STAGES, round = it / STAGES;
+                    if (!mbar_wait(&empty[s], (round & 1) ^ 1)) {
+                        record_status(STATUS_TIMEOUT_PRODUCER);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *st = smem + s * STAGE_BYTES;
+                    mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
+                    int kx = kb * BK;
+                    tma_load_2d(st, &tm_ahi, &full[s], kx, tm * BM);
+                    tma_load_2d(st + A_TILE_BYTES, &tm_alo, &full[s], kx, tm * BM);
+                    tma_load_2d(st + 2 * A_TILE_BYTES, &tm_bhi, &full[s], kx, tn * BN);
+                    tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_blo, &full[s], kx, tn * BN);
+                }
+            }
+            // drain: every copy this thread issued has landed before the CTA may exit
+            uint32_t first = it > STAGES ? it - STAGES : 0;
+            for (uint32_t j = first; j < it; ++j)
+                if (!mbar_wait(&full[j % STAGES], (j / STAGES) & 1)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+            uint32_t it = 0, chunk = 0;
+            bool ok = true;
+            for (int t = blockIdx.x; ok && t < args.num_tiles && !*abort_flag; t += gridDim.x) {
+                for (int kb0 = 0; ok && kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk) {
+                    const int acc = chunk & 1;
+                    const uint32_t use = chunk >> 1;
+                    if (!mbar_wait(&tempty[acc], (use & 1) ^ 1)) {
+                        record_status(STATUS_TIMEOUT_MMA);
+                        *abort_flag = 1;
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * BN;
+                    const int kb1 = min(kb0 + KC_BLOCKS, kb_total);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        uint32_t s = it % STAGES, round = it / STAGES;
+                        if (!mbar_wait(&full[s], round & 1)) {
+                            record_status(STATUS_TIMEOUT_MMA);
+                            *abort_flag = 1;
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+                        uint32_t a_hi = base, a_lo = base + A_TILE_BYTES;
+                        uint32_t b_hi = base + 2 * A_TILE_BYTES, b_lo = b_hi + B_TILE_BYTES;
+#pragma unroll
+                        for (int ks = 0; ks < BK / 8; ++ks) {
+                            uint32_t off = ks * 32;   // 8 tf32 = 32 bytes along K inside the swizzled row
+                            uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
+                            mma_tf32(d_tmem, dal, dbh, IDESC, first);   // A_lo B_hi
+                            mma_tf32(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
+                            mma_tf32(d_tmem, dah, dbh, IDESC, 1u);      // A_hi B_hi
+                        }
+                        mma_commit(&empty[s]);   // stage s free once these MMAs have read it
+                    }
+                    if (!ok) break;
+                    mma_commit(&tfull[acc]);     // chunk ready for the epilogue
+                }
+            }
+            // drain: all MMAs issued by this thread complete before TMEM is freed
+            mma_commit(drain);
+            if (!mbar_wait(drain, 0)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else {
+        // ---------------- epilogue (warps 2-9) ----------------
+        const int quarter = warp & 3;                 // TMEM lanes [32*quarter, 32*quarter + 32)
+        const int half = (warp - 2) >> 2;             // columns [128*half, 128*half + 128)
+        float sum[BN / 2];
+        uint32_t chunk = 0;
+        bool ok = true;
+        for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+            for (int kb0 = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk) {
+                const int acc = chunk & 1;
+                const uint32_t use = chunk >> 1;
+                bool got = !*abort_flag && mbar_wait(&tfull[acc], use & 1);
+                if (!__all_sync(0xffffffffu, got)) {   // one decision per warp: tcgen05.ld is warp-wide
+                    if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BN + half * (BN / 2);
+                if (kb0 == 0) {
+#pragma unroll
+                    for (int j = 0; j < BN / 2; ++j) sum[j] = 0.0f;
+                }
+#pragma unroll
+                for (int part = 0; part < BN / 2 / 16; ++part) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + part * 16, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum[part * 16 + j] += __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[acc]);   // TMEM buffer free for the next chunk
+            }
+            if (!ok) break;
+            int tm, tn;
+            tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+            const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
+            if (row < args.M) {
+                float *crow = args.c + row * args.scm;
+                const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
+                const bool vec = args.scn == 1 &&
+                                 ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0 &&
+                                 col0 + BN / 2 <= args.N;
+                if (vec) {
+#pragma unroll
+                    for (int j = 0; j < BN / 2; j += 4)
+                        *reinterpret_cast<float4 *>(crow + col0 + j) =
+                            make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                } else {
+#pragma unroll
+                    for (int j = 0; j < BN / 2; ++j)
+                        if (col0 + j < args.N) crow[(col0 + j) * args.scn] = sum[j];
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc<TMEM_COLS>(tmem_base);
+    }
+}
+
+// ---- host side -------------------------------------------------------------------
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+// Row-major [rows, ld] fp32 (inner extent `cols`), box [box_rows, BK], 64-byte swizzle.
+int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PITON_B200_OK;
+}
+
+int64_t ld_of(int64_t K) { return (K + 3) / 4 * 4; }
+size_t region(int64_t rows, int64_t K) { return ((size_t)rows * ld_of(K) * 4 + 1023) / 1024 * 1024; }
+
+}  // namespace
+
+bool tc_gemm_supported(const TcGemmShape &s) {
+    // tiny problems are cheaper on the CUDA cores; the tensor-core path needs a
+    // device new enough for cudaGetDriverEntryPoint to find the TMA encoder
+    if (s.M < 128 || s.N < 128 || s.K < 16) return false;
+    if ((double)s.M * s.N * s.K < 4.0e6) return false;
+    if (s.M > (1ll << 31) || s.N > (1ll << 31) || s.K > (1ll << 31)) return false;
+    if (cdiv(s.M, 32) > 65535 || cdiv(s.N, 32) > 65535) return false;   // split-kernel grid.y
+    return encode_fn() != nullptr;
+}
+
+size_t tc_gemm_workspace_bytes(const TcGemmShape &s) { return 2 * region(s.M, s.K) + 2 * region(s.N, s.K); }
+
+int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
+    const int64_t ld = ld_of(s.K);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    float *a_hi = reinterpret_cast<float *>(ws);
+    float *a_lo = reinterpret_cast<float *>(ws + region(s.M, s.K));
+    float *b_hi = reinterpret_cast<float *>(ws + 2 * region(s.M, s.K));
+    float *b_lo = reinterpret_cast<float *>(ws + 2 * region(s.M, s.K) + region(s.N, s.K));
+
+    // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves
+    {
+        dim3 ga((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.M, 32));
+        int along_rows_a = llabs(s.sam) < llabs(s.sak);
+        split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
+        dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
+        int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
+        split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_lo, ld, along_rows_b);
+    }
+    // 2. persistent tcgen05 GEMM
+    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    int rc;
+    if ((rc = make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) || (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
+        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, BN)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, BN)))
+        return rc;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr[dev] = true;
+    }
+    GemmArgs g;
+    g.c = s.c;
+    g.M = s.M; g.N = s.N; g.K = s.K; g.scm = s.scm; g.scn = s.scn;
+    g.tiles_m = (int)cdiv(s.M, BM);
+    g.tiles_n = (int)cdiv(s.N, BN);
+    g.num_tiles = g.tiles_m * g.tiles_n;
+    g.k_blocks = (int)cdiv(s.K, BK);
+    int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
+    gemm_3xtf32_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
+    return check_launch("gemm_3xtf32", 3);
+}
+
+int tc_status_read_and_clear(int *status) {
+    int zero = 0;
+    PITON_CUDA(cudaMemcpyFromSymbol(status, g_tc_status, sizeof(int)));
+    PITON_CUDA(cudaMemcpyToSymbol(g_tc_status, &zero, sizeof(int)));
+    return PITON_B200_OK;
+}
+
 }  // namespace piton
+
+extern "C" int piton_b200_device_status(int *status) {
+    PITON_REQUIRE(status != nullptr, "status is NULL");
+    return piton::tc_status_read_and_clear(status);
+}

@@ -76,6 +76,7 @@ PROTOTYPES = {
     "piton_b200_memcpy_d2h": (C.c_int, [C.c_void_p, u64, C.c_size_t, C.c_void_p]),
     "piton_b200_memset": (C.c_int, [u64, C.c_int, C.c_size_t, C.c_void_p]),
     "piton_b200_stream_wait": (C.c_int, [C.c_void_p, C.c_double]),
+    "piton_b200_device_status": (C.c_int, [C.POINTER(C.c_int)]),
     "piton_b200_add_f32": (C.c_int, [C.POINTER(AddArgs), C.c_void_p]),
     "piton_b200_softmax_f32": (C.c_int, [C.POINTER(SoftmaxArgs), C.c_void_p]),
     "piton_b200_matmul_workspace_size": (C.c_size_t, [C.POINTER(MatmulArgs)]),
