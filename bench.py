@@ -371,43 +371,44 @@ def run_reference(args):
     if D.rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    rows = args.cpu_rows
-    vals = []
-    for _ in range(args.warmup if args.warmup < 1 else 1):
-        cpu_baseline_matmul(max(1, rows // 8), threads)
-    t_all = 0.0
+    # calibrate on a 2-row sample, then size each step to ~min(10 s, 120 s / steps)
+    rate, _ = cpu_baseline_matmul(2, threads)
+    per_step = min(10.0, 120.0 / max(1, args.steps))
+    rows = max(1, min(MM, int(per_step * rate * 1e12 / (2.0 * MM * MM))))
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_baseline_matmul(max(1, rows // 4), threads)
+    vals, t_all = [], 0.0
     for _ in range(args.steps):
         v, sec = cpu_baseline_matmul(rows, threads)
         vals.append(v)
         t_all += sec
     value = statistics.median(vals)
-    sample = f"{rows} rows of C (of 8192) per step: {rows}x8192x8192 sequential-k round-toward-zero dots"
+    sample = (f"{rows} of 8192 rows of C per step ({rows}x8192x8192 multiply-adds), the oracle's restatement of the "
+              f"emulator's sequential-k round-toward-zero dot on {threads} threads")
     line = {"metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": args.gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * t_all / max(1, args.steps), "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": "matmul 8192x8192x8192 fp32, A,B ~ U[-1,1] (bounded row sample)"},
+            "config": {"workload": f"matmul C=A@B fp32 {MM}x{MM}x{MM}, A,B ~ U[-1,1] (bounded row sample)"},
             "impl": "reference",
-            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                             "sample": sample},
+            "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
             "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
     return 0
 
 
 def main():
+    global MM
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--ops", default="matmul,softmax,attention,add")
-    ap.add_argument("--cpu-rows", type=int, default=48, help="rows of the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mm-size", type=int, default=MM, help="matmul M=N=K (profiling runs use a smaller case)")
     ap.add_argument("--no-e2e", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    global MM
     MM = args.mm_size
     if args.impl == "reference":
         return run_reference(args)
@@ -485,10 +486,12 @@ def main():
     line["clocks"] = sampler.summary()
     if "matmul" in ops and D.world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        v, s = cpu_baseline_matmul(args.cpu_rows, threads)
+        rate, _ = cpu_baseline_matmul(2, threads)
+        rows = max(1, min(MM, int(15.0 * rate * 1e12 / (2.0 * MM * MM))))
+        v, s = cpu_baseline_matmul(rows, threads)
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
-                                "sample": f"{args.cpu_rows} rows of the 8192^3 product ({s:.1f} s), oracle "
-                                          f"restatement of the emulator's sequential-k RTZ dot"}
+                                "sample": f"{rows} of {MM} rows of the {MM}^3 product ({s:.1f} s): the oracle's "
+                                          f"restatement of the emulator's sequential-k round-toward-zero dot"}
     print(json.dumps(line), flush=True)
     return 0
 
