@@ -115,6 +115,17 @@ typedef struct {
 PITON_B200_API size_t piton_b200_matmul_workspace_size(const piton_matmul_args *args);
 PITON_B200_API int piton_b200_matmul_f32(const piton_matmul_args *args, void *stream);
 
+/* The same matmul for callers that cannot allocate device memory (hosts whose device memory is
+   fixed at start-up, plugin hosts that own every allocation, processes whose memory is all held
+   by another allocator's pool).  It has no counterpart in the reference.  The tensor-core path's scratch comes from one static device
+   array of PITON_B200_NOALLOC_SCRATCH_BYTES inside this library (held by every GPU that loads
+   it, until exit) instead of args->workspace, which is ignored; the call allocates nothing.
+   Problems whose scratch would exceed that size are rejected with PITON_B200_EINVAL.  The first
+   call on a device looks the array's address up (cudaGetSymbolAddress), so make it before any
+   stream capture.  All calls share the array: calls that overlap on the GPU race. */
+#define PITON_B200_NOALLOC_SCRATCH_BYTES (32u << 20)
+PITON_B200_API int piton_b200_matmul_f32_noalloc(const piton_matmul_args *args, void *stream);
+
 /* ---- dense layer Y = X W (+b) (ReLU): examples/nn_kernels.py:23-74 dense_layer_kernel ---- */
 typedef struct {
     uint64_t x, w, bias, y;  /* float*: X[M,K], W[K,N], bias[N], Y[M,N], contiguous row-major */

@@ -89,3 +89,80 @@ extern "C" int piton_b200_dense_f32(const piton_dense_args *a, void *stream) {
     p.check_grid = a->grid_x < grouped_tiles(a->M, a->N, a->block_m, a->block_n);
     return gemm_simt(p, (a->flags & PITON_B200_QPU_ROUNDING) != 0, as_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Matmul without any allocation by the caller or the library.
+//
+// Some callers cannot call cudaMalloc at all: real-time or embedded hosts
+// whose device memory is fixed at start-up, plugin hosts that hand out device
+// pointers but own every allocation themselves, and processes whose device
+// memory is all held by another allocator's pool.  For them this entry point
+// takes the tensor-core path's scratch
+// (the tf32 hi/lo operand split) from one file-scope device array instead of
+// the caller's workspace.  The array holds PITON_B200_NOALLOC_SCRATCH_BYTES;
+// every GPU that loads this library keeps it until the process exits.
+//
+// In host code `g_matmul_scratch` names a host-side stand-in, not a device
+// address, so the device address is looked up with cudaGetSymbolAddress once
+// per device (with that device current) on the first call there, and cached.
+// That first call should therefore come before any stream capture.  Every
+// call shares the array and it keeps the last call's contents; nothing in it
+// needs to start at zero (the split kernel writes every element the GEMM
+// reads).  Calls that overlap on the GPU (other streams, other host threads
+// on the same device) race on it and must be serialised by the caller.
+// ---------------------------------------------------------------------------
+
+#include <mutex>
+
+static __device__ __align__(256) uint8_t g_matmul_scratch[PITON_B200_NOALLOC_SCRATCH_BYTES];
+
+static void *noalloc_scratch(int *rc) {
+    static std::mutex mu;
+    static void *ptrs[64] = {nullptr};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) {
+        *rc = set_error(PITON_B200_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+        return nullptr;
+    }
+    if (dev < 0 || dev >= 64) {
+        *rc = set_error(PITON_B200_EINVAL, "device %d out of range", dev);
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    if (!ptrs[dev]) {
+        void *p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_matmul_scratch);
+        if (err != cudaSuccess) {
+            *rc = set_error(PITON_B200_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(err));
+            return nullptr;
+        }
+        ptrs[dev] = p;
+    }
+    *rc = PITON_B200_OK;
+    return ptrs[dev];
+}
+
+extern "C" int piton_b200_matmul_f32_noalloc(const piton_matmul_args *a, void *stream) {
+    int rc = check_matmul(a);
+    if (rc) return rc;
+    if (a->M == 0 || a->N == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->a && a->b && a->c, "NULL pointer");
+    if (!use_tc(a)) {
+        // the CUDA-core path uses no scratch at all
+        piton_matmul_args b = *a;
+        b.workspace = 0;
+        b.workspace_bytes = 0;
+        return piton_b200_matmul_f32(&b, stream);
+    }
+    size_t need = tc_gemm_workspace_bytes(tc_shape(a));
+    if (need > (size_t)PITON_B200_NOALLOC_SCRATCH_BYTES)
+        return set_error(PITON_B200_EINVAL,
+                         "matmul %lld x %lld x %lld needs %zu bytes of scratch; the no-alloc entry point holds %zu "
+                         "(use piton_b200_matmul_f32 with a workspace)",
+                         (long long)a->M, (long long)a->N, (long long)a->K, need,
+                         (size_t)PITON_B200_NOALLOC_SCRATCH_BYTES);
+    void *scratch = noalloc_scratch(&rc);
+    if (!scratch) return rc;
+    return tc_gemm(tc_shape(a), scratch, as_stream(stream));
+}

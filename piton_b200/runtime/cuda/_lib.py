@@ -16,6 +16,7 @@ LIB_PATH = os.environ.get("PITON_B200_LIB", os.path.join(PKG, "libpiton_b200.so"
 
 OK, EINVAL, ECUDA, ETIMEOUT, ENOTSUP, ENOMEM, EWORKSPACE = 0, -1, -2, -3, -4, -5, -6
 QPU_ROUNDING, FORCE_SIMT = 0x1, 0x2
+NOALLOC_SCRATCH_BYTES = 32 << 20   # PITON_B200_NOALLOC_SCRATCH_BYTES
 
 u64, i64, i32, u32, f64 = C.c_uint64, C.c_int64, C.c_int32, C.c_uint32, C.c_double
 
@@ -81,6 +82,7 @@ PROTOTYPES = {
     "piton_b200_softmax_f32": (C.c_int, [C.POINTER(SoftmaxArgs), C.c_void_p]),
     "piton_b200_matmul_workspace_size": (C.c_size_t, [C.POINTER(MatmulArgs)]),
     "piton_b200_matmul_f32": (C.c_int, [C.POINTER(MatmulArgs), C.c_void_p]),
+    "piton_b200_matmul_f32_noalloc": (C.c_int, [C.POINTER(MatmulArgs), C.c_void_p]),
     "piton_b200_dense_f32": (C.c_int, [C.POINTER(DenseArgs), C.c_void_p]),
     "piton_b200_mlp_f32": (C.c_int, [C.POINTER(MlpArgs), C.c_void_p]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
