@@ -7,8 +7,10 @@ operator the metric names first, sharded by M-tiles across ranks with an
 NCCL all-gather of C at the end of every step (strong scaling: the total
 problem is fixed).  The same line carries the other operators of the metric
 in ``secondary``: row softmax (M = 32768 x N = 16384, GB/s), causal
-attention (B=32, H=32, S=4096, D=64, TFLOP/s and GB/s) and vector add
-(n = 2^28, GB/s), each sharded the same way (rows / batch x head / elements).
+attention (B=32, H=32, S=4096, D=64, TFLOP/s and GB/s), vector add
+(n = 2^28, GB/s), the digits MLP on 1797 images (images/s) and TinyGPT
+greedy decoding at batch 1 and 256 (tokens/s), each sharded the same way
+(rows / batch x head / elements / images / sequences).
 
 Timing: W untimed warm-up steps, then K steps bracketed by a barrier and
 ``torch.cuda.synchronize()``, measured with CUDA events on the launching
@@ -298,6 +300,51 @@ def bench_add(torch, D, args, lib_calls):
     return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc}
 
 
+def bench_tinygpt(torch, D, args, lib_calls, batch):
+    from piton_b200 import tinygpt
+    model = tinygpt.TinyGPT(tinygpt.init_weights(0))
+    per = max(1, batch // D.world)
+    prompts = tinygpt.random_prompts(per, seed=100 + D.rank)
+    buf = np.zeros((per, tinygpt.CTX), np.int32)
+    buf[:, :tinygpt.PROMPT_LEN] = prompts
+    base = torch.from_numpy(buf).cuda()
+    toks = base.clone()
+    full = torch.empty(per * D.world, tinygpt.CTX, dtype=torch.int32, device="cuda") if D.world > 1 else toks
+
+    def step():
+        toks.copy_(base)
+        model.generate_device(toks, tinygpt.PROMPT_LEN, tinygpt.NEW_TOKENS)
+        D.allgather(torch, full, toks)
+
+    steps = max(2, args.steps // 4)
+    t = timed(torch, D, step, steps, args.warmup)
+    lib_calls["launches"] += steps * (tinygpt.PROMPT_LEN + tinygpt.NEW_TOKENS - 1)
+    return {"tokens": per * D.world * tinygpt.NEW_TOKENS, "t_step": t}
+
+
+def bench_mlp(torch, D, args, lib_calls):
+    from piton_b200 import digits, workloads as W
+    rows = 1797
+    per = -(-rows // D.world)
+    imgs = np.zeros((per, 64), np.uint8)
+    lo = D.rank * per
+    mine = W.digits_images(rows, 0)[lo:lo + per]
+    imgs[:len(mine)] = mine
+    model = digits.DigitsMLP(W.digits_model(0))
+    x = torch.from_numpy(imgs).cuda()
+    logits = torch.empty(per, 16, device="cuda")
+    pred = torch.empty(per, dtype=torch.int32, device="cuda")
+    full = torch.empty(per * D.world, dtype=torch.int32, device="cuda") if D.world > 1 else pred
+
+    def step():
+        model.forward_device(x, logits, pred)
+        D.allgather(torch, full, pred)
+
+    t = timed(torch, D, step, args.steps, args.warmup)
+    lib_calls["launches"] += args.steps
+    return {"images": rows, "t_step": t}
+
+
 def tf32_peak(torch):
     """cuBLAS TF32 GEMM throughput at 8192^3 (the denominator of the 3xTF32 roofline)."""
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -336,10 +383,10 @@ def e2e_matmul(torch, D, steps):
     grid = (triton.cdiv(mloc, 8) * triton.cdiv(N, 64),)
 
     def step():
-        matmul_kernel[grid](A, B, Cm, mloc, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
-                            BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200")
+        return matmul_kernel[grid](A, B, Cm, mloc, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
+                                   BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
 
-    step()
+    st = step()
     D.barrier(torch)
     t0 = time.perf_counter()
     s = torch.cuda.current_stream()
@@ -351,7 +398,7 @@ def e2e_matmul(torch, D, steps):
     e1.synchronize()
     sec = D.max(torch, max(e0.elapsed_time(e1) / 1e3, 0.0) / steps)
     _ = t0
-    return {"sec": sec, "h2d": 4 * (mloc * K + K * N), "d2h": 4 * mloc * N, "flops": 2.0 * M * N * K}
+    return {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"], "flops": 2.0 * M * N * K}
 
 
 def cpu_baseline_matmul(rows: int, threads: int):
@@ -403,7 +450,7 @@ def main():
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--ops", default="matmul,softmax,attention,add")
+    ap.add_argument("--ops", default="matmul,softmax,attention,add,mlp,tinygpt")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mm-size", type=int, default=MM, help="matmul M=N=K (profiling runs use a smaller case)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -431,6 +478,11 @@ def main():
             res["attention"] = bench_attention(torch, D, args, lib_calls)
         if "add" in ops:
             res["add"] = bench_add(torch, D, args, lib_calls)
+        if "mlp" in ops:
+            res["mlp"] = bench_mlp(torch, D, args, lib_calls)
+        if "tinygpt" in ops:
+            res["tinygpt_b1"] = bench_tinygpt(torch, D, args, lib_calls, D.world)
+            res["tinygpt_b256"] = bench_tinygpt(torch, D, args, lib_calls, 256)
     finally:
         sampler.stop()
     e2e = e2e_matmul(torch, D, max(2, args.steps // 5)) if "matmul" in ops and not args.no_e2e else None
@@ -454,6 +506,15 @@ def main():
                             "gbs": r["bytes"] / r["t_step"] / 1e9,
                             "kernel_tflops_per_gpu": r["local_flops"] / r["t_kernel"] / 1e12,
                             "ms_per_step": 1e3 * r["t_step"], "max_abs_err_vs_f64": r["err"]}
+    if "mlp" in res:
+        r = res["mlp"]
+        sec["mlp_digits_1797"] = {"value": r["images"] / r["t_step"], "unit": "images/s",
+                                  "ms_per_step": 1e3 * r["t_step"]}
+    for key in ("tinygpt_b1", "tinygpt_b256"):
+        if key in res:
+            r = res[key]
+            sec[key] = {"value": r["tokens"] / r["t_step"], "unit": "tokens/s", "ms_per_step": 1e3 * r["t_step"],
+                        "workload": "greedy decode of 64 tokens after 16-token prompts (79 launches per step)"}
     line = {"metric": METRIC, "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.rand / randn on device)"}

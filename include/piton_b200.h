@@ -179,6 +179,22 @@ typedef struct {
 } piton_layernorm_args;
 PITON_B200_API int piton_b200_layernorm_f32(const piton_layernorm_args *args, void *stream);
 
+/* ---- TinyGPT greedy decoding (a model the reference does not have; built from its pieces:
+   dense layers examples/nn_kernels.py:23-74, attention examples/attention.py:75-113, layer norm
+   tests/test_reroll_reduce.py:199-208).  Only vocab 65, d_model 128, 4 layers, 4 heads, context
+   128 is built.  tokens: int32 [batch, 128]; positions [0, prompt_len) hold the prompt, and
+   positions [prompt_len, prompt_len + new_tokens) receive the greedy tokens.  weights: packed fp32,
+   piton_b200_tinygpt_weight_floats() floats (layout in csrc/tinygpt.cu).  kv_cache: caller scratch,
+   fp32 [4][2][batch][128][128].  logits (optional): fp32 [batch, 65] of the last fed position. ---- */
+typedef struct {
+    uint64_t weights, kv_cache, tokens, logits;
+    int64_t batch, prompt_len, new_tokens;
+    int32_t vocab, d_model, n_layer, n_head, ctx;
+    uint32_t flags;
+} piton_tinygpt_args;
+PITON_B200_API int64_t piton_b200_tinygpt_weight_floats(void);
+PITON_B200_API int piton_b200_tinygpt_generate(const piton_tinygpt_args *args, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

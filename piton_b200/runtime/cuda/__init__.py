@@ -52,9 +52,12 @@ class Buffer:
     """A pointer argument resolved to a device address.
 
     ``addr`` is the address the kernel indexes from; ``lo``/``hi`` bound the
-    element indices (relative to ``addr``) that lie inside the allocation."""
+    element indices (relative to ``addr``) that lie inside the allocation.
+    numpy arrays are copied to a device buffer on the launch's stream
+    (asynchronously from page-locked memory); ``copy_back`` copies the device
+    buffer into the array again."""
 
-    def __init__(self, name, value, device):
+    def __init__(self, name, value, device, stream):
         torch = _torch()
         self.name = name
         off = 0
@@ -62,10 +65,15 @@ class Buffer:
         if isinstance(value, offset_ptr):
             base, off = value.base, value.elements
         self.host = None
+        self.h2d_bytes = 0
         if isinstance(base, np.ndarray):
             self.host = base
             host_t = torch.from_numpy(np.ascontiguousarray(base).reshape(-1))
-            self.tensor = host_t.to(device, non_blocking=host_t.is_pinned())
+            self.pinned = bool(host_t.is_pinned())
+            self.tensor = torch.empty(host_t.shape, dtype=host_t.dtype, device=device)
+            with torch.cuda.stream(stream):
+                self.tensor.copy_(host_t, non_blocking=self.pinned)
+            self.h2d_bytes = host_t.numel() * host_t.element_size()
         elif _is_torch_tensor(base):
             if base.device.type != "cuda":
                 raise TypeError(f"argument {name}: tensor on {base.device}, expected a CUDA tensor or numpy array")
@@ -88,9 +96,18 @@ class Buffer:
             raise ValueError(f"argument {self.name}: the launch reads/writes elements [{lo}, {hi}] "
                              f"but the buffer holds [{self.lo}, {self.hi}]")
 
-    def copy_back(self):
-        if self.host is not None:
+    def copy_back(self, stream):
+        """Enqueue the device-to-host copy; returns its byte count."""
+        if self.host is None:
+            return 0
+        torch = _torch()
+        if self.host.flags.c_contiguous:
+            dst = torch.from_numpy(self.host.reshape(-1))
+            with torch.cuda.stream(stream):
+                dst.copy_(self.tensor, non_blocking=self.pinned)
+        else:
             self.host[...] = self.tensor.cpu().numpy().reshape(self.host.shape)
+        return self.tensor.numel() * self.itemsize
 
 
 def extent(*dims):
@@ -113,6 +130,7 @@ class Launch:
         self.device = device
         self.qpu = qpu
         self.buffers = {}
+        self.written = set()
         torch = _torch()
         self.stream = torch.cuda.current_stream(device)
         self.stream_ptr = C.c_void_p(self.stream.cuda_stream)
@@ -129,10 +147,14 @@ class Launch:
         self.called = True
         check(rc, what)
 
-    def ptr(self, name) -> Buffer:
+    def ptr(self, name, written: bool = False) -> Buffer:
+        """The device buffer of pointer argument `name`; `written` marks the
+        arguments the operator stores to (the ones copied back)."""
         if name not in self.buffers:
             v = self.args[name]
-            self.buffers[name] = Buffer(name, v, self.device)
+            self.buffers[name] = Buffer(name, v, self.device, self.stream)
+        if written:
+            self.written.add(name)
         return self.buffers[name]
 
     def int(self, name) -> int:
@@ -158,8 +180,12 @@ class Launch:
         return buf.data_ptr()
 
     def finish(self):
-        for b in self.buffers.values():
-            b.copy_back()
+        """Copy the written arrays back to the host (the reference copies every
+        array back, launcher.py:209-211; arrays a kernel only reads come back
+        unchanged, so only the written ones need the copy)."""
+        d2h = sum(self.buffers[n].copy_back(self.stream) for n in self.written)
+        self.stream.synchronize()
+        return sum(b.h2d_bytes for b in self.buffers.values()), d2h
 
 
 def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
@@ -179,10 +205,10 @@ def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
     with torch.cuda.device(dev):
         launch = Launch(values, constants, dev, qpu)
         stats = dict(handler(launch, tuple(grid) + (1,) * (3 - len(grid))) or {})
+        h2d, d2h = launch.finish()
         if launch.called:
-            launch.ev1.synchronize()
             stats["time_us"] = launch.ev0.elapsed_time(launch.ev1) * 1e3
-        launch.finish()
+        stats["h2d_bytes"], stats["d2h_bytes"] = h2d, d2h
     return stats
 
 
@@ -200,7 +226,7 @@ def _flags(launch, allowed_qpu=True):
 def _add(L: Launch, grid):
     n, blk = L.int("n_elements"), L.int("BLOCK_SIZE")
     n_eff = max(0, min(n, grid[0] * blk))
-    x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr")
+    x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr", written=True)
     for b in (x, y, out):
         b.require(0, n_eff - 1)
     a = _lib.AddArgs(x.addr, y.addr, out.addr, n, blk, grid[0], _flags(L), 0)
@@ -214,7 +240,7 @@ def _softmax(L: Launch, grid):
     rows, ncols, blk = grid[0], L.int("n_cols"), L.int("BLOCK_SIZE")
     sin, sout = L.int("input_row_stride"), L.int("output_row_stride")
     n = max(0, min(ncols, blk))
-    out, inp = L.ptr("output_ptr"), L.ptr("input_ptr")
+    out, inp = L.ptr("output_ptr", written=True), L.ptr("input_ptr")
     inp.require(*extent((rows, sin), (n, 1)))
     out.require(*extent((rows, sout), (n, 1)))
     a = _lib.SoftmaxArgs(out.addr, inp.addr, sin, sout, ncols, blk, rows, _flags(L, False), 0)
@@ -229,7 +255,7 @@ def _matmul(L: Launch, grid):
     M, N, K = L.int("M"), L.int("N"), L.int("K")
     s = {k: L.int(k) for k in ("stride_am", "stride_ak", "stride_bk", "stride_bn", "stride_cm", "stride_cn")}
     bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
-    A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr")
+    A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True)
     if M > 0 and N > 0 and grid[0] > 0:
         A.require(*extent((M, s["stride_am"]), (K, s["stride_ak"])))
         B.require(*extent((K, s["stride_bk"]), (N, s["stride_bn"])))
@@ -250,7 +276,7 @@ def _dense(L: Launch, grid):
     M, N, K = L.int("M"), L.int("N"), L.int("K")
     bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
     add_bias, relu = bool(L.args["ADD_BIAS"]), bool(L.args["RELU"])
-    X, Wt, Y = L.ptr("x_ptr"), L.ptr("w_ptr"), L.ptr("y_ptr")
+    X, Wt, Y = L.ptr("x_ptr"), L.ptr("w_ptr"), L.ptr("y_ptr", written=True)
     bias = L.ptr("bias_ptr") if add_bias else None
     if M > 0 and grid[0] > 0:
         X.require(0, M * K - 1)
@@ -276,7 +302,7 @@ def _attention(L: Launch, grid):
     heads = grid[1]
     rows = max(0, min(n_ctx, grid[0] * bm))
     keys = n_ctx if (causal or not even) else (n_ctx // bn) * bn
-    Q, K, V, O = L.ptr("Q"), L.ptr("K"), L.ptr("V"), L.ptr("Out")
+    Q, K, V, O = L.ptr("Q"), L.ptr("K"), L.ptr("V"), L.ptr("Out", written=True)
     if rows > 0 and heads > 0:
         Q.require(*extent((heads, st["stride_qh"]), (rows, st["stride_qm"]), (d, 1)))
         O.require(*extent((heads, st["stride_oh"]), (rows, st["stride_om"]), (d, 1)))
@@ -296,7 +322,7 @@ def _attention(L: Launch, grid):
 def _layernorm(L: Launch, grid):
     rows, n, blk = grid[0], L.int("n"), L.int("BLOCK")
     n_eff = max(0, min(n, blk))
-    X, Y = L.ptr("x_ptr"), L.ptr("out_ptr")
+    X, Y = L.ptr("x_ptr"), L.ptr("out_ptr", written=True)
     X.require(*extent((rows, blk), (n_eff, 1)))
     Y.require(*extent((rows, blk), (n_eff, 1)))
     a = _lib.LayernormArgs(X.addr, Y.addr, rows, n_eff, blk, blk, L.float("eps"), _flags(L, False), 0)

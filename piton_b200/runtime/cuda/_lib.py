@@ -64,6 +64,12 @@ class LayernormArgs(C.Structure):
                 ("y_row_stride", i64), ("eps", f64), ("flags", u32), ("_pad", u32)]
 
 
+class TinyGPTArgs(C.Structure):
+    _fields_ = [("weights", u64), ("kv_cache", u64), ("tokens", u64), ("logits", u64), ("batch", i64),
+                ("prompt_len", i64), ("new_tokens", i64), ("vocab", i32), ("d_model", i32), ("n_layer", i32),
+                ("n_head", i32), ("ctx", i32), ("flags", u32)]
+
+
 # name -> (restype, argtypes); every function include/piton_b200.h declares
 PROTOTYPES = {
     "piton_b200_abi_version": (C.c_int, []),
@@ -87,11 +93,13 @@ PROTOTYPES = {
     "piton_b200_mlp_f32": (C.c_int, [C.POINTER(MlpArgs), C.c_void_p]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
     "piton_b200_layernorm_f32": (C.c_int, [C.POINTER(LayernormArgs), C.c_void_p]),
+    "piton_b200_tinygpt_weight_floats": (C.c_int64, []),
+    "piton_b200_tinygpt_generate": (C.c_int, [C.POINTER(TinyGPTArgs), C.c_void_p]),
 }
 
 STRUCTS = {"piton_add_args": AddArgs, "piton_softmax_args": SoftmaxArgs, "piton_matmul_args": MatmulArgs,
            "piton_dense_args": DenseArgs, "piton_mlp_args": MlpArgs, "piton_attention_args": AttentionArgs,
-           "piton_layernorm_args": LayernormArgs}
+           "piton_layernorm_args": LayernormArgs, "piton_tinygpt_args": TinyGPTArgs}
 
 _lib = None
 
