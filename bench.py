@@ -138,9 +138,10 @@ class Dist:
         self.pg.all_reduce(t, op=self.pg.ReduceOp.MAX)
         return float(t.item())
 
-    def allgather(self, torch, out, shard):
+    def allgather(self, torch, out, piece):
         if self.pg is not None:
-            self.pg.all_gather_into_tensor(out, shard)
+            from piton_b200 import sharding
+            sharding.gather(self.pg, out, piece)
 
     def close(self):
         if self.pg is not None:
@@ -165,8 +166,8 @@ def timed(torch, D, step, steps, warmup):
 
 
 def shard(n, world, rank):
-    per = n // world
-    return rank * per, per
+    from piton_b200 import sharding
+    return sharding.shard(n, world, rank)
 
 
 def bench_matmul(torch, D, args, lib_calls):
