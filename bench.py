@@ -171,7 +171,11 @@ def shard(n, world, rank):
 
 
 def bench_matmul(torch, D, args, lib_calls):
+    """Rank r computes rows [r*M/N, (r+1)*M/N) of C.  At N > 1 the all-gather is fused into the
+    GEMM epilogue (every finished tile is stored into each rank's full C over NVLink) and a
+    1-element NCCL all-reduce after it is the completion barrier."""
     import ctypes as C
+    from piton_b200 import sharding
     from piton_b200.runtime.cuda import _lib
     from piton_b200.runtime.cuda._lib import lib
     M = N = K = MM
@@ -180,7 +184,6 @@ def bench_matmul(torch, D, args, lib_calls):
     A = torch.rand(mloc, K, device="cuda", generator=g) * 2 - 1
     B = torch.rand(K, N, device="cuda", generator=torch.Generator(device="cuda").manual_seed(99)) * 2 - 1
     Cl = torch.empty(mloc, N, device="cuda")
-    Cfull = torch.empty(M, N, device="cuda") if D.world > 1 else Cl
     a = _lib.MatmulArgs(A.data_ptr(), B.data_ptr(), Cl.data_ptr(), mloc, N, K, K, 1, N, 1, N, 1, 8, 64, 8, 8,
                         (mloc // 8) * (N // 64), 0, 0, 0, 0)
     ws = lib().piton_b200_matmul_workspace_size(C.byref(a))
@@ -192,9 +195,21 @@ def bench_matmul(torch, D, args, lib_calls):
     def kernel_only():
         _lib.check(f(C.byref(a), stream), "matmul")
 
-    def step():
-        kernel_only()
-        D.allgather(torch, Cfull, Cl)
+    peer = None
+    if D.world > 1:
+        peer = sharding.PeerOutput(D.pg, M * N * 4)
+        gargs = _lib.AllgatherArgs()
+        for r, p in enumerate(peer.peer_ptrs):
+            gargs.peer_c[r] = p
+        gargs.world, gargs.rank, gargs.row_offset, gargs.ldc = D.world, D.rank, r0, N
+        done = torch.zeros(1, device="cuda")
+        fg = lib().piton_b200_matmul_allgather_f32
+
+        def step():
+            _lib.check(fg(C.byref(a), C.byref(gargs), stream), "matmul_allgather")
+            D.pg.all_reduce(done)
+    else:
+        step = kernel_only
 
     n0 = lib().piton_b200_launch_count()
     kernel_only()
@@ -204,9 +219,17 @@ def bench_matmul(torch, D, args, lib_calls):
     t_step = timed(torch, D, step, args.steps, args.warmup)
     lib_calls["launches"] += per_call * args.steps
     flops = 2.0 * M * N * K
-    # correctness spot check of this rank's first rows against float64
+    # correctness spot check of this rank's first rows against float64 (and, with the fused
+    # all-gather, of the rows every rank wrote into this rank's full C)
     ref = A[:4].double() @ B.double()
     err = float((Cl[:4].double() - ref).abs().max() / ref.abs().max())
+    if peer is not None:
+        torch.cuda.synchronize()
+        D.pg.barrier()
+        got = peer.read(r0 * N * 4, 4 * N * 4).view(np.float32).reshape(4, N)
+        err = max(err, float(np.abs(got - ref.cpu().numpy()).max() / float(ref.abs().max())))
+        D.pg.barrier()
+        peer.close()
     return {"flops": flops, "t_step": t_step, "t_kernel": t_kernel, "tc": ws > 0, "per_call": per_call,
             "err": err, "local_flops": 2.0 * mloc * N * K}
 
@@ -526,7 +549,8 @@ def main():
         peak = tf32 / 3.0
         line.update({"value": value, "unit": "TFLOP/s", "ms_per_step": 1e3 * r["t_step"],
                      "config": {"workload": f"matmul C=A@B fp32 {MM}x{MM}x{MM}, A,B ~ U[-1,1], sharded by M-tiles, "
-                                            f"NCCL all-gather of C each step",
+                                            f"all-gather of C each step" + (" fused into the GEMM epilogue (NVLink "
+                                            f"peer stores)" if D.world > 1 else ""),
                                 "M": MM, "N": MM, "K": MM, "parallelism": f"m-tiles x{D.world}",
                                 "l2": "inputs larger than L2 (A+B = 512 MB)",
                                 "path": "tcgen05 3xTF32" if r["tc"] else "CUDA-core fp32 FFMA"},

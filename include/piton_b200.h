@@ -126,6 +126,27 @@ PITON_B200_API int piton_b200_matmul_f32(const piton_matmul_args *args, void *st
 #define PITON_B200_NOALLOC_SCRATCH_BYTES (32u << 20)
 PITON_B200_API int piton_b200_matmul_f32_noalloc(const piton_matmul_args *args, void *stream);
 
+/* ---- matmul sharded by M rows with the output all-gather fused into the GEMM epilogue ----
+   No counterpart in the reference (it runs on one device); this is the north star's
+   "matmul by M-tiles + all-gather" as one kernel: this rank computes rows
+   [row_offset, row_offset + args->M) of the full C (args->c and stride_cm/cn are ignored), and
+   every finished tile is stored into each rank's full row-major C (peer_c[r], row stride ldc)
+   through NVLink peer stores.  peer_c holds device pointers valid in this process: the own
+   buffer and the others opened with piton_b200_ipc_open.  Tensor-core path only (ENOTSUP
+   otherwise).  Every rank must pass a barrier after its call before C is read anywhere. */
+typedef struct {
+    uint64_t peer_c[8];
+    int32_t world, rank;
+    int64_t row_offset;
+    int64_t ldc;
+} piton_allgather_args;
+PITON_B200_API int piton_b200_matmul_allgather_f32(const piton_matmul_args *args, const piton_allgather_args *g,
+                                                   void *stream);
+/* CUDA IPC of a cudaMalloc'd buffer (64-byte handle) for the peer pointers above. */
+PITON_B200_API int piton_b200_ipc_handle(uint64_t ptr, void *handle);
+PITON_B200_API int piton_b200_ipc_open(const void *handle, uint64_t *ptr);
+PITON_B200_API int piton_b200_ipc_close(uint64_t ptr);
+
 /* ---- dense layer Y = X W (+b) (ReLU): examples/nn_kernels.py:23-74 dense_layer_kernel ---- */
 typedef struct {
     uint64_t x, w, bias, y;  /* float*: X[M,K], W[K,N], bias[N], Y[M,N], contiguous row-major */

@@ -112,6 +112,29 @@ int piton_b200_memset(uint64_t dst, int value, size_t bytes, void *stream) {
     return PITON_B200_OK;
 }
 
+int piton_b200_ipc_handle(uint64_t ptr, void *handle) {
+    PITON_REQUIRE(ptr && handle, "NULL pointer");
+    cudaIpcMemHandle_t h;
+    PITON_CUDA(cudaIpcGetMemHandle(&h, reinterpret_cast<void *>(ptr)));
+    memcpy(handle, &h, sizeof h);
+    return PITON_B200_OK;
+}
+
+int piton_b200_ipc_open(const void *handle, uint64_t *ptr) {
+    PITON_REQUIRE(ptr && handle, "NULL pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void *p = nullptr;
+    PITON_CUDA(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+    *ptr = reinterpret_cast<uint64_t>(p);
+    return PITON_B200_OK;
+}
+
+int piton_b200_ipc_close(uint64_t ptr) {
+    PITON_CUDA(cudaIpcCloseMemHandle(reinterpret_cast<void *>(ptr)));
+    return PITON_B200_OK;
+}
+
 int piton_b200_stream_wait(void *stream, double timeout_s) {
     using clock = std::chrono::steady_clock;
     auto deadline = clock::now() + std::chrono::duration<double>(timeout_s);

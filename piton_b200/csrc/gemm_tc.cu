@@ -86,6 +86,9 @@ struct GemmArgs {
     float *c;
     int64_t M, N, K, scm, scn;
     int tiles_m, tiles_n, num_tiles, k_blocks;
+    int world, rank;                 // world > 0: all-gather epilogue into peer_c
+    int64_t row_offset, ldc_peer;
+    float *peer_c[MAX_PEERS];
 };
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
@@ -262,20 +265,39 @@ __global__ void __launch_bounds__(THREADS, 1)
             tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
             const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
             if (row < args.M) {
-                float *crow = args.c + row * args.scm;
                 const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
-                const bool vec = args.scn == 1 &&
-                                 ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0 &&
-                                 col0 + BN / 2 <= args.N;
-                if (vec) {
+                if (args.world > 0) {
+                    // all-gather epilogue: the tile goes straight into every rank's output over
+                    // NVLink (peer stores), starting with the next rank so the links share the load
+                    const bool full = col0 + BN / 2 <= args.N;
+                    for (int i = 1; i <= args.world; ++i) {
+                        float *crow = args.peer_c[(args.rank + i) % args.world] + (args.row_offset + row) * args.ldc_peer;
+                        if (full) {
 #pragma unroll
-                    for (int j = 0; j < BN / 2; j += 4)
-                        *reinterpret_cast<float4 *>(crow + col0 + j) =
-                            make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                            for (int j = 0; j < BN / 2; j += 4)
+                                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                    make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < BN / 2; ++j)
+                                if (col0 + j < args.N) crow[col0 + j] = sum[j];
+                        }
+                    }
                 } else {
+                    float *crow = args.c + row * args.scm;
+                    const bool vec = args.scn == 1 &&
+                                     ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0 &&
+                                     col0 + BN / 2 <= args.N;
+                    if (vec) {
 #pragma unroll
-                    for (int j = 0; j < BN / 2; ++j)
-                        if (col0 + j < args.N) crow[(col0 + j) * args.scn] = sum[j];
+                        for (int j = 0; j < BN / 2; j += 4)
+                            *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < BN / 2; ++j)
+                            if (col0 + j < args.N) crow[(col0 + j) * args.scn] = sum[j];
+                    }
                 }
             }
         }
@@ -376,6 +398,11 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.tiles_n = (int)cdiv(s.N, BN);
     g.num_tiles = g.tiles_m * g.tiles_n;
     g.k_blocks = (int)cdiv(s.K, BK);
+    g.world = s.world;
+    g.rank = s.rank;
+    g.row_offset = s.row_offset;
+    g.ldc_peer = s.ldc_peer;
+    for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     gemm_3xtf32_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
     return check_launch("gemm_3xtf32", 3);

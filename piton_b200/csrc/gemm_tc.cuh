@@ -6,11 +6,18 @@
 
 namespace piton {
 
+constexpr int MAX_PEERS = 8;
+
 struct TcGemmShape {
     const float *a, *b;
     float *c;
     int64_t M, N, K;
     int64_t sam, sak, sbk, sbn, scm, scn;
+    // all-gather epilogue (world > 0): every C tile is stored into each peer's
+    // row-major [*, ldc_peer] output at rows row_offset + m, instead of into c
+    int world = 0, rank = 0;
+    int64_t row_offset = 0, ldc_peer = 0;
+    float *peer_c[MAX_PEERS] = {};
 };
 
 // True when the tensor-core path can run this problem (layout and alignment).

@@ -166,3 +166,39 @@ extern "C" int piton_b200_matmul_f32_noalloc(const piton_matmul_args *a, void *s
     if (!scratch) return rc;
     return tc_gemm(tc_shape(a), scratch, as_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Matmul sharded by M rows with the output all-gather fused into the GEMM:
+// this rank computes rows [row_offset, row_offset + M) of the full C and the
+// epilogue stores every finished tile into each rank's full C through peer
+// pointers (NVLink stores, overlapped with the next tiles' MMAs), so no
+// separate all-gather runs.  The caller orders completion across ranks (a
+// barrier after the call on every rank) before reading C.
+// ---------------------------------------------------------------------------
+extern "C" int piton_b200_matmul_allgather_f32(const piton_matmul_args *a, const piton_allgather_args *g,
+                                               void *stream) {
+    int rc = check_matmul(a);
+    if (rc) return rc;
+    PITON_REQUIRE(g != nullptr, "allgather args is NULL");
+    PITON_REQUIRE(g->world >= 1 && g->world <= MAX_PEERS && g->rank >= 0 && g->rank < g->world,
+                  "world %d / rank %d outside 1..%d", g->world, g->rank, MAX_PEERS);
+    PITON_REQUIRE(g->row_offset >= 0 && g->ldc >= a->N && g->ldc % 4 == 0, "bad row_offset / ldc");
+    for (int i = 0; i < g->world; ++i)
+        PITON_REQUIRE(g->peer_c[i] != 0 && (g->peer_c[i] & 15) == 0, "peer output %d is NULL or misaligned", i);
+    if (a->M == 0 || a->N == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->a && a->b, "NULL pointer");
+    if (!use_tc(a))
+        return set_error(PITON_B200_ENOTSUP, "the all-gather matmul runs on the tensor-core path only "
+                                             "(full grid, no QPU rounding, M, N >= 128)");
+    size_t need = tc_gemm_workspace_bytes(tc_shape(a));
+    if (a->workspace_bytes < need || !a->workspace)
+        return set_error(PITON_B200_EWORKSPACE, "matmul needs %zu bytes of workspace, got %llu", need,
+                         (unsigned long long)a->workspace_bytes);
+    TcGemmShape t = tc_shape(a);
+    t.world = g->world;
+    t.rank = g->rank;
+    t.row_offset = g->row_offset;
+    t.ldc_peer = g->ldc;
+    for (int i = 0; i < g->world; ++i) t.peer_c[i] = reinterpret_cast<float *>(g->peer_c[i]);
+    return tc_gemm(t, reinterpret_cast<void *>(a->workspace), as_stream(stream));
+}

@@ -39,6 +39,10 @@ class MatmulArgs(C.Structure):
                 ("flags", u32), ("_pad", u32)]
 
 
+class AllgatherArgs(C.Structure):
+    _fields_ = [("peer_c", u64 * 8), ("world", i32), ("rank", i32), ("row_offset", i64), ("ldc", i64)]
+
+
 class DenseArgs(C.Structure):
     _fields_ = [("x", u64), ("w", u64), ("bias", u64), ("y", u64), ("M", i64), ("N", i64), ("K", i64),
                 ("block_m", i64), ("block_n", i64), ("block_k", i64), ("group_m", i64), ("grid_x", i64),
@@ -89,6 +93,10 @@ PROTOTYPES = {
     "piton_b200_matmul_workspace_size": (C.c_size_t, [C.POINTER(MatmulArgs)]),
     "piton_b200_matmul_f32": (C.c_int, [C.POINTER(MatmulArgs), C.c_void_p]),
     "piton_b200_matmul_f32_noalloc": (C.c_int, [C.POINTER(MatmulArgs), C.c_void_p]),
+    "piton_b200_matmul_allgather_f32": (C.c_int, [C.POINTER(MatmulArgs), C.POINTER(AllgatherArgs), C.c_void_p]),
+    "piton_b200_ipc_handle": (C.c_int, [u64, C.c_void_p]),
+    "piton_b200_ipc_open": (C.c_int, [C.c_void_p, C.POINTER(u64)]),
+    "piton_b200_ipc_close": (C.c_int, [u64]),
     "piton_b200_dense_f32": (C.c_int, [C.POINTER(DenseArgs), C.c_void_p]),
     "piton_b200_mlp_f32": (C.c_int, [C.POINTER(MlpArgs), C.c_void_p]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
@@ -97,7 +105,7 @@ PROTOTYPES = {
     "piton_b200_tinygpt_generate": (C.c_int, [C.POINTER(TinyGPTArgs), C.c_void_p]),
 }
 
-STRUCTS = {"piton_add_args": AddArgs, "piton_softmax_args": SoftmaxArgs, "piton_matmul_args": MatmulArgs,
+STRUCTS = {"piton_allgather_args": AllgatherArgs, "piton_add_args": AddArgs, "piton_softmax_args": SoftmaxArgs, "piton_matmul_args": MatmulArgs,
            "piton_dense_args": DenseArgs, "piton_mlp_args": MlpArgs, "piton_attention_args": AttentionArgs,
            "piton_layernorm_args": LayernormArgs, "piton_tinygpt_args": TinyGPTArgs}
 

@@ -40,3 +40,91 @@ def max_over_ranks(dist, value: float, device=None) -> float:
     t = torch.tensor([value], dtype=torch.float64, device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+class PeerOutput:
+    """A full-size output buffer on every rank whose peers' copies this process
+    can write: allocated with cudaMalloc (piton_b200_malloc), shared with CUDA
+    IPC handles exchanged over `dist`, opened with peer access.  `peer_ptrs[r]`
+    is rank r's buffer as an address valid in this process."""
+
+    def __init__(self, dist, nbytes: int):
+        import ctypes as C
+
+        from .runtime.cuda import _lib
+        lib = _lib.lib()
+        self._lib = lib
+        self.nbytes = nbytes
+        self.world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+        self.rank = dist.get_rank() if self.world > 1 else 0
+        ptr = C.c_uint64(0)
+        _lib.check(lib.piton_b200_malloc(C.byref(ptr), nbytes), "malloc")
+        self.ptr = ptr.value
+        self.opened = []
+        self.peer_ptrs = [0] * self.world
+        self.peer_ptrs[self.rank] = self.ptr
+        if self.world > 1:
+            h = (C.c_uint8 * 64)()
+            _lib.check(lib.piton_b200_ipc_handle(self.ptr, h), "ipc handle")
+            handles = [None] * self.world
+            dist.all_gather_object(handles, bytes(h))
+            for r, hb in enumerate(handles):
+                if r == self.rank:
+                    continue
+                buf = (C.c_uint8 * 64).from_buffer_copy(hb)
+                p = C.c_uint64(0)
+                _lib.check(lib.piton_b200_ipc_open(buf, C.byref(p)), "ipc open")
+                self.peer_ptrs[r] = p.value
+                self.opened.append(p.value)
+
+    def read(self, offset_bytes: int, nbytes: int):
+        """Copy bytes of this rank's buffer to a new numpy uint8 array (synchronous)."""
+        import ctypes as C
+
+        import numpy as np
+        out = np.empty(nbytes, np.uint8)
+        from .runtime.cuda import _lib
+        _lib.check(self._lib.piton_b200_memcpy_d2h(out.ctypes.data_as(C.c_void_p), self.ptr + offset_bytes, nbytes,
+                                                   None), "d2h")
+        _lib.check(self._lib.piton_b200_stream_wait(None, 60.0), "sync")
+        return out
+
+    def close(self):
+        for p in self.opened:
+            self._lib.piton_b200_ipc_close(p)
+        self.opened = []
+        if self.ptr:
+            self._lib.piton_b200_free(self.ptr)
+            self.ptr = 0
+
+
+def matmul_allgather(a_piece, b, out: "PeerOutput", row_offset: int, ldc: int, stream=None):
+    """This rank's rows of C = A @ B (a_piece [m, K], b [K, N] CUDA float32 tensors),
+    stored into every rank's full output by the fused all-gather epilogue."""
+    import ctypes as C
+
+    import torch
+
+    from .runtime.cuda import _lib
+    lib = _lib.lib()
+    m, K = a_piece.shape
+    N = b.shape[1]
+    a = _lib.MatmulArgs(a_piece.data_ptr(), b.data_ptr(), 0, m, N, K, a_piece.stride(0), a_piece.stride(1),
+                        b.stride(0), b.stride(1), N, 1, 8, 64, 8, 8, -(-m // 8) * -(-N // 64), 0, 0, 0, 0)
+    ws = lib.piton_b200_matmul_workspace_size(C.byref(a))
+    key = (torch.cuda.current_device(), "allgather_ws")
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < ws:
+        buf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+        _WS[key] = buf
+    a.workspace, a.workspace_bytes = buf.data_ptr(), ws
+    g = _lib.AllgatherArgs()
+    for r, p in enumerate(out.peer_ptrs):
+        g.peer_c[r] = p
+    g.world, g.rank, g.row_offset, g.ldc = out.world, out.rank, row_offset, ldc
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(lib.piton_b200_matmul_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
+               "matmul_allgather")
+
+
+_WS = {}

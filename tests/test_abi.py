@@ -32,9 +32,9 @@ def declared_structs():
             decl = decl.strip()
             if not decl:
                 continue
-            m = re.match(r"([\w\s]+?)\s+([\w\s,]+)$", decl)
+            m = re.match(r"([\w\s]+?)\s+([\w\s,\[\]]+)$", decl)
             assert m, decl
-            fields += [f.strip() for f in m.group(2).split(",")]
+            fields += [re.sub(r"\[\d+\]", "", f).strip() for f in m.group(2).split(",")]
         out[name] = fields
     return out
 

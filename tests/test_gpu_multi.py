@@ -1,0 +1,70 @@
+"""Multi-GPU matmul with the all-gather fused into the GEMM epilogue (NVLink peer
+stores), on 2 GPUs when the box has them (skipped otherwise).  Every rank must
+end with the full C = A @ B: rows computed by every rank are checked against
+float64 on every rank."""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    from piton_b200 import sharding
+    from piton_b200.runtime.cuda import _lib
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    out = None
+    try:
+        M, N, K = 1024, 768, 640
+        g = torch.Generator(device="cuda").manual_seed(5)
+        A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1      # same on every rank (same seed)
+        B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+        r0, per = sharding.shard(M, world, rank)
+        out = sharding.PeerOutput(dist, M * N * 4)
+        for _ in range(2):
+            sharding.matmul_allgather(A[r0:r0 + per], B, out, r0, N)
+            torch.cuda.synchronize()
+            dist.barrier()
+        full = out.read(0, M * N * 4).view(np.float32).reshape(M, N)
+        ref = (A.double() @ B.double()).cpu().numpy()
+        err = float(np.abs(full - ref).max() / np.abs(ref).max())
+        import ctypes as C
+        st = C.c_int(-1)
+        _lib.lib().piton_b200_device_status(C.byref(st))
+        results[rank] = (err, st.value)
+        dist.barrier()
+    finally:
+        if out is not None:
+            out.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allgather_matmul_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_worker, args=(2, _port(), results), nprocs=2, join=True)
+        res = dict(results)
+    assert len(res) == 2
+    for rank, (err, status) in res.items():
+        assert status == 0, rank
+        assert err <= 4e-6, (rank, err)
