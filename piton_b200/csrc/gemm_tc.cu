@@ -103,6 +103,34 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
 
+// All-gather epilogue: rows [r0, r1) of finished tile (tm, tn), already stored in
+// this rank's own output, are copied to every other rank's output (float4 peer
+// stores).  Called by the 256 epilogue threads (`et` = 0..255), a few rows per
+// accumulation chunk of the next tile, so the NVLink traffic is spread evenly
+// over the MMAs instead of bursting at the end of each tile.
+__device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int tm, int tn, int r0, int r1, int et) {
+    const float *src_base = args.peer_c[args.rank];
+    const int64_t col_base = (int64_t)tn * BN;
+    const int per_row = BN / 4;
+    for (int i = et; i < (r1 - r0) * per_row; i += 256) {
+        const int r = r0 + i / per_row, q = i % per_row;
+        const int64_t row = (int64_t)tm * BM + r;
+        const int64_t col = col_base + 4 * q;
+        if (row >= args.M || col >= args.N) continue;
+        const int64_t off = (args.row_offset + row) * args.ldc_peer + col;
+        if (col + 4 <= args.N) {
+            float4 v = *reinterpret_cast<const float4 *>(src_base + off);
+            for (int p = 1; p < args.world; ++p)
+                *reinterpret_cast<float4 *>(args.peer_c[(args.rank + p) % args.world] + off) = v;
+        } else {
+            for (int j = 0; col + j < args.N; ++j) {
+                float v = src_base[off + j];
+                for (int p = 1; p < args.world; ++p) args.peer_c[(args.rank + p) % args.world][off + j] = v;
+            }
+        }
+    }
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                        const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
@@ -114,7 +142,8 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *tfull = empty + STAGES;
     uint64_t *tempty = tfull + 2;
     uint64_t *drain = tempty + 2;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    uint64_t *epi_bar = drain + 1;   // the 8 epilogue warps: a finished tile is in the own output
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_bar + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -129,6 +158,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&tempty[b], EPI_WARPS);
         }
         mbar_init(drain, 1);
+        mbar_init(epi_bar, EPI_WARPS);
         *abort_flag = 0;
         fence_mbarrier_init();
         prefetch_tmap(&tm_ahi);
@@ -231,8 +261,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         float sum[BN / 2];
         uint32_t chunk = 0;
         bool ok = true;
+        const int et = threadIdx.x - 64;                      // epilogue thread index 0..255
+        const int n_chunks = (kb_total + KC_BLOCKS - 1) / KC_BLOCKS;
+        const int rows_per_chunk = (BM + n_chunks - 1) / n_chunks;
+        int pend_tm = -1, pend_tn = -1;                       // finished tile still to be sent to peers
+        uint32_t tiles_done = 0;
         for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
-            for (int kb0 = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk) {
+            for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk, ++ci) {
                 const int acc = chunk & 1;
                 const uint32_t use = chunk >> 1;
                 bool got = !*abort_flag && mbar_wait(&tfull[acc], use & 1);
@@ -259,6 +294,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[acc]);   // TMEM buffer free for the next chunk
+                if (args.world > 1 && pend_tm >= 0)
+                    copy_rows_to_peers(args, pend_tm, pend_tn, min(ci * rows_per_chunk, BM),
+                                       min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
             int tm, tn;
@@ -267,21 +305,18 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (row < args.M) {
                 const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
                 if (args.world > 0) {
-                    // all-gather epilogue: the tile goes straight into every rank's output over
-                    // NVLink (peer stores), starting with the next rank so the links share the load
-                    const bool full = col0 + BN / 2 <= args.N;
-                    for (int i = 1; i <= args.world; ++i) {
-                        float *crow = args.peer_c[(args.rank + i) % args.world] + (args.row_offset + row) * args.ldc_peer;
-                        if (full) {
+                    // all-gather epilogue: the tile goes into this rank's own full output now,
+                    // and to the other ranks' outputs during the next tile's chunks
+                    float *crow = args.peer_c[args.rank] + (args.row_offset + row) * args.ldc_peer;
+                    if (col0 + BN / 2 <= args.N) {
 #pragma unroll
-                            for (int j = 0; j < BN / 2; j += 4)
-                                *reinterpret_cast<float4 *>(crow + col0 + j) =
-                                    make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
-                        } else {
+                        for (int j = 0; j < BN / 2; j += 4)
+                            *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                    } else {
 #pragma unroll
-                            for (int j = 0; j < BN / 2; ++j)
-                                if (col0 + j < args.N) crow[col0 + j] = sum[j];
-                        }
+                        for (int j = 0; j < BN / 2; ++j)
+                            if (col0 + j < args.N) crow[col0 + j] = sum[j];
                     }
                 } else {
                     float *crow = args.c + row * args.scm;
@@ -300,7 +335,25 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
+            if (args.world > 1) {
+                // every epilogue warp has stored its part of the tile (bounded wait, not bar.sync:
+                // a warp that gave up must not leave the others waiting for ever)
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_bar);
+                bool got = mbar_wait(epi_bar, tiles_done & 1);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                pend_tm = tm;
+                pend_tn = tn;
+            }
+            ++tiles_done;
         }
+        if (ok && args.world > 1 && pend_tm >= 0) copy_rows_to_peers(args, pend_tm, pend_tn, 0, BM, et);
     }
     tc_fence_before();
     __syncthreads();
