@@ -274,7 +274,10 @@ def bench_attention(torch, D, args, lib_calls):
     ofull = torch.empty(BH, AT_S, AT_D, device="cuda") if D.world > 1 else o
     sd = AT_S * AT_D
     a = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1.0 / np.sqrt(AT_D), sd, AT_D, sd,
-                           AT_D, 1, sd, AT_D, sd, AT_D, AT_S, AT_D, 64, 64, AT_S // 64, hloc, 1, 1, 0, 0)
+                           AT_D, 1, sd, AT_D, sd, AT_D, AT_S, AT_D, 64, 64, AT_S // 64, hloc, 1, 1, 0, 0, 0, 0)
+    ws = lib().piton_b200_attention_workspace_size(C.byref(a))
+    wbuf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+    a.workspace, a.workspace_bytes = wbuf.data_ptr(), ws
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
 
     def kernel_only():
@@ -296,7 +299,7 @@ def bench_attention(torch, D, args, lib_calls):
     err = float((o[0, :64].double() - ref).abs().max())
     flops = 4.0 * BH * AT_S * AT_S * AT_D * 0.5
     return {"flops": flops, "bytes": 16.0 * BH * AT_S * AT_D, "t_step": t_step, "t_kernel": t_kernel, "err": err,
-            "local_flops": flops * hloc / BH}
+            "local_flops": flops * hloc / BH, "tc": ws > 0}
 
 
 def bench_add(torch, D, args, lib_calls):
@@ -529,6 +532,7 @@ def main():
         sec["attention"] = {"value": r["flops"] / r["t_step"] / 1e12, "unit": "TFLOP/s",
                             "gbs": r["bytes"] / r["t_step"] / 1e9,
                             "kernel_tflops_per_gpu": r["local_flops"] / r["t_kernel"] / 1e12,
+                            "path": "tcgen05 3xTF32" if r.get("tc") else "CUDA-core fp32",
                             "ms_per_step": 1e3 * r["t_step"], "max_abs_err_vs_f64": r["err"]}
     if "mlp" in res:
         r = res["mlp"]

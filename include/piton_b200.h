@@ -52,7 +52,7 @@ extern "C" {
 #define PITON_B200_QPU_ROUNDING 0x1u /* reproduce the QPU's float semantics bit for bit: round-toward-zero
                                         adds and multiplies, no FMA, sequential-k dots, denormals read and
                                         written as +0 (piton/qpu/emulator.py:137-212). add, matmul, dense. */
-#define PITON_B200_FORCE_SIMT 0x2u   /* matmul/dense: take the CUDA-core path even where tensor cores apply */
+#define PITON_B200_FORCE_SIMT 0x2u   /* matmul/dense/attention: take the CUDA-core path even where tensor cores apply */
 
 /* ---- runtime (replaces pi/runtime/piton_rt.h:37-107: allocation, launch, sync, timers) ---- */
 
@@ -185,9 +185,13 @@ typedef struct {
     int64_t n_ctx, head_dim, block_m, block_n;
     int64_t grid_x, grid_y;
     int32_t causal, even_n;
-    uint32_t flags;
+    uint64_t workspace;   /* device scratch for the tensor-core path, >= piton_b200_attention_workspace_size() */
+    uint64_t workspace_bytes;
+    uint32_t flags;       /* PITON_B200_FORCE_SIMT */
     uint32_t _pad;
 } piton_attention_args;
+/* Bytes of workspace the call needs (0 when it takes the CUDA-core path: HEAD_DIM != 64, n_ctx < 64). */
+PITON_B200_API size_t piton_b200_attention_workspace_size(const piton_attention_args *args);
 PITON_B200_API int piton_b200_attention_f32(const piton_attention_args *args, void *stream);
 
 /* ---- row LayerNorm without affine: tests/test_reroll_reduce.py:199-208 layernorm_kernel ---- */

@@ -169,8 +169,6 @@ static int launch_attn_simt(const AttnParams &p, cudaStream_t s) {
     return check_launch("attention");
 }
 
-int attention_dispatch(const AttnParams &p, cudaStream_t s) { return attention_simt(p, s); }
-
 int attention_simt(const AttnParams &p, cudaStream_t s) {
     switch (p.head_dim) {
         case 16: return launch_attn_simt<16>(p, s);
@@ -185,13 +183,13 @@ int attention_simt(const AttnParams &p, cudaStream_t s) {
 
 using namespace piton;
 
-extern "C" int piton_b200_attention_f32(const piton_attention_args *a, void *stream) {
+static int attn_params(const piton_attention_args *a, AttnParams &p) {
     PITON_REQUIRE(a != nullptr, "args is NULL");
     PITON_REQUIRE(a->n_ctx >= 0 && a->head_dim > 0 && a->block_m > 0 && a->block_n > 0 && a->grid_x >= 0 &&
                       a->grid_y >= 0,
                   "bad shape");
-    PITON_REQUIRE(a->flags == 0, "unknown flags 0x%x", a->flags);
-    AttnParams p{};
+    PITON_REQUIRE((a->flags & ~PITON_B200_FORCE_SIMT) == 0, "unknown flags 0x%x", a->flags);
+    p = AttnParams{};
     p.q = reinterpret_cast<const float *>(a->q);
     p.k = reinterpret_cast<const float *>(a->k);
     p.v = reinterpret_cast<const float *>(a->v);
@@ -208,8 +206,32 @@ extern "C" int piton_b200_attention_f32(const piton_attention_args *a, void *str
     p.key_end = (!a->causal && a->even_n) ? (a->n_ctx / a->block_n) * a->block_n : a->n_ctx;
     int64_t rows = a->grid_x * a->block_m;
     p.row_end = rows < a->n_ctx ? rows : a->n_ctx;
+    return PITON_B200_OK;
+}
+
+static bool use_tc(const piton_attention_args *a, const AttnParams &p) {
+    return !(a->flags & PITON_B200_FORCE_SIMT) && p.row_end > 0 && p.heads > 0 && attention_tc_supported(p);
+}
+
+extern "C" size_t piton_b200_attention_workspace_size(const piton_attention_args *a) {
+    AttnParams p;
+    if (attn_params(a, p) != PITON_B200_OK || !use_tc(a, p)) return 0;
+    return attention_tc_workspace_bytes(p);
+}
+
+extern "C" int piton_b200_attention_f32(const piton_attention_args *a, void *stream) {
+    AttnParams p;
+    int rc = attn_params(a, p);
+    if (rc) return rc;
     if (p.row_end <= 0 || p.heads == 0) return PITON_B200_OK;
     PITON_REQUIRE(p.heads < 65536, "too many heads for one launch");
     PITON_REQUIRE(a->q && a->k && a->v && a->out, "NULL pointer");
-    return attention_dispatch(p, as_stream(stream));
+    if (use_tc(a, p)) {
+        size_t need = attention_tc_workspace_bytes(p);
+        if (a->workspace_bytes < need || !a->workspace)
+            return set_error(PITON_B200_EWORKSPACE, "attention needs %zu bytes of workspace, got %llu", need,
+                             (unsigned long long)a->workspace_bytes);
+        return attention_tc(p, reinterpret_cast<void *>(a->workspace), as_stream(stream));
+    }
+    return attention_simt(p, as_stream(stream));
 }

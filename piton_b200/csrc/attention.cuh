@@ -17,7 +17,9 @@ struct AttnParams {
 };
 
 int attention_simt(const AttnParams &p, cudaStream_t s);
-// Picks the tensor-core kernel where it applies, else the CUDA-core one.
-int attention_dispatch(const AttnParams &p, cudaStream_t s);
+// tcgen05 3xTF32 kernel (attention_tc.cu): HEAD_DIM 64, n_ctx >= 64.
+bool attention_tc_supported(const AttnParams &p);
+size_t attention_tc_workspace_bytes(const AttnParams &p);
+int attention_tc(const AttnParams &p, void *workspace, cudaStream_t s);
 
 }  // namespace piton

@@ -1,0 +1,438 @@
+// Flash-attention forward on the 5th-generation tensor cores with the 3xTF32
+// split (examples/attention.py:33-113; the semantics are those of
+// attention.cu's header: key_end, causal mask, row_end, base-2 online softmax).
+//
+// Per call:
+//  1. split: K -> K_hi, K_lo as [heads * n_ctx, D] and V -> V^T_hi, V^T_lo as
+//     [heads * D, ld] (ld = n_ctx rounded up to 4), tf32 hi/lo halves, into the
+//     workspace.
+//  2. one CTA per (head, 128-query block), 192 threads:
+//     * warps 2-5 (one thread per query row = TMEM lane) load the row of Q,
+//       split it and store Q_hi, Q_lo into TMEM; per 64-key block they read
+//       the scores S from TMEM, apply scale and masks, update the running max
+//       and sum in registers (no shuffles: a row lives in one thread), write
+//       P_hi over S and P_lo next to it in TMEM, then fold the block's P.V
+//       into an fp32 register accumulator (round to nearest) and finally
+//       store O / l;
+//     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle, 2 stages);
+//     * warp 1 issues, from one thread, S = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi
+//       (A from TMEM, B from shared memory, 128x64x8 kind::tf32) and
+//       O_blk = P_lo V_hi + P_hi V_lo + P_hi V_hi (A = P from TMEM).
+//     A block's P.V lands in its own TMEM accumulator that the softmax warps
+//     add into registers, so the tensor core's truncating accumulation never
+//     spans more than one 64-key block.
+// TMEM columns: Q_hi [0,64) Q_lo [64,128) S/P_hi [128,192) P_lo [192,256)
+// O_blk [256,320) (512 allocated).  All waits are bounded (2 s): on expiry
+// the kernel records a status, drains its copies and MMAs, frees TMEM, returns.
+#include "attention.cuh"
+#include "common.cuh"
+#include "sm100.cuh"
+
+namespace piton {
+
+extern __device__ int g_tc_status;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int BM = 128, BN = 64, HD = 64, STAGES = 2, THREADS = 192;
+constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes
+constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;            // one 64 x 64 fp32 operand tile
+constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;          // K_hi, K_lo, V^T_hi, V^T_lo
+constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
+constexpr int TMEM_COLS = 512;
+constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S = 128, COL_PLO = 192, COL_O = 256;
+
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
+
+// hi/lo[h][r][c] (row stride ld) from src + h*s_h + r*s_r + c*s_c, r < rows, c < cols,
+// through 32 x 32 shared-memory tiles (grid.z = heads)
+__global__ void __launch_bounds__(256) attn_split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
+                                                         int64_t s_h, int64_t s_r, int64_t s_c,
+                                                         float *__restrict__ hi, float *__restrict__ lo, int64_t ld,
+                                                         int lanes_along_rows) {
+    __shared__ float tile[32][33];
+    const int64_t h = blockIdx.z;
+    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
+    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+    const float *base = src + h * s_h;
+    for (int j = ty; j < 32; j += 8) {
+        int64_t r = lanes_along_rows ? r0 + tx : r0 + j;
+        int64_t c = lanes_along_rows ? c0 + j : c0 + tx;
+        float v = (r < rows && c < cols) ? base[r * s_r + c * s_c] : 0.0f;
+        if (lanes_along_rows) tile[tx][j] = v;
+        else tile[j][tx] = v;
+    }
+    __syncthreads();
+    float *hh = hi + h * rows * ld, *ll = lo + h * rows * ld;
+    for (int j = ty; j < 32; j += 8) {
+        int64_t r = r0 + j, c = c0 + tx;
+        if (r < rows && c < cols) {
+            float v = tile[j][tx];
+            float x = tf32_trunc(v);
+            hh[r * ld + c] = x;
+            ll[r * ld + c] = isfinite(v) ? tf32_trunc(v - x) : 0.0f;
+        }
+    }
+}
+
+struct TcAttnArgs {
+    const float *q;
+    float *o;
+    int64_t sqh, sqm, soh, som;
+    int64_t n_ctx, key_end, row_end, heads, q_blocks;
+    float qk_scale;
+    int causal;
+};
+
+__device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
+    bool ok = mbar_wait(bar, parity);
+    return __all_sync(0xffffffffu, ok);
+}
+
+__global__ void __launch_bounds__(THREADS, 1)
+    attn_3xtf32_kernel(const __grid_constant__ CUtensorMap m_khi, const __grid_constant__ CUtensorMap m_klo,
+                       const __grid_constant__ CUtensorMap m_vhi, const __grid_constant__ CUtensorMap m_vlo,
+                       TcAttnArgs a) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *kv_full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
+    uint64_t *kv_empty = kv_full + STAGES;
+    uint64_t *q_ready = kv_empty + STAGES;
+    uint64_t *s_full = q_ready + 1;
+    uint64_t *p_full = s_full + 1;
+    uint64_t *o_full = p_full + 1;
+    uint64_t *o_empty = o_full + 1;
+    uint64_t *drain = o_empty + 1;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    // heavy (late) query blocks first, heads fastest
+    const int64_t qb = a.q_blocks - 1 - (int64_t)blockIdx.x / a.heads;
+    const int64_t head = (int64_t)blockIdx.x % a.heads;
+    const int64_t q0 = qb * BM;
+    int64_t kend = a.key_end;
+    if (a.causal && q0 + BM < kend) kend = q0 + BM;
+    const int nblocks = kend > 0 ? (int)((kend + BN - 1) / BN) : 0;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES; ++s) {
+            mbar_init(&kv_full[s], 1);
+            mbar_init(&kv_empty[s], 1);
+        }
+        mbar_init(q_ready, 4);
+        mbar_init(s_full, 1);
+        mbar_init(p_full, 4);
+        mbar_init(o_full, 1);
+        mbar_init(o_empty, 4);
+        mbar_init(drain, 1);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        prefetch_tmap(&m_khi);
+        prefetch_tmap(&m_klo);
+        prefetch_tmap(&m_vhi);
+        prefetch_tmap(&m_vlo);
+    }
+    if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_holder);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tmem_holder;
+
+    if (warp == 0) {
+        // ---------------- TMA producer: K and V^T tiles ----------------
+        if (lane == 0) {
+            int issued = 0;
+            for (int j = 0; j < nblocks && !*abort_flag; ++j, ++issued) {
+                const int s = j % STAGES;
+                if (!mbar_wait(&kv_empty[s], ((j / STAGES) & 1) ^ 1)) {
+                    record_status(STATUS_TIMEOUT_PRODUCER);
+                    *abort_flag = 1;
+                    break;
+                }
+                uint8_t *st = smem + s * STAGE_BYTES;
+                mbar_arrive_expect_tx(&kv_full[s], STAGE_BYTES);
+                const int krow = (int)(head * a.n_ctx + (int64_t)j * BN);
+                const int vrow = (int)(head * HD);
+                const int kx = j * BN;
+                for (int box = 0; box < 2; ++box) {
+                    tma_load_2d(st + box * BOX_BYTES, &m_khi, &kv_full[s], box * 32, krow);
+                    tma_load_2d(st + TILE_BYTES + box * BOX_BYTES, &m_klo, &kv_full[s], box * 32, krow);
+                    tma_load_2d(st + 2 * TILE_BYTES + box * BOX_BYTES, &m_vhi, &kv_full[s], kx + box * 32, vrow);
+                    tma_load_2d(st + 3 * TILE_BYTES + box * BOX_BYTES, &m_vlo, &kv_full[s], kx + box * 32, vrow);
+                }
+            }
+            for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
+                if (!mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        if (lane == 0) {
+            constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+            bool ok = mbar_wait(q_ready, 0);
+            if (!ok) {
+                record_status(STATUS_TIMEOUT_MMA);
+                *abort_flag = 1;
+            }
+            tc_fence_after();
+            for (int j = 0; ok && j < nblocks && !*abort_flag; ++j) {
+                const int s = j % STAGES;
+                if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+                const uint32_t khi = base, klo = base + TILE_BYTES, vhi = base + 2 * TILE_BYTES,
+                               vlo = base + 3 * TILE_BYTES;
+                // S = Q K^T over d (8 k-steps of 8)
+#pragma unroll
+                for (int ks = 0; ks < HD / 8; ++ks) {
+                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                    const uint64_t bh = smem_desc_kmajor(khi + off, 128, LAYOUT_SWIZZLE_128B);
+                    const uint64_t bl = smem_desc_kmajor(klo + off, 128, LAYOUT_SWIZZLE_128B);
+                    mma_tf32_ts(tmem + COL_S, tmem + COL_QLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + COL_S, tmem + COL_QHI + 8 * ks, bl, IDESC, 1u);
+                    mma_tf32_ts(tmem + COL_S, tmem + COL_QHI + 8 * ks, bh, IDESC, 1u);
+                }
+                mma_commit(s_full);
+                if (!mbar_wait(p_full, j & 1)) {
+                    ok = false;
+                    break;
+                }
+                if (j > 0 && !mbar_wait(o_empty, (j - 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                // O_blk = P V over the block's keys (8 k-steps of 8)
+#pragma unroll
+                for (int ks = 0; ks < BN / 8; ++ks) {
+                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
+                    const uint64_t bh = smem_desc_kmajor(vhi + off, 128, LAYOUT_SWIZZLE_128B);
+                    const uint64_t bl = smem_desc_kmajor(vlo + off, 128, LAYOUT_SWIZZLE_128B);
+                    mma_tf32_ts(tmem + COL_O, tmem + COL_PLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + COL_O, tmem + COL_S + 8 * ks, bl, IDESC, 1u);
+                    mma_tf32_ts(tmem + COL_O, tmem + COL_S + 8 * ks, bh, IDESC, 1u);
+                }
+                mma_commit(o_full);
+                mma_commit(&kv_empty[s]);
+            }
+            if (!ok) {
+                record_status(STATUS_TIMEOUT_MMA);
+                *abort_flag = 1;
+            }
+            mma_commit(drain);
+            if (!mbar_wait(drain, 0)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else {
+        // ---------------- softmax / accumulate / store (warps 2-5) ----------------
+        const int quarter = warp & 3;
+        const int64_t row = q0 + quarter * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        bool ok = true;
+        {
+            // Q row -> tf32 hi / lo -> TMEM
+            const float *qr = a.q + head * a.sqh + row * a.sqm;
+            const bool live = row < a.n_ctx;
+#pragma unroll
+            for (int c = 0; c < HD; c += 16) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    float v = live ? qr[c + j] : 0.0f;
+                    float h = tf32_trunc(v);
+                    hi[j] = __float_as_uint(h);
+                    lo[j] = __float_as_uint(isfinite(v) ? tf32_trunc(v - h) : 0.0f);
+                }
+                tmem_st_32x32b_x16(lane_base + COL_QHI + c, hi);
+                tmem_st_32x32b_x16(lane_base + COL_QLO + c, lo);
+            }
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(q_ready);
+        }
+        float m_i = -INFINITY, l_i = 0.0f;
+        float acc[HD];
+#pragma unroll
+        for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
+        for (int j = 0; j < nblocks; ++j) {
+            if (*abort_flag || !warp_wait(s_full, j & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int64_t k0 = (int64_t)j * BN;
+            float sc[BN];
+#pragma unroll
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(lane_base + COL_S + c, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) sc[c + e] = __uint_as_float(r[e]);
+            }
+            float mx = -INFINITY;
+#pragma unroll
+            for (int c = 0; c < BN; ++c) {
+                const int64_t col = k0 + c;
+                float v = sc[c] * a.qk_scale;
+                if (col >= a.key_end || (a.causal && col > row)) v = -INFINITY;
+                sc[c] = v;
+                mx = fmaxf(mx, v);
+            }
+            const float m_new = fmaxf(m_i, mx);
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            const float alpha = exp2f(m_i - m_use);
+            float psum = 0.0f;
+#pragma unroll
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    float p = exp2f(sc[c + e] - m_use);
+                    psum += p;
+                    float h = tf32_trunc(p);
+                    hi[e] = __float_as_uint(h);
+                    lo[e] = __float_as_uint(tf32_trunc(p - h));
+                }
+                tmem_st_32x32b_x16(lane_base + COL_S + c, hi);
+                tmem_st_32x32b_x16(lane_base + COL_PLO + c, lo);
+            }
+            l_i = l_i * alpha + psum;
+            m_i = m_new;
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(p_full);
+            if (*abort_flag || !warp_wait(o_full, j & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+#pragma unroll
+            for (int c = 0; c < HD; c += 16) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(lane_base + COL_O + c, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) acc[c + e] = fmaf(acc[c + e], alpha, __uint_as_float(r[e]));
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(o_empty);
+        }
+        if (!ok) {
+            if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+            *abort_flag = 1;
+        } else if (row < a.row_end) {
+            const float inv = 1.0f / l_i;
+            float *orow = a.o + head * a.soh + row * a.som;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) orow[d] = acc[d] * inv;
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        __syncwarp();
+        tc_fence_after();
+        tmem_dealloc<TMEM_COLS>(tmem);
+    }
+}
+
+using EncodeTiled = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                 const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                 CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiled encode_fn() {
+    static EncodeTiled fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiled>(p);
+    }
+    return fn;
+}
+
+// row-major fp32 [rows, ld] with inner extent `cols`; boxes of 64 rows x 32 columns, 128-byte swizzle
+int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+    cuuint32_t box[2] = {32, 64};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    return PITON_B200_OK;
+}
+
+int64_t v_ld(int64_t n_ctx) { return (n_ctx + 3) / 4 * 4; }
+size_t k_region(const AttnParams &p) { return ((size_t)p.heads * p.n_ctx * HD * 4 + 1023) / 1024 * 1024; }
+size_t v_region(const AttnParams &p) { return ((size_t)p.heads * HD * v_ld(p.n_ctx) * 4 + 1023) / 1024 * 1024; }
+
+}  // namespace
+
+bool attention_tc_supported(const AttnParams &p) {
+    if (p.head_dim != HD || p.n_ctx < 64 || p.heads < 1) return false;
+    if (p.heads * p.n_ctx >= (1ll << 31) || p.heads * HD >= (1ll << 31)) return false;
+    if ((p.n_ctx + 31) / 32 > 65535 || p.heads > 65535) return false;
+    int64_t q_blocks = (p.row_end + BM - 1) / BM;
+    if (q_blocks * p.heads >= (1ll << 31)) return false;
+    return encode_fn() != nullptr;
+}
+
+size_t attention_tc_workspace_bytes(const AttnParams &p) { return 2 * k_region(p) + 2 * v_region(p); }
+
+int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    float *k_hi = reinterpret_cast<float *>(ws);
+    float *k_lo = reinterpret_cast<float *>(ws + k_region(p));
+    float *v_hi = reinterpret_cast<float *>(ws + 2 * k_region(p));
+    float *v_lo = reinterpret_cast<float *>(ws + 2 * k_region(p) + v_region(p));
+    const int64_t ldv = v_ld(p.n_ctx);
+    // K [n_ctx, D] per head (strides skn, skk) -> [heads * n_ctx, D]
+    {
+        dim3 g((unsigned)cdiv(HD, 32), (unsigned)cdiv(p.n_ctx, 32), (unsigned)p.heads);
+        int along_rows = llabs(p.skn) < llabs(p.skk);
+        attn_split_kernel<<<g, 256, 0, stream>>>(p.k, p.n_ctx, HD, p.skh, p.skn, p.skk, k_hi, k_lo, HD, along_rows);
+    }
+    // V [n_ctx, D] per head (strides svn, 1) -> V^T [heads * D, ldv]
+    {
+        dim3 g((unsigned)cdiv(p.n_ctx, 32), (unsigned)cdiv(HD, 32), (unsigned)p.heads);
+        attn_split_kernel<<<g, 256, 0, stream>>>(p.v, HD, p.n_ctx, p.svh, 1, p.svn, v_hi, v_lo, ldv, 1);
+    }
+    CUtensorMap mkh, mkl, mvh, mvl;
+    int rc;
+    if ((rc = make_map(&mkh, k_hi, p.heads * p.n_ctx, HD, HD)) || (rc = make_map(&mkl, k_lo, p.heads * p.n_ctx, HD, HD)) ||
+        (rc = make_map(&mvh, v_hi, p.heads * HD, p.n_ctx, ldv)) || (rc = make_map(&mvl, v_lo, p.heads * HD, p.n_ctx, ldv)))
+        return rc;
+    static bool attr[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        attr[dev] = true;
+    }
+    TcAttnArgs a;
+    a.q = p.q;
+    a.o = p.o;
+    a.sqh = p.sqh; a.sqm = p.sqm; a.soh = p.soh; a.som = p.som;
+    a.n_ctx = p.n_ctx; a.key_end = p.key_end; a.row_end = p.row_end; a.heads = p.heads;
+    a.q_blocks = (p.row_end + BM - 1) / BM;
+    a.qk_scale = p.qk_scale;
+    a.causal = p.causal;
+    attn_3xtf32_kernel<<<(unsigned)(a.q_blocks * p.heads), THREADS, SMEM_BYTES, stream>>>(mkh, mkl, mvh, mvl, a);
+    return check_launch("attention_3xtf32", 3);
+}
+
+}  // namespace piton

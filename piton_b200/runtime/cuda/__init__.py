@@ -21,6 +21,7 @@ A kernel (or constexpr combination) without a B200 implementation raises
 from __future__ import annotations
 
 import ctypes as C
+import os
 
 import numpy as np
 
@@ -212,10 +213,15 @@ def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
     return stats
 
 
-def _flags(launch, allowed_qpu=True):
+def _flags(launch, allowed_qpu=True, simt_ok=False):
+    """Flags word of an entry point: QPU rounding (launch option), and the CUDA-core
+    path forced where an operator has both (PITON_B200_FORCE_SIMT=1, for comparisons)."""
     if launch.qpu and not allowed_qpu:
         raise NotImplementedError("qpu_rounding is implemented for add, matmul and dense only")
-    return _lib.QPU_ROUNDING if launch.qpu else 0
+    f = _lib.QPU_ROUNDING if launch.qpu else 0
+    if simt_ok and os.environ.get("PITON_B200_FORCE_SIMT", "0") not in ("", "0"):
+        f |= _lib.FORCE_SIMT
+    return f
 
 
 # ---------------------------------------------------------------------------------------
@@ -262,7 +268,7 @@ def _matmul(L: Launch, grid):
         Cb.require(*extent((M, s["stride_cm"]), (N, s["stride_cn"])))
     a = _lib.MatmulArgs(A.addr, B.addr, Cb.addr, M, N, K, s["stride_am"], s["stride_ak"], s["stride_bk"],
                         s["stride_bn"], s["stride_cm"], s["stride_cn"], bm, bn, bk, g, grid[0], 0, 0,
-                        _flags(L), 0)
+                        _flags(L, simt_ok=True), 0)
     ws = lib().piton_b200_matmul_workspace_size(C.byref(a))
     a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_matmul_f32", a, "matmul_kernel")
@@ -312,10 +318,13 @@ def _attention(L: Launch, grid):
     a = _lib.AttentionArgs(Q.addr, K.addr, V.addr, O.addr, L.float("sm_scale"), st["stride_qh"], st["stride_qm"],
                            st["stride_kh"], st["stride_kn"], st["stride_kk"], st["stride_vh"], st["stride_vn"],
                            st["stride_oh"], st["stride_om"], n_ctx, d, bm, bn, grid[0], heads, int(causal),
-                           int(even), _flags(L, False), 0)
+                           int(even), 0, 0, _flags(L, False, simt_ok=True), 0)
+    ws = lib().piton_b200_attention_workspace_size(C.byref(a))
+    a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_attention_f32", a, "attn_fwd_kernel")
     flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
-    return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops, "path": "attention"}
+    return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops,
+            "path": "tcgen05_3xtf32" if ws else "cuda_core"}
 
 
 @register("layernorm_kernel", ("x_ptr", "out_ptr", "n", "eps", "BLOCK"))

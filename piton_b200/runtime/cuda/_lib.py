@@ -60,7 +60,8 @@ class AttentionArgs(C.Structure):
                 ("stride_qh", i64), ("stride_qm", i64), ("stride_kh", i64), ("stride_kn", i64), ("stride_kk", i64),
                 ("stride_vh", i64), ("stride_vn", i64), ("stride_oh", i64), ("stride_om", i64),
                 ("n_ctx", i64), ("head_dim", i64), ("block_m", i64), ("block_n", i64), ("grid_x", i64),
-                ("grid_y", i64), ("causal", i32), ("even_n", i32), ("flags", u32), ("_pad", u32)]
+                ("grid_y", i64), ("causal", i32), ("even_n", i32), ("workspace", u64), ("workspace_bytes", u64),
+                ("flags", u32), ("_pad", u32)]
 
 
 class LayernormArgs(C.Structure):
@@ -99,6 +100,7 @@ PROTOTYPES = {
     "piton_b200_ipc_close": (C.c_int, [u64]),
     "piton_b200_dense_f32": (C.c_int, [C.POINTER(DenseArgs), C.c_void_p]),
     "piton_b200_mlp_f32": (C.c_int, [C.POINTER(MlpArgs), C.c_void_p]),
+    "piton_b200_attention_workspace_size": (C.c_size_t, [C.POINTER(AttentionArgs)]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
     "piton_b200_layernorm_f32": (C.c_int, [C.POINTER(LayernormArgs), C.c_void_p]),
     "piton_b200_tinygpt_weight_floats": (C.c_int64, []),

@@ -138,3 +138,46 @@ def test_even_n_promise_skips_ragged_tail_like_the_reference(cuda):
     q, k, v = qkv(40, 16, seed=2)
     out = run(q, k, v, False, 2, 16, even_n=True)
     np.testing.assert_allclose(out, O.qpu_attention(q, k, v, False, 2, 16, even_n=True), rtol=0, atol=ATOL)
+
+
+def _status():
+    import ctypes
+    from piton_b200.runtime.cuda._lib import lib
+    st = ctypes.c_int(-1)
+    assert lib().piton_b200_device_status(ctypes.byref(st)) == 0
+    return st.value
+
+
+@pytest.mark.parametrize("heads,n,causal", [(1, 64, True), (2, 100, False), (3, 200, True), (1, 1000, True),
+                                            (2, 513, False), (1, 64, False)])
+def test_tensor_core_path(cuda, monkeypatch, heads, n, causal):
+    q, k, v = qkv(n, 64, seed=heads * n, heads=heads)
+    sentinel = np.float32(-1234.5)
+    out = np.full((heads, n + 2, 64), sentinel, np.float32)
+    h, _, d = q.shape
+    stats = attn_fwd_kernel[(-(-n // 2), h)](q, k, v, out, float(1 / np.sqrt(d)), n * d, d, n * d, d, 1, n * d, d,
+                                              (n + 2) * d, d, n, HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16,
+                                              CAUSAL=causal, EVEN_N=n % 16 == 0, device="b200").last_stats
+    assert stats["path"] == "tcgen05_3xtf32"
+    assert _status() == 0
+    np.testing.assert_array_equal(out[:, n:], sentinel)
+    np.testing.assert_allclose(out[:, :n], O.attention_f64(q, k, v, causal), rtol=0, atol=ATOL)
+    monkeypatch.setenv("PITON_B200_FORCE_SIMT", "1")
+    simt = run(q, k, v, causal, 2, 16)
+    np.testing.assert_allclose(out[:, :n], simt, rtol=0, atol=ATOL)
+
+
+def test_tensor_core_path_strided_k_and_padded_rows(cuda):
+    # K pre-transposed [D, N] and Q / Out rows padded to 80 floats
+    heads, n, d = 2, 192, 64
+    rng = np.random.default_rng(17)
+    q = rng.standard_normal((heads, n, 80)).astype(np.float32)
+    k, v = (rng.standard_normal((heads, n, d)).astype(np.float32) for _ in range(2))
+    kt = np.ascontiguousarray(k.transpose(0, 2, 1))
+    out = np.zeros((heads, n, 80), np.float32)
+    stats = attn_fwd_kernel[(n // 2, heads)](q, kt, v, out, 0.125, n * 80, 80, n * d, 1, n, n * d, d, n * 80, 80, n,
+                                             HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=True,
+                                             device="b200").last_stats
+    assert stats["path"] == "tcgen05_3xtf32"
+    np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, True), rtol=0, atol=ATOL)
+    assert np.all(out[:, :, d:] == 0)
