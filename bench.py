@@ -47,6 +47,7 @@ MM = 8192
 SM_M, SM_N = 32768, 16384
 AT_B, AT_H, AT_S, AT_D = 32, 32, 4096, 64
 ADD_N = 1 << 28
+ATTN_BH = AT_B * AT_H
 
 
 def load_peaks():
@@ -267,7 +268,7 @@ def bench_attention(torch, D, args, lib_calls):
     import ctypes as C
     from piton_b200.runtime.cuda import _lib
     from piton_b200.runtime.cuda._lib import lib
-    BH = AT_B * AT_H
+    BH = ATTN_BH
     h0, hloc = shard(BH, D.world, D.rank)
     q, k, v = (torch.randn(hloc, AT_S, AT_D, device="cuda") for _ in range(3))
     o = torch.empty_like(q)
@@ -481,9 +482,12 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mm-size", type=int, default=MM, help="matmul M=N=K (profiling runs use a smaller case)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--attn-bh", type=int, default=AT_B * AT_H, help="attention batch x heads (profiling runs use fewer)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     MM = args.mm_size
+    global ATTN_BH
+    ATTN_BH = args.attn_bh
     if args.impl == "reference":
         return run_reference(args)
 
