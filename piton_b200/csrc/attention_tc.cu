@@ -14,15 +14,19 @@
 //       P_hi over S and P_lo next to it in TMEM, then fold the block's P.V
 //       into an fp32 register accumulator (round to nearest) and finally
 //       store O / l;
-//     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle, 2 stages);
+//     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle);
 //     * warp 1 issues, from one thread, S = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi
 //       (A from TMEM, B from shared memory, 128x64x8 kind::tf32) and
 //       O_blk = P_lo V_hi + P_hi V_lo + P_hi V_hi (A = P from TMEM).
 //     A block's P.V lands in its own TMEM accumulator that the softmax warps
 //     add into registers, so the tensor core's truncating accumulation never
 //     spans more than one 64-key block.
-// TMEM columns: Q_hi [0,64) Q_lo [64,128) S/P_hi [128,192) P_lo [192,256)
-// O_blk [256,320) (512 allocated).  All waits are bounded (2 s): on expiry
+// The scores of block j+1 are computed while the softmax warps work on block
+// j (two S/P buffers), and a block's P.V accumulator is folded into the
+// registers after the next block's P is written, so the tensor core and the
+// softmax warps overlap.  TMEM columns: Q_hi [0,64) Q_lo [64,128)
+// S/P_hi x2 [128,256) P_lo x2 [256,384) O_blk [384,448) (512 allocated).
+// K / V^T tiles: 3-stage TMA ring.  All waits are bounded (2 s): on expiry
 // the kernel records a status, drains its copies and MMAs, frees TMEM, returns.
 #include "attention.cuh"
 #include "common.cuh"
@@ -36,13 +40,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HD = 64, STAGES = 2, THREADS = 192;
+constexpr int BM = 128, BN = 64, HD = 64, STAGES = 3, THREADS = 192;
 constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes
 constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;            // one 64 x 64 fp32 operand tile
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;          // K_hi, K_lo, V^T_hi, V^T_lo
 constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S = 128, COL_PLO = 192, COL_O = 256;
+constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_PLO0 = 256, COL_O = 384;   // S, P_lo: two buffers each
 
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
@@ -92,6 +96,12 @@ __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
     return __all_sync(0xffffffffu, ok);
 }
 
+__device__ __forceinline__ float fast_exp2(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
+
 __global__ void __launch_bounds__(THREADS, 1)
     attn_3xtf32_kernel(const __grid_constant__ CUtensorMap m_khi, const __grid_constant__ CUtensorMap m_klo,
                        const __grid_constant__ CUtensorMap m_vhi, const __grid_constant__ CUtensorMap m_vlo,
@@ -100,19 +110,19 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *kv_full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *kv_empty = kv_full + STAGES;
-    uint64_t *q_ready = kv_empty + STAGES;
-    uint64_t *s_full = q_ready + 1;
-    uint64_t *p_full = s_full + 1;
-    uint64_t *o_full = p_full + 1;
+    uint64_t *s_full = kv_empty + STAGES;     // [2]
+    uint64_t *p_full = s_full + 2;            // [2]
+    uint64_t *q_ready = p_full + 2;
+    uint64_t *o_full = q_ready + 1;
     uint64_t *o_empty = o_full + 1;
     uint64_t *drain = o_empty + 1;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    // heavy (late) query blocks first, heads fastest
-    const int64_t qb = a.q_blocks - 1 - (int64_t)blockIdx.x / a.heads;
-    const int64_t head = (int64_t)blockIdx.x % a.heads;
+    // all query blocks of a head run close together (its K / V stay in L2), heavy (late) blocks first
+    const int64_t head = (int64_t)blockIdx.x / a.q_blocks;
+    const int64_t qb = a.q_blocks - 1 - (int64_t)blockIdx.x % a.q_blocks;
     const int64_t q0 = qb * BM;
     int64_t kend = a.key_end;
     if (a.causal && q0 + BM < kend) kend = q0 + BM;
@@ -123,9 +133,11 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_full[b], 4);
+        }
         mbar_init(q_ready, 4);
-        mbar_init(s_full, 1);
-        mbar_init(p_full, 4);
         mbar_init(o_full, 1);
         mbar_init(o_empty, 4);
         mbar_init(drain, 1);
@@ -169,54 +181,53 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1)) record_status(STATUS_TIMEOUT_DRAIN);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
+        // ---------------- MMA issuer: S_{j+1} is issued before P_j V so it overlaps softmax j ----------------
         if (lane == 0) {
             constexpr uint32_t IDESC = idesc_tf32(BM, BN);
             bool ok = mbar_wait(q_ready, 0);
-            if (!ok) {
-                record_status(STATUS_TIMEOUT_MMA);
-                *abort_flag = 1;
-            }
             tc_fence_after();
-            for (int j = 0; ok && j < nblocks && !*abort_flag; ++j) {
+            auto issue_s = [&](int j) -> bool {
                 const int s = j % STAGES;
-                if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) {
-                    ok = false;
-                    break;
-                }
+                if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) return false;
                 tc_fence_after();
                 const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-                const uint32_t khi = base, klo = base + TILE_BYTES, vhi = base + 2 * TILE_BYTES,
-                               vlo = base + 3 * TILE_BYTES;
-                // S = Q K^T over d (8 k-steps of 8)
+                const uint32_t khi = base, klo = base + TILE_BYTES;
+                const uint32_t d = tmem + COL_S0 + (j & 1) * BN;
 #pragma unroll
                 for (int ks = 0; ks < HD / 8; ++ks) {
                     const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
                     const uint64_t bh = smem_desc_kmajor(khi + off, 128, LAYOUT_SWIZZLE_128B);
                     const uint64_t bl = smem_desc_kmajor(klo + off, 128, LAYOUT_SWIZZLE_128B);
-                    mma_tf32_ts(tmem + COL_S, tmem + COL_QLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
-                    mma_tf32_ts(tmem + COL_S, tmem + COL_QHI + 8 * ks, bl, IDESC, 1u);
-                    mma_tf32_ts(tmem + COL_S, tmem + COL_QHI + 8 * ks, bh, IDESC, 1u);
+                    mma_tf32_ts(d, tmem + COL_QLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, bl, IDESC, 1u);
+                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, bh, IDESC, 1u);
                 }
-                mma_commit(s_full);
-                if (!mbar_wait(p_full, j & 1)) {
+                mma_commit(&s_full[j & 1]);
+                return true;
+            };
+            if (ok && nblocks > 0) ok = issue_s(0);
+            for (int j = 0; ok && j < nblocks && !*abort_flag; ++j) {
+                if (j + 1 < nblocks && !issue_s(j + 1)) {
                     ok = false;
                     break;
                 }
-                if (j > 0 && !mbar_wait(o_empty, (j - 1) & 1)) {
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || (j > 0 && !mbar_wait(o_empty, (j - 1) & 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                // O_blk = P V over the block's keys (8 k-steps of 8)
+                const int s = j % STAGES;
+                const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
+                const uint32_t vhi = base + 2 * TILE_BYTES, vlo = base + 3 * TILE_BYTES;
+                const uint32_t phi = tmem + COL_S0 + (j & 1) * BN, plo = tmem + COL_PLO0 + (j & 1) * BN;
 #pragma unroll
                 for (int ks = 0; ks < BN / 8; ++ks) {
                     const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
                     const uint64_t bh = smem_desc_kmajor(vhi + off, 128, LAYOUT_SWIZZLE_128B);
                     const uint64_t bl = smem_desc_kmajor(vlo + off, 128, LAYOUT_SWIZZLE_128B);
-                    mma_tf32_ts(tmem + COL_O, tmem + COL_PLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
-                    mma_tf32_ts(tmem + COL_O, tmem + COL_S + 8 * ks, bl, IDESC, 1u);
-                    mma_tf32_ts(tmem + COL_O, tmem + COL_S + 8 * ks, bh, IDESC, 1u);
+                    mma_tf32_ts(tmem + COL_O, plo + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(tmem + COL_O, phi + 8 * ks, bl, IDESC, 1u);
+                    mma_tf32_ts(tmem + COL_O, phi + 8 * ks, bh, IDESC, 1u);
                 }
                 mma_commit(o_full);
                 mma_commit(&kv_empty[s]);
@@ -256,63 +267,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(q_ready);
         }
-        float m_i = -INFINITY, l_i = 0.0f;
+        float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
         float acc[HD];
 #pragma unroll
         for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
-        for (int j = 0; j < nblocks; ++j) {
-            if (*abort_flag || !warp_wait(s_full, j & 1)) {
-                ok = false;
-                break;
-            }
-            tc_fence_after();
-            const int64_t k0 = (int64_t)j * BN;
-            float sc[BN];
-#pragma unroll
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(lane_base + COL_S + c, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) sc[c + e] = __uint_as_float(r[e]);
-            }
-            float mx = -INFINITY;
-#pragma unroll
-            for (int c = 0; c < BN; ++c) {
-                const int64_t col = k0 + c;
-                float v = sc[c] * a.qk_scale;
-                if (col >= a.key_end || (a.causal && col > row)) v = -INFINITY;
-                sc[c] = v;
-                mx = fmaxf(mx, v);
-            }
-            const float m_new = fmaxf(m_i, mx);
-            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
-            const float alpha = exp2f(m_i - m_use);
-            float psum = 0.0f;
-#pragma unroll
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t hi[16], lo[16];
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    float p = exp2f(sc[c + e] - m_use);
-                    psum += p;
-                    float h = tf32_trunc(p);
-                    hi[e] = __float_as_uint(h);
-                    lo[e] = __float_as_uint(tf32_trunc(p - h));
-                }
-                tmem_st_32x32b_x16(lane_base + COL_S + c, hi);
-                tmem_st_32x32b_x16(lane_base + COL_PLO + c, lo);
-            }
-            l_i = l_i * alpha + psum;
-            m_i = m_new;
-            tmem_st_wait();
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(p_full);
-            if (*abort_flag || !warp_wait(o_full, j & 1)) {
-                ok = false;
-                break;
-            }
+        // acc = acc * alpha + O_blk of block jj (its P.V accumulator in TMEM)
+        auto fold = [&](int jj, float alpha) -> bool {
+            if (*abort_flag || !warp_wait(o_full, jj & 1)) return false;
             tc_fence_after();
 #pragma unroll
             for (int c = 0; c < HD; c += 16) {
@@ -325,7 +286,76 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_empty);
+            return true;
+        };
+        for (int j = 0; j < nblocks; ++j) {
+            if (*abort_flag || !warp_wait(&s_full[j & 1], (j >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const int64_t k0 = (int64_t)j * BN;
+            const uint32_t scol = COL_S0 + (j & 1) * BN, pcol = COL_PLO0 + (j & 1) * BN;
+            float sc[BN];
+#pragma unroll
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t r[16];
+                tmem_ld_32x32b_x16(lane_base + scol + c, r);
+                tmem_ld_wait();
+#pragma unroll
+                for (int e = 0; e < 16; ++e) sc[c + e] = __uint_as_float(r[e]);
+            }
+            // masks only on the blocks that reach past key_end or the causal diagonal
+            const bool masked = k0 + BN > a.key_end || (a.causal && k0 + BN - 1 > q0);
+            if (masked) {
+#pragma unroll
+                for (int c = 0; c < BN; ++c) {
+                    const int64_t col = k0 + c;
+                    if (col >= a.key_end || (a.causal && col > row)) sc[c] = -INFINITY;
+                }
+            }
+            float m0 = sc[0], m1 = sc[1], m2 = sc[2], m3 = sc[3];
+#pragma unroll
+            for (int c = 4; c < BN; c += 4) {
+                m0 = fmaxf(m0, sc[c]);
+                m1 = fmaxf(m1, sc[c + 1]);
+                m2 = fmaxf(m2, sc[c + 2]);
+                m3 = fmaxf(m3, sc[c + 3]);
+            }
+            // scale > 0, so max(s) * scale = max(s * scale)
+            const float m_new = fmaxf(m_i, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * a.qk_scale);
+            const float m_use = m_new == -INFINITY ? 0.0f : m_new;
+            const float alpha = fast_exp2(m_i - m_use);
+            float ps0 = 0.0f, ps1 = 0.0f;
+#pragma unroll
+            for (int c = 0; c < BN; c += 16) {
+                uint32_t hi[16], lo[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    float p = fast_exp2(fmaf(sc[c + e], a.qk_scale, -m_use));
+                    if (e & 1) ps1 += p;
+                    else ps0 += p;
+                    float h = tf32_trunc(p);
+                    hi[e] = __float_as_uint(h);
+                    lo[e] = __float_as_uint(tf32_trunc(p - h));
+                }
+                tmem_st_32x32b_x16(lane_base + scol + c, hi);
+                tmem_st_32x32b_x16(lane_base + pcol + c, lo);
+            }
+            l_i = l_i * alpha + (ps0 + ps1);
+            m_i = m_new;
+            tmem_st_wait();
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&p_full[j & 1]);
+            // fold the previous block's P.V while this block's runs on the tensor core
+            if (j > 0 && !fold(j - 1, alpha_prev)) {
+                ok = false;
+                break;
+            }
+            alpha_prev = alpha;
         }
+        if (ok && nblocks > 0 && !fold(nblocks - 1, alpha_prev)) ok = false;
         if (!ok) {
             if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
             *abort_flag = 1;
