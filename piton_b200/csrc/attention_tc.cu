@@ -275,14 +275,13 @@ __global__ void __launch_bounds__(THREADS, 1)
         auto fold = [&](int jj, float alpha) -> bool {
             if (*abort_flag || !warp_wait(o_full, jj & 1)) return false;
             tc_fence_after();
+            uint32_t r[HD];
 #pragma unroll
-            for (int c = 0; c < HD; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(lane_base + COL_O + c, r);
-                tmem_ld_wait();
+            for (int c = 0; c < HD; c += 16)
+                tmem_ld_32x32b_x16(lane_base + COL_O + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+            tmem_ld_wait();
 #pragma unroll
-                for (int e = 0; e < 16; ++e) acc[c + e] = fmaf(acc[c + e], alpha, __uint_as_float(r[e]));
-            }
+            for (int c = 0; c < HD; ++c) acc[c] = fmaf(acc[c], alpha, __uint_as_float(r[c]));
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_empty);
@@ -297,13 +296,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t k0 = (int64_t)j * BN;
             const uint32_t scol = COL_S0 + (j & 1) * BN, pcol = COL_PLO0 + (j & 1) * BN;
             float sc[BN];
+            {
+                uint32_t r[BN];
 #pragma unroll
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(lane_base + scol + c, r);
-                tmem_ld_wait();
+                for (int c = 0; c < BN; c += 16)
+                    tmem_ld_32x32b_x16(lane_base + scol + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+                tmem_ld_wait();   // one wait for all four loads
 #pragma unroll
-                for (int e = 0; e < 16; ++e) sc[c + e] = __uint_as_float(r[e]);
+                for (int c = 0; c < BN; ++c) sc[c] = __uint_as_float(r[c]);
             }
             // masks only on the blocks that reach past key_end or the causal diagonal
             const bool masked = k0 + BN > a.key_end || (a.causal && k0 + BN - 1 > q0);
@@ -337,7 +337,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     else ps0 += p;
                     float h = tf32_trunc(p);
                     hi[e] = __float_as_uint(h);
-                    lo[e] = __float_as_uint(tf32_trunc(p - h));
+                    lo[e] = __float_as_uint(p - h);   // exact; the tensor core reads its tf32 part
                 }
                 tmem_st_32x32b_x16(lane_base + scol + c, hi);
                 tmem_st_32x32b_x16(lane_base + pcol + c, lo);
