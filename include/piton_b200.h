@@ -204,6 +204,62 @@ typedef struct {
 } piton_layernorm_args;
 PITON_B200_API int piton_b200_layernorm_f32(const piton_layernorm_args *args, void *stream);
 
+/* ---- element-wise float operators: out[i] = f(x[i] (, y[i])) for i < min(n, grid_x * BLOCK) ----
+   op: 0 copy (examples/primitive_kernels.py:12-17 copy_kernel), 1 mul (examples/elementwise.py:5-9 mul_kernel),
+   2 fma x*alpha + y with two roundings (primitive_kernels.py:20-27 fma_kernel), 3 scaled ReLU x > 0 ? x*alpha : 0
+   (examples/kernels.py:79-85), 4 exp2, 5 log2, 6 1/x, 7 rsqrt, 8 exp, 9 sqrt (examples/sfu_tests.py sfu_kernel
+   OP 0-5), 10 natural log (primitive_kernels.py log_kernel).  QPU rounding: ops 0-3. */
+typedef struct {
+    uint64_t x, y, out;   /* float*; y only for mul and fma */
+    int64_t n_elements, block_size, grid_x;
+    double alpha;
+    int32_t op;
+    uint32_t flags;
+} piton_elementwise_args;
+PITON_B200_API int piton_b200_elementwise_f32(const piton_elementwise_args *args, void *stream);
+
+/* ---- exact 32-bit // and % (examples/primitive_kernels.py:30-38 idiv_kernel): C truncation semantics,
+   int32 (is_signed; INT_MIN / -1 = INT_MIN rem 0) or uint32; a zero divisor gives q = all ones, r = x. ---- */
+typedef struct {
+    uint64_t x, y, q, r;  /* int32_t* or uint32_t* */
+    int64_t n_elements, block_size, grid_x;
+    int32_t is_signed;
+    uint32_t flags;
+} piton_idiv_args;
+PITON_B200_API int piton_b200_idiv_i32(const piton_idiv_args *args, void *stream);
+
+/* ---- row sum / row max (examples/kernels.py:88-96 row_sum_kernel, primitive_kernels.py:41-50 row_max_kernel):
+   out[r] for r < grid_x*BLOCK_M over the ceil(n_cols/BLOCK_N)*BLOCK_N columns the reference loads. ---- */
+typedef struct {
+    uint64_t x, out;
+    int64_t n_cols, stride, block_m, block_n, grid_x;
+    int32_t reduce;       /* 0 sum, 1 max (from -FLT_MAX) */
+    uint32_t flags;
+} piton_row_reduce_args;
+PITON_B200_API int piton_b200_row_reduce_f32(const piton_row_reduce_args *args, void *stream);
+
+/* ---- tile transpose (examples/primitive_kernels.py:53-66 transpose_kernel): out[c*stride_out + r] =
+   x[r*stride_x + c] for the tiles of programs below grid_x. ---- */
+typedef struct {
+    uint64_t x, out;
+    int64_t n_rows, n_cols, stride_x, stride_out, block_m, block_n, grid_x;
+    uint32_t flags;
+    uint32_t _pad;
+} piton_transpose_args;
+PITON_B200_API int piton_b200_transpose_f32(const piton_transpose_args *args, void *stream);
+
+/* ---- one Game of Life generation on a torus (examples/life.py:39-147): mode 0 life_kernel (int32 cells,
+   BLOCK_R x BLOCK_C tiles in row-major order, tile ids < grid_x), 1 life_rows_kernel (int32 cells, BLOCK-column
+   strips on grid axis 0 by ROWS rows on axis 1), 2 life_bits_kernel (32 cells per uint32 word, n_cols = words).
+   block_r / block_c: BLOCK_R / BLOCK_C, or ROWS / BLOCK. ---- */
+typedef struct {
+    uint64_t src, dst;
+    int64_t n_rows, n_cols, stride, block_r, block_c, grid_x, grid_y;
+    int32_t mode;
+    uint32_t flags;
+} piton_life_args;
+PITON_B200_API int piton_b200_life_step(const piton_life_args *args, void *stream);
+
 /* ---- TinyGPT greedy decoding (a model the reference does not have; built from its pieces:
    dense layers examples/nn_kernels.py:23-74, attention examples/attention.py:75-113, layer norm
    tests/test_reroll_reduce.py:199-208).  Only vocab 65, d_model 128, 4 layers, 4 heads, context

@@ -173,3 +173,50 @@ def mlp_f64_with_bounds(images, model):
         if layer < 3:
             act = np.maximum(act, 0.0)
     return act, err
+
+
+# ---- integer division, Life, element-wise QPU ops -----------------------------------------
+
+def idiv_c(x, y, signed=True):
+    """C-semantics 32-bit // and % as uint32 bit patterns (INT_MIN / -1 wraps), the
+    definition the reference checks its exact division against (tests/test_fast_idiv.py:146-155)."""
+    M32 = 0xFFFFFFFF
+    a = np.asarray(x).view(np.uint32)
+    b = np.asarray(y).view(np.uint32)
+    if signed:
+        xa, yb = a.view(np.int32).astype(np.int64), b.view(np.int32).astype(np.int64)
+        q = np.sign(xa) * np.sign(yb) * (np.abs(xa) // np.abs(yb))
+        r = xa - q * yb
+    else:
+        xa, yb = a.astype(np.int64), b.astype(np.int64)
+        q, r = xa // yb, xa % yb
+    return (q & M32).astype(np.uint32), (r & M32).astype(np.uint32)
+
+
+def life_step(cells):
+    """One generation on a torus: alive next iff the 3x3 block (cell included) holds 3 live
+    cells, or 4 and the cell is alive (examples/life.py:1-20)."""
+    c = np.asarray(cells).astype(np.int64)
+    t = sum(np.roll(np.roll(c, dr, 0), dc, 1) for dr in (-1, 0, 1) for dc in (-1, 0, 1))
+    return ((t == 3) | ((t == 4) & (c != 0))).astype(np.int32)
+
+
+def pack_bits(cells):
+    """32 cells per uint32 word, bit j of word k = column 32k + j."""
+    return np.packbits(np.asarray(cells, np.uint8), axis=1, bitorder="little").view(np.uint32)
+
+
+def unpack_bits(words, n_cols):
+    return np.unpackbits(np.ascontiguousarray(words).view(np.uint8), axis=1, bitorder="little")[:, :n_cols]
+
+
+def qpu_fma(x, y, alpha):
+    """x * alpha + y as two round-toward-zero operations (no fused multiply-add on the QPU)."""
+    a = np.full(np.shape(x), np.float32(alpha), np.float32)
+    return qpu_binary("fadd", qpu_binary("fmul", x, a), y)
+
+
+def qpu_scaled_relu(x, alpha):
+    x = _f32(x)
+    p = qpu_binary("fmul", x, np.full(x.shape, np.float32(alpha), np.float32))
+    return np.where(x > 0, p, np.float32(0)).astype(np.float32)

@@ -62,3 +62,73 @@ def dense_tiles(output_features):
     """(BM, BN, BK) the reference launches the digits layers with
     (examples/nn_kernels.py:14-20); on B200 they only decide grid coverage."""
     return (4, 64, 4) if output_features >= 64 else (8, 16, 4)
+
+
+# ---- the other example / primitive operators (examples/primitive_kernels.py, elementwise.py,
+# ---- sfu_tests.py, kernels.py:79-96, life.py)
+
+@jit
+def copy_kernel(x_ptr, out_ptr, n, BLOCK: tl.constexpr):
+    """out[i] = x[i], i < n.  (examples/primitive_kernels.py:12-17)"""
+
+
+@jit
+def mul_kernel(x_ptr, y_ptr, out_ptr, n, BLOCK: tl.constexpr):
+    """out[i] = x[i] * y[i].  (examples/elementwise.py:5-9)"""
+
+
+@jit
+def fma_kernel(x_ptr, y_ptr, out_ptr, n, alpha, BLOCK: tl.constexpr):
+    """out[i] = x[i] * alpha + y[i] (multiply, then add).  (examples/primitive_kernels.py:20-27)"""
+
+
+@jit
+def scaled_relu_kernel(x_ptr, out_ptr, n, alpha, BLOCK: tl.constexpr):
+    """out[i] = x[i] * alpha where x[i] > 0, else 0.  (examples/kernels.py:79-85)"""
+
+
+@jit
+def sfu_kernel(x_ptr, out_ptr, n, OP: tl.constexpr, BLOCK: tl.constexpr):
+    """OP 0 exp2, 1 log2, 2 1/x, 3 rsqrt, 4 exp, 5 sqrt.  (examples/sfu_tests.py:5-21)"""
+
+
+@jit
+def log_kernel(x_ptr, out_ptr, n, BLOCK: tl.constexpr):
+    """Natural log.  (examples/primitive_kernels.py:69-76)"""
+
+
+@jit
+def idiv_kernel(x_ptr, y_ptr, q_ptr, r_ptr, n, BLOCK: tl.constexpr):
+    """Exact 32-bit x // y and x % y, C truncation (int32 or uint32 arrays).
+    (examples/primitive_kernels.py:30-38)"""
+
+
+@jit
+def row_sum_kernel(x_ptr, out_ptr, n_cols, stride, BLOCK_M: tl.constexpr, BLOCK_N: tl.constexpr):
+    """out[r] = sum of row r over ceil(n_cols / BLOCK_N) * BLOCK_N columns.  (examples/kernels.py:88-96)"""
+
+
+@jit
+def row_max_kernel(x_ptr, out_ptr, n_cols, stride, BLOCK_M: tl.constexpr, BLOCK_N: tl.constexpr):
+    """out[r] = max of row r (from -FLT_MAX).  (examples/primitive_kernels.py:41-50)"""
+
+
+@jit
+def transpose_kernel(x_ptr, out_ptr, n_rows, n_cols, stride_x, stride_out, BLOCK_M: tl.constexpr,
+                     BLOCK_N: tl.constexpr):
+    """out[c, r] = x[r, c] per BLOCK_M x BLOCK_N tile.  (examples/primitive_kernels.py:53-66)"""
+
+
+@jit
+def life_kernel(src_ptr, dst_ptr, n_rows, n_cols, stride, BLOCK_R: tl.constexpr, BLOCK_C: tl.constexpr):
+    """One Game of Life generation on a torus, int32 0/1 cells, tiles.  (examples/life.py:39-70)"""
+
+
+@jit
+def life_rows_kernel(src_ptr, dst_ptr, n_rows, n_cols, stride, ROWS: tl.constexpr, BLOCK: tl.constexpr):
+    """The same generation, column strips walking rows.  (examples/life.py:73-101)"""
+
+
+@jit
+def life_bits_kernel(src_ptr, dst_ptr, n_rows, n_words, stride, ROWS: tl.constexpr, BLOCK: tl.constexpr):
+    """The same generation on 32 cells per uint32 word.  (examples/life.py:113-147)"""

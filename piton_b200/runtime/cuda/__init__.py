@@ -347,3 +347,136 @@ def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
 
 
 __all__ = ["run_on_b200", "register", "registered", "Buffer", "Launch", "extent", "pinned_empty", "lib", "check"]
+
+
+# ---- element-wise, integer, reduction, transpose and Life operators --------------------------
+
+_ELEM_OPS = {"copy": 0, "mul": 1, "fma": 2, "scaled_relu": 3, "exp2": 4, "log2": 5, "recip": 6, "rsqrt": 7,
+             "exp": 8, "sqrt": 9, "log": 10}
+
+
+def _elementwise(L: Launch, grid, op: str, x: str, y, out: str, alpha: float = 0.0):
+    n, blk = L.int("n"), L.int("BLOCK")
+    n_eff = max(0, min(n, grid[0] * blk))
+    bx, bo = L.ptr(x), L.ptr(out, written=True)
+    by = L.ptr(y) if y else None
+    for b in (bx, bo, by):
+        if b is not None:
+            b.require(0, n_eff - 1)
+    qpu = L.qpu and _ELEM_OPS[op] <= 3
+    if L.qpu and not qpu:
+        raise NotImplementedError("qpu_rounding applies to copy, mul, fma and scaled_relu")
+    a = _lib.ElementwiseArgs(bx.addr, by.addr if by else 0, bo.addr, n, blk, grid[0], float(alpha), _ELEM_OPS[op],
+                             _lib.QPU_ROUNDING if qpu else 0)
+    L.call("piton_b200_elementwise_f32", a, op)
+    return {"bytes": 4 * n_eff * (3 if by else 2), "flops": n_eff, "path": f"elementwise_{op}"}
+
+
+@register("copy_kernel", ("x_ptr", "out_ptr", "n", "BLOCK"))
+def _copy(L, grid):
+    return _elementwise(L, grid, "copy", "x_ptr", None, "out_ptr")
+
+
+@register("mul_kernel", ("x_ptr", "y_ptr", "out_ptr", "n", "BLOCK"))
+def _mul(L, grid):
+    return _elementwise(L, grid, "mul", "x_ptr", "y_ptr", "out_ptr")
+
+
+@register("fma_kernel", ("x_ptr", "y_ptr", "out_ptr", "n", "alpha", "BLOCK"))
+def _fma(L, grid):
+    return _elementwise(L, grid, "fma", "x_ptr", "y_ptr", "out_ptr", L.float("alpha"))
+
+
+@register("scaled_relu_kernel", ("x_ptr", "out_ptr", "n", "alpha", "BLOCK"))
+def _scaled_relu(L, grid):
+    return _elementwise(L, grid, "scaled_relu", "x_ptr", None, "out_ptr", L.float("alpha"))
+
+
+@register("sfu_kernel", ("x_ptr", "out_ptr", "n", "OP", "BLOCK"))
+def _sfu(L, grid):
+    op = ["exp2", "log2", "recip", "rsqrt", "exp", "sqrt"][min(max(L.int("OP"), 0), 5)]
+    return _elementwise(L, grid, op, "x_ptr", None, "out_ptr")
+
+
+@register("log_kernel", ("x_ptr", "out_ptr", "n", "BLOCK"))
+def _log(L, grid):
+    return _elementwise(L, grid, "log", "x_ptr", None, "out_ptr")
+
+
+@register("idiv_kernel", ("x_ptr", "y_ptr", "q_ptr", "r_ptr", "n", "BLOCK"))
+def _idiv(L, grid):
+    n, blk = L.int("n"), L.int("BLOCK")
+    n_eff = max(0, min(n, grid[0] * blk))
+    X, Y = L.ptr("x_ptr"), L.ptr("y_ptr")
+    Q, R = L.ptr("q_ptr", written=True), L.ptr("r_ptr", written=True)
+    for b in (X, Y, Q, R):
+        if b.itemsize != 4:
+            raise TypeError("idiv_kernel takes int32 or uint32 arrays")
+        b.require(0, n_eff - 1)
+    signed = str(X.tensor.dtype) in ("torch.int32",)
+    a = _lib.IdivArgs(X.addr, Y.addr, Q.addr, R.addr, n, blk, grid[0], int(signed), 0)
+    L.call("piton_b200_idiv_i32", a, "idiv_kernel")
+    return {"bytes": 16 * n_eff, "flops": n_eff, "path": "idiv"}
+
+
+def _row_reduce(L, grid, reduce):
+    bm, bn = L.int("BLOCK_M"), L.int("BLOCK_N")
+    n_cols, stride = L.int("n_cols"), L.int("stride")
+    rows = grid[0] * bm
+    cols = -(-n_cols // bn) * bn
+    X, O = L.ptr("x_ptr"), L.ptr("out_ptr", written=True)
+    X.require(*extent((rows, stride), (cols, 1)))
+    O.require(0, rows - 1)
+    a = _lib.RowReduceArgs(X.addr, O.addr, n_cols, stride, bm, bn, grid[0], reduce, 0)
+    L.call("piton_b200_row_reduce_f32", a, "row_reduce")
+    return {"bytes": 4 * rows * (cols + 1), "flops": rows * cols, "path": "row_max" if reduce else "row_sum"}
+
+
+@register("row_sum_kernel", ("x_ptr", "out_ptr", "n_cols", "stride", "BLOCK_M", "BLOCK_N"))
+def _row_sum(L, grid):
+    return _row_reduce(L, grid, 0)
+
+
+@register("row_max_kernel", ("x_ptr", "out_ptr", "n_cols", "stride", "BLOCK_M", "BLOCK_N"))
+def _row_max(L, grid):
+    return _row_reduce(L, grid, 1)
+
+
+@register("transpose_kernel", ("x_ptr", "out_ptr", "n_rows", "n_cols", "stride_x", "stride_out", "BLOCK_M",
+                               "BLOCK_N"))
+def _transpose(L, grid):
+    nr, nc = L.int("n_rows"), L.int("n_cols")
+    sx, so = L.int("stride_x"), L.int("stride_out")
+    X, O = L.ptr("x_ptr"), L.ptr("out_ptr", written=True)
+    X.require(*extent((nr, sx), (nc, 1)))
+    O.require(*extent((nc, so), (nr, 1)))
+    a = _lib.TransposeArgs(X.addr, O.addr, nr, nc, sx, so, L.int("BLOCK_M"), L.int("BLOCK_N"), grid[0], 0, 0)
+    L.call("piton_b200_transpose_f32", a, "transpose_kernel")
+    return {"bytes": 8 * nr * nc, "flops": 0, "path": "transpose"}
+
+
+def _life(L, grid, mode, cols_name, br_name, bc_name):
+    nr, nc, st = L.int("n_rows"), L.int(cols_name), L.int("stride")
+    S, D = L.ptr("src_ptr"), L.ptr("dst_ptr", written=True)
+    for b in (S, D):
+        if b.itemsize != 4:
+            raise TypeError("Life grids are int32 cells or uint32 words")
+        b.require(*extent((nr, st), (nc, 1)))
+    a = _lib.LifeArgs(S.addr, D.addr, nr, nc, st, L.int(br_name), L.int(bc_name), grid[0], grid[1], mode, 0)
+    L.call("piton_b200_life_step", a, "life")
+    return {"bytes": 8 * nr * nc, "flops": 0, "path": ["life_tiles", "life_rows", "life_bits"][mode]}
+
+
+@register("life_kernel", ("src_ptr", "dst_ptr", "n_rows", "n_cols", "stride", "BLOCK_R", "BLOCK_C"))
+def _life_tiles(L, grid):
+    return _life(L, grid, 0, "n_cols", "BLOCK_R", "BLOCK_C")
+
+
+@register("life_rows_kernel", ("src_ptr", "dst_ptr", "n_rows", "n_cols", "stride", "ROWS", "BLOCK"))
+def _life_rows(L, grid):
+    return _life(L, grid, 1, "n_cols", "ROWS", "BLOCK")
+
+
+@register("life_bits_kernel", ("src_ptr", "dst_ptr", "n_rows", "n_words", "stride", "ROWS", "BLOCK"))
+def _life_bits(L, grid):
+    return _life(L, grid, 2, "n_words", "ROWS", "BLOCK")

@@ -69,6 +69,31 @@ class LayernormArgs(C.Structure):
                 ("y_row_stride", i64), ("eps", f64), ("flags", u32), ("_pad", u32)]
 
 
+class ElementwiseArgs(C.Structure):
+    _fields_ = [("x", u64), ("y", u64), ("out", u64), ("n_elements", i64), ("block_size", i64), ("grid_x", i64),
+                ("alpha", f64), ("op", i32), ("flags", u32)]
+
+
+class IdivArgs(C.Structure):
+    _fields_ = [("x", u64), ("y", u64), ("q", u64), ("r", u64), ("n_elements", i64), ("block_size", i64),
+                ("grid_x", i64), ("is_signed", i32), ("flags", u32)]
+
+
+class RowReduceArgs(C.Structure):
+    _fields_ = [("x", u64), ("out", u64), ("n_cols", i64), ("stride", i64), ("block_m", i64), ("block_n", i64),
+                ("grid_x", i64), ("reduce", i32), ("flags", u32)]
+
+
+class TransposeArgs(C.Structure):
+    _fields_ = [("x", u64), ("out", u64), ("n_rows", i64), ("n_cols", i64), ("stride_x", i64), ("stride_out", i64),
+                ("block_m", i64), ("block_n", i64), ("grid_x", i64), ("flags", u32), ("_pad", u32)]
+
+
+class LifeArgs(C.Structure):
+    _fields_ = [("src", u64), ("dst", u64), ("n_rows", i64), ("n_cols", i64), ("stride", i64), ("block_r", i64),
+                ("block_c", i64), ("grid_x", i64), ("grid_y", i64), ("mode", i32), ("flags", u32)]
+
+
 class TinyGPTArgs(C.Structure):
     _fields_ = [("weights", u64), ("kv_cache", u64), ("tokens", u64), ("logits", u64), ("batch", i64),
                 ("prompt_len", i64), ("new_tokens", i64), ("vocab", i32), ("d_model", i32), ("n_layer", i32),
@@ -103,13 +128,20 @@ PROTOTYPES = {
     "piton_b200_attention_workspace_size": (C.c_size_t, [C.POINTER(AttentionArgs)]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
     "piton_b200_layernorm_f32": (C.c_int, [C.POINTER(LayernormArgs), C.c_void_p]),
+    "piton_b200_elementwise_f32": (C.c_int, [C.POINTER(ElementwiseArgs), C.c_void_p]),
+    "piton_b200_idiv_i32": (C.c_int, [C.POINTER(IdivArgs), C.c_void_p]),
+    "piton_b200_row_reduce_f32": (C.c_int, [C.POINTER(RowReduceArgs), C.c_void_p]),
+    "piton_b200_transpose_f32": (C.c_int, [C.POINTER(TransposeArgs), C.c_void_p]),
+    "piton_b200_life_step": (C.c_int, [C.POINTER(LifeArgs), C.c_void_p]),
     "piton_b200_tinygpt_weight_floats": (C.c_int64, []),
     "piton_b200_tinygpt_generate": (C.c_int, [C.POINTER(TinyGPTArgs), C.c_void_p]),
 }
 
 STRUCTS = {"piton_allgather_args": AllgatherArgs, "piton_add_args": AddArgs, "piton_softmax_args": SoftmaxArgs, "piton_matmul_args": MatmulArgs,
            "piton_dense_args": DenseArgs, "piton_mlp_args": MlpArgs, "piton_attention_args": AttentionArgs,
-           "piton_layernorm_args": LayernormArgs, "piton_tinygpt_args": TinyGPTArgs}
+           "piton_layernorm_args": LayernormArgs, "piton_tinygpt_args": TinyGPTArgs,
+           "piton_elementwise_args": ElementwiseArgs, "piton_idiv_args": IdivArgs,
+           "piton_row_reduce_args": RowReduceArgs, "piton_transpose_args": TransposeArgs, "piton_life_args": LifeArgs}
 
 _lib = None
 

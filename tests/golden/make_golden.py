@@ -311,6 +311,78 @@ def case_attention(fp, procs, big):
             save(name, meta, heads_kept=np.arange(2), out_first_heads=out[:2])
 
 
+def case_idiv(fp, procs, big):
+    import piton
+    from primitive_kernels import idiv_kernel
+    M32 = 0xFFFFFFFF
+    for signed in (True, False):
+        name = f"idiv_{'i32' if signed else 'u32'}"
+        if exists(name):
+            continue
+        rng = np.random.default_rng(10 + signed)
+        edges = [0, 1, 2, 3, 7, 255, 256, 0x7FFFFFFF, 0x80000000, 0xFFFFFFFF, 0x80000001, 0xFFFFFFFE]
+        edges += [((1 << e) + d) & M32 for e in range(33) for d in (-1, 0, 1)]
+        xe = np.array(edges, np.uint64)
+        x = np.concatenate([xe, rng.integers(0, 1 << 32, 300, dtype=np.uint64)]).astype(np.uint32)
+        y = np.concatenate([xe[::-1], rng.integers(0, 1 << 32, 300, dtype=np.uint64)
+                            >> rng.integers(0, 32, 300).astype(np.uint64)]).astype(np.uint32)
+        y[y == 0] = 1
+        if signed:
+            x, y = x.view(np.int32), y.view(np.int32)
+        n = x.size
+        q = np.zeros_like(x)
+        r = np.zeros_like(x)
+        t = time.time()
+        idiv_kernel[(piton.cdiv(n, 64),)](x, y, q, r, n, BLOCK=64)
+        save(name, dict(op="idiv", signed=signed, n=n, ref=fp, emu_seconds=time.time() - t), x=x, y=y, q=q, r=r)
+
+
+def case_life(fp, procs, big):
+    import piton
+    import life as Lf
+    for kname, shape, seed in (("tile", (13, 37), 1), ("rows", (21, 50), 2), ("bits", (9, 128), 3)):
+        name = f"life_{kname}_{shape[0]}x{shape[1]}"
+        if exists(name):
+            continue
+        rng = np.random.default_rng(seed)
+        cells = (rng.random(shape) < 0.35).astype(np.int32)
+        kern, _, consts, per = Lf.KERNELS[kname]
+        if kname == "bits":
+            words = np.packbits(cells.astype(np.uint8), axis=1, bitorder="little").view(np.uint32)
+            src = np.ascontiguousarray(words)
+            ncols = src.shape[1]
+        else:
+            src = cells.copy()
+            ncols = shape[1]
+        dst = np.zeros_like(src)
+        t = time.time()
+        if kname == "tile":
+            grid = (piton.cdiv(shape[0], consts["BLOCK_R"]) * piton.cdiv(ncols, consts["BLOCK_C"]),)
+        else:
+            grid = (piton.cdiv(ncols, consts["BLOCK"]), piton.cdiv(shape[0], consts["ROWS"]))
+        kern[grid](src, dst, shape[0], ncols, ncols, **consts)
+        save(name, dict(op="life", kernel=kname, shape=list(shape), constants=consts, grid=list(grid), ref=fp,
+                        emu_seconds=time.time() - t), src=src, dst=dst)
+
+
+def case_elem(fp, procs, big):
+    import piton
+    from elementwise import mul_kernel
+    from primitive_kernels import fma_kernel
+    from kernels import scaled_relu_kernel
+    n = 1000
+    x, y = W.vector_add(n, 77)
+    for name, fn in (("elem_mul", lambda o: mul_kernel[(piton.cdiv(n, 64),)](x, y, o, n, BLOCK=64)),
+                     ("elem_fma", lambda o: fma_kernel[(piton.cdiv(n, 64),)](x, y, o, n, 0.3, BLOCK=64)),
+                     ("elem_scaled_relu", lambda o: scaled_relu_kernel[(piton.cdiv(n, 128),)](x, o, n, 0.5,
+                                                                                                BLOCK=128))):
+        if exists(name):
+            continue
+        out = np.zeros(n, np.float32)
+        fn(out)
+        save(name, dict(op=name, n=n, seed=77, ref=fp), x=x, y=y, out=out)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--ref", default=os.environ.get("PITON_REFERENCE", ""), required=False)
@@ -326,7 +398,8 @@ def main():
     fp = ref_fingerprint(args.ref)
     only = set(filter(None, args.only.split(",")))
     for name, fn in (("add", case_add), ("softmax", case_softmax), ("matmul", case_matmul),
-                     ("dense", case_dense), ("attention", case_attention)):
+                     ("dense", case_dense), ("attention", case_attention), ("idiv", case_idiv), ("life", case_life),
+                     ("elem", case_elem)):
         if not only or name in only:
             fn(fp, args.procs, args.big)
 

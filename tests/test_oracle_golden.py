@@ -100,3 +100,37 @@ def test_attention(g):
         np.testing.assert_array_equal(bits(o), bits(g["out"]))
     else:
         np.testing.assert_array_equal(bits(o[:2]), bits(g["out_first_heads"]))
+
+
+IDIV = goldens("idiv_")
+LIFE = goldens("life_")
+ELEM = goldens("elem_")
+
+
+@pytest.mark.parametrize("g", IDIV, ids=golden_ids(IDIV))
+def test_idiv(g):
+    q, r = O.idiv_c(g["x"], g["y"], g.meta["signed"])
+    np.testing.assert_array_equal(q, g["q"].view(np.uint32))
+    np.testing.assert_array_equal(r, g["r"].view(np.uint32))
+
+
+@pytest.mark.parametrize("g", LIFE, ids=golden_ids(LIFE))
+def test_life(g):
+    if g.meta["kernel"] == "bits":
+        n_cols = g.meta["shape"][1]
+        want = O.pack_bits(O.life_step(O.unpack_bits(g["src"], n_cols)))
+        np.testing.assert_array_equal(want, g["dst"])
+    else:
+        np.testing.assert_array_equal(O.life_step(g["src"]), g["dst"])
+
+
+@pytest.mark.parametrize("g", ELEM, ids=golden_ids(ELEM))
+def test_elementwise_qpu(g):
+    x, y = g["x"], g["y"]
+    if g.meta["op"] == "elem_mul":
+        got = O.qpu_binary("fmul", x, y)
+    elif g.meta["op"] == "elem_fma":
+        got = O.qpu_fma(x, y, 0.3)
+    else:
+        got = O.qpu_scaled_relu(x, 0.5)
+    np.testing.assert_array_equal(bits(got), bits(g["out"]))
