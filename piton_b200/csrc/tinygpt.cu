@@ -39,58 +39,66 @@ struct StepArgs {
     int end;          // prompt_len + new_tokens
 };
 
-// out[s][n] = act(sum_k in[s][k] W[k][n] + b[n]) for the CTA's SEQ rows.  Threads
-// are spread over n; when N < THREADS the k range is split between thread groups
-// and the partial sums are added through `scratch` (SEQ * THREADS floats).
+// out[s][n] = act(sum_k in[s][k] W[k][n] + b[n]) for the CTA's SEQ rows.  A
+// thread owns 4 adjacent columns (16-byte weight loads) of one k-group; the
+// k range is split into G groups so that every thread has work, and the
+// partial sums meet in `scratch` (SEQ * THREADS * 4 floats).  Eight k-steps
+// are unrolled so 8 x 16 bytes of weights are in flight per thread: the
+// weights come from L2 and this loop is latency-bound otherwise.
 template <int K, int N, bool GELU>
 __device__ __forceinline__ void linear(const float *in, float *out, const float *__restrict__ W,
                                        const float *__restrict__ b, float *scratch, bool residual) {
-    constexpr int G = N >= THREADS ? 1 : THREADS / N;   // k-groups
+    constexpr int NQ = N / 4;                             // column quads
+    constexpr int G = THREADS / NQ > 0 ? THREADS / NQ : 1;  // k-groups
     constexpr int KG = K / G;
+    static_assert(N % 4 == 0 && K % G == 0 && NQ * G <= THREADS && G >= 2, "linear tiling");
     const int tid = threadIdx.x;
-    if constexpr (G == 1) {
-        for (int n = tid; n < N; n += THREADS) {
-            float acc[SEQ];
+    const int q = tid % NQ, g = tid / NQ;
+    float4 acc[SEQ];
 #pragma unroll
-            for (int s = 0; s < SEQ; ++s) acc[s] = __ldg(b + n);
-#pragma unroll 8
-            for (int k = 0; k < K; ++k) {
-                float w = __ldg(W + (int64_t)k * N + n);
-#pragma unroll
-                for (int s = 0; s < SEQ; ++s) acc[s] = fmaf(in[s * K + k], w, acc[s]);
-            }
-#pragma unroll
-            for (int s = 0; s < SEQ; ++s) {
-                float v = acc[s];
-                if (GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-                out[s * N + n] = residual ? out[s * N + n] + v : v;
-            }
-        }
-        __syncthreads();
-    } else {
-        const int n = tid % N, g = tid / N;
-        float acc[SEQ];
-#pragma unroll
-        for (int s = 0; s < SEQ; ++s) acc[s] = 0.0f;
+    for (int s = 0; s < SEQ; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (g < G) {
+        const float4 *w4 = reinterpret_cast<const float4 *>(W) + q;
 #pragma unroll 8
         for (int k = g * KG; k < (g + 1) * KG; ++k) {
-            float w = __ldg(W + (int64_t)k * N + n);
+            float4 w = __ldg(w4 + (int64_t)k * NQ);
 #pragma unroll
-            for (int s = 0; s < SEQ; ++s) acc[s] = fmaf(in[s * K + k], w, acc[s]);
+            for (int s = 0; s < SEQ; ++s) {
+                float xv = in[s * K + k];
+                acc[s].x = fmaf(xv, w.x, acc[s].x);
+                acc[s].y = fmaf(xv, w.y, acc[s].y);
+                acc[s].z = fmaf(xv, w.z, acc[s].z);
+                acc[s].w = fmaf(xv, w.w, acc[s].w);
+            }
         }
+    }
+    {
+        float4 *sc4 = reinterpret_cast<float4 *>(scratch);
+        if (g < G) {
 #pragma unroll
-        for (int s = 0; s < SEQ; ++s) scratch[s * THREADS + tid] = acc[s];
-        __syncthreads();
-        for (int i = tid; i < SEQ * N; i += THREADS) {
-            int s = i / N, nn = i % N;
-            float v = __ldg(b + nn);
-#pragma unroll
-            for (int gg = 0; gg < G; ++gg) v += scratch[s * THREADS + gg * N + nn];
-            if (GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
-            out[s * N + nn] = residual ? out[s * N + nn] + v : v;
+            for (int s = 0; s < SEQ; ++s) sc4[s * THREADS + g * NQ + q] = acc[s];
         }
         __syncthreads();
     }
+    for (int i = tid; i < SEQ * NQ; i += THREADS) {
+        const int s = i / NQ, qq = i % NQ;
+        const float4 *sc4 = reinterpret_cast<const float4 *>(scratch);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int gg = 0; gg < G; ++gg) {
+            float4 p = sc4[s * THREADS + gg * NQ + qq];
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        float4 bb = __ldg(reinterpret_cast<const float4 *>(b) + qq);
+        float r[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            if (GELU) r[j] = 0.5f * r[j] * (1.0f + erff(r[j] * 0.70710678118654752f));
+            const int n = 4 * qq + j;
+            out[s * N + n] = residual ? out[s * N + n] + r[j] : r[j];
+        }
+    }
+    __syncthreads();
 }
 
 // y[s] = LayerNorm(x[s]) * g + b, one warp per sequence (biased variance, eps 1e-5).
@@ -126,9 +134,9 @@ __device__ __forceinline__ void layernorm(const float *x, float *y, const float 
 }
 
 __global__ void __launch_bounds__(THREADS) tinygpt_step_kernel(StepArgs a) {
-    __shared__ float x[SEQ * D], h[SEQ * D], qkv[SEQ * 3 * D], att[SEQ * D], f[SEQ * F];
+    __shared__ __align__(16) float x[SEQ * D], h[SEQ * D], qkv[SEQ * 3 * D], att[SEQ * D], f[SEQ * F];
     __shared__ float probs[SEQ * H][CTX];
-    __shared__ float scratch[SEQ * THREADS];
+    __shared__ __align__(16) float scratch[SEQ * THREADS * 4];
     __shared__ float lg[SEQ][V + 3];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t b0 = (int64_t)blockIdx.x * SEQ;
