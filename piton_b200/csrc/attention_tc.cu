@@ -6,26 +6,29 @@
 //  1. split: K -> K_hi, K_lo as [heads * n_ctx, D] and V -> V^T_hi, V^T_lo as
 //     [heads * D, ld] (ld = n_ctx rounded up to 4), tf32 hi/lo halves, into the
 //     workspace.
-//  2. one CTA per (head, 128-query block), 320 threads:
-//     * two softmax groups of 4 warps (one thread per query row = TMEM lane):
-//       group 0 takes the even 64-key blocks, group 1 the odd ones, each with
-//       its own online softmax state, so two warps per SM sub-partition hide
-//       each other's TMEM and barrier latency; per block a group reads the
-//       scores S from TMEM (twice: row max, then exponentials), writes P_hi
-//       over S and P_lo beside it, and folds its previous block's P.V
-//       accumulator into fp32 registers (round to nearest).  At the end group
-//       1 hands (max, sum, accumulator) to group 0, which merges and stores O;
-//     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle, 3 stages);
+//  2. one CTA per (head, 128-query block), 192 threads:
+//     * warps 2-5 (one thread per query row = TMEM lane) load the row of Q,
+//       split it and store Q_hi, Q_lo into TMEM; per 64-key block they read
+//       the scores S from TMEM, apply scale and masks, update the running max
+//       and sum in registers (no shuffles: a row lives in one thread), write
+//       P_hi over S and P_lo next to it in TMEM, then fold the block's P.V
+//       into an fp32 register accumulator (round to nearest) and finally
+//       store O / l;
+//     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle);
 //     * warp 1 issues, from one thread, S = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi
-//       (A = Q from TMEM, B from shared memory, 128x64x8 kind::tf32) and
-//       O_blk = P_lo V_hi + P_hi V_lo + P_hi V_hi (A = P from TMEM), and the
-//       next S of a group right after its P.V.
-//     A block's P.V lands in its own TMEM accumulator, so the tensor core's
-//     truncating accumulation never spans more than one 64-key block.
-// TMEM columns: Q_hi [0,64) Q_lo [64,128), group g at 128 + 192 g:
-// S/P_hi +0, P_lo +64, O_blk +128 (512 allocated).  All waits are bounded
-// (2 s): on expiry the kernel records a status, drains its copies and MMAs,
-// frees TMEM and returns.
+//       (A from TMEM, B from shared memory, 128x64x8 kind::tf32) and
+//       O_blk = P_lo V_hi + P_hi V_lo + P_hi V_hi (A = P from TMEM).
+//     A block's P.V lands in its own TMEM accumulator that the softmax warps
+//     add into registers, so the tensor core's truncating accumulation never
+//     spans more than one 64-key block.
+// The scores of block j+1 are computed while the softmax warps work on block
+// j (two S/P buffers), and a block's P.V accumulator (two O_blk buffers) is
+// folded into the registers two blocks later, in the same TMEM round trip as
+// that block's scores, so the tensor core and the softmax warps overlap.
+// TMEM columns: Q_hi [0,64) Q_lo [64,128) S/P_hi x2 [128,256) P_lo x2
+// [256,384) O_blk x2 [384,512).
+// K / V^T tiles: 3-stage TMA ring.  All waits are bounded (2 s): on expiry
+// the kernel records a status, drains its copies and MMAs, frees TMEM, returns.
 #include "attention.cuh"
 #include "common.cuh"
 #include "sm100.cuh"
@@ -38,14 +41,13 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HD = 64, STAGES = 3, THREADS = 320;
+constexpr int BM = 128, BN = 64, HD = 64, STAGES = 3, THREADS = 192;
 constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes
 constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;            // one 64 x 64 fp32 operand tile
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;          // K_hi, K_lo, V^T_hi, V^T_lo
 constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
-// TMEM columns: Q_hi, Q_lo, then per softmax group S/P_hi, P_lo and O_blk
-constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_G0 = 128, COL_GROUP = 192, OFF_S = 0, OFF_PLO = 64, OFF_O = 128;
+constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_PLO0 = 256, COL_O0 = 384;   // S, P_lo, O: two buffers each
 
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
@@ -109,14 +111,13 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *kv_full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
     uint64_t *kv_empty = kv_full + STAGES;
-    uint64_t *s_full = kv_empty + STAGES;     // [2]: one per softmax group
+    uint64_t *s_full = kv_empty + STAGES;     // [2]
     uint64_t *p_full = s_full + 2;            // [2]
     uint64_t *o_full = p_full + 2;            // [2]
     uint64_t *o_empty = o_full + 2;           // [2]
     uint64_t *q_ready = o_empty + 2;
     uint64_t *drain = q_ready + 1;
-    uint64_t *merge_bar = drain + 1;
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(merge_bar + 1);
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -133,15 +134,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             mbar_init(&kv_full[s], 1);
             mbar_init(&kv_empty[s], 1);
         }
-        for (int w = 0; w < 2; ++w) {
-            mbar_init(&s_full[w], 1);
-            mbar_init(&p_full[w], 4);
-            mbar_init(&o_full[w], 1);
-            mbar_init(&o_empty[w], 4);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&s_full[b], 1);
+            mbar_init(&p_full[b], 4);
+            mbar_init(&o_full[b], 1);
+            mbar_init(&o_empty[b], 4);
         }
         mbar_init(q_ready, 4);
         mbar_init(drain, 1);
-        mbar_init(merge_bar, 4);
         *abort_flag = 0;
         fence_mbarrier_init();
         prefetch_tmap(&m_khi);
@@ -182,10 +182,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!mbar_wait(&kv_full[j % STAGES], (j / STAGES) & 1)) record_status(STATUS_TIMEOUT_DRAIN);
         }
     } else if (warp == 1) {
-        // ---------------- MMA issuer ----------------
-        // block j belongs to softmax group w = j & 1 (its S/P, P_lo and O columns); S of
-        // block j + 2 is issued right after P_j V, so each group's next scores are ready
-        // when it finishes its current block
+        // ---------------- MMA issuer: S_{j+1} is issued before P_j V so it overlaps softmax j ----------------
         if (lane == 0) {
             constexpr uint32_t IDESC = idesc_tf32(BM, BN);
             bool ok = mbar_wait(q_ready, 0);
@@ -196,7 +193,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tc_fence_after();
                 const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
                 const uint32_t khi = base, klo = base + TILE_BYTES;
-                const uint32_t d = tmem + COL_G0 + (j & 1) * COL_GROUP + OFF_S;
+                const uint32_t d = tmem + COL_S0 + (j & 1) * BN;
 #pragma unroll
                 for (int ks = 0; ks < HD / 8; ++ks) {
                     const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
@@ -209,10 +206,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                 mma_commit(&s_full[j & 1]);
                 return true;
             };
-            for (int j = 0; ok && j < 2 && j < nblocks; ++j) ok = issue_s(j);
+            if (ok && nblocks > 0) ok = issue_s(0);
             for (int j = 0; ok && j < nblocks && !*abort_flag; ++j) {
-                const int w = j & 1, u = j >> 1;
-                if (!mbar_wait(&p_full[w], u & 1) || (u > 0 && !mbar_wait(&o_empty[w], (u - 1) & 1))) {
+                if (j + 1 < nblocks && !issue_s(j + 1)) {
+                    ok = false;
+                    break;
+                }
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) ||
+                    (j > 1 && !mbar_wait(&o_empty[j & 1], ((j >> 1) - 1) & 1))) {
                     ok = false;
                     break;
                 }
@@ -220,22 +221,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int s = j % STAGES;
                 const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
                 const uint32_t vhi = base + 2 * TILE_BYTES, vlo = base + 3 * TILE_BYTES;
-                const uint32_t g = tmem + COL_G0 + w * COL_GROUP;
+                const uint32_t phi = tmem + COL_S0 + (j & 1) * BN, plo = tmem + COL_PLO0 + (j & 1) * BN;
+                const uint32_t ocol = tmem + COL_O0 + (j & 1) * HD;
 #pragma unroll
                 for (int ks = 0; ks < BN / 8; ++ks) {
                     const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
                     const uint64_t bh = smem_desc_kmajor(vhi + off, 128, LAYOUT_SWIZZLE_128B);
                     const uint64_t bl = smem_desc_kmajor(vlo + off, 128, LAYOUT_SWIZZLE_128B);
-                    mma_tf32_ts(g + OFF_O, g + OFF_PLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
-                    mma_tf32_ts(g + OFF_O, g + OFF_S + 8 * ks, bl, IDESC, 1u);
-                    mma_tf32_ts(g + OFF_O, g + OFF_S + 8 * ks, bh, IDESC, 1u);
+                    mma_tf32_ts(ocol, plo + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(ocol, phi + 8 * ks, bl, IDESC, 1u);
+                    mma_tf32_ts(ocol, phi + 8 * ks, bh, IDESC, 1u);
                 }
-                mma_commit(&o_full[w]);
+                mma_commit(&o_full[j & 1]);
                 mma_commit(&kv_empty[s]);
-                if (j + 2 < nblocks && !issue_s(j + 2)) {
-                    ok = false;
-                    break;
-                }
             }
             if (!ok) {
                 record_status(STATUS_TIMEOUT_MMA);
@@ -245,18 +243,12 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!mbar_wait(drain, 0)) record_status(STATUS_TIMEOUT_DRAIN);
         }
     } else {
-        // ---------------- softmax groups: warps 2-5 (even blocks) and 6-9 (odd blocks) ----------------
-        // Each group runs its own online softmax over its blocks for all 128 rows (thread =
-        // row = TMEM lane); at the end group 1 hands (m, l, acc) to group 0 through shared
-        // memory and group 0 merges and stores.
-        const int grp = (warp - 2) >> 2;
+        // ---------------- softmax / accumulate / store (warps 2-5) ----------------
         const int quarter = warp & 3;
-        const int rrow = quarter * 32 + lane;                 // row inside the tile
-        const int64_t row = q0 + rrow;
+        const int64_t row = q0 + quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
-        const uint32_t gcol = COL_G0 + grp * COL_GROUP;
         bool ok = true;
-        if (grp == 0) {
+        {
             // Q row -> tf32 hi / lo -> TMEM
             const float *qr = a.q + head * a.sqh + row * a.sqm;
             const bool live = row < a.n_ctx;
@@ -278,126 +270,112 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(q_ready);
         }
-        float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
+        float m_i = -INFINITY, l_i = 0.0f;
+        float alpha_hist[2] = {1.0f, 1.0f};   // alpha of blocks j-2 and j-1
         float acc[HD];
 #pragma unroll
         for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
-        // acc = acc * alpha + this group's P.V accumulator of its u-th block
-        auto fold = [&](int u, float alpha) -> bool {
-            if (*abort_flag || !warp_wait(&o_full[grp], u & 1)) return false;
-            tc_fence_after();
+        // fold O_blk of block jj (buffer jj & 1): acc = acc * alpha + O_blk, then free the buffer
+        auto fold_from = [&](const uint32_t (&r)[HD], float alpha, int jj) {
 #pragma unroll
-            for (int c = 0; c < HD; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(lane_base + gcol + OFF_O + c, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) acc[c + e] = fmaf(acc[c + e], alpha, __uint_as_float(r[e]));
-            }
+            for (int c = 0; c < HD; ++c) acc[c] = fmaf(acc[c], alpha, __uint_as_float(r[c]));
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[grp]);
-            return true;
+            if (lane == 0) mbar_arrive(&o_empty[jj & 1]);
         };
-        int u = 0;
-        for (int j = grp; j < nblocks; j += 2, ++u) {
-            if (*abort_flag || !warp_wait(&s_full[grp], u & 1)) {
+        for (int j = 0; j < nblocks; ++j) {
+            // block j's scores and, two blocks behind, block j-2's P.V: one TMEM round trip
+            bool got = !*abort_flag && warp_wait(&s_full[j & 1], (j >> 1) & 1);
+            if (got && j > 1) got = warp_wait(&o_full[j & 1], ((j >> 1) - 1) & 1);
+            if (!got) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int64_t k0 = (int64_t)j * BN;
+            const uint32_t scol = COL_S0 + (j & 1) * BN, pcol = COL_PLO0 + (j & 1) * BN;
+            uint32_t rs[BN], ro[HD];
+#pragma unroll
+            for (int c = 0; c < BN; c += 16)
+                tmem_ld_32x32b_x16(lane_base + scol + c, *reinterpret_cast<uint32_t(*)[16]>(rs + c));
+            if (j > 1) {
+#pragma unroll
+                for (int c = 0; c < HD; c += 16)
+                    tmem_ld_32x32b_x16(lane_base + COL_O0 + (j & 1) * HD + c, *reinterpret_cast<uint32_t(*)[16]>(ro + c));
+            }
+            tmem_ld_wait();
+            if (j > 1) fold_from(ro, alpha_hist[0], j - 2);
+            float sc[BN];
+#pragma unroll
+            for (int c = 0; c < BN; ++c) sc[c] = __uint_as_float(rs[c]);
+            // masks only on the blocks that reach past key_end or the causal diagonal
             const bool masked = k0 + BN > a.key_end || (a.causal && k0 + BN - 1 > q0);
-            // pass 1: row max of the raw scores (scale > 0 commutes with max)
-            float m0 = -INFINITY, m1 = -INFINITY;
+            if (masked) {
 #pragma unroll
-            for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16];
-                tmem_ld_32x32b_x16(lane_base + gcol + OFF_S + c, r);
-                tmem_ld_wait();
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    float v = __uint_as_float(r[e]);
-                    if (masked) {
-                        const int64_t col = k0 + c + e;
-                        if (col >= a.key_end || (a.causal && col > row)) v = -INFINITY;
-                    }
-                    if (e & 1) m1 = fmaxf(m1, v);
-                    else m0 = fmaxf(m0, v);
+                for (int c = 0; c < BN; ++c) {
+                    const int64_t col = k0 + c;
+                    if (col >= a.key_end || (a.causal && col > row)) sc[c] = -INFINITY;
                 }
             }
-            const float m_new = fmaxf(m_i, fmaxf(m0, m1) * a.qk_scale);
+            float m0 = sc[0], m1 = sc[1], m2 = sc[2], m3 = sc[3];
+#pragma unroll
+            for (int c = 4; c < BN; c += 4) {
+                m0 = fmaxf(m0, sc[c]);
+                m1 = fmaxf(m1, sc[c + 1]);
+                m2 = fmaxf(m2, sc[c + 2]);
+                m3 = fmaxf(m3, sc[c + 3]);
+            }
+            // scale > 0, so max(s) * scale = max(s * scale)
+            const float m_new = fmaxf(m_i, fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * a.qk_scale);
             const float m_use = m_new == -INFINITY ? 0.0f : m_new;
             const float alpha = fast_exp2(m_i - m_use);
-            // pass 2: p = exp2(s * scale - m), P_hi over S, P_lo beside it
             float ps0 = 0.0f, ps1 = 0.0f;
 #pragma unroll
             for (int c = 0; c < BN; c += 16) {
-                uint32_t r[16], hi[16], lo[16];
-                tmem_ld_32x32b_x16(lane_base + gcol + OFF_S + c, r);
-                tmem_ld_wait();
+                uint32_t hi[16], lo[16];
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                    float v = __uint_as_float(r[e]);
-                    if (masked) {
-                        const int64_t col = k0 + c + e;
-                        if (col >= a.key_end || (a.causal && col > row)) v = -INFINITY;
-                    }
-                    float p = fast_exp2(fmaf(v, a.qk_scale, -m_use));
+                    float p = fast_exp2(fmaf(sc[c + e], a.qk_scale, -m_use));
                     if (e & 1) ps1 += p;
                     else ps0 += p;
                     float h = tf32_trunc(p);
                     hi[e] = __float_as_uint(h);
                     lo[e] = __float_as_uint(p - h);   // exact; the tensor core reads its tf32 part
                 }
-                tmem_st_32x32b_x16(lane_base + gcol + OFF_S + c, hi);
-                tmem_st_32x32b_x16(lane_base + gcol + OFF_PLO + c, lo);
+                tmem_st_32x32b_x16(lane_base + scol + c, hi);
+                tmem_st_32x32b_x16(lane_base + pcol + c, lo);
             }
             l_i = l_i * alpha + (ps0 + ps1);
             m_i = m_new;
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&p_full[grp]);
-            // fold this group's previous block while the tensor core works on this one
-            if (u > 0 && !fold(u - 1, alpha_prev)) {
+            if (lane == 0) mbar_arrive(&p_full[j & 1]);
+            alpha_hist[0] = alpha_hist[1];
+            alpha_hist[1] = alpha;
+        }
+        // the last two blocks' P.V
+        for (int jj = nblocks > 2 ? nblocks - 2 : 0; ok && jj < nblocks; ++jj) {
+            if (*abort_flag || !warp_wait(&o_full[jj & 1], (jj >> 1) & 1)) {
                 ok = false;
                 break;
             }
-            alpha_prev = alpha;
-        }
-        if (ok && u > 0 && !fold(u - 1, alpha_prev)) ok = false;
-        // every MMA has completed (and read its shared-memory operands) before stage 0 is reused
-        if (ok && !warp_wait(drain, 0)) ok = false;
-        float *mrg = reinterpret_cast<float *>(smem);          // [BM][HD + 2] merge area in stage 0
-        if (ok && grp == 1) {
-            float *mine = mrg + rrow * (HD + 2);
+            tc_fence_after();
+            uint32_t ro[HD];
 #pragma unroll
-            for (int d = 0; d < HD; ++d) mine[d] = acc[d];
-            mine[HD] = m_i;
-            mine[HD + 1] = l_i;
-            __threadfence_block();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(merge_bar);
-        }
-        if (ok && grp == 0) {
-            if (!warp_wait(merge_bar, 0)) {
-                ok = false;
-            } else if (row < a.row_end) {
-                const float *theirs = mrg + rrow * (HD + 2);
-                const float m_b = theirs[HD], l_b = theirs[HD + 1];
-                const float m = fmaxf(m_i, m_b);
-                const float mu = m == -INFINITY ? 0.0f : m;
-                const float sa = fast_exp2(m_i - mu), sb = fast_exp2(m_b - mu);
-                const float inv = 1.0f / (l_i * sa + l_b * sb);
-                float *orow = a.o + head * a.soh + row * a.som;
-#pragma unroll
-                for (int d = 0; d < HD; ++d) orow[d] = (acc[d] * sa + theirs[d] * sb) * inv;
-            }
+            for (int c = 0; c < HD; c += 16)
+                tmem_ld_32x32b_x16(lane_base + COL_O0 + (jj & 1) * HD + c, *reinterpret_cast<uint32_t(*)[16]>(ro + c));
+            tmem_ld_wait();
+            fold_from(ro, jj == nblocks - 1 ? alpha_hist[1] : alpha_hist[0], jj);
         }
         if (!ok) {
             if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
             *abort_flag = 1;
+        } else if (row < a.row_end) {
+            const float inv = 1.0f / l_i;
+            float *orow = a.o + head * a.soh + row * a.som;
+#pragma unroll
+            for (int d = 0; d < HD; ++d) orow[d] = acc[d] * inv;
         }
     }
     tc_fence_before();
