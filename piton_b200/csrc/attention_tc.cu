@@ -15,18 +15,21 @@
 //       into an fp32 register accumulator (round to nearest) and finally
 //       store O / l;
 //     * warp 0 streams K and V^T tiles with TMA (128-byte swizzle);
-//     * warp 1 issues, from one thread, S = Q_lo K_hi + Q_hi K_lo + Q_hi K_hi
-//       (A from TMEM, B from shared memory, 128x64x8 kind::tf32) and
-//       O_blk = P_lo V_hi + P_hi V_lo + P_hi V_hi (A = P from TMEM).
+//     * warp 1 issues, from one thread, per 8-wide k-step two MMAs: Q_hi
+//       against the stacked [K_hi; K_lo] tile (N = 128: Q_hi K_hi in columns
+//       0-63, Q_hi K_lo in 64-127) and Q_lo against K_hi (N = 64, added to
+//       columns 0-63); likewise P_hi [V_hi; V_lo] and P_lo V_hi for P.V.  The
+//       softmax warps add the two halves in fp32 registers (round to
+//       nearest), so each MMA instruction carries more work and the hi/lo sums
+//       are not truncated by the tensor core.
 //     A block's P.V lands in its own TMEM accumulator that the softmax warps
 //     add into registers, so the tensor core's truncating accumulation never
 //     spans more than one 64-key block.
 // The scores of block j+1 are computed while the softmax warps work on block
-// j (two S/P buffers), and a block's P.V accumulator (two O_blk buffers) is
-// folded into the registers two blocks later, in the same TMEM round trip as
-// that block's scores, so the tensor core and the softmax warps overlap.
-// TMEM columns: Q_hi [0,64) Q_lo [64,128) S/P_hi x2 [128,256) P_lo x2
-// [256,384) O_blk x2 [384,512).
+// j (two S/P buffers), and a block's P.V accumulator is folded into the
+// registers after the next block's P is written, so the tensor core and the
+// softmax warps overlap.  TMEM columns: Q_hi [0,64) Q_lo [64,128)
+// S/P x2 [128,384) (128 each) O_blk [384,512) (512 allocated).
 // K / V^T tiles: 3-stage TMA ring.  All waits are bounded (2 s): on expiry
 // the kernel records a status, drains its copies and MMAs, frees TMEM, returns.
 #include "attention.cuh"
@@ -45,9 +48,17 @@ constexpr int BM = 128, BN = 64, HD = 64, STAGES = 3, THREADS = 192;
 constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes
 constexpr uint32_t TILE_BYTES = 2 * BOX_BYTES;            // one 64 x 64 fp32 operand tile
 constexpr uint32_t STAGE_BYTES = 4 * TILE_BYTES;          // K_hi, K_lo, V^T_hi, V^T_lo
+// Stage layout: for each 32-wide box b (d for K, keys for V^T) the hi box and the lo
+// box are adjacent, [K_hi b0][K_lo b0][K_hi b1][K_lo b1][V_hi b0][V_lo b0][V_hi b1][V_lo b1],
+// so one 128-row B operand covers hi rows 0-63 and lo rows 64-127.
+constexpr uint32_t PAIR_BYTES = 2 * BOX_BYTES;
+constexpr uint32_t V_BASE = 2 * PAIR_BYTES;
 constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
-constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_PLO0 = 256, COL_O0 = 384;   // S, P_lo, O: two buffers each
+// TMEM: Q_hi, Q_lo, two 128-column S/P buffers (S: Q_hi.K_hi (+ Q_lo.K_hi) in 0-63 and
+// Q_hi.K_lo in 64-127; P: P_hi in 0-63, P_lo in 64-127) and a 128-column O_blk
+// (P_hi.V_hi (+ P_lo.V_hi) in 0-63, P_hi.V_lo in 64-127)
+constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_O = 384;
 
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
@@ -113,10 +124,10 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *kv_empty = kv_full + STAGES;
     uint64_t *s_full = kv_empty + STAGES;     // [2]
     uint64_t *p_full = s_full + 2;            // [2]
-    uint64_t *o_full = p_full + 2;            // [2]
-    uint64_t *o_empty = o_full + 2;           // [2]
-    uint64_t *q_ready = o_empty + 2;
-    uint64_t *drain = q_ready + 1;
+    uint64_t *q_ready = p_full + 2;
+    uint64_t *o_full = q_ready + 1;
+    uint64_t *o_empty = o_full + 1;
+    uint64_t *drain = o_empty + 1;
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(drain + 1);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
 
@@ -137,10 +148,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int b = 0; b < 2; ++b) {
             mbar_init(&s_full[b], 1);
             mbar_init(&p_full[b], 4);
-            mbar_init(&o_full[b], 1);
-            mbar_init(&o_empty[b], 4);
         }
         mbar_init(q_ready, 4);
+        mbar_init(o_full, 1);
+        mbar_init(o_empty, 4);
         mbar_init(drain, 1);
         *abort_flag = 0;
         fence_mbarrier_init();
@@ -172,10 +183,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int vrow = (int)(head * HD);
                 const int kx = j * BN;
                 for (int box = 0; box < 2; ++box) {
-                    tma_load_2d(st + box * BOX_BYTES, &m_khi, &kv_full[s], box * 32, krow);
-                    tma_load_2d(st + TILE_BYTES + box * BOX_BYTES, &m_klo, &kv_full[s], box * 32, krow);
-                    tma_load_2d(st + 2 * TILE_BYTES + box * BOX_BYTES, &m_vhi, &kv_full[s], kx + box * 32, vrow);
-                    tma_load_2d(st + 3 * TILE_BYTES + box * BOX_BYTES, &m_vlo, &kv_full[s], kx + box * 32, vrow);
+                    tma_load_2d(st + box * PAIR_BYTES, &m_khi, &kv_full[s], box * 32, krow);
+                    tma_load_2d(st + box * PAIR_BYTES + BOX_BYTES, &m_klo, &kv_full[s], box * 32, krow);
+                    tma_load_2d(st + V_BASE + box * PAIR_BYTES, &m_vhi, &kv_full[s], kx + box * 32, vrow);
+                    tma_load_2d(st + V_BASE + box * PAIR_BYTES + BOX_BYTES, &m_vlo, &kv_full[s], kx + box * 32, vrow);
                 }
             }
             for (int j = issued > STAGES ? issued - STAGES : 0; j < issued; ++j)
@@ -184,7 +195,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer: S_{j+1} is issued before P_j V so it overlaps softmax j ----------------
         if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+            constexpr uint32_t IDESC_N128 = idesc_tf32(BM, 2 * BN), IDESC_N64 = idesc_tf32(BM, BN);
             bool ok = mbar_wait(q_ready, 0);
             tc_fence_after();
             auto issue_s = [&](int j) -> bool {
@@ -192,16 +203,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (!mbar_wait(&kv_full[s], (j / STAGES) & 1)) return false;
                 tc_fence_after();
                 const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-                const uint32_t khi = base, klo = base + TILE_BYTES;
-                const uint32_t d = tmem + COL_S0 + (j & 1) * BN;
+                const uint32_t d = tmem + COL_S0 + (j & 1) * 2 * BN;
 #pragma unroll
                 for (int ks = 0; ks < HD / 8; ++ks) {
-                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
-                    const uint64_t bh = smem_desc_kmajor(khi + off, 128, LAYOUT_SWIZZLE_128B);
-                    const uint64_t bl = smem_desc_kmajor(klo + off, 128, LAYOUT_SWIZZLE_128B);
-                    mma_tf32_ts(d, tmem + COL_QLO + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
-                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, bl, IDESC, 1u);
-                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, bh, IDESC, 1u);
+                    const uint32_t pair = base + (ks >> 2) * PAIR_BYTES + (ks & 3) * 32;
+                    const uint64_t b_pair = smem_desc_kmajor(pair, 128, LAYOUT_SWIZZLE_128B);   // K_hi; K_lo rows
+                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, b_pair, IDESC_N128, ks > 0 ? 1u : 0u);
+                    mma_tf32_ts(d, tmem + COL_QLO + 8 * ks, b_pair, IDESC_N64, 1u);              // K_hi rows only
                 }
                 mma_commit(&s_full[j & 1]);
                 return true;
@@ -212,27 +220,22 @@ __global__ void __launch_bounds__(THREADS, 1)
                     ok = false;
                     break;
                 }
-                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) ||
-                    (j > 1 && !mbar_wait(&o_empty[j & 1], ((j >> 1) - 1) & 1))) {
+                if (!mbar_wait(&p_full[j & 1], (j >> 1) & 1) || (j > 0 && !mbar_wait(o_empty, (j - 1) & 1))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
                 const int s = j % STAGES;
-                const uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-                const uint32_t vhi = base + 2 * TILE_BYTES, vlo = base + 3 * TILE_BYTES;
-                const uint32_t phi = tmem + COL_S0 + (j & 1) * BN, plo = tmem + COL_PLO0 + (j & 1) * BN;
-                const uint32_t ocol = tmem + COL_O0 + (j & 1) * HD;
+                const uint32_t base = smem_u32(smem + s * STAGE_BYTES) + V_BASE;
+                const uint32_t p = tmem + COL_S0 + (j & 1) * 2 * BN;
 #pragma unroll
                 for (int ks = 0; ks < BN / 8; ++ks) {
-                    const uint32_t off = (ks >> 2) * BOX_BYTES + (ks & 3) * 32;
-                    const uint64_t bh = smem_desc_kmajor(vhi + off, 128, LAYOUT_SWIZZLE_128B);
-                    const uint64_t bl = smem_desc_kmajor(vlo + off, 128, LAYOUT_SWIZZLE_128B);
-                    mma_tf32_ts(ocol, plo + 8 * ks, bh, IDESC, ks > 0 ? 1u : 0u);
-                    mma_tf32_ts(ocol, phi + 8 * ks, bl, IDESC, 1u);
-                    mma_tf32_ts(ocol, phi + 8 * ks, bh, IDESC, 1u);
+                    const uint32_t pair = base + (ks >> 2) * PAIR_BYTES + (ks & 3) * 32;
+                    const uint64_t b_pair = smem_desc_kmajor(pair, 128, LAYOUT_SWIZZLE_128B);   // V^T_hi; V^T_lo rows
+                    mma_tf32_ts(tmem + COL_O, p + 8 * ks, b_pair, IDESC_N128, ks > 0 ? 1u : 0u);        // P_hi
+                    mma_tf32_ts(tmem + COL_O, p + BN + 8 * ks, b_pair, IDESC_N64, 1u);                // P_lo . V_hi
                 }
-                mma_commit(&o_full[j & 1]);
+                mma_commit(o_full);
                 mma_commit(&kv_empty[s]);
             }
             if (!ok) {
@@ -270,44 +273,45 @@ __global__ void __launch_bounds__(THREADS, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive(q_ready);
         }
-        float m_i = -INFINITY, l_i = 0.0f;
-        float alpha_hist[2] = {1.0f, 1.0f};   // alpha of blocks j-2 and j-1
+        float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
         float acc[HD];
 #pragma unroll
         for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
-        // fold O_blk of block jj (buffer jj & 1): acc = acc * alpha + O_blk, then free the buffer
-        auto fold_from = [&](const uint32_t (&r)[HD], float alpha, int jj) {
+        // acc = acc * alpha + O_blk of block jj (its P.V accumulator in TMEM)
+        auto fold = [&](int jj, float alpha) -> bool {
+            if (*abort_flag || !warp_wait(o_full, jj & 1)) return false;
+            tc_fence_after();
+            uint32_t r[2 * HD];
 #pragma unroll
-            for (int c = 0; c < HD; ++c) acc[c] = fmaf(acc[c], alpha, __uint_as_float(r[c]));
+            for (int c = 0; c < 2 * HD; c += 16)
+                tmem_ld_32x32b_x16(lane_base + COL_O + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+            tmem_ld_wait();
+#pragma unroll
+            for (int c = 0; c < HD; ++c)
+                acc[c] = fmaf(acc[c], alpha, __uint_as_float(r[c]) + __uint_as_float(r[HD + c]));
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) mbar_arrive(&o_empty[jj & 1]);
+            if (lane == 0) mbar_arrive(o_empty);
+            return true;
         };
         for (int j = 0; j < nblocks; ++j) {
-            // block j's scores and, two blocks behind, block j-2's P.V: one TMEM round trip
-            bool got = !*abort_flag && warp_wait(&s_full[j & 1], (j >> 1) & 1);
-            if (got && j > 1) got = warp_wait(&o_full[j & 1], ((j >> 1) - 1) & 1);
-            if (!got) {
+            if (*abort_flag || !warp_wait(&s_full[j & 1], (j >> 1) & 1)) {
                 ok = false;
                 break;
             }
             tc_fence_after();
             const int64_t k0 = (int64_t)j * BN;
-            const uint32_t scol = COL_S0 + (j & 1) * BN, pcol = COL_PLO0 + (j & 1) * BN;
-            uint32_t rs[BN], ro[HD];
-#pragma unroll
-            for (int c = 0; c < BN; c += 16)
-                tmem_ld_32x32b_x16(lane_base + scol + c, *reinterpret_cast<uint32_t(*)[16]>(rs + c));
-            if (j > 1) {
-#pragma unroll
-                for (int c = 0; c < HD; c += 16)
-                    tmem_ld_32x32b_x16(lane_base + COL_O0 + (j & 1) * HD + c, *reinterpret_cast<uint32_t(*)[16]>(ro + c));
-            }
-            tmem_ld_wait();
-            if (j > 1) fold_from(ro, alpha_hist[0], j - 2);
+            const uint32_t scol = COL_S0 + (j & 1) * 2 * BN, pcol = scol + BN;
             float sc[BN];
+            {
+                uint32_t r[2 * BN];
 #pragma unroll
-            for (int c = 0; c < BN; ++c) sc[c] = __uint_as_float(rs[c]);
+                for (int c = 0; c < 2 * BN; c += 16)
+                    tmem_ld_32x32b_x16(lane_base + scol + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+                tmem_ld_wait();   // one wait for all eight loads
+#pragma unroll
+                for (int c = 0; c < BN; ++c) sc[c] = __uint_as_float(r[c]) + __uint_as_float(r[BN + c]);
+            }
             // masks only on the blocks that reach past key_end or the causal diagonal
             const bool masked = k0 + BN > a.key_end || (a.causal && k0 + BN - 1 > q0);
             if (masked) {
@@ -351,23 +355,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&p_full[j & 1]);
-            alpha_hist[0] = alpha_hist[1];
-            alpha_hist[1] = alpha;
-        }
-        // the last two blocks' P.V
-        for (int jj = nblocks > 2 ? nblocks - 2 : 0; ok && jj < nblocks; ++jj) {
-            if (*abort_flag || !warp_wait(&o_full[jj & 1], (jj >> 1) & 1)) {
+            // fold the previous block's P.V while this block's runs on the tensor core
+            if (j > 0 && !fold(j - 1, alpha_prev)) {
                 ok = false;
                 break;
             }
-            tc_fence_after();
-            uint32_t ro[HD];
-#pragma unroll
-            for (int c = 0; c < HD; c += 16)
-                tmem_ld_32x32b_x16(lane_base + COL_O0 + (jj & 1) * HD + c, *reinterpret_cast<uint32_t(*)[16]>(ro + c));
-            tmem_ld_wait();
-            fold_from(ro, jj == nblocks - 1 ? alpha_hist[1] : alpha_hist[0], jj);
+            alpha_prev = alpha;
         }
+        if (ok && nblocks > 0 && !fold(nblocks - 1, alpha_prev)) ok = false;
         if (!ok) {
             if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
             *abort_flag = 1;
