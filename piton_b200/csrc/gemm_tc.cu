@@ -82,6 +82,25 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
     }
 }
 
+// Row-major source with unit column stride and 16-byte aligned rows: the split
+// needs no transpose, so it streams float4 in and two float4 out per thread.
+__global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__restrict__ src, int64_t rows,
+                                                              int64_t cols, int64_t s_row, float *__restrict__ hi,
+                                                              float *__restrict__ lo, int64_t ld) {
+    const int64_t q_per_row = cols / 4;
+    const int64_t total = rows * q_per_row;
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
+         i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t r = i / q_per_row, c = 4 * (i % q_per_row);
+        float4 v = __ldcs(reinterpret_cast<const float4 *>(src + r * s_row + c));
+        float4 h = make_float4(tf32_trunc(v.x), tf32_trunc(v.y), tf32_trunc(v.z), tf32_trunc(v.w));
+        float4 l = make_float4(isfinite(v.x) ? tf32_trunc(v.x - h.x) : 0.0f, isfinite(v.y) ? tf32_trunc(v.y - h.y) : 0.0f,
+                               isfinite(v.z) ? tf32_trunc(v.z - h.z) : 0.0f, isfinite(v.w) ? tf32_trunc(v.w - h.w) : 0.0f);
+        *reinterpret_cast<float4 *>(hi + r * ld + c) = h;
+        *reinterpret_cast<float4 *>(lo + r * ld + c) = l;
+    }
+}
+
 struct GemmArgs {
     float *c;
     int64_t M, N, K, scm, scn;
@@ -425,8 +444,15 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves
     {
         dim3 ga((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.M, 32));
-        int along_rows_a = llabs(s.sam) < llabs(s.sak);
-        split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
+        const bool vec_a = s.sak == 1 && s.K % 4 == 0 && s.sam % 4 == 0 && (reinterpret_cast<uintptr_t>(s.a) & 15) == 0;
+        if (vec_a) {
+            int64_t blocks = cdiv(s.M * (s.K / 4), 256);
+            if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
+            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, a_hi, a_lo, ld);
+        } else {
+            int along_rows_a = llabs(s.sam) < llabs(s.sak);
+            split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
+        }
         dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
         int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
         split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_lo, ld, along_rows_b);

@@ -58,7 +58,7 @@ class Buffer:
     (asynchronously from page-locked memory); ``copy_back`` copies the device
     buffer into the array again."""
 
-    def __init__(self, name, value, device, stream):
+    def __init__(self, name, value, device, stream, overwrite=False):
         torch = _torch()
         self.name = name
         off = 0
@@ -72,9 +72,10 @@ class Buffer:
             host_t = torch.from_numpy(np.ascontiguousarray(base).reshape(-1))
             self.pinned = bool(host_t.is_pinned())
             self.tensor = torch.empty(host_t.shape, dtype=host_t.dtype, device=device)
-            with torch.cuda.stream(stream):
-                self.tensor.copy_(host_t, non_blocking=self.pinned)
-            self.h2d_bytes = host_t.numel() * host_t.element_size()
+            if not overwrite:   # an output the launch writes in full needs no copy in
+                with torch.cuda.stream(stream):
+                    self.tensor.copy_(host_t, non_blocking=self.pinned)
+                self.h2d_bytes = host_t.numel() * host_t.element_size()
         elif _is_torch_tensor(base):
             if base.device.type != "cuda":
                 raise TypeError(f"argument {name}: tensor on {base.device}, expected a CUDA tensor or numpy array")
@@ -148,12 +149,17 @@ class Launch:
         self.called = True
         check(rc, what)
 
-    def ptr(self, name, written: bool = False) -> Buffer:
+    def ptr(self, name, written: bool = False, covers: int = -1) -> Buffer:
         """The device buffer of pointer argument `name`; `written` marks the
-        arguments the operator stores to (the ones copied back)."""
+        arguments the operator stores to (the ones copied back).  `covers` is the
+        number of leading elements the launch writes, every one of them: when that
+        is the whole of a plain numpy array, its old contents are never observable
+        and the copy to the device is skipped."""
         if name not in self.buffers:
             v = self.args[name]
-            self.buffers[name] = Buffer(name, v, self.device, self.stream)
+            overwrite = (written and isinstance(v, np.ndarray) and covers == v.size and
+                         not any(b.host is v for b in self.buffers.values()))
+            self.buffers[name] = Buffer(name, v, self.device, self.stream, overwrite)
         if written:
             self.written.add(name)
         return self.buffers[name]
@@ -232,7 +238,7 @@ def _flags(launch, allowed_qpu=True, simt_ok=False):
 def _add(L: Launch, grid):
     n, blk = L.int("n_elements"), L.int("BLOCK_SIZE")
     n_eff = max(0, min(n, grid[0] * blk))
-    x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr", written=True)
+    x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr", written=True, covers=n_eff)
     for b in (x, y, out):
         b.require(0, n_eff - 1)
     a = _lib.AddArgs(x.addr, y.addr, out.addr, n, blk, grid[0], _flags(L), 0)
@@ -246,7 +252,7 @@ def _softmax(L: Launch, grid):
     rows, ncols, blk = grid[0], L.int("n_cols"), L.int("BLOCK_SIZE")
     sin, sout = L.int("input_row_stride"), L.int("output_row_stride")
     n = max(0, min(ncols, blk))
-    out, inp = L.ptr("output_ptr", written=True), L.ptr("input_ptr")
+    out, inp = L.ptr("output_ptr", written=True, covers=rows * n if sout == n else -1), L.ptr("input_ptr")
     inp.require(*extent((rows, sin), (n, 1)))
     out.require(*extent((rows, sout), (n, 1)))
     a = _lib.SoftmaxArgs(out.addr, inp.addr, sin, sout, ncols, blk, rows, _flags(L, False), 0)
@@ -261,7 +267,9 @@ def _matmul(L: Launch, grid):
     M, N, K = L.int("M"), L.int("N"), L.int("K")
     s = {k: L.int(k) for k in ("stride_am", "stride_ak", "stride_bk", "stride_bn", "stride_cm", "stride_cn")}
     bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
-    A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True)
+    full_grid = grid[0] >= -(-M // bm) * -(-N // bn)
+    dense_c = s["stride_cm"] == N and s["stride_cn"] == 1 and full_grid
+    A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True, covers=M * N if dense_c else -1)
     if M > 0 and N > 0 and grid[0] > 0:
         A.require(*extent((M, s["stride_am"]), (K, s["stride_ak"])))
         B.require(*extent((K, s["stride_bk"]), (N, s["stride_bn"])))
@@ -358,7 +366,7 @@ _ELEM_OPS = {"copy": 0, "mul": 1, "fma": 2, "scaled_relu": 3, "exp2": 4, "log2":
 def _elementwise(L: Launch, grid, op: str, x: str, y, out: str, alpha: float = 0.0):
     n, blk = L.int("n"), L.int("BLOCK")
     n_eff = max(0, min(n, grid[0] * blk))
-    bx, bo = L.ptr(x), L.ptr(out, written=True)
+    bx, bo = L.ptr(x), L.ptr(out, written=True, covers=n_eff)
     by = L.ptr(y) if y else None
     for b in (bx, bo, by):
         if b is not None:
