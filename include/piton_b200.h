@@ -63,6 +63,8 @@ PITON_B200_API uint64_t piton_b200_launch_count(void);
 /* Make `device` current for the calling thread and create its context. */
 PITON_B200_API int piton_b200_init(int device);
 PITON_B200_API int piton_b200_device_count(int *count);
+/* The calling thread's current device (cudaGetDevice). */
+PITON_B200_API int piton_b200_get_device(int *device);
 PITON_B200_API int piton_b200_malloc(uint64_t *ptr, size_t bytes);
 PITON_B200_API int piton_b200_free(uint64_t ptr);
 PITON_B200_API int piton_b200_memcpy_h2d(uint64_t dst, const void *src, size_t bytes, void *stream);

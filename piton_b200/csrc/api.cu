@@ -80,6 +80,12 @@ int piton_b200_device_count(int *count) {
     return PITON_B200_OK;
 }
 
+int piton_b200_get_device(int *device) {
+    PITON_REQUIRE(device != nullptr, "device is NULL");
+    PITON_CUDA(cudaGetDevice(device));
+    return PITON_B200_OK;
+}
+
 int piton_b200_malloc(uint64_t *ptr, size_t bytes) {
     PITON_REQUIRE(ptr != nullptr, "ptr is NULL");
     void *p = nullptr;

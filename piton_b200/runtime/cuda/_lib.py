@@ -107,6 +107,7 @@ PROTOTYPES = {
     "piton_b200_launch_count": (C.c_uint64, []),
     "piton_b200_init": (C.c_int, [C.c_int]),
     "piton_b200_device_count": (C.c_int, [C.POINTER(C.c_int)]),
+    "piton_b200_get_device": (C.c_int, [C.POINTER(C.c_int)]),
     "piton_b200_malloc": (C.c_int, [C.POINTER(u64), C.c_size_t]),
     "piton_b200_free": (C.c_int, [u64]),
     "piton_b200_memcpy_h2d": (C.c_int, [u64, C.c_void_p, C.c_size_t, C.c_void_p]),
