@@ -128,6 +128,21 @@ PITON_B200_API int piton_b200_matmul_f32(const piton_matmul_args *args, void *st
 #define PITON_B200_NOALLOC_SCRATCH_BYTES (32u << 20)
 PITON_B200_API int piton_b200_matmul_f32_noalloc(const piton_matmul_args *args, void *stream);
 
+/* The same matmul on HOST buffers, replacing the copy-in / launch / copy-back sequence of the
+   reference's launch (run_emulator, piton/runtime/launcher.py:168-214) for this operator: args->a, b, c are
+   host addresses (pinned memory makes the copies asynchronous; pageable memory works, each copy then waits
+   for the host), A [M,K], B [K,N], C [M,N] dense row-major (stride_am == K, stride_ak == 1, stride_bk == N,
+   stride_bn == 1, stride_cm == N, stride_cn == 1), a grid that covers every tile and no flags, so that every
+   element of C is written.  B is copied first, then A in row blocks on a copy stream; each block's GEMM
+   starts when its rows have landed and its C rows go back on a second copy stream while the next block
+   computes.  Bit-identical to piton_b200_matmul_f32.  args->workspace: device scratch of
+   piton_b200_matmul_host_workspace_size() bytes (device copies of A, B, C and the split operands; 0 when the
+   problem does not qualify, and the call then returns PITON_B200_ENOTSUP).  C must not overlap A or B.
+   Enqueues on `stream` like every entry point: the host buffers must stay valid until it has finished.
+   One host thread per device (the copy streams are per device). */
+PITON_B200_API size_t piton_b200_matmul_host_workspace_size(const piton_matmul_args *args);
+PITON_B200_API int piton_b200_matmul_f32_host(const piton_matmul_args *args, void *stream);
+
 /* ---- matmul sharded by M rows with the output all-gather fused into the GEMM epilogue ----
    No counterpart in the reference (it runs on one device); this is the north star's
    "matmul by M-tiles + all-gather" as one kernel: this rank computes rows

@@ -436,10 +436,10 @@ size_t tc_gemm_workspace_bytes(const TcGemmShape &s) { return 2 * region(s.M, s.
 int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     const int64_t ld = ld_of(s.K);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    float *a_hi = reinterpret_cast<float *>(ws);
-    float *a_lo = reinterpret_cast<float *>(ws + region(s.M, s.K));
-    float *b_hi = reinterpret_cast<float *>(ws + 2 * region(s.M, s.K));
-    float *b_lo = reinterpret_cast<float *>(ws + 2 * region(s.M, s.K) + region(s.N, s.K));
+    float *b_hi = reinterpret_cast<float *>(ws);
+    float *b_lo = reinterpret_cast<float *>(ws + region(s.N, s.K));
+    float *a_hi = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K));
+    float *a_lo = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K) + region(s.M, s.K));
 
     // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves
     {
@@ -453,9 +453,11 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
             int along_rows_a = llabs(s.sam) < llabs(s.sak);
             split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
         }
-        dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
-        int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
-        split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_lo, ld, along_rows_b);
+        if (s.split_b) {
+            dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
+            int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
+            split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_lo, ld, along_rows_b);
+        }
     }
     // 2. persistent tcgen05 GEMM
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
@@ -484,7 +486,7 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     gemm_3xtf32_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
-    return check_launch("gemm_3xtf32", 3);
+    return check_launch("gemm_3xtf32", s.split_b ? 3 : 2);
 }
 
 int tc_status_read_and_clear(int *status) {

@@ -202,3 +202,175 @@ extern "C" int piton_b200_matmul_allgather_f32(const piton_matmul_args *a, const
     for (int i = 0; i < g->world; ++i) t.peer_c[i] = reinterpret_cast<float *>(g->peer_c[i]);
     return tc_gemm(t, reinterpret_cast<void *>(a->workspace), as_stream(stream));
 }
+
+// ---------------------------------------------------------------------------
+// Matmul on host buffers with the copies pipelined against the GEMM.
+//
+// The reference's launch copies every array to the device, runs the kernel
+// and copies every array back, one after the other (run_emulator,
+// piton/runtime/launcher.py:168-214).  Here A is cut into row blocks: B goes
+// over PCIe first, then A's blocks, each on a copy stream; the GEMM of block i
+// starts as soon as its rows have landed (B split once, by the first block's
+// call) and C's block i goes back on a second copy stream while block i + 1
+// computes.  The call's stream waits for the last D2H, so it completes like
+// any other entry point.  The result is bit-identical to
+// piton_b200_matmul_f32: each element of C is the same dot product whatever
+// block its row falls in.
+// ---------------------------------------------------------------------------
+
+namespace {
+
+constexpr int HOST_MAX_BLOCKS = 16;
+constexpr int64_t HOST_MIN_BLOCK_ROWS = 1024;
+
+struct HostPipe {
+    cudaStream_t h2d = nullptr, d2h = nullptr;
+    cudaEvent_t start = nullptr, b_in = nullptr, done = nullptr;
+    cudaEvent_t a_in[HOST_MAX_BLOCKS] = {}, c_out[HOST_MAX_BLOCKS] = {};
+};
+
+// Row blocks of A / C: multiples of 128 rows, at least HOST_MIN_BLOCK_ROWS, at
+// most HOST_MAX_BLOCKS of them; a tail under 128 rows joins the block before it.
+int host_blocks(int64_t M, int64_t *start, int64_t *rows) {
+    int64_t per = cdiv(cdiv(M, (int64_t)HOST_MAX_BLOCKS), (int64_t)128) * 128;
+    if (per < HOST_MIN_BLOCK_ROWS) per = HOST_MIN_BLOCK_ROWS;
+    int n = (int)cdiv(M, per);
+    if (n > 1 && M - (int64_t)(n - 1) * per < 128) --n;
+    for (int i = 0; i < n; ++i) {
+        start[i] = (int64_t)i * per;
+        rows[i] = (i == n - 1) ? M - start[i] : per;
+    }
+    return n;
+}
+
+size_t align1k(size_t b) { return (b + 1023) / 1024 * 1024; }
+
+// Byte offsets of the device copies of B, A, C and the split scratch in the workspace.
+struct HostLayout {
+    size_t b, a, c, split, total;
+};
+
+bool host_layout(const piton_matmul_args *a, HostLayout *L, int *n_blocks, int64_t *start, int64_t *rows) {
+    if (a->flags != 0) return false;
+    if (a->grid_x < grouped_tiles(a->M, a->N, a->block_m, a->block_n)) return false;
+    if (a->stride_am != a->K || a->stride_ak != 1 || a->stride_bk != a->N || a->stride_bn != 1 ||
+        a->stride_cm != a->N || a->stride_cn != 1)
+        return false;
+    int n = host_blocks(a->M, start, rows);
+    size_t split = 0;
+    for (int i = 0; i < n; ++i) {
+        TcGemmShape t = tc_shape(a);
+        t.M = rows[i];
+        if (!tc_gemm_supported(t)) return false;
+        size_t need = tc_gemm_workspace_bytes(t);
+        if (need > split) split = need;
+    }
+    L->b = 0;
+    L->a = L->b + align1k((size_t)a->K * a->N * 4);
+    L->c = L->a + align1k((size_t)a->M * a->K * 4);
+    L->split = L->c + align1k((size_t)a->M * a->N * 4);
+    L->total = L->split + split;
+    *n_blocks = n;
+    return true;
+}
+
+HostPipe *host_pipe(int *rc) {
+    static std::mutex mu;
+    static HostPipe pipes[64];
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess || dev < 0 || dev >= 64) {
+        *rc = set_error(PITON_B200_ECUDA, "cudaGetDevice: %s", cudaGetErrorString(err));
+        return nullptr;
+    }
+    std::lock_guard<std::mutex> lock(mu);
+    HostPipe &p = pipes[dev];
+    if (!p.h2d) {
+        HostPipe q;
+        bool ok = cudaStreamCreateWithFlags(&q.h2d, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaStreamCreateWithFlags(&q.d2h, cudaStreamNonBlocking) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&q.start, cudaEventDisableTiming) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&q.b_in, cudaEventDisableTiming) == cudaSuccess &&
+                  cudaEventCreateWithFlags(&q.done, cudaEventDisableTiming) == cudaSuccess;
+        for (int i = 0; ok && i < HOST_MAX_BLOCKS; ++i)
+            ok = cudaEventCreateWithFlags(&q.a_in[i], cudaEventDisableTiming) == cudaSuccess &&
+                 cudaEventCreateWithFlags(&q.c_out[i], cudaEventDisableTiming) == cudaSuccess;
+        if (!ok) {
+            *rc = set_error(PITON_B200_ECUDA, "creating the copy streams: %s", cudaGetErrorString(cudaGetLastError()));
+            return nullptr;
+        }
+        p = q;
+    }
+    *rc = PITON_B200_OK;
+    return &p;
+}
+
+}  // namespace
+
+extern "C" size_t piton_b200_matmul_host_workspace_size(const piton_matmul_args *a) {
+    if (check_matmul(a) != PITON_B200_OK) return 0;
+    HostLayout L;
+    int n = 0;
+    int64_t start[HOST_MAX_BLOCKS], rows[HOST_MAX_BLOCKS];
+    if (a->M == 0 || a->N == 0 || !host_layout(a, &L, &n, start, rows)) return 0;
+    return L.total;
+}
+
+extern "C" int piton_b200_matmul_f32_host(const piton_matmul_args *a, void *stream) {
+    int rc = check_matmul(a);
+    if (rc) return rc;
+    if (a->M == 0 || a->N == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->a && a->b && a->c, "NULL pointer");
+    HostLayout L;
+    int n = 0;
+    int64_t start[HOST_MAX_BLOCKS], rows[HOST_MAX_BLOCKS];
+    if (!host_layout(a, &L, &n, start, rows))
+        return set_error(PITON_B200_ENOTSUP, "the host-buffer matmul needs dense row-major A, B, C, a grid that "
+                                             "covers C, no flags, and blocks the tensor-core path takes");
+    if (!a->workspace || a->workspace_bytes < L.total)
+        return set_error(PITON_B200_EWORKSPACE, "host matmul needs %zu bytes of workspace, got %llu", L.total,
+                         (unsigned long long)a->workspace_bytes);
+    // C must not share host memory with A or B: its blocks go back while later A blocks are still copied in
+    const uintptr_t c0 = a->c, c1 = a->c + (uintptr_t)a->M * a->N * 4;
+    const uintptr_t a0 = a->a, a1 = a->a + (uintptr_t)a->M * a->K * 4;
+    const uintptr_t b0 = a->b, b1 = a->b + (uintptr_t)a->K * a->N * 4;
+    PITON_REQUIRE((c1 <= a0 || a1 <= c0) && (c1 <= b0 || b1 <= c0), "C overlaps A or B in host memory");
+    HostPipe *p = host_pipe(&rc);
+    if (!p) return rc;
+    cudaStream_t s = as_stream(stream);
+    uint8_t *ws = reinterpret_cast<uint8_t *>(a->workspace);
+    float *dB = reinterpret_cast<float *>(ws + L.b), *dA = reinterpret_cast<float *>(ws + L.a);
+    float *dC = reinterpret_cast<float *>(ws + L.c);
+    const float *hA = reinterpret_cast<const float *>(a->a), *hB = reinterpret_cast<const float *>(a->b);
+    float *hC = reinterpret_cast<float *>(a->c);
+
+    // the copy streams start after everything already queued on the call's stream
+    PITON_CUDA(cudaEventRecord(p->start, s));
+    PITON_CUDA(cudaStreamWaitEvent(p->h2d, p->start, 0));
+    PITON_CUDA(cudaStreamWaitEvent(p->d2h, p->start, 0));
+    PITON_CUDA(cudaMemcpyAsync(dB, hB, (size_t)a->K * a->N * 4, cudaMemcpyDefault, p->h2d));
+    PITON_CUDA(cudaEventRecord(p->b_in, p->h2d));
+    for (int i = 0; i < n; ++i) {
+        PITON_CUDA(cudaMemcpyAsync(dA + start[i] * a->K, hA + start[i] * a->K, (size_t)rows[i] * a->K * 4,
+                                   cudaMemcpyDefault, p->h2d));
+        PITON_CUDA(cudaEventRecord(p->a_in[i], p->h2d));
+    }
+    PITON_CUDA(cudaStreamWaitEvent(s, p->b_in, 0));
+    for (int i = 0; i < n; ++i) {
+        PITON_CUDA(cudaStreamWaitEvent(s, p->a_in[i], 0));
+        TcGemmShape t = tc_shape(a);
+        t.a = dA + start[i] * a->K;
+        t.b = dB;
+        t.c = dC + start[i] * a->N;
+        t.M = rows[i];
+        t.split_b = (i == 0);
+        if ((rc = tc_gemm(t, ws + L.split, s)) != PITON_B200_OK) return rc;
+        PITON_CUDA(cudaEventRecord(p->c_out[i], s));
+        PITON_CUDA(cudaStreamWaitEvent(p->d2h, p->c_out[i], 0));
+        PITON_CUDA(cudaMemcpyAsync(hC + start[i] * a->N, dC + start[i] * a->N, (size_t)rows[i] * a->N * 4,
+                                   cudaMemcpyDefault, p->d2h));
+    }
+    PITON_CUDA(cudaEventRecord(p->done, p->d2h));
+    PITON_CUDA(cudaStreamWaitEvent(s, p->done, 0));
+    return PITON_B200_OK;
+}

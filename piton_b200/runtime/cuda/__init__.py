@@ -139,6 +139,7 @@ class Launch:
         self.ev0 = torch.cuda.Event(enable_timing=True)
         self.ev1 = torch.cuda.Event(enable_timing=True)
         self.called = False
+        self.host_h2d = self.host_d2h = 0   # bytes an entry point copied itself (host-buffer paths)
 
     def call(self, fname: str, args, what: str):
         """Run one C-ABI entry point on the launch's stream, timed with CUDA events."""
@@ -190,9 +191,9 @@ class Launch:
         """Copy the written arrays back to the host (the reference copies every
         array back, launcher.py:209-211; arrays a kernel only reads come back
         unchanged, so only the written ones need the copy)."""
-        d2h = sum(self.buffers[n].copy_back(self.stream) for n in self.written)
+        d2h = sum(self.buffers[n].copy_back(self.stream) for n in self.written) + self.host_d2h
         self.stream.synchronize()
-        return sum(b.h2d_bytes for b in self.buffers.values()), d2h
+        return sum(b.h2d_bytes for b in self.buffers.values()) + self.host_h2d, d2h
 
 
 def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
@@ -269,6 +270,8 @@ def _matmul(L: Launch, grid):
     bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
     full_grid = grid[0] >= -(-M // bm) * -(-N // bn)
     dense_c = s["stride_cm"] == N and s["stride_cn"] == 1 and full_grid
+    if full_grid and M > 0 and N > 0 and _matmul_on_host_buffers(L, M, N, K, s, bm, bn, bk, g, grid):
+        return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K, "path": "tcgen05_3xtf32_host_pipelined"}
     A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True, covers=M * N if dense_c else -1)
     if M > 0 and N > 0 and grid[0] > 0:
         A.require(*extent((M, s["stride_am"]), (K, s["stride_ak"])))
@@ -282,6 +285,36 @@ def _matmul(L: Launch, grid):
     L.call("piton_b200_matmul_f32", a, "matmul_kernel")
     return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K,
             "path": "tcgen05_3xtf32" if ws else "cuda_core"}
+
+
+def _matmul_on_host_buffers(L: Launch, M, N, K, s, bm, bn, bk, g, grid) -> bool:
+    """numpy A, B, C in dense row-major layout: one call of the host-buffer entry point,
+    which pipelines the copies of A's row blocks and C's with the GEMM (the generic path
+    copies everything in, launches, and copies back, one after the other).  False when the
+    launch does not qualify; the generic path then runs."""
+    arrs = [L.args[k] for k in ("a_ptr", "b_ptr", "c_ptr")]
+    if not all(type(x) is np.ndarray and x.dtype == np.float32 and x.flags.c_contiguous for x in arrs):
+        return False
+    A, B, Cm = arrs
+    if not Cm.flags.writeable or np.shares_memory(Cm, A) or np.shares_memory(Cm, B):
+        return False
+    if (s["stride_am"], s["stride_ak"], s["stride_bk"], s["stride_bn"], s["stride_cm"], s["stride_cn"]) != (K, 1, N, 1,
+                                                                                                           N, 1):
+        return False
+    if A.size < M * K or B.size < K * N or Cm.size < M * N:
+        return False
+    flags = _flags(L, simt_ok=True)
+    if flags:
+        return False
+    a = _lib.MatmulArgs(A.ctypes.data, B.ctypes.data, Cm.ctypes.data, M, N, K, K, 1, N, 1, N, 1, bm, bn, bk, g,
+                        grid[0], 0, 0, 0, 0)
+    ws = lib().piton_b200_matmul_host_workspace_size(C.byref(a))
+    if ws == 0:
+        return False
+    a.workspace, a.workspace_bytes = L.workspace(ws), ws
+    L.call("piton_b200_matmul_f32_host", a, "matmul_kernel")
+    L.host_h2d, L.host_d2h = 4 * (M * K + K * N), 4 * M * N
+    return True
 
 
 @register("dense_layer_kernel", ("x_ptr", "w_ptr", "bias_ptr", "y_ptr", "M", "N", "K", "BLOCK_SIZE_M",
