@@ -217,7 +217,8 @@ def bench_matmul(torch, D, args, lib_calls):
     torch.cuda.synchronize()
     per_call = lib().piton_b200_launch_count() - n0
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
-    t_step = timed(torch, D, step, args.steps, args.warmup)
+    # at N = 1 the step is the kernel-only call itself: one measurement serves both
+    t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
     lib_calls["launches"] += per_call * args.steps
     flops = 2.0 * M * N * K
     # correctness spot check of this rank's first rows against float64 (and, with the fused
@@ -255,7 +256,8 @@ def bench_softmax(torch, D, args, lib_calls):
         D.allgather(torch, yfull, y)
 
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
-    t_step = timed(torch, D, step, args.steps, args.warmup)
+    # at N = 1 the step is the kernel-only call itself: one measurement serves both
+    t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
     lib_calls["launches"] += args.steps
     ref = torch.softmax(x[:8].double(), 1)
     err = float(((y[:8].double() - ref).abs() / ref.abs().clamp_min(1e-37)).max())
@@ -322,7 +324,8 @@ def bench_add(torch, D, args, lib_calls):
         D.allgather(torch, ofull, out)
 
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
-    t_step = timed(torch, D, step, args.steps, args.warmup)
+    # at N = 1 the step is the kernel-only call itself: one measurement serves both
+    t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
     lib_calls["launches"] += args.steps
     err = float((out[:1 << 20] - (x[:1 << 20] + y[:1 << 20])).abs().max())
     return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc}

@@ -41,14 +41,16 @@ __device__ int g_tc_status = 0;
 
 namespace {
 
-constexpr int BM = 128, BN = 256, BK = 16, STAGES = 4;
+constexpr int BM = 128, BK = 16, STAGES = 4;
 constexpr int THREADS = 320;
 constexpr int EPI_WARPS = 8;
 constexpr int KC_BLOCKS = 16;   // k-blocks of BK per accumulation chunk (KC = 256)
 constexpr uint32_t A_TILE_BYTES = BM * BK * 4;   // 8 KB
-constexpr uint32_t B_TILE_BYTES = BN * BK * 4;   // 16 KB
-constexpr uint32_t STAGE_BYTES = 2 * A_TILE_BYTES + 2 * B_TILE_BYTES;   // 48 KB
-constexpr uint32_t SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*alignment slack*/;
+// BN (tile width along N) is 256, or 224 where that packs the tiles into fewer
+// rounds over the SMs (tile_width()); a B tile is BN x 16 fp32 (14 or 16 KB)
+__host__ __device__ constexpr uint32_t b_tile_bytes(int bn) { return (uint32_t)bn * BK * 4; }
+__host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_TILE_BYTES + 2 * b_tile_bytes(bn); }
+__host__ __device__ constexpr uint32_t smem_bytes(int bn) { return STAGES * stage_bytes(bn) + 1024 /*barriers*/ + 1024 /*alignment*/; }
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 
@@ -127,6 +129,7 @@ __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status
 // stores).  Called by the 256 epilogue threads (`et` = 0..255), a few rows per
 // accumulation chunk of the next tile, so the NVLink traffic is spread evenly
 // over the MMAs instead of bursting at the end of each tile.
+template <int BN>
 __device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int tm, int tn, int r0, int r1, int et) {
     const float *src_base = args.peer_c[args.rank];
     const int64_t col_base = (int64_t)tn * BN;
@@ -150,10 +153,13 @@ __device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int tm,
     }
 }
 
+template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
                        const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
                        GemmArgs args) {
+    constexpr uint32_t B_TILE_BYTES = b_tile_bytes(BN);
+    constexpr uint32_t STAGE_BYTES = stage_bytes(BN);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE_BYTES);
@@ -314,7 +320,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[acc]);   // TMEM buffer free for the next chunk
                 if (args.world > 1 && pend_tm >= 0)
-                    copy_rows_to_peers(args, pend_tm, pend_tn, min(ci * rows_per_chunk, BM),
+                    copy_rows_to_peers<BN>(args, pend_tm, pend_tn, min(ci * rows_per_chunk, BM),
                                        min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
@@ -327,26 +333,33 @@ __global__ void __launch_bounds__(THREADS, 1)
                     // all-gather epilogue: the tile goes into this rank's own full output now,
                     // and to the other ranks' outputs during the next tile's chunks
                     float *crow = args.peer_c[args.rank] + (args.row_offset + row) * args.ldc_peer;
-                    if (col0 + BN / 2 <= args.N) {
 #pragma unroll
-                        for (int j = 0; j < BN / 2; j += 4)
+                    for (int j = 0; j < BN / 2; j += 4) {
+                        if (col0 + j + 4 <= args.N) {
                             *reinterpret_cast<float4 *>(crow + col0 + j) =
                                 make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
-                    } else {
+                        } else {
 #pragma unroll
-                        for (int j = 0; j < BN / 2; ++j)
-                            if (col0 + j < args.N) crow[col0 + j] = sum[j];
+                            for (int q = 0; q < 4; ++q)
+                                if (col0 + j + q < args.N) crow[col0 + j + q] = sum[j + q];
+                        }
                     }
                 } else {
                     float *crow = args.c + row * args.scm;
                     const bool vec = args.scn == 1 &&
-                                     ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0 &&
-                                     col0 + BN / 2 <= args.N;
+                                     ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0;
                     if (vec) {
 #pragma unroll
-                        for (int j = 0; j < BN / 2; j += 4)
-                            *reinterpret_cast<float4 *>(crow + col0 + j) =
-                                make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                        for (int j = 0; j < BN / 2; j += 4) {
+                            if (col0 + j + 4 <= args.N) {
+                                *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                    make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                            } else {
+#pragma unroll
+                                for (int q = 0; q < 4; ++q)
+                                    if (col0 + j + q < args.N) crow[col0 + j + q] = sum[j + q];
+                            }
+                        }
                     } else {
 #pragma unroll
                         for (int j = 0; j < BN / 2; ++j)
@@ -372,7 +385,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             ++tiles_done;
         }
-        if (ok && args.world > 1 && pend_tm >= 0) copy_rows_to_peers(args, pend_tm, pend_tn, 0, BM, et);
+        if (ok && args.world > 1 && pend_tm >= 0) copy_rows_to_peers<BN>(args, pend_tm, pend_tn, 0, BM, et);
     }
     tc_fence_before();
     __syncthreads();
@@ -417,6 +430,17 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
 }
 
 int64_t ld_of(int64_t K) { return (K + 3) / 4 * 4; }
+
+// Tile width along N: the persistent grid runs ceil(tiles / SMs) rounds, each as long as
+// one tile (proportional to its width), so take the width with the fewer column-rounds;
+// 256 on a tie (fewer, larger tiles).  E.g. M = 1024, N = 8192 on 148 SMs: 256 wide is
+// 256 tiles in 2 rounds, 224 wide is 296 tiles in 2 rounds of 7/8 the length.
+int tile_width(int64_t M, int64_t N) {
+    const int64_t sms = num_sms(), tm = cdiv(M, (int64_t)BM);
+    const int64_t cost256 = cdiv(tm * cdiv(N, (int64_t)256), sms) * 256;
+    const int64_t cost224 = cdiv(tm * cdiv(N, (int64_t)224), sms) * 224;
+    return cost224 < cost256 ? 224 : 256;
+}
 size_t region(int64_t rows, int64_t K) { return ((size_t)rows * ld_of(K) * 4 + 1023) / 1024 * 1024; }
 
 }  // namespace
@@ -460,23 +484,29 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
         }
     }
     // 2. persistent tcgen05 GEMM
+    const int bn = tile_width(s.M, s.N);
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     int rc;
     if ((rc = make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) || (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
-        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, BN)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, BN)))
+        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, bn)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, bn)))
         return rc;
-    static bool attr[64] = {false};
+    static bool attr[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        attr[dev] = true;
+    if (dev < 64 && !attr[dev][bn == 224]) {
+        if (bn == 224)
+            PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<224>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            smem_bytes(224)));
+        else
+            PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            smem_bytes(256)));
+        attr[dev][bn == 224] = true;
     }
     GemmArgs g;
     g.c = s.c;
     g.M = s.M; g.N = s.N; g.K = s.K; g.scm = s.scm; g.scn = s.scn;
     g.tiles_m = (int)cdiv(s.M, BM);
-    g.tiles_n = (int)cdiv(s.N, BN);
+    g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
     g.num_tiles = g.tiles_m * g.tiles_n;
     g.k_blocks = (int)cdiv(s.K, BK);
     g.world = s.world;
@@ -485,7 +515,10 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.ldc_peer = s.ldc_peer;
     for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
-    gemm_3xtf32_kernel<<<grid, THREADS, SMEM_BYTES, stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
+    if (bn == 224)
+        gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
+    else
+        gemm_3xtf32_kernel<256><<<grid, THREADS, smem_bytes(256), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
     return check_launch("gemm_3xtf32", s.split_b ? 3 : 2);
 }
 

@@ -231,6 +231,7 @@ struct HostPipe {
 
 // Row blocks of A / C: multiples of 128 rows, at least HOST_MIN_BLOCK_ROWS, at
 // most HOST_MAX_BLOCKS of them; a tail under 128 rows joins the block before it.
+// Every block has at least 128 rows (the tensor-core path's minimum).
 int host_blocks(int64_t M, int64_t *start, int64_t *rows) {
     int64_t per = cdiv(cdiv(M, (int64_t)HOST_MAX_BLOCKS), (int64_t)128) * 128;
     if (per < HOST_MIN_BLOCK_ROWS) per = HOST_MIN_BLOCK_ROWS;
@@ -239,6 +240,24 @@ int host_blocks(int64_t M, int64_t *start, int64_t *rows) {
     for (int i = 0; i < n; ++i) {
         start[i] = (int64_t)i * per;
         rows[i] = (i == n - 1) ? M - start[i] : per;
+    }
+    // Nothing overlaps the last block's GEMM and D2H, so cut it in halves down to
+    // ~256 rows (1024 -> 512, 256, 256): the pipeline's tail shrinks to a small block.
+    if (n >= 2) {
+        int64_t s0 = start[n - 1], rem = rows[n - 1];
+        --n;
+        while (rem > 256 && n < HOST_MAX_BLOCKS - 1) {
+            const int64_t piece = cdiv(cdiv(rem, (int64_t)2), (int64_t)128) * 128;
+            if (rem - piece < 128) break;
+            start[n] = s0;
+            rows[n] = piece;
+            ++n;
+            s0 += piece;
+            rem -= piece;
+        }
+        start[n] = s0;
+        rows[n] = rem;
+        ++n;
     }
     return n;
 }

@@ -136,6 +136,27 @@ def device_status():
     return s.value
 
 
+@pytest.mark.parametrize("M,N,K", [(1024, 8192, 256), (2048, 1000, 512), (640, 4000, 64)])
+def test_tensor_core_224_wide_tiles_ragged_n(cuda, M, N, K):
+    """Shapes whose tiles pack into fewer rounds 224 columns wide (the last N tile is
+    partial): C's padding columns past N stay untouched."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(M * 3 + N)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    ldc = N + 12
+    Cp = torch.full((M, ldc), 5.0, device="cuda")
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, Cp, M, N, K, K, 1, N, 1, ldc, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
+        device="b200").last_stats
+    assert st["path"] == "tcgen05_3xtf32"
+    ref = A.double() @ B.double()
+    err = float((Cp[:, :N].double() - ref).abs().max() / ref.abs().max())
+    assert err <= fp32_bound(K), err
+    assert bool((Cp[:, N:] == 5.0).all())
+    assert device_status() == 0
+
+
 @pytest.mark.parametrize("K", [16, 17, 255, 256, 257, 4099])
 def test_tensor_core_k_edges(cuda, K):
     # K not a multiple of the 16-wide k-block or of the 256-wide accumulation chunk
