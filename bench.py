@@ -197,12 +197,22 @@ def bench_matmul(torch, D, args, lib_calls):
         _lib.check(f(C.byref(a), stream), "matmul")
 
     peer = None
+    multicast = False
     if D.world > 1:
-        peer = sharding.PeerOutput(D.pg, M * N * 4)
+        # NVSwitch multicast (one multimem store per element reaches every rank) where every
+        # rank has it, else CUDA IPC peer buffers and per-peer stores
+        flag = torch.tensor([1 if sharding.SymmetricOutput.multicast_supported(torch.cuda.current_device()) else 0],
+                            device="cuda")
+        D.pg.all_reduce(flag, op=D.pg.ReduceOp.MIN)
+        multicast = bool(flag.item())
+        peer = sharding.SymmetricOutput(D.pg, M * N * 4) if multicast else sharding.PeerOutput(D.pg, M * N * 4)
+        multicast = multicast and peer.multicast_ptr != 0
         gargs = _lib.AllgatherArgs()
         for r, p in enumerate(peer.peer_ptrs):
             gargs.peer_c[r] = p
         gargs.world, gargs.rank, gargs.row_offset, gargs.ldc = D.world, D.rank, r0, N
+        if multicast:
+            gargs.multicast_c = peer.multicast_ptr
         done = torch.zeros(1, device="cuda")
         fg = lib().piton_b200_matmul_allgather_f32
 
@@ -233,7 +243,7 @@ def bench_matmul(torch, D, args, lib_calls):
         D.pg.barrier()
         peer.close()
     return {"flops": flops, "t_step": t_step, "t_kernel": t_kernel, "tc": ws > 0, "per_call": per_call,
-            "err": err, "local_flops": 2.0 * mloc * N * K}
+            "err": err, "local_flops": 2.0 * mloc * N * K, "multicast": multicast}
 
 
 def bench_softmax(torch, D, args, lib_calls):
@@ -560,8 +570,11 @@ def main():
         peak = tf32 / 3.0
         line.update({"value": value, "unit": "TFLOP/s", "ms_per_step": 1e3 * r["t_step"],
                      "config": {"workload": f"matmul C=A@B fp32 {MM}x{MM}x{MM}, A,B ~ U[-1,1], sharded by M-tiles, "
-                                            f"all-gather of C each step" + (" fused into the GEMM epilogue (NVLink "
-                                            f"peer stores)" if D.world > 1 else ""),
+                                            f"all-gather of C each step" + (
+                                                (" fused into the GEMM epilogue (multimem stores to an NVSwitch "
+                                                 "multicast address)" if r["multicast"] else
+                                                 " fused into the GEMM epilogue (NVLink peer stores)")
+                                                if D.world > 1 else ""),
                                 "M": MM, "N": MM, "K": MM, "parallelism": f"m-tiles x{D.world}",
                                 "l2": "inputs larger than L2 (A+B = 512 MB)",
                                 "path": "tcgen05 3xTF32" if r["tc"] else "CUDA-core fp32 FFMA"},

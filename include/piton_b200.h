@@ -149,13 +149,16 @@ PITON_B200_API int piton_b200_matmul_f32_host(const piton_matmul_args *args, voi
    [row_offset, row_offset + args->M) of the full C (args->c and stride_cm/cn are ignored), and
    every finished tile is stored into each rank's full row-major C (peer_c[r], row stride ldc)
    through NVLink peer stores.  peer_c holds device pointers valid in this process: the own
-   buffer and the others opened with piton_b200_ipc_open.  Tensor-core path only (ENOTSUP
+   buffer and the others opened with piton_b200_ipc_open (or symmetric-memory peer mappings).  Tensor-core path only (ENOTSUP
    otherwise).  Every rank must pass a barrier after its call before C is read anywhere. */
 typedef struct {
     uint64_t peer_c[8];
     int32_t world, rank;
     int64_t row_offset;
     int64_t ldc;
+    uint64_t multicast_c; /* 0, or an NVSwitch multicast address bound to every rank's full C (16-byte
+                             aligned): each tile is then stored once with multimem.st, which the switch
+                             writes into all ranks' C; peer_c is not used */
 } piton_allgather_args;
 PITON_B200_API int piton_b200_matmul_allgather_f32(const piton_matmul_args *args, const piton_allgather_args *g,
                                                    void *stream);

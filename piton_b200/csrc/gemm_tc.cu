@@ -110,7 +110,19 @@ struct GemmArgs {
     int world, rank;                 // world > 0: all-gather epilogue into peer_c
     int64_t row_offset, ldc_peer;
     float *peer_c[MAX_PEERS];
+    float *mc_c;                     // multicast all-gather: one multimem store reaches every rank
 };
+
+// multimem stores: the NVSwitch writes the value into the memory of every GPU bound
+// to the multicast address (relaxed, system scope; the kernel ends with a system fence)
+__device__ __forceinline__ void multimem_st_v4(float *addr, float a, float b, float c, float d) {
+    asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b),
+                 "f"(c), "f"(d)
+                 : "memory");
+}
+__device__ __forceinline__ void multimem_st(float *addr, float a) {
+    asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(addr), "f"(a) : "memory");
+}
 
 __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
     int per_group = GROUP_M * tiles_n;
@@ -329,7 +341,20 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
             if (row < args.M) {
                 const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
-                if (args.world > 0) {
+                if (args.mc_c) {
+                    // multicast all-gather: one store per element, replicated to every rank by the switch
+                    float *mrow = args.mc_c + (args.row_offset + row) * args.ldc_peer;
+#pragma unroll
+                    for (int j = 0; j < BN / 2; j += 4) {
+                        if (col0 + j + 4 <= args.N) {
+                            multimem_st_v4(mrow + col0 + j, sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if (col0 + j + q < args.N) multimem_st(mrow + col0 + j + q, sum[j + q]);
+                        }
+                    }
+                } else if (args.world > 0) {
                     // all-gather epilogue: the tile goes into this rank's own full output now,
                     // and to the other ranks' outputs during the next tile's chunks
                     float *crow = args.peer_c[args.rank] + (args.row_offset + row) * args.ldc_peer;
@@ -367,7 +392,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             }
-            if (args.world > 1) {
+            if (args.world > 1 && !args.mc_c) {
                 // every epilogue warp has stored its part of the tile (bounded wait, not bar.sync:
                 // a warp that gave up must not leave the others waiting for ever)
                 __threadfence_block();
@@ -386,6 +411,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ++tiles_done;
         }
         if (ok && args.world > 1 && pend_tm >= 0) copy_rows_to_peers<BN>(args, pend_tm, pend_tn, 0, BM, et);
+        if (args.mc_c) __threadfence_system();
     }
     tc_fence_before();
     __syncthreads();
@@ -514,6 +540,7 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.row_offset = s.row_offset;
     g.ldc_peer = s.ldc_peer;
     for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
+    g.mc_c = s.multicast_c;
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     if (bn == 224)
         gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);

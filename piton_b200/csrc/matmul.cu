@@ -183,8 +183,11 @@ extern "C" int piton_b200_matmul_allgather_f32(const piton_matmul_args *a, const
     PITON_REQUIRE(g->world >= 1 && g->world <= MAX_PEERS && g->rank >= 0 && g->rank < g->world,
                   "world %d / rank %d outside 1..%d", g->world, g->rank, MAX_PEERS);
     PITON_REQUIRE(g->row_offset >= 0 && g->ldc >= a->N && g->ldc % 4 == 0, "bad row_offset / ldc");
-    for (int i = 0; i < g->world; ++i)
-        PITON_REQUIRE(g->peer_c[i] != 0 && (g->peer_c[i] & 15) == 0, "peer output %d is NULL or misaligned", i);
+    if (g->multicast_c)
+        PITON_REQUIRE((g->multicast_c & 15) == 0, "multicast output is misaligned");
+    else
+        for (int i = 0; i < g->world; ++i)
+            PITON_REQUIRE(g->peer_c[i] != 0 && (g->peer_c[i] & 15) == 0, "peer output %d is NULL or misaligned", i);
     if (a->M == 0 || a->N == 0 || a->grid_x == 0) return PITON_B200_OK;
     PITON_REQUIRE(a->a && a->b, "NULL pointer");
     if (!use_tc(a))
@@ -200,6 +203,7 @@ extern "C" int piton_b200_matmul_allgather_f32(const piton_matmul_args *a, const
     t.row_offset = g->row_offset;
     t.ldc_peer = g->ldc;
     for (int i = 0; i < g->world; ++i) t.peer_c[i] = reinterpret_cast<float *>(g->peer_c[i]);
+    t.multicast_c = reinterpret_cast<float *>(g->multicast_c);
     return tc_gemm(t, reinterpret_cast<void *>(a->workspace), as_stream(stream));
 }
 

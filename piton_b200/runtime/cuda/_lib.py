@@ -40,7 +40,8 @@ class MatmulArgs(C.Structure):
 
 
 class AllgatherArgs(C.Structure):
-    _fields_ = [("peer_c", u64 * 8), ("world", i32), ("rank", i32), ("row_offset", i64), ("ldc", i64)]
+    _fields_ = [("peer_c", u64 * 8), ("world", i32), ("rank", i32), ("row_offset", i64), ("ldc", i64),
+                ("multicast_c", u64)]
 
 
 class DenseArgs(C.Structure):

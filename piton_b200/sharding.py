@@ -4,7 +4,9 @@ Every operator partitions into independent pieces (matmul: row blocks of A and
 C with B replicated; softmax: rows; attention: batch x head; add: element
 ranges; MLP / TinyGPT: batch rows), so a rank computes its piece with no
 exchange, and the only collective is the final all-gather of the output
-pieces over NCCL (NVLink), which leaves the whole output on every rank.
+pieces over NVLink, which leaves the whole output on every rank: NCCL for most
+operators, and for matmul stores from the GEMM epilogue itself (NVSwitch
+multicast or peer stores).
 
 Functions here are backend-agnostic (``torch.distributed`` with ``nccl`` on
 GPUs or ``gloo`` on CPU), so the host-side logic is tested on CPU.
@@ -98,9 +100,54 @@ class PeerOutput:
             self.ptr = 0
 
 
-def matmul_allgather(a_piece, b, out: "PeerOutput", row_offset: int, ldc: int, stream=None):
+class SymmetricOutput:
+    """A full-size output buffer on every rank in torch symmetric memory: the
+    buffers are mapped into every rank (`peer_ptrs`) and, where the NVSwitch
+    supports it, bound to one multicast address (`multicast_ptr`, else 0): a
+    multimem store there is written by the switch into every rank's buffer, so
+    each GPU sends its output once instead of once per peer."""
+
+    def __init__(self, dist, nbytes: int, group=None):
+        import torch
+        import torch.distributed._symmetric_memory as symm
+        self.nbytes = nbytes
+        dev = torch.cuda.current_device()
+        self.tensor = symm.empty(nbytes, dtype=torch.uint8, device=torch.device("cuda", dev))
+        self.handle = symm.rendezvous(self.tensor, group if group is not None else dist.group.WORLD)
+        self.world, self.rank = self.handle.world_size, self.handle.rank
+        self.ptr = self.tensor.data_ptr()
+        self.peer_ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.multicast_ptr = int(self.handle.multicast_ptr)
+
+    @staticmethod
+    def multicast_supported(device: int) -> bool:
+        import torch
+        import torch.distributed._symmetric_memory as symm
+        try:
+            return bool(symm._SymmetricMemory.has_multicast_support(torch._C._autograd.DeviceType.CUDA, device))
+        except (AttributeError, RuntimeError):
+            return False
+
+    def read(self, offset_bytes: int, nbytes: int):
+        import torch
+        torch.cuda.synchronize()
+        return self.tensor[offset_bytes:offset_bytes + nbytes].cpu().numpy()
+
+    def close(self):
+        """Every rank calls this together: the buffers leave the multicast group only
+        after all ranks are done with them."""
+        if self.handle is not None:
+            import torch
+            torch.cuda.synchronize()
+            self.handle.barrier()
+            self.handle = None
+            self.tensor = None
+
+
+def matmul_allgather(a_piece, b, out, row_offset: int, ldc: int, stream=None, multicast: bool = True):
     """This rank's rows of C = A @ B (a_piece [m, K], b [K, N] CUDA float32 tensors),
-    stored into every rank's full output by the fused all-gather epilogue."""
+    stored into every rank's full output by the fused all-gather epilogue: through the
+    output's multicast address when it has one (and `multicast`), else with peer stores."""
     import ctypes as C
 
     import torch
@@ -122,6 +169,8 @@ def matmul_allgather(a_piece, b, out: "PeerOutput", row_offset: int, ldc: int, s
     for r, p in enumerate(out.peer_ptrs):
         g.peer_c[r] = p
     g.world, g.rank, g.row_offset, g.ldc = out.world, out.rank, row_offset, ldc
+    if multicast and getattr(out, "multicast_ptr", 0):
+        g.multicast_c = out.multicast_ptr
     s = stream if stream is not None else torch.cuda.current_stream()
     _lib.check(lib.piton_b200_matmul_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
                "matmul_allgather")

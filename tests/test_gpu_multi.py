@@ -1,5 +1,6 @@
 """Multi-GPU matmul with the all-gather fused into the GEMM epilogue (NVLink peer
-stores), on 2 GPUs when the box has them (skipped otherwise).  Every rank must
+stores, or multimem stores to an NVSwitch multicast address), on 2 GPUs when
+the box has them (skipped otherwise).  Every rank must
 end with the full C = A @ B: rows computed by every rank are checked against
 float64 on every rank."""
 
@@ -19,7 +20,7 @@ def _port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, results):
+def _worker(rank, world, port, results, kind="peer"):
     import datetime
 
     import torch.distributed as dist
@@ -37,7 +38,11 @@ def _worker(rank, world, port, results):
         A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1      # same on every rank (same seed)
         B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
         r0, per = sharding.shard(M, world, rank)
-        out = sharding.PeerOutput(dist, M * N * 4)
+        if kind == "multicast":
+            out = sharding.SymmetricOutput(dist, M * N * 4)
+            assert out.multicast_ptr != 0
+        else:
+            out = sharding.PeerOutput(dist, M * N * 4)
         for _ in range(2):
             sharding.matmul_allgather(A[r0:r0 + per], B, out, r0, N)
             torch.cuda.synchronize()
@@ -56,13 +61,18 @@ def _worker(rank, world, port, results):
         dist.destroy_process_group()
 
 
-def test_fused_allgather_matmul_two_gpus():
+@pytest.mark.parametrize("kind", ["peer", "multicast"])
+def test_fused_allgather_matmul_two_gpus(kind):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
+    if kind == "multicast":
+        from piton_b200.sharding import SymmetricOutput
+        if not SymmetricOutput.multicast_supported(0):
+            pytest.skip("no NVSwitch multicast on this box")
     import torch.multiprocessing as mp
     with mp.Manager() as manager:
         results = manager.dict()
-        mp.spawn(_worker, args=(2, _port(), results), nprocs=2, join=True)
+        mp.spawn(_worker, args=(2, _port(), results, kind), nprocs=2, join=True)
         res = dict(results)
     assert len(res) == 2
     for rank, (err, status) in res.items():
