@@ -199,12 +199,16 @@ def bench_matmul(torch, D, args, lib_calls):
     peer = None
     multicast = False
     if D.world > 1:
-        # NVSwitch multicast (one multimem store per element reaches every rank) where every
-        # rank has it, else CUDA IPC peer buffers and per-peer stores
-        flag = torch.tensor([1 if sharding.SymmetricOutput.multicast_supported(torch.cuda.current_device()) else 0],
-                            device="cuda")
-        D.pg.all_reduce(flag, op=D.pg.ReduceOp.MIN)
-        multicast = bool(flag.item())
+        # Peer stores (CUDA IPC buffers), spread over the next tile's chunks.  The NVSwitch
+        # multicast variant (--allgather multicast) stores each element once, but every GPU then
+        # also receives its own shard back through the switch: the all-gather is bound by each
+        # GPU's NVLink ingress, which multicast raises from (N-1) to N shards.
+        multicast = args.allgather == "multicast"
+        if multicast:
+            flag = torch.tensor([1 if sharding.SymmetricOutput.multicast_supported(torch.cuda.current_device())
+                                 else 0], device="cuda")
+            D.pg.all_reduce(flag, op=D.pg.ReduceOp.MIN)
+            multicast = bool(flag.item())
         peer = sharding.SymmetricOutput(D.pg, M * N * 4) if multicast else sharding.PeerOutput(D.pg, M * N * 4)
         multicast = multicast and peer.multicast_ptr != 0
         gargs = _lib.AllgatherArgs()
@@ -495,6 +499,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--mm-size", type=int, default=MM, help="matmul M=N=K (profiling runs use a smaller case)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--allgather", default="peer", choices=["peer", "multicast"],
+                    help="matmul all-gather at N > 1: peer stores, or multimem stores to an NVSwitch multicast address")
     ap.add_argument("--attn-bh", type=int, default=AT_B * AT_H, help="attention batch x heads (profiling runs use fewer)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
