@@ -53,6 +53,8 @@ extern "C" {
                                         adds and multiplies, no FMA, sequential-k dots, denormals read and
                                         written as +0 (piton/qpu/emulator.py:137-212). add, matmul, dense. */
 #define PITON_B200_FORCE_SIMT 0x2u   /* matmul/dense/attention: take the CUDA-core path even where tensor cores apply */
+#define PITON_B200_CUDA_GRAPH 0x4u   /* tinygpt_generate: capture the per-position launches into a CUDA graph once
+                                        per distinct argument set and replay it with one graph launch afterwards */
 
 /* ---- runtime (replaces pi/runtime/piton_rt.h:37-107: allocation, launch, sync, timers) ---- */
 
@@ -294,7 +296,15 @@ typedef struct {
     uint32_t flags;
 } piton_tinygpt_args;
 PITON_B200_API int64_t piton_b200_tinygpt_weight_floats(void);
+/* flags: 0 or PITON_B200_CUDA_GRAPH.  With the graph flag the launches are captured on an internal stream
+   the first time an argument set (every field, pointers included) is seen on a device, instantiated, and
+   cached (16 per device, least recently used evicted); every call, the first included, then enqueues one
+   cudaGraphLaunch on `stream`.  A replay does exactly what the launches with those arguments would do, so
+   the caller's buffers need only be valid at each call, as without the flag. */
 PITON_B200_API int piton_b200_tinygpt_generate(const piton_tinygpt_args *args, void *stream);
+/* Instantiated graphs cached on the current device; piton_b200_graph_cache_clear() destroys them. */
+PITON_B200_API int piton_b200_graph_cache_entries(int *entries);
+PITON_B200_API int piton_b200_graph_cache_clear(void);
 
 #ifdef __cplusplus
 }

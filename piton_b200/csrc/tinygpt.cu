@@ -270,6 +270,66 @@ using namespace piton;
 
 extern "C" int64_t piton_b200_tinygpt_weight_floats(void) { return tg::TOTAL_FLOATS; }
 
+// ---------------------------------------------------------------------------
+// CUDA-graph cache: a decode is ~80 launches of one small kernel, so the host
+// launch path costs a few microseconds a token.  With PITON_B200_CUDA_GRAPH the
+// sequence is captured once per argument set (stream capture on an internal
+// stream, thread-local mode), instantiated, and replayed with one
+// cudaGraphLaunch on the caller's stream.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+namespace {
+
+constexpr int GRAPH_CACHE = 16;
+
+struct GraphEntry {
+    piton_tinygpt_args key{};
+    cudaGraphExec_t exec = nullptr;
+    uint64_t used = 0;
+    int launches = 0;
+};
+
+struct DeviceGraphs {
+    cudaStream_t capture = nullptr;
+    GraphEntry entries[GRAPH_CACHE];
+    uint64_t clock = 0;
+};
+
+std::mutex g_graph_mu;
+DeviceGraphs g_graphs[64];
+
+bool same_args(const piton_tinygpt_args &a, const piton_tinygpt_args &b) {
+    return a.weights == b.weights && a.kv_cache == b.kv_cache && a.tokens == b.tokens && a.logits == b.logits &&
+           a.batch == b.batch && a.prompt_len == b.prompt_len && a.new_tokens == b.new_tokens && a.flags == b.flags;
+}
+
+}  // namespace
+
+extern "C" int piton_b200_graph_cache_entries(int *entries) {
+    PITON_REQUIRE(entries != nullptr, "entries is NULL");
+    int dev = 0;
+    PITON_CUDA(cudaGetDevice(&dev));
+    PITON_REQUIRE(dev >= 0 && dev < 64, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    int n = 0;
+    for (auto &e : g_graphs[dev].entries) n += e.exec != nullptr;
+    *entries = n;
+    return PITON_B200_OK;
+}
+
+extern "C" int piton_b200_graph_cache_clear(void) {
+    int dev = 0;
+    PITON_CUDA(cudaGetDevice(&dev));
+    PITON_REQUIRE(dev >= 0 && dev < 64, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    for (auto &e : g_graphs[dev].entries) {
+        if (e.exec) cudaGraphExecDestroy(e.exec);
+        e = GraphEntry{};
+    }
+    return PITON_B200_OK;
+}
+
 extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *stream) {
     using namespace tg;
     PITON_REQUIRE(a != nullptr, "args is NULL");
@@ -279,7 +339,7 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     PITON_REQUIRE(a->batch >= 0 && a->prompt_len >= 1 && a->new_tokens >= 0, "bad batch/prompt/new_tokens");
     PITON_REQUIRE(a->prompt_len + a->new_tokens <= CTX, "prompt_len + new_tokens = %lld exceeds the context %d",
                   (long long)(a->prompt_len + a->new_tokens), CTX);
-    PITON_REQUIRE(a->flags == 0, "unknown flags 0x%x", a->flags);
+    PITON_REQUIRE((a->flags & ~PITON_B200_CUDA_GRAPH) == 0, "unknown flags 0x%x", a->flags);
     if (a->batch == 0) return PITON_B200_OK;
     PITON_REQUIRE(a->weights && a->kv_cache && a->tokens, "NULL pointer");
     PITON_REQUIRE(a->batch <= (int64_t)SEQ * 65535 * 1024, "batch too large");
@@ -295,11 +355,65 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     if (a->new_tokens == 0 && a->logits) steps = (int)a->prompt_len;
     const unsigned grid = (unsigned)cdiv(a->batch, SEQ);
     cudaStream_t st = as_stream(stream);
-    for (int p = 0; p < steps; ++p) {
-        s.pos = p;
-        s.logits = p == steps - 1 ? reinterpret_cast<float *>(a->logits) : nullptr;
-        tinygpt_step_kernel<<<grid, THREADS, 0, st>>>(s);
+    auto enqueue = [&](cudaStream_t q) {
+        for (int p = 0; p < steps; ++p) {
+            s.pos = p;
+            s.logits = p == steps - 1 ? reinterpret_cast<float *>(a->logits) : nullptr;
+            tinygpt_step_kernel<<<grid, THREADS, 0, q>>>(s);
+        }
+    };
+    if (!(a->flags & PITON_B200_CUDA_GRAPH)) {
+        enqueue(st);
+        return check_launch("tinygpt", steps);
     }
-    const int launched = steps;
-    return check_launch("tinygpt", launched);
+    int dev = 0;
+    PITON_CUDA(cudaGetDevice(&dev));
+    PITON_REQUIRE(dev >= 0 && dev < 64, "device %d out of range", dev);
+    std::lock_guard<std::mutex> lock(g_graph_mu);
+    DeviceGraphs &G = g_graphs[dev];
+    GraphEntry *hit = nullptr;
+    for (auto &e : G.entries)
+        if (e.exec && same_args(e.key, *a)) {
+            hit = &e;
+            break;
+        }
+    if (!hit) {
+        // a free entry, else the least recently used one
+        GraphEntry *victim = nullptr;
+        for (auto &e : G.entries)
+            if (!e.exec) {
+                victim = &e;
+                break;
+            }
+        if (!victim) {
+            victim = &G.entries[0];
+            for (auto &e : G.entries)
+                if (e.used < victim->used) victim = &e;
+        }
+        if (!G.capture) PITON_CUDA(cudaStreamCreateWithFlags(&G.capture, cudaStreamNonBlocking));
+        if (victim->exec) cudaGraphExecDestroy(victim->exec);
+        *victim = GraphEntry{};
+        cudaGraph_t graph = nullptr;
+        PITON_CUDA(cudaStreamBeginCapture(G.capture, cudaStreamCaptureModeThreadLocal));
+        enqueue(G.capture);
+        cudaError_t launch_err = cudaGetLastError();
+        cudaError_t end_err = cudaStreamEndCapture(G.capture, &graph);
+        if (launch_err != cudaSuccess || end_err != cudaSuccess) {
+            if (graph) cudaGraphDestroy(graph);
+            return set_error(PITON_B200_ECUDA, "tinygpt graph capture: %s",
+                             cudaGetErrorString(launch_err != cudaSuccess ? launch_err : end_err));
+        }
+        cudaError_t inst = cudaGraphInstantiate(&victim->exec, graph, 0);
+        cudaGraphDestroy(graph);
+        if (inst != cudaSuccess) {
+            victim->exec = nullptr;
+            return set_error(PITON_B200_ECUDA, "tinygpt graph instantiate: %s", cudaGetErrorString(inst));
+        }
+        victim->key = *a;
+        victim->launches = steps;
+        hit = victim;
+    }
+    hit->used = ++G.clock;
+    PITON_CUDA(cudaGraphLaunch(hit->exec, st));
+    return check_launch("tinygpt graph", hit->launches);
 }

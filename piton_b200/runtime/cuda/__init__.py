@@ -136,17 +136,22 @@ class Launch:
         torch = _torch()
         self.stream = torch.cuda.current_stream(device)
         self.stream_ptr = C.c_void_p(self.stream.cuda_stream)
-        self.ev0 = torch.cuda.Event(enable_timing=True)
-        self.ev1 = torch.cuda.Event(enable_timing=True)
+        # under CUDA-graph capture the launch is recorded, not run: no host copies, no
+        # timing events, no synchronisation (torch.cuda.graph / CUDAGraph.capture_begin)
+        self.capturing = torch.cuda.is_current_stream_capturing()
+        self.ev0 = None if self.capturing else torch.cuda.Event(enable_timing=True)
+        self.ev1 = None if self.capturing else torch.cuda.Event(enable_timing=True)
         self.called = False
         self.host_h2d = self.host_d2h = 0   # bytes an entry point copied itself (host-buffer paths)
 
     def call(self, fname: str, args, what: str):
         """Run one C-ABI entry point on the launch's stream, timed with CUDA events."""
         f = getattr(lib(), fname)
-        self.ev0.record(self.stream)
+        if self.ev0 is not None:
+            self.ev0.record(self.stream)
         rc = f(C.byref(args), self.stream_ptr)
-        self.ev1.record(self.stream)
+        if self.ev1 is not None:
+            self.ev1.record(self.stream)
         self.called = True
         check(rc, what)
 
@@ -158,6 +163,9 @@ class Launch:
         and the copy to the device is skipped."""
         if name not in self.buffers:
             v = self.args[name]
+            if self.capturing and not _is_torch_tensor(getattr(v, "base", v)):
+                raise TypeError(f"argument {name}: under CUDA-graph capture pass CUDA tensors (numpy arrays "
+                                f"need host copies, which a graph cannot hold)")
             overwrite = (written and isinstance(v, np.ndarray) and covers == v.size and
                          not any(b.host is v for b in self.buffers.values()))
             self.buffers[name] = Buffer(name, v, self.device, self.stream, overwrite)
@@ -180,6 +188,11 @@ class Launch:
         torch = _torch()
         if nbytes == 0:
             return 0
+        if self.capturing:
+            # from the graph's private pool: it stays reserved for the graph's replays
+            buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device or "cuda")
+            self._keep = getattr(self, "_keep", []) + [buf]
+            return buf.data_ptr()
         key = torch.cuda.current_device() if self.device is None else self.device
         buf = _WORKSPACE.get(key)
         if buf is None or buf.numel() < nbytes:
@@ -192,7 +205,8 @@ class Launch:
         array back, launcher.py:209-211; arrays a kernel only reads come back
         unchanged, so only the written ones need the copy)."""
         d2h = sum(self.buffers[n].copy_back(self.stream) for n in self.written) + self.host_d2h
-        self.stream.synchronize()
+        if not self.capturing:
+            self.stream.synchronize()
         return sum(b.h2d_bytes for b in self.buffers.values()) + self.host_h2d, d2h
 
 
@@ -214,7 +228,7 @@ def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
         launch = Launch(values, constants, dev, qpu)
         stats = dict(handler(launch, tuple(grid) + (1,) * (3 - len(grid))) or {})
         h2d, d2h = launch.finish()
-        if launch.called:
+        if launch.called and launch.ev0 is not None:
             stats["time_us"] = launch.ev0.elapsed_time(launch.ev1) * 1e3
         stats["h2d_bytes"], stats["d2h_bytes"] = h2d, d2h
     return stats
@@ -270,7 +284,8 @@ def _matmul(L: Launch, grid):
     bm, bn, bk, g = (L.int(k) for k in ("BLOCK_SIZE_M", "BLOCK_SIZE_N", "BLOCK_SIZE_K", "GROUP_SIZE_M"))
     full_grid = grid[0] >= -(-M // bm) * -(-N // bn)
     dense_c = s["stride_cm"] == N and s["stride_cn"] == 1 and full_grid
-    if full_grid and M > 0 and N > 0 and _matmul_on_host_buffers(L, M, N, K, s, bm, bn, bk, g, grid):
+    if full_grid and M > 0 and N > 0 and not L.capturing and _matmul_on_host_buffers(L, M, N, K, s, bm, bn, bk, g,
+                                                                                     grid):
         return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K, "path": "tcgen05_3xtf32_host_pipelined"}
     A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True, covers=M * N if dense_c else -1)
     if M > 0 and N > 0 and grid[0] > 0:

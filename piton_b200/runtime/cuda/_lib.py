@@ -15,7 +15,7 @@ PKG = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("PITON_B200_LIB", os.path.join(PKG, "libpiton_b200.so"))
 
 OK, EINVAL, ECUDA, ETIMEOUT, ENOTSUP, ENOMEM, EWORKSPACE = 0, -1, -2, -3, -4, -5, -6
-QPU_ROUNDING, FORCE_SIMT = 0x1, 0x2
+QPU_ROUNDING, FORCE_SIMT, CUDA_GRAPH = 0x1, 0x2, 0x4
 NOALLOC_SCRATCH_BYTES = 32 << 20   # PITON_B200_NOALLOC_SCRATCH_BYTES
 
 u64, i64, i32, u32, f64 = C.c_uint64, C.c_int64, C.c_int32, C.c_uint32, C.c_double
@@ -139,6 +139,8 @@ PROTOTYPES = {
     "piton_b200_life_step": (C.c_int, [C.POINTER(LifeArgs), C.c_void_p]),
     "piton_b200_tinygpt_weight_floats": (C.c_int64, []),
     "piton_b200_tinygpt_generate": (C.c_int, [C.POINTER(TinyGPTArgs), C.c_void_p]),
+    "piton_b200_graph_cache_entries": (C.c_int, [C.POINTER(C.c_int)]),
+    "piton_b200_graph_cache_clear": (C.c_int, []),
 }
 
 STRUCTS = {"piton_allgather_args": AllgatherArgs, "piton_add_args": AddArgs, "piton_softmax_args": SoftmaxArgs, "piton_matmul_args": MatmulArgs,

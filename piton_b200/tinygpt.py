@@ -93,9 +93,12 @@ class TinyGPT:
             self._kv = torch.empty(need, dtype=torch.float32, device=self.device)
         return self._kv
 
-    def generate_device(self, tokens, prompt_len: int, new_tokens: int, logits=None, stream=None):
+    def generate_device(self, tokens, prompt_len: int, new_tokens: int, logits=None, stream=None,
+                        graph: bool = False):
         """tokens: CUDA int32 [batch, 128] with the prompts in [:, :prompt_len]; fills
-        [:, prompt_len:prompt_len + new_tokens] on the stream (asynchronous)."""
+        [:, prompt_len:prompt_len + new_tokens] on the stream (asynchronous).  graph=True
+        replays a CUDA graph of the decode's launches, captured by the library the first
+        time these buffers and sizes are seen."""
         torch = self.torch
         if tokens.dtype != torch.int32 or tokens.dim() != 2 or tokens.shape[1] != CTX or not tokens.is_contiguous():
             raise ValueError("tokens must be a contiguous CUDA int32 tensor [batch, 128]")
@@ -103,7 +106,7 @@ class TinyGPT:
         kv = self.kv_cache(batch)
         a = _lib.TinyGPTArgs(self.w.data_ptr(), kv.data_ptr(), tokens.data_ptr(),
                              logits.data_ptr() if logits is not None else 0, batch, prompt_len, new_tokens,
-                             VOCAB, D_MODEL, N_LAYER, N_HEAD, CTX, 0)
+                             VOCAB, D_MODEL, N_LAYER, N_HEAD, CTX, _lib.CUDA_GRAPH if graph else 0)
         s = stream if stream is not None else torch.cuda.current_stream(self.device)
         _lib.check(lib().piton_b200_tinygpt_generate(C.byref(a), C.c_void_p(s.cuda_stream)), "tinygpt")
 
