@@ -21,5 +21,7 @@ int attention_simt(const AttnParams &p, cudaStream_t s);
 bool attention_tc_supported(const AttnParams &p);
 size_t attention_tc_workspace_bytes(const AttnParams &p);
 int attention_tc(const AttnParams &p, void *workspace, cudaStream_t s);
+// The tensor-core attention kernel's status word (0, or the bounded wait that ran out), then reset.
+int attention_tc_status_read_and_clear(int *status);
 
 }  // namespace piton

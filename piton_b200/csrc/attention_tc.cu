@@ -38,7 +38,10 @@
 
 namespace piton {
 
-extern __device__ int g_tc_status;
+// Status word of this file's kernels (a device variable is private to its translation
+// unit without relocatable device code; piton_b200_device_status reads it through
+// attention_tc_status_read_and_clear).
+__device__ int g_attn_status = 0;
 
 namespace {
 
@@ -61,7 +64,7 @@ constexpr int TMEM_COLS = 512;
 constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_O = 384;
 
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
-__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
+__device__ __forceinline__ void record_status(int code) { atomicCAS(&g_attn_status, 0, code); }
 
 // hi/lo[h][r][c] (row stride ld) from src + h*s_h + r*s_r + c*s_c, r < rows, c < cols,
 // through 32 x 32 shared-memory tiles (grid.z = heads)
@@ -470,6 +473,13 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     a.causal = p.causal;
     attn_3xtf32_kernel<<<(unsigned)(a.q_blocks * p.heads), THREADS, SMEM_BYTES, stream>>>(mkh, mkl, mvh, mvl, a);
     return check_launch("attention_3xtf32", 3);
+}
+
+int attention_tc_status_read_and_clear(int *status) {
+    int zero = 0;
+    PITON_CUDA(cudaMemcpyFromSymbol(status, g_attn_status, sizeof(int)));
+    PITON_CUDA(cudaMemcpyToSymbol(g_attn_status, &zero, sizeof(int)));
+    return PITON_B200_OK;
 }
 
 }  // namespace piton

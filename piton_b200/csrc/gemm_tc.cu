@@ -29,6 +29,7 @@
 // returns.
 #include <vector>
 
+#include "attention.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "sm100.cuh"
@@ -560,5 +561,9 @@ int tc_status_read_and_clear(int *status) {
 
 extern "C" int piton_b200_device_status(int *status) {
     PITON_REQUIRE(status != nullptr, "status is NULL");
-    return piton::tc_status_read_and_clear(status);
+    int gemm = 0, attn = 0, rc;
+    if ((rc = piton::tc_status_read_and_clear(&gemm)) != PITON_B200_OK) return rc;
+    if ((rc = piton::attention_tc_status_read_and_clear(&attn)) != PITON_B200_OK) return rc;
+    *status = gemm ? gemm : attn;
+    return PITON_B200_OK;
 }
