@@ -233,7 +233,7 @@ def bench_matmul(torch, D, args, lib_calls):
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
     # at N = 1 the step is the kernel-only call itself: one measurement serves both
     t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
-    lib_calls["launches"] += per_call * args.steps
+    lib_calls["launches"] += per_call * args.steps * (2 if D.world > 1 else 1)
     flops = 2.0 * M * N * K
     # correctness spot check of this rank's first rows against float64 (and, with the fused
     # all-gather, of the rows every rank wrote into this rank's full C)
@@ -272,7 +272,7 @@ def bench_softmax(torch, D, args, lib_calls):
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
     # at N = 1 the step is the kernel-only call itself: one measurement serves both
     t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
-    lib_calls["launches"] += args.steps
+    lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     ref = torch.softmax(x[:8].double(), 1)
     err = float(((y[:8].double() - ref).abs() / ref.abs().clamp_min(1e-37)).max())
     _ = softmax_kernel
@@ -305,9 +305,13 @@ def bench_attention(torch, D, args, lib_calls):
         D.allgather(torch, ofull, o)
 
     steps = max(1, args.steps // 4)
-    t_kernel = timed(torch, D, kernel_only, steps, max(1, args.warmup // 2))
-    t_step = timed(torch, D, step, steps, 1)
-    lib_calls["launches"] += steps
+    n0 = lib().piton_b200_launch_count()
+    kernel_only()
+    per_call = lib().piton_b200_launch_count() - n0
+    t_kernel = timed(torch, D, kernel_only, steps, args.warmup)
+    # at N = 1 the step is the kernel-only call itself: one measurement serves both
+    t_step = timed(torch, D, step, steps, args.warmup) if D.world > 1 else t_kernel
+    lib_calls["launches"] += per_call * steps * (2 if D.world > 1 else 1)
     # spot check: head 0, first 64 query rows against float64
     qs, ks, vs = q[0].double(), k[0].double(), v[0].double()
     s = (qs[:64] @ ks.t()) / np.sqrt(AT_D)
@@ -340,7 +344,7 @@ def bench_add(torch, D, args, lib_calls):
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
     # at N = 1 the step is the kernel-only call itself: one measurement serves both
     t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
-    lib_calls["launches"] += args.steps
+    lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     err = float((out[:1 << 20] - (x[:1 << 20] + y[:1 << 20])).abs().max())
     return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc}
 
