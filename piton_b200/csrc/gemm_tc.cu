@@ -27,6 +27,7 @@
 // Every mbarrier wait is bounded (2 s of global time): on expiry the kernel
 // records a status word, drains its own TMA copies and MMAs, frees TMEM and
 // returns.
+#include <algorithm>
 #include <vector>
 
 #include "attention.cuh"
@@ -108,6 +109,7 @@ struct GemmArgs {
     float *c;
     int64_t M, N, K, scm, scn;
     int tiles_m, tiles_n, num_tiles, k_blocks;
+    int group;                       // tile rows per group of the tile order (L2 reuse of B)
     int world, rank;                 // world > 0: all-gather epilogue into peer_c
     int64_t row_offset, ldc_peer;
     float *peer_c[MAX_PEERS];
@@ -125,11 +127,11 @@ __device__ __forceinline__ void multimem_st(float *addr, float a) {
     asm volatile("multimem.st.relaxed.sys.global.f32 [%0], %1;" ::"l"(addr), "f"(a) : "memory");
 }
 
-__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int &tm, int &tn) {
-    int per_group = GROUP_M * tiles_n;
+__device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int group_m, int &tm, int &tn) {
+    int per_group = group_m * tiles_n;
     int group = t / per_group;
-    int first = group * GROUP_M;
-    int gsize = min(tiles_m - first, GROUP_M);
+    int first = group * group_m;
+    int gsize = min(tiles_m - first, group_m);
     int in = t % per_group;
     tm = first + in % gsize;
     tn = in / gsize;
@@ -137,19 +139,20 @@ __device__ __forceinline__ void tile_coords(int t, int tiles_m, int tiles_n, int
 
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_tc_status, 0, code); }
 
-// All-gather epilogue: rows [r0, r1) of finished tile (tm, tn), already stored in
-// this rank's own output, are copied to every other rank's output (float4 peer
-// stores).  Called by the 256 epilogue threads (`et` = 0..255), a few rows per
+// All-gather epilogue: rows [row_base + r0, row_base + r1) of finished tile column
+// tn, already stored in this rank's own output, are copied to every other rank's
+// output (float4 peer stores).  Called by the 256 epilogue threads (`et` = 0..255), a few rows per
 // accumulation chunk of the next tile, so the NVLink traffic is spread evenly
 // over the MMAs instead of bursting at the end of each tile.
 template <int BN>
-__device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int tm, int tn, int r0, int r1, int et) {
+__device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int64_t row_base, int tn, int r0, int r1,
+                                                   int et) {
     const float *src_base = args.peer_c[args.rank];
     const int64_t col_base = (int64_t)tn * BN;
     const int per_row = BN / 4;
     for (int i = et; i < (r1 - r0) * per_row; i += 256) {
         const int r = r0 + i / per_row, q = i % per_row;
-        const int64_t row = (int64_t)tm * BM + r;
+        const int64_t row = row_base + r;
         const int64_t col = col_base + 4 * q;
         if (row >= args.M || col >= args.N) continue;
         const int64_t off = (args.row_offset + row) * args.ldc_peer + col;
@@ -217,7 +220,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t it = 0;
             for (int t = blockIdx.x; t < args.num_tiles && !*abort_flag; t += gridDim.x) {
                 int tm, tn;
-                tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+                tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
                 for (int kb = 0; kb < kb_total; ++kb, ++it) {
                     uint32_t s = it % STAGES, round = it / STAGES;
                     if (!mbar_wait(&empty[s], (round & 1) ^ 1)) {
@@ -333,12 +336,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&tempty[acc]);   // TMEM buffer free for the next chunk
                 if (args.world > 1 && pend_tm >= 0)
-                    copy_rows_to_peers<BN>(args, pend_tm, pend_tn, min(ci * rows_per_chunk, BM),
+                    copy_rows_to_peers<BN>(args, (int64_t)pend_tm * BM, pend_tn, min(ci * rows_per_chunk, BM),
                                        min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
             int tm, tn;
-            tile_coords(t, args.tiles_m, args.tiles_n, tm, tn);
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
             const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
             if (row < args.M) {
                 const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
@@ -411,7 +414,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             ++tiles_done;
         }
-        if (ok && args.world > 1 && pend_tm >= 0) copy_rows_to_peers<BN>(args, pend_tm, pend_tn, 0, BM, et);
+        if (ok && args.world > 1 && pend_tm >= 0)
+            copy_rows_to_peers<BN>(args, (int64_t)pend_tm * BM, pend_tn, 0, BM, et);
         if (args.mc_c) __threadfence_system();
     }
     tc_fence_before();
@@ -420,6 +424,317 @@ __global__ void __launch_bounds__(THREADS, 1)
         __syncwarp();
         tc_fence_after();
         tmem_dealloc<TMEM_COLS>(tmem_base);
+    }
+}
+
+// ---- the same GEMM on CTA pairs: tcgen05.mma.cta_group::2 --------------------------------
+//
+// A cluster of two CTAs on neighbouring SMs computes a 256 x BNP tile: each CTA loads
+// its 128 rows of A and its BNP / 2 rows of B^T (hi and lo), the even CTA issues
+// tcgen05.mma.cta_group::2 (M = 256, N = BNP), which reads both CTAs' shared memory
+// and writes each CTA's 128 rows of the accumulator into its own TMEM.  Per SM a
+// 128 x BNP x 8 product then reads 4 KB of A and only BNP / 2 rows of B from shared
+// memory (the shared-memory path feeding the tensor core is what bounds the one-CTA
+// kernel).  The TMA loads of both CTAs complete on the even CTA's stage barrier; its
+// MMA commits (multicast) free the stage in both CTAs and hand finished accumulator
+// chunks to both CTAs' epilogue warps, which release the accumulator by arriving on
+// the even CTA's barrier.  Waits are bounded as in the one-CTA kernel; the two
+// cluster barriers (after set-up, before TMEM is freed) are reached unconditionally.
+
+constexpr int STAGES2 = 6;
+constexpr uint32_t A2_TILE_BYTES = BM * BK * 4;   // 8 KB: this CTA's 128 rows
+__host__ __device__ constexpr uint32_t b2_tile_bytes(int bnp) { return (uint32_t)(bnp / 2) * BK * 4; }
+__host__ __device__ constexpr uint32_t stage2_bytes(int bnp) { return 2 * A2_TILE_BYTES + 2 * b2_tile_bytes(bnp); }
+__host__ __device__ constexpr uint32_t smem2_bytes(int bnp) { return STAGES2 * stage2_bytes(bnp) + 1024 + 1024; }
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// shared::cluster address of the same variable in CTA rank 0 of the cluster
+__device__ __forceinline__ uint32_t cluster_addr_rank0(const void *p) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, 0;" : "=r"(r) : "r"(smem_u32(p)));
+    return r;
+}
+__device__ __forceinline__ void cluster_barrier() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile load into this CTA's shared memory, completing on a barrier of the pair (cta_group::2, no multicast)
+__device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *map, uint32_t bar_cluster, int x, int y) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], "
+        "[%2];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
+        : "memory");
+}
+__device__ __forceinline__ void mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
+// arrives on `bar` in both CTAs of the pair once this thread's MMAs have completed
+__device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
+    asm volatile(
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;" ::"r"(
+            smem_u32(bar)),
+        "h"((uint16_t)3)
+        : "memory");
+}
+
+template <int BNP>
+__global__ void __launch_bounds__(THREADS, 1)
+    gemm_3xtf32_2sm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
+                           const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+                           GemmArgs args) {
+    constexpr uint32_t B_TILE = b2_tile_bytes(BNP), STAGE = stage2_bytes(BNP);
+    constexpr int HALF = BNP / 2;   // accumulator columns per epilogue warpgroup, and B rows per CTA
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES2 * STAGE);
+    uint64_t *empty = full + STAGES2;
+    uint64_t *tfull = empty + STAGES2;
+    uint64_t *tempty = tfull + 2;
+    uint64_t *drain = tempty + 2;
+    uint64_t *epi_bar = drain + 1;
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(epi_bar + 1);
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < STAGES2; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&tfull[b], 1);
+            mbar_init(&tempty[b], 2 * EPI_WARPS);   // the epilogue warps of both CTAs
+        }
+        mbar_init(drain, 1);
+        mbar_init(epi_bar, EPI_WARPS);
+        *abort_flag = 0;
+        fence_mbarrier_init();
+        prefetch_tmap(&tm_ahi);
+        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_bhi);
+        prefetch_tmap(&tm_blo);
+    }
+    if (warp == 1) {   // the same warp of both CTAs allocates the pair's TMEM
+        asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
+                     "r"(TMEM_COLS)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_barrier();   // both CTAs' barriers initialised and TMEM allocated
+    tc_fence_after();
+    const uint32_t tmem_base = *tmem_holder;
+    const int kb_total = args.k_blocks;
+
+    if (warp == 0) {
+        // ---------------- TMA producer (both CTAs) ----------------
+        if (lane == 0) {
+            uint32_t it = 0;
+            for (int t = pair; t < args.num_tiles && !*abort_flag; t += npairs) {
+                int tm, tn;
+                tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
+                const int arow = tm * 2 * BM + (int)rank * BM, brow = tn * BNP + (int)rank * HALF;
+                for (int kb = 0; kb < kb_total; ++kb, ++it) {
+                    const uint32_t s = it % STAGES2, round = it / STAGES2;
+                    if (!mbar_wait(&empty[s], (round & 1) ^ 1)) {
+                        record_status(STATUS_TIMEOUT_PRODUCER);
+                        *abort_flag = 1;
+                        break;
+                    }
+                    uint8_t *st = smem + s * STAGE;
+                    const uint32_t bar = cluster_addr_rank0(&full[s]);
+                    if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE);   // both CTAs' bytes
+                    const int kx = kb * BK;
+                    tma_load_2d_pair(st, &tm_ahi, bar, kx, arow);
+                    tma_load_2d_pair(st + A2_TILE_BYTES, &tm_alo, bar, kx, arow);
+                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES, &tm_bhi, bar, kx, brow);
+                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES + B_TILE, &tm_blo, bar, kx, brow);
+                }
+            }
+            // drain: every copy of both CTAs completes on the even CTA's stage barriers
+            if (leader) {
+                const uint32_t first = it > STAGES2 ? it - STAGES2 : 0;
+                for (uint32_t j = first; j < it; ++j)
+                    if (!mbar_wait(&full[j % STAGES2], (j / STAGES2) & 1)) record_status(STATUS_TIMEOUT_DRAIN);
+            }
+        }
+    } else if (warp == 1) {
+        // ---------------- MMA issuer (even CTA) ----------------
+        if (lane == 0 && leader) {
+            constexpr uint32_t IDESC = idesc_tf32(2 * BM, BNP);
+            uint32_t it = 0, chunk = 0;
+            bool ok = true;
+            for (int t = pair; ok && t < args.num_tiles && !*abort_flag; t += npairs) {
+                for (int kb0 = 0; ok && kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk) {
+                    const int acc = chunk & 1;
+                    const uint32_t use = chunk >> 1;
+                    if (!mbar_wait(&tempty[acc], (use & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t d_tmem = tmem_base + acc * BNP;
+                    const int kb1 = min(kb0 + KC_BLOCKS, kb_total);
+                    for (int kb = kb0; kb < kb1; ++kb, ++it) {
+                        const uint32_t s = it % STAGES2, round = it / STAGES2;
+                        if (!mbar_wait(&full[s], round & 1)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        const uint32_t base = smem_u32(smem + s * STAGE);
+                        const uint32_t a_hi = base, a_lo = base + A2_TILE_BYTES;
+                        const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_lo = b_hi + B_TILE;
+#pragma unroll
+                        for (int ks = 0; ks < BK / 8; ++ks) {
+                            const uint32_t off = ks * 32;
+                            const uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
+                            mma_tf32_pair(d_tmem, dal, dbh, IDESC, first);   // A_lo B_hi
+                            mma_tf32_pair(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
+                            mma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);      // A_hi B_hi
+                        }
+                        mma_commit_pair(&empty[s]);   // stage s free in both CTAs
+                    }
+                    if (!ok) break;
+                    mma_commit_pair(&tfull[acc]);     // chunk ready for both CTAs' epilogues
+                }
+            }
+            if (!ok) {
+                record_status(STATUS_TIMEOUT_MMA);
+                *abort_flag = 1;
+            }
+            asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                             smem_u32(drain))
+                         : "memory");
+            if (!mbar_wait(drain, 0)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else {
+        // ---------------- epilogue (warps 2-9 of both CTAs): this CTA's 128 rows ----------------
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;
+        float sum[HALF];
+        uint32_t chunk = 0;
+        bool ok = true;
+        const int et = threadIdx.x - 64;
+        const int n_chunks = (kb_total + KC_BLOCKS - 1) / KC_BLOCKS;
+        const int rows_per_chunk = (BM + n_chunks - 1) / n_chunks;
+        const uint32_t tempty_pair[2] = {cluster_addr_rank0(&tempty[0]), cluster_addr_rank0(&tempty[1])};
+        int pend_tn = -1;
+        int64_t pend_row = -1;
+        uint32_t tiles_done = 0;
+        for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+            for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk, ++ci) {
+                const int acc = chunk & 1;
+                const uint32_t use = chunk >> 1;
+                bool got = !*abort_flag && mbar_wait(&tfull[acc], use & 1);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+                const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + acc * BNP + half * HALF;
+                if (kb0 == 0) {
+#pragma unroll
+                    for (int j = 0; j < HALF; ++j) sum[j] = 0.0f;
+                }
+#pragma unroll
+                for (int part = 0; part < HALF / 16; ++part) {
+                    uint32_t r[16];
+                    tmem_ld_32x32b_x16(taddr + part * 16, r);
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) sum[part * 16 + j] += __uint_as_float(r[j]);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive_cluster(tempty_pair[acc]);   // accumulator free (even CTA's barrier)
+                if (args.world > 1 && pend_row >= 0)
+                    copy_rows_to_peers<BNP>(args, pend_row, pend_tn, min(ci * rows_per_chunk, BM),
+                                            min((ci + 1) * rows_per_chunk, BM), et);
+            }
+            if (!ok) break;
+            int tm, tn;
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
+            const int64_t row_base = (int64_t)tm * 2 * BM + (int64_t)rank * BM;
+            const int64_t row = row_base + quarter * 32 + lane;
+            if (row < args.M) {
+                const int64_t col0 = (int64_t)tn * BNP + half * HALF;
+                float *crow;
+                bool vec;
+                int64_t scn;
+                if (args.world > 0) {
+                    crow = args.peer_c[args.rank] + (args.row_offset + row) * args.ldc_peer;
+                    vec = true;
+                    scn = 1;
+                } else {
+                    crow = args.c + row * args.scm;
+                    scn = args.scn;
+                    vec = scn == 1 && ((reinterpret_cast<uintptr_t>(args.c) | (uintptr_t)(args.scm * 4)) & 15) == 0;
+                }
+                if (vec) {
+#pragma unroll
+                    for (int j = 0; j < HALF; j += 4) {
+                        if (col0 + j + 4 <= args.N) {
+                            *reinterpret_cast<float4 *>(crow + col0 + j) =
+                                make_float4(sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                        } else {
+#pragma unroll
+                            for (int q = 0; q < 4; ++q)
+                                if (col0 + j + q < args.N) crow[col0 + j + q] = sum[j + q];
+                        }
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < HALF; ++j)
+                        if (col0 + j < args.N) crow[(col0 + j) * scn] = sum[j];
+                }
+            }
+            if (args.world > 1) {
+                __threadfence_block();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(epi_bar);
+                bool got = mbar_wait(epi_bar, tiles_done & 1);
+                if (!__all_sync(0xffffffffu, got)) {
+                    if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+                    *abort_flag = 1;
+                    ok = false;
+                    break;
+                }
+                pend_row = row_base;
+                pend_tn = tn;
+            }
+            ++tiles_done;
+        }
+        if (ok && args.world > 1 && pend_row >= 0) copy_rows_to_peers<BNP>(args, pend_row, pend_tn, 0, BM, et);
+    }
+    tc_fence_before();
+    __syncthreads();
+    cluster_barrier();   // the even CTA's MMAs are done with both CTAs' shared memory and TMEM
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(TMEM_COLS) : "memory");
     }
 }
 
@@ -457,6 +772,44 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
 }
 
 int64_t ld_of(int64_t K) { return (K + 3) / 4 * 4; }
+
+// CTA pairs (2-SM MMAs) for problems with at least two 256-row tiles; tile width along N
+// chosen as for one CTA, over the pairs.
+bool use_pairs(int64_t M, int64_t N) { return M >= 512 && N >= 256 && num_sms() >= 2; }
+int pair_tile_width(int64_t M, int64_t N) {
+    const int64_t pairs = num_sms() / 2, tm = cdiv(M, (int64_t)(2 * BM));
+    const int64_t cost256 = cdiv(tm * cdiv(N, (int64_t)256), pairs) * 256;
+    const int64_t cost224 = cdiv(tm * cdiv(N, (int64_t)224), pairs) * 224;
+    return cost224 < cost256 ? 224 : 256;
+}
+
+template <int BNP>
+int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtensorMap &b_hi, const CUtensorMap &b_lo,
+                 GemmArgs g, cudaStream_t stream) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr[dev]) {
+        PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_2sm_kernel<BNP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        smem2_bytes(BNP)));
+        attr[dev] = true;
+    }
+    const int pairs = std::min<int>(g.num_tiles, num_sms() / 2);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(2 * pairs));
+    cfg.blockDim = dim3(THREADS);
+    cfg.dynamicSmemBytes = smem2_bytes(BNP);
+    cfg.stream = stream;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = 2;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_3xtf32_2sm_kernel<BNP>, a_hi, a_lo, b_hi, b_lo, g));
+    return PITON_B200_OK;
+}
 
 // Tile width along N: the persistent grid runs ceil(tiles / SMs) rounds, each as long as
 // one tile (proportional to its width), so take the width with the fewer column-rounds;
@@ -511,12 +864,36 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
         }
     }
     // 2. persistent tcgen05 GEMM
-    const int bn = tile_width(s.M, s.N);
+    const bool pairs = use_pairs(s.M, s.N);
+    const int bn = pairs ? pair_tile_width(s.M, s.N) : tile_width(s.M, s.N);
+    const int b_box = pairs ? bn / 2 : bn;   // rows of B^T one CTA loads
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     int rc;
     if ((rc = make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) || (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
-        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, bn)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, bn)))
+        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, b_box)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, b_box)))
         return rc;
+    GemmArgs g;
+    g.c = s.c;
+    g.M = s.M; g.N = s.N; g.K = s.K; g.scm = s.scm; g.scn = s.scn;
+    g.k_blocks = (int)cdiv(s.K, BK);
+    g.world = s.world;
+    g.rank = s.rank;
+    g.row_offset = s.row_offset;
+    g.ldc_peer = s.ldc_peer;
+    for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
+    g.mc_c = s.multicast_c;
+    if (pairs) {
+        g.tiles_m = (int)cdiv(s.M, (int64_t)(2 * BM));
+        g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
+        g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
+        g.num_tiles = g.tiles_m * g.tiles_n;
+        if (g.mc_c)
+            return set_error(PITON_B200_ENOTSUP, "the multicast all-gather runs on the one-CTA kernel only");
+        rc = bn == 224 ? launch_pairs<224>(m_ahi, m_alo, m_bhi, m_blo, g, stream)
+                       : launch_pairs<256>(m_ahi, m_alo, m_bhi, m_blo, g, stream);
+        if (rc) return rc;
+        return check_launch("gemm_3xtf32_2sm", s.split_b ? 3 : 2);
+    }
     static bool attr[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -529,19 +906,10 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
                                             smem_bytes(256)));
         attr[dev][bn == 224] = true;
     }
-    GemmArgs g;
-    g.c = s.c;
-    g.M = s.M; g.N = s.N; g.K = s.K; g.scm = s.scm; g.scn = s.scn;
     g.tiles_m = (int)cdiv(s.M, BM);
+    g.group = GROUP_M;
     g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
     g.num_tiles = g.tiles_m * g.tiles_n;
-    g.k_blocks = (int)cdiv(s.K, BK);
-    g.world = s.world;
-    g.rank = s.rank;
-    g.row_offset = s.row_offset;
-    g.ldc_peer = s.ldc_peer;
-    for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
-    g.mc_c = s.multicast_c;
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     if (bn == 224)
         gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);

@@ -136,6 +136,35 @@ def device_status():
     return s.value
 
 
+@pytest.mark.parametrize("M,N,K,neg", [(768, 520, 300, False), (1100, 300, 200, True), (512, 256, 16, False)])
+def test_tensor_core_pairs_strided_c(cuda, M, N, K, neg):
+    """Problems the CTA-pair kernel (2-SM MMAs, M >= 512) takes, with C transposed in
+    memory (scalar stores) or with a negative row stride."""
+    torch = cuda
+    g = torch.Generator(device="cuda").manual_seed(M + 7 * N + K)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    base = torch.full((N * M + 64,), 7.0, device="cuda")
+    if neg:
+        Cv = base[:M * N].view(M, N)
+        st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+            A, B, offset_ptr(base, (M - 1) * N), M, N, K, K, 1, N, 1, -N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
+            BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
+        got = Cv.flip(0)
+    else:
+        Ct = base[:M * N].view(N, M).t()                  # stride_cm = 1, stride_cn = M
+        st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+            A, B, Ct, M, N, K, K, 1, N, 1, Ct.stride(0), Ct.stride(1), BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
+            BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
+        got = Ct
+    assert st["path"] == "tcgen05_3xtf32"
+    ref = A.double() @ B.double()
+    err = float((got.double() - ref).abs().max() / ref.abs().max())
+    assert err <= fp32_bound(K), err
+    assert bool((base[M * N:] == 7.0).all())
+    assert device_status() == 0
+
+
 @pytest.mark.parametrize("M,N,K", [(1024, 8192, 256), (2048, 1000, 512), (640, 4000, 64)])
 def test_tensor_core_224_wide_tiles_ragged_n(cuda, M, N, K):
     """Shapes whose tiles pack into fewer rounds 224 columns wide (the last N tile is
