@@ -136,7 +136,7 @@ def device_status():
     return s.value
 
 
-@pytest.mark.parametrize("M,N,K,neg", [(768, 520, 300, False), (1100, 300, 200, True), (512, 256, 16, False)])
+@pytest.mark.parametrize("M,N,K,neg", [(768, 520, 300, False), (1100, 300, 200, True), (512, 256, 64, False)])
 def test_tensor_core_pairs_strided_c(cuda, M, N, K, neg):
     """Problems the CTA-pair kernel (2-SM MMAs, M >= 512) takes, with C transposed in
     memory (scalar stores) or with a negative row stride."""
