@@ -679,7 +679,21 @@ __global__ void __launch_bounds__(THREADS, 1)
             tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
             const int64_t row_base = (int64_t)tm * 2 * BM + (int64_t)rank * BM;
             const int64_t row = row_base + quarter * 32 + lane;
-            if (row < args.M) {
+            if (row < args.M && args.mc_c) {
+                // multicast all-gather: one store per element, replicated to every rank by the switch
+                const int64_t col0 = (int64_t)tn * BNP + half * HALF;
+                float *mrow = args.mc_c + (args.row_offset + row) * args.ldc_peer;
+#pragma unroll
+                for (int j = 0; j < HALF; j += 4) {
+                    if (col0 + j + 4 <= args.N) {
+                        multimem_st_v4(mrow + col0 + j, sum[j], sum[j + 1], sum[j + 2], sum[j + 3]);
+                    } else {
+#pragma unroll
+                        for (int q = 0; q < 4; ++q)
+                            if (col0 + j + q < args.N) multimem_st(mrow + col0 + j + q, sum[j + q]);
+                    }
+                }
+            } else if (row < args.M) {
                 const int64_t col0 = (int64_t)tn * BNP + half * HALF;
                 float *crow;
                 bool vec;
@@ -711,7 +725,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (col0 + j < args.N) crow[(col0 + j) * scn] = sum[j];
                 }
             }
-            if (args.world > 1) {
+            if (args.world > 1 && !args.mc_c) {
                 __threadfence_block();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(epi_bar);
@@ -728,6 +742,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             ++tiles_done;
         }
         if (ok && args.world > 1 && pend_row >= 0) copy_rows_to_peers<BNP>(args, pend_row, pend_tn, 0, BM, et);
+        if (args.mc_c) __threadfence_system();
     }
     tc_fence_before();
     __syncthreads();
@@ -887,8 +902,6 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
         g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
         g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
         g.num_tiles = g.tiles_m * g.tiles_n;
-        if (g.mc_c)
-            return set_error(PITON_B200_ENOTSUP, "the multicast all-gather runs on the one-CTA kernel only");
         rc = bn == 224 ? launch_pairs<224>(m_ahi, m_alo, m_bhi, m_blo, g, stream)
                        : launch_pairs<256>(m_ahi, m_alo, m_bhi, m_blo, g, stream);
         if (rc) return rc;
