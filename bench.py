@@ -466,6 +466,54 @@ def cpu_baseline_matmul(rows: int, threads: int):
     return 2.0 * rows * MM * MM / sec / 1e12, sec
 
 
+def cpu_baselines_secondary(threads: int) -> dict:
+    """The oracle's restatements of the reference's CPU path for the other operators, each on a
+    bounded sample of its benchmark workload (a few seconds in all), reported beside the B200
+    figures (the oracle's C kernels are single-threaded unless noted)."""
+    from oracle import oracle as O
+    from oracle import tinygpt_ref
+    from piton_b200 import tinygpt, workloads as W
+    out = {}
+    rng = np.random.default_rng(0)
+    n = 1 << 24
+    x, y = rng.uniform(-1, 1, n).astype(np.float32), rng.uniform(-1, 1, n).astype(np.float32)
+    t0 = time.perf_counter()
+    O.qpu_add(x, y)
+    sec = time.perf_counter() - t0
+    out["add"] = {"value": 12.0 * n / sec / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                  "sample": f"n = 2^24 of the 2^28-element workload, round-toward-zero adds"}
+    rows = 128
+    xs = W.softmax_input(rows, SM_N, 0)
+    t0 = time.perf_counter()
+    O.qpu_softmax(xs, SM_N)
+    sec = time.perf_counter() - t0
+    out["softmax"] = {"value": 8.0 * rows * SM_N / sec / 1e9, "unit": "GB/s", "cores": 1, "kind": "port",
+                      "sample": f"{rows} of the 32768 rows x {SM_N} columns, the QPU exp polynomial and butterflies"}
+    s_len = 1024
+    q, k, v = W.attention_inputs(1, s_len, AT_D, 0)
+    t0 = time.perf_counter()
+    O.qpu_attention(q, k, v, True, 2, 16)
+    sec = time.perf_counter() - t0
+    out["attention"] = {"value": 4.0 * s_len * s_len * AT_D * 0.5 / sec / 1e12, "unit": "TFLOP/s", "cores": 1,
+                        "kind": "port", "sample": f"one head, S = {s_len}, D = 64, causal (the benchmark has 1024 "
+                                                  f"heads of S = 4096)"}
+    imgs = W.digits_images(1797, 0)
+    t0 = time.perf_counter()
+    O.qpu_mlp(imgs, W.digits_model(0), threads=threads)
+    sec = time.perf_counter() - t0
+    out["mlp_digits_1797"] = {"value": 1797 / sec, "unit": "images/s", "cores": threads, "kind": "port",
+                              "sample": "all 1797 images, the three dense layers with round-toward-zero dots"}
+    w = tinygpt.init_weights(0)
+    prompts = tinygpt.random_prompts(1, seed=100)
+    new = 8
+    t0 = time.perf_counter()
+    tinygpt_ref.generate(w, prompts, new)
+    sec = time.perf_counter() - t0
+    out["tinygpt_b1"] = {"value": new / sec, "unit": "tokens/s", "cores": 1, "kind": "port",
+                         "sample": f"batch 1, {new} of the 64 greedy tokens, float64 numpy host model"}
+    return out
+
+
 def run_reference(args):
     D = Dist()
     if D.rank != 0:
@@ -618,6 +666,11 @@ def main():
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                 "sample": f"{rows} of {MM} rows of the {MM}^3 product ({s:.1f} s): the oracle's "
                                           f"restatement of the emulator's sequential-k round-toward-zero dot"}
+    if D.world == 1 and not args.no_cpu_baseline and line.get("secondary"):
+        # the reference's CPU path for the other operators, beside their B200 figures
+        for key, cb in cpu_baselines_secondary(os.cpu_count() or 1).items():
+            if key in line["secondary"]:
+                line["secondary"][key]["cpu_baseline"] = cb
     print(json.dumps(line), flush=True)
     return 0
 
