@@ -263,12 +263,315 @@ __global__ void __launch_bounds__(THREADS) tinygpt_step_kernel(StepArgs a) {
     }
 }
 
+// ---------------------------------------------------------------------------
+// Small batches: one thread-block cluster of CS = 16 CTAs per sequence, one
+// launch per decode.  The weights (3.2 MB) are split by output column across
+// the 16 CTAs and held in their shared memory for the whole decode (each CTA
+// keeps its 1/16 of every matrix, ~195 KB); every CTA keeps a full copy of the
+// residual stream.  Per linear layer each CTA computes its slice of the outputs
+// (a warp per output column, lanes over k) and stores it into all 16 CTAs'
+// shared memory (st.shared::cluster), then the cluster barrier makes the whole
+// vector visible everywhere: five exchanges per layer plus one for the logits.
+// Attention head h runs in CTA h.  Every CTA computes the same greedy argmax,
+// so all of them feed the same next token.
+// ---------------------------------------------------------------------------
+
+constexpr int CS = 16;                           // CTAs per cluster (non-portable size)
+constexpr int QKV_C = 3 * D / CS, O_C = D / CS, FC_C = F / CS, PR_C = D / CS;   // columns per CTA
+constexpr int V_C = (V + CS - 1) / CS;           // vocabulary rows per CTA (5)
+// shared-memory weight slices, column-major (column j of the slice is contiguous in k)
+constexpr int W_QKV = QKV_C * D, W_O = O_C * D, W_FC = FC_C * D, W_PR = PR_C * F, W_TE = V_C * D;
+constexpr int W_LAYER = W_QKV + W_O + W_FC + W_PR;
+constexpr int ACT = D /*x*/ + D /*h*/ + 3 * D /*qkv*/ + D /*att*/ + D /*o*/ + F /*f*/ + D /*pr*/ + CS * V_C /*logits*/;
+constexpr size_t CLUSTER_SMEM = (size_t)(L * W_LAYER + W_TE + ACT + 3 * 256) * 4;
+
+struct ClusterArgs {
+    const float *w;
+    float *kv;
+    int32_t *tokens;
+    float *logits;
+    int64_t batch;
+    int prompt_len, end, steps;
+};
+
+__device__ __forceinline__ uint32_t cl_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cl_id() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ uint32_t cl_count() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+    return r;
+}
+__device__ __forceinline__ void cl_sync() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// v into the same shared-memory slot in CTA `rank` of the cluster
+__device__ __forceinline__ void st_cluster(float *local, uint32_t rank, float v) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(local), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
+}
+
+// This CTA's NC output columns [c0, c0 + NC) of act(in . W + b), W [K][ncols] in global
+// order but held here column-major as ws[j][k]; each column's value goes to out[c0 + j]
+// in all CS CTAs.  Warp w handles columns w, w + 8, ...; lanes split k.
+template <int K, int NC, bool GELU>
+__device__ __forceinline__ void slice_linear(const float *in, const float *ws, const float *__restrict__ b, int c0,
+                                             float *out) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int j = warp; j < NC; j += THREADS / 32) {
+        const float *wc = ws + j * K;
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int k = lane; k < K; k += 32) acc = fmaf(in[k], wc[k], acc);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        float v = acc + __ldg(b + c0 + j);
+        if (GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+        if (lane < CS) st_cluster(out + c0 + j, lane, v);
+    }
+}
+
+// LayerNorm of x (D) into y by warp 0, then the CTA syncs
+__device__ __forceinline__ void ln_cta(const float *x, float *y, const float *__restrict__ g,
+                                       const float *__restrict__ b) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (warp == 0) {
+        float v[D / 32], sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            v[i] = x[lane + 32 * i];
+            sum += v[i];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum * (1.0f / D);
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            v[i] -= mean;
+            q += v[i] * v[i];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        const float r = rsqrtf(q * (1.0f / D) + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            const int c = lane + 32 * i;
+            y[c] = v[i] * r * __ldg(g + c) + __ldg(b + c);
+        }
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs a) {
+    extern __shared__ __align__(16) float sm[];
+    const uint32_t rank = cl_rank();
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    float *wl = sm;                                  // [L][W_LAYER]
+    float *wte_s = wl + L * W_LAYER;                 // [V_C][D]
+    float *x = wte_s + W_TE, *h = x + D, *qkv = h + D, *att = qkv + 3 * D, *ob = att + D, *f = ob + D;
+    float *pr = f + F, *lg = pr + D, *red = lg + CS * V_C;   // red: 3 x 256 scratch
+    const float *wte = a.w, *wpe = a.w + V * D;
+    const float *lw0 = a.w + V * D + CTX * D;
+
+    // this CTA's weight slices, once per decode (column-major: ws[j][k] = W[k][c0 + j])
+    for (int l = 0; l < L; ++l) {
+        const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
+        const float *w_qkv = lw + 2 * D, *w_o = w_qkv + D * 3 * D + 3 * D, *w_fc = w_o + D * D + D + 2 * D;
+        const float *w_pr = w_fc + D * F + F;
+        float *s_qkv = wl + l * W_LAYER, *s_o = s_qkv + W_QKV, *s_fc = s_o + W_O, *s_pr = s_fc + W_FC;
+        for (int i = tid; i < W_QKV; i += THREADS) s_qkv[i] = __ldg(w_qkv + (i % D) * 3 * D + rank * QKV_C + i / D);
+        for (int i = tid; i < W_O; i += THREADS) s_o[i] = __ldg(w_o + (i % D) * D + rank * O_C + i / D);
+        for (int i = tid; i < W_FC; i += THREADS) s_fc[i] = __ldg(w_fc + (i % D) * F + rank * FC_C + i / D);
+        for (int i = tid; i < W_PR; i += THREADS) s_pr[i] = __ldg(w_pr + (i % F) * D + rank * PR_C + i / F);
+    }
+    for (int i = tid; i < W_TE; i += THREADS) {
+        const int v = (int)rank * V_C + i / D;
+        wte_s[i] = v < V ? __ldg(wte + v * D + i % D) : 0.0f;
+    }
+    __syncthreads();
+    cl_sync();   // every CTA of the cluster is running before any stores into its shared memory
+
+    for (int64_t b = cl_id(); b < a.batch; b += cl_count()) {
+        int tok = a.tokens[b * CTX];
+        for (int pos = 0; pos < a.steps; ++pos) {
+            if (pos < a.prompt_len) tok = a.tokens[b * CTX + pos];
+            tok = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
+            for (int c = tid; c < D; c += THREADS) x[c] = __ldg(wte + tok * D + c) + __ldg(wpe + pos * D + c);
+            __syncthreads();
+            for (int l = 0; l < L; ++l) {
+                const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
+                const float *ln1_g = lw, *ln1_b = ln1_g + D, *b_qkv = ln1_b + D + D * 3 * D;
+                const float *b_o = b_qkv + 3 * D + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
+                const float *b_fc = ln2_b + D + D * F, *b_pr = b_fc + F + F * D;
+                const float *s_qkv = wl + l * W_LAYER, *s_o = s_qkv + W_QKV, *s_fc = s_o + W_O, *s_pr = s_fc + W_FC;
+                float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
+                float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
+
+                ln_cta(x, h, ln1_g, ln1_b);
+                slice_linear<D, QKV_C, false>(h, s_qkv, b_qkv, rank * QKV_C, qkv);
+                cl_sync();
+                // attention: head rank (CTAs 0..H-1) over positions 0..pos
+                if (rank < H) {
+                    const int hh = rank;
+                    float *kr_base = kc + (b * CTX) * D + hh * HD, *vr_base = vc + (b * CTX) * D + hh * HD;
+                    if (tid < HD) {
+                        kr_base[pos * D + tid] = qkv[D + hh * HD + tid];
+                        vr_base[pos * D + tid] = qkv[2 * D + hh * HD + tid];
+                    }
+                    __syncthreads();
+                    const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
+                    float sc = -INFINITY;
+                    if (tid <= pos) {
+                        const float *kr = kr_base + tid * D;
+                        float acc = 0.0f;
+#pragma unroll
+                        for (int d = 0; d < HD; d += 4) {
+                            const float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+                            acc = fmaf(qkv[hh * HD + d], k4.x, acc);
+                            acc = fmaf(qkv[hh * HD + d + 1], k4.y, acc);
+                            acc = fmaf(qkv[hh * HD + d + 2], k4.z, acc);
+                            acc = fmaf(qkv[hh * HD + d + 3], k4.w, acc);
+                        }
+                        sc = acc * scale;
+                    }
+                    // max and sum over the (at most 128) scores
+                    float m = sc;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+                    if (lane == 0) red[warp] = m;
+                    __syncthreads();
+                    m = red[0];
+                    for (int w2 = 1; w2 < THREADS / 32; ++w2) m = fmaxf(m, red[w2]);
+                    const float p = tid <= pos ? expf(sc - m) : 0.0f;
+                    float ssum = p;
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
+                    red[256 + tid] = p;
+                    if (lane == 0) red[512 + warp] = ssum;
+                    __syncthreads();
+                    float tot = 0.0f;
+                    for (int w2 = 0; w2 < THREADS / 32; ++w2) tot += red[512 + w2];
+                    // output dimension d = tid % 32 over positions t = tid / 32, tid / 32 + 8, ...
+                    const int d = tid & 31, tg0 = tid >> 5;
+                    float o_acc = 0.0f;
+                    for (int t = tg0; t <= pos; t += THREADS / 32) o_acc = fmaf(red[256 + t], vr_base[t * D + d], o_acc);
+                    __syncthreads();
+                    red[tid] = o_acc;
+                    __syncthreads();
+                    if (tid < HD) {
+                        float v = 0.0f;
+                        for (int g2 = 0; g2 < THREADS / 32; ++g2) v += red[g2 * 32 + tid];
+                        v /= tot;
+                        for (uint32_t r = 0; r < CS; ++r) st_cluster(att + hh * HD + tid, r, v);
+                    }
+                }
+                cl_sync();
+                slice_linear<D, O_C, false>(att, s_o, b_o, rank * O_C, ob);
+                cl_sync();
+                for (int c = tid; c < D; c += THREADS) x[c] += ob[c];
+                __syncthreads();
+                ln_cta(x, h, ln2_g, ln2_b);
+                slice_linear<D, FC_C, true>(h, s_fc, b_fc, rank * FC_C, f);
+                cl_sync();
+                slice_linear<F, PR_C, false>(f, s_pr, b_pr, rank * PR_C, pr);
+                cl_sync();
+                for (int c = tid; c < D; c += THREADS) x[c] += pr[c];
+                __syncthreads();
+            }
+            const float *lnf = lw0 + (int64_t)L * LAYER_FLOATS;
+            ln_cta(x, h, lnf, lnf + D);
+            // tied head: this CTA's vocabulary rows, a warp per row
+            for (int j = warp; j < V_C; j += THREADS / 32) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int k = lane; k < D; k += 32) acc = fmaf(h[k], wte_s[j * D + k], acc);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane < CS) st_cluster(lg + rank * V_C + j, lane, acc);
+            }
+            cl_sync();
+            int best = 0;
+            for (int v = 1; v < V; ++v)
+                if (lg[v] > lg[best]) best = v;     // first maximum, as numpy.argmax
+            if (pos + 1 >= a.prompt_len && pos + 1 < a.end) {
+                tok = best;
+                if (rank == 0 && tid == 0) a.tokens[b * CTX + pos + 1] = best;
+            }
+            if (a.logits && pos == a.steps - 1 && rank == 0)
+                for (int v = tid; v < V; v += THREADS) a.logits[b * V + v] = lg[v];
+            __syncthreads();
+        }
+    }
+    cl_sync();   // no CTA leaves while another may still store into its shared memory
+}
+
 }  // namespace tg
 }  // namespace piton
 
 using namespace piton;
 
 extern "C" int64_t piton_b200_tinygpt_weight_floats(void) { return tg::TOTAL_FLOATS; }
+
+namespace {
+
+// Clusters of 16 CTAs with the cluster kernel's shared memory that fit on the current
+// device at once (0: the cluster path is unavailable), looked up once per device.
+int cluster_capacity() {
+    static int cache[64];
+    static bool known[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (known[dev]) return cache[dev];
+    int n = 0;
+    if (cudaFuncSetAttribute(tg::tinygpt_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
+            cudaSuccess &&
+        cudaFuncSetAttribute(tg::tinygpt_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)tg::CLUSTER_SMEM) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(tg::CS);
+        cfg.blockDim = dim3(tg::THREADS);
+        cfg.dynamicSmemBytes = tg::CLUSTER_SMEM;
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = tg::CS;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, tg::tinygpt_cluster_kernel, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();   // a refused attribute or query only disables this path
+    cache[dev] = n;
+    known[dev] = true;
+    return n;
+}
+
+void launch_cluster(const tg::ClusterArgs &c, int clusters, cudaStream_t q) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(clusters * tg::CS));
+    cfg.blockDim = dim3(tg::THREADS);
+    cfg.dynamicSmemBytes = tg::CLUSTER_SMEM;
+    cfg.stream = q;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = tg::CS;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, tg::tinygpt_cluster_kernel, c);
+}
+
+}  // namespace
 
 // ---------------------------------------------------------------------------
 // CUDA-graph cache: a decode is ~80 launches of one small kernel, so the host
@@ -355,7 +658,24 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     if (a->new_tokens == 0 && a->logits) steps = (int)a->prompt_len;
     const unsigned grid = (unsigned)cdiv(a->batch, SEQ);
     cudaStream_t st = as_stream(stream);
+    // small batches: one 16-CTA cluster per sequence, weights resident in shared memory, one launch
+    const int clusters = cluster_capacity();
+    const bool use_cluster = clusters > 0 && a->batch <= clusters;
+    const int launches = use_cluster ? 1 : steps;
     auto enqueue = [&](cudaStream_t q) {
+        if (use_cluster) {
+            ClusterArgs c;
+            c.w = s.w;
+            c.kv = s.kv;
+            c.tokens = s.tokens;
+            c.logits = reinterpret_cast<float *>(a->logits);
+            c.batch = a->batch;
+            c.prompt_len = s.prompt_len;
+            c.end = s.end;
+            c.steps = steps;
+            launch_cluster(c, (int)a->batch, q);
+            return;
+        }
         for (int p = 0; p < steps; ++p) {
             s.pos = p;
             s.logits = p == steps - 1 ? reinterpret_cast<float *>(a->logits) : nullptr;
@@ -364,7 +684,7 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     };
     if (!(a->flags & PITON_B200_CUDA_GRAPH)) {
         enqueue(st);
-        return check_launch("tinygpt", steps);
+        return check_launch("tinygpt", launches);
     }
     int dev = 0;
     PITON_CUDA(cudaGetDevice(&dev));
@@ -410,7 +730,7 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
             return set_error(PITON_B200_ECUDA, "tinygpt graph instantiate: %s", cudaGetErrorString(inst));
         }
         victim->key = *a;
-        victim->launches = steps;
+        victim->launches = launches;
         hit = victim;
     }
     hit->used = ++G.clock;
