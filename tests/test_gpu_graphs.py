@@ -45,7 +45,8 @@ def test_tinygpt_graph_replay_same_tokens(cuda):
     model.generate_device(graphed, 16, 64, graph=True)
     torch.cuda.synchronize()
     assert entries() == 1
-    assert lib().piton_b200_launch_count() - n0 == 16 + 64 - 1
+    # one launch per position, or one cluster launch for the whole decode (small batches)
+    assert lib().piton_b200_launch_count() - n0 in (1, 16 + 64 - 1)
     np.testing.assert_array_equal(graphed.cpu().numpy(), eager.cpu().numpy())
     # replay: same buffers and sizes, the prompt region rewritten, no new capture
     graphed[:, 16:] = 0
