@@ -532,10 +532,12 @@ int cluster_capacity() {
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
     if (known[dev]) return cache[dev];
     int n = 0;
+    bool failed = true;
     if (cudaFuncSetAttribute(tg::tinygpt_cluster_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1) ==
             cudaSuccess &&
         cudaFuncSetAttribute(tg::tinygpt_cluster_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)tg::CLUSTER_SMEM) == cudaSuccess) {
+        failed = false;
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(tg::CS);
         cfg.blockDim = dim3(tg::THREADS);
@@ -547,9 +549,12 @@ int cluster_capacity() {
         at[0].val.clusterDim.z = 1;
         cfg.attrs = at;
         cfg.numAttrs = 1;
-        if (cudaOccupancyMaxActiveClusters(&n, tg::tinygpt_cluster_kernel, &cfg) != cudaSuccess) n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tg::tinygpt_cluster_kernel, &cfg) != cudaSuccess) {
+            n = 0;
+            failed = true;
+        }
     }
-    cudaGetLastError();   // a refused attribute or query only disables this path
+    if (failed) cudaGetLastError();   // a refused attribute or query only disables this path
     cache[dev] = n;
     known[dev] = true;
     return n;
