@@ -277,13 +277,23 @@ __global__ void __launch_bounds__(THREADS) tinygpt_step_kernel(StepArgs a) {
 // ---------------------------------------------------------------------------
 
 constexpr int CS = 16;                           // CTAs per cluster (non-portable size)
-constexpr int QKV_C = 3 * D / CS, O_C = D / CS, FC_C = F / CS, PR_C = D / CS;   // columns per CTA
+constexpr int QKV_C = 3 * D / CS;                // q/k/v columns per CTA (24)
 constexpr int V_C = (V + CS - 1) / CS;           // vocabulary rows per CTA (5)
-// shared-memory weight slices, column-major (column j of the slice is contiguous in k)
-constexpr int W_QKV = QKV_C * D, W_O = O_C * D, W_FC = FC_C * D, W_PR = PR_C * F, W_TE = V_C * D;
-constexpr int W_LAYER = W_QKV + W_O + W_FC + W_PR;
-constexpr int ACT = D /*x*/ + D /*h*/ + 3 * D /*qkv*/ + D /*att*/ + D /*o*/ + F /*f*/ + D /*pr*/ + CS * V_C /*logits*/;
-constexpr size_t CLUSTER_SMEM = (size_t)(L * W_LAYER + W_TE + ACT + 3 * 256) * 4;
+// The MLP's hidden units are split unevenly: CTAs 0..H-1 also run an attention head and
+// hold that head's 32 rows of W_o, so they take FC_SMALL hidden units, the others FC_BIG.
+constexpr int FC_SMALL = 8, FC_BIG = (F - H * FC_SMALL) / (CS - H);   // 8 and 40
+static_assert(H * FC_SMALL + (CS - H) * FC_BIG == F, "hidden-unit split");
+__host__ __device__ constexpr int fc_count(int r) { return r < H ? FC_SMALL : FC_BIG; }
+__host__ __device__ constexpr int fc_first(int r) { return r < H ? r * FC_SMALL : H * FC_SMALL + (r - H) * FC_BIG; }
+// per-layer weight floats of one CTA: W_qkv columns (column-major), then for head CTAs the
+// head's W_o rows, then W_fc columns (column-major) and the matching W_pr rows
+constexpr int W_QKV = QKV_C * D, W_OH = HD * D, W_TE = V_C * D;
+__host__ __device__ constexpr int layer_floats(int r) { return W_QKV + (r < H ? W_OH : 0) + 2 * fc_count(r) * D; }
+constexpr int W_LAYER_MAX = W_QKV + 2 * FC_BIG * D;                  // the larger of the two kinds
+static_assert(W_LAYER_MAX >= W_QKV + W_OH + 2 * FC_SMALL * D, "layer slice bound");
+constexpr int ACT = D /*x*/ + D /*h*/ + 3 * D /*qkv*/ + FC_BIG /*f*/ + H * D /*o partials*/ + CS * D /*pr partials*/ +
+                    CS * V_C /*logits*/ + 2 * 256 + 16 /*reductions*/;
+constexpr size_t CLUSTER_SMEM = (size_t)(L * W_LAYER_MAX + W_TE + ACT) * 4;
 
 struct ClusterArgs {
     const float *w;
@@ -319,23 +329,30 @@ __device__ __forceinline__ void st_cluster(float *local, uint32_t rank, float v)
     asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(r), "f"(v) : "memory");
 }
 
-// This CTA's NC output columns [c0, c0 + NC) of act(in . W + b), W [K][ncols] in global
-// order but held here column-major as ws[j][k]; each column's value goes to out[c0 + j]
-// in all CS CTAs.  Warp w handles columns w, w + 8, ...; lanes split k.
-template <int K, int NC, bool GELU>
-__device__ __forceinline__ void slice_linear(const float *in, const float *ws, const float *__restrict__ b, int c0,
-                                             float *out) {
+// This CTA's nc output columns [c0, c0 + nc) of in . W + b, W held column-major as ws[j][k];
+// a warp per column, lanes over k.  Each value goes to out[c0 + j] in all CS CTAs.
+template <int K>
+__device__ __forceinline__ void slice_linear_bcast(const float *in, const float *ws, const float *__restrict__ b, int c0,
+                                                   int nc, float *out) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    for (int j = warp; j < NC; j += THREADS / 32) {
+    for (int j = warp; j < nc; j += THREADS / 32) {
         const float *wc = ws + j * K;
         float acc = 0.0f;
 #pragma unroll 4
         for (int k = lane; k < K; k += 32) acc = fmaf(in[k], wc[k], acc);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        float v = acc + __ldg(b + c0 + j);
-        if (GELU) v = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+        const float v = acc + __ldg(b + c0 + j);
         if (lane < CS) st_cluster(out + c0 + j, lane, v);
+    }
+}
+
+// out[n] = sum_i in[i] * wr[i][n] for n < D (wr: `rows` rows of D), sent to slot[n] of all CS CTAs
+__device__ __forceinline__ void rows_partial_bcast(const float *in, const float *wr, int rows, float *slot) {
+    for (int n = threadIdx.x; n < D; n += THREADS) {
+        float acc = 0.0f;
+        for (int i = 0; i < rows; ++i) acc = fmaf(in[i], wr[i * D + n], acc);
+        for (uint32_t r = 0; r < CS; ++r) st_cluster(slot + n, r, acc);
     }
 }
 
@@ -371,27 +388,39 @@ __device__ __forceinline__ void ln_cta(const float *x, float *y, const float *__
     __syncthreads();
 }
 
+// Per layer, three cluster exchanges:
+//  1. q/k/v: each CTA's 24 columns to every CTA;
+//  2. attention head h in CTA h, which also multiplies its 32 outputs by the head's rows of
+//     W_o: the four 128-wide partial products go to every CTA, which adds them to x;
+//  3. each CTA's hidden units of the MLP (GELU) times the matching rows of W_pr: sixteen
+//     128-wide partial products, added to x everywhere.
 __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs a) {
     extern __shared__ __align__(16) float sm[];
     const uint32_t rank = cl_rank();
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    float *wl = sm;                                  // [L][W_LAYER]
-    float *wte_s = wl + L * W_LAYER;                 // [V_C][D]
-    float *x = wte_s + W_TE, *h = x + D, *qkv = h + D, *att = qkv + 3 * D, *ob = att + D, *f = ob + D;
-    float *pr = f + F, *lg = pr + D, *red = lg + CS * V_C;   // red: 3 x 256 scratch
+    const int nfc = fc_count((int)rank), fc0 = fc_first((int)rank);
+    const int lfl = layer_floats((int)rank);
+    float *wl = sm;                                  // [L][lfl]
+    float *wte_s = wl + L * W_LAYER_MAX;             // [V_C][D]
+    float *x = wte_s + W_TE, *h = x + D, *qkv = h + D, *fl = qkv + 3 * D, *opart = fl + FC_BIG;
+    float *prpart = opart + H * D, *lg = prpart + CS * D, *red = lg + CS * V_C;   // red: 2 x 256 + 16
     const float *wte = a.w, *wpe = a.w + V * D;
     const float *lw0 = a.w + V * D + CTX * D;
 
-    // this CTA's weight slices, once per decode (column-major: ws[j][k] = W[k][c0 + j])
+    // this CTA's weight slices, once per decode
     for (int l = 0; l < L; ++l) {
         const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
         const float *w_qkv = lw + 2 * D, *w_o = w_qkv + D * 3 * D + 3 * D, *w_fc = w_o + D * D + D + 2 * D;
         const float *w_pr = w_fc + D * F + F;
-        float *s_qkv = wl + l * W_LAYER, *s_o = s_qkv + W_QKV, *s_fc = s_o + W_O, *s_pr = s_fc + W_FC;
+        float *s_qkv = wl + l * lfl, *s_oh = s_qkv + W_QKV, *s_fc = s_oh + (rank < H ? W_OH : 0);
+        float *s_pr = s_fc + nfc * D;
         for (int i = tid; i < W_QKV; i += THREADS) s_qkv[i] = __ldg(w_qkv + (i % D) * 3 * D + rank * QKV_C + i / D);
-        for (int i = tid; i < W_O; i += THREADS) s_o[i] = __ldg(w_o + (i % D) * D + rank * O_C + i / D);
-        for (int i = tid; i < W_FC; i += THREADS) s_fc[i] = __ldg(w_fc + (i % D) * F + rank * FC_C + i / D);
-        for (int i = tid; i < W_PR; i += THREADS) s_pr[i] = __ldg(w_pr + (i % F) * D + rank * PR_C + i / F);
+        if (rank < H)
+            for (int i = tid; i < W_OH; i += THREADS) s_oh[i] = __ldg(w_o + (rank * HD + i / D) * D + i % D);
+        for (int i = tid; i < nfc * D; i += THREADS) {
+            s_fc[i] = __ldg(w_fc + (i % D) * F + fc0 + i / D);     // column-major [j][k]
+            s_pr[i] = __ldg(w_pr + (fc0 + i / D) * D + i % D);      // rows [j][n]
+        }
     }
     for (int i = tid; i < W_TE; i += THREADS) {
         const int v = (int)rank * V_C + i / D;
@@ -412,14 +441,16 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
                 const float *ln1_g = lw, *ln1_b = ln1_g + D, *b_qkv = ln1_b + D + D * 3 * D;
                 const float *b_o = b_qkv + 3 * D + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
                 const float *b_fc = ln2_b + D + D * F, *b_pr = b_fc + F + F * D;
-                const float *s_qkv = wl + l * W_LAYER, *s_o = s_qkv + W_QKV, *s_fc = s_o + W_O, *s_pr = s_fc + W_FC;
+                const float *s_qkv = wl + l * lfl, *s_oh = s_qkv + W_QKV, *s_fc = s_oh + (rank < H ? W_OH : 0);
+                const float *s_pr = s_fc + nfc * D;
                 float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
                 float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
 
+                // 1. q, k, v
                 ln_cta(x, h, ln1_g, ln1_b);
-                slice_linear<D, QKV_C, false>(h, s_qkv, b_qkv, rank * QKV_C, qkv);
+                slice_linear_bcast<D>(h, s_qkv, b_qkv, rank * QKV_C, QKV_C, qkv);
                 cl_sync();
-                // attention: head rank (CTAs 0..H-1) over positions 0..pos
+                // 2. attention head `rank` over positions 0..pos, then its share of the output projection
                 if (rank < H) {
                     const int hh = rank;
                     float *kr_base = kc + (b * CTX) * D + hh * HD, *vr_base = vc + (b * CTX) * D + hh * HD;
@@ -443,48 +474,67 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
                         }
                         sc = acc * scale;
                     }
-                    // max and sum over the (at most 128) scores
                     float m = sc;
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-                    if (lane == 0) red[warp] = m;
+                    if (lane == 0) red[512 + warp] = m;
                     __syncthreads();
-                    m = red[0];
-                    for (int w2 = 1; w2 < THREADS / 32; ++w2) m = fmaxf(m, red[w2]);
+                    m = red[512];
+                    for (int w2 = 1; w2 < THREADS / 32; ++w2) m = fmaxf(m, red[512 + w2]);
                     const float p = tid <= pos ? expf(sc - m) : 0.0f;
                     float ssum = p;
 #pragma unroll
                     for (int o = 16; o > 0; o >>= 1) ssum += __shfl_xor_sync(0xffffffffu, ssum, o);
-                    red[256 + tid] = p;
-                    if (lane == 0) red[512 + warp] = ssum;
+                    red[tid] = p;
                     __syncthreads();
-                    float tot = 0.0f;
-                    for (int w2 = 0; w2 < THREADS / 32; ++w2) tot += red[512 + w2];
+                    if (lane == 0) red[512 + 8 + warp] = ssum;
                     // output dimension d = tid % 32 over positions t = tid / 32, tid / 32 + 8, ...
                     const int d = tid & 31, tg0 = tid >> 5;
                     float o_acc = 0.0f;
-                    for (int t = tg0; t <= pos; t += THREADS / 32) o_acc = fmaf(red[256 + t], vr_base[t * D + d], o_acc);
-                    __syncthreads();
-                    red[tid] = o_acc;
+                    for (int t = tg0; t <= pos; t += THREADS / 32) o_acc = fmaf(red[t], vr_base[t * D + d], o_acc);
+                    red[256 + tid] = o_acc;
                     __syncthreads();
                     if (tid < HD) {
+                        float tot = 0.0f;
+                        for (int w2 = 0; w2 < THREADS / 32; ++w2) tot += red[512 + 8 + w2];
                         float v = 0.0f;
-                        for (int g2 = 0; g2 < THREADS / 32; ++g2) v += red[g2 * 32 + tid];
-                        v /= tot;
-                        for (uint32_t r = 0; r < CS; ++r) st_cluster(att + hh * HD + tid, r, v);
+                        for (int g2 = 0; g2 < THREADS / 32; ++g2) v += red[256 + g2 * 32 + tid];
+                        red[tid] = v / tot;   // this head's 32 attention outputs
                     }
+                    __syncthreads();
+                    rows_partial_bcast(red, s_oh, HD, opart + hh * D);
                 }
                 cl_sync();
-                slice_linear<D, O_C, false>(att, s_o, b_o, rank * O_C, ob);
-                cl_sync();
-                for (int c = tid; c < D; c += THREADS) x[c] += ob[c];
+                for (int c = tid; c < D; c += THREADS) {
+                    float v = __ldg(b_o + c);
+#pragma unroll
+                    for (int hh = 0; hh < H; ++hh) v += opart[hh * D + c];
+                    x[c] += v;
+                }
                 __syncthreads();
+                // 3. this CTA's hidden units, then their share of the projection back to D
                 ln_cta(x, h, ln2_g, ln2_b);
-                slice_linear<D, FC_C, true>(h, s_fc, b_fc, rank * FC_C, f);
+                for (int j = warp; j < nfc; j += THREADS / 32) {
+                    const float *wc = s_fc + j * D;
+                    float acc = 0.0f;
+#pragma unroll 4
+                    for (int k = lane; k < D; k += 32) acc = fmaf(h[k], wc[k], acc);
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (lane == 0) {
+                        const float v = acc + __ldg(b_fc + fc0 + j);
+                        fl[j] = 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+                    }
+                }
+                __syncthreads();
+                rows_partial_bcast(fl, s_pr, nfc, prpart + rank * D);
                 cl_sync();
-                slice_linear<F, PR_C, false>(f, s_pr, b_pr, rank * PR_C, pr);
-                cl_sync();
-                for (int c = tid; c < D; c += THREADS) x[c] += pr[c];
+                for (int c = tid; c < D; c += THREADS) {
+                    float v = __ldg(b_pr + c);
+#pragma unroll
+                    for (int r = 0; r < CS; ++r) v += prpart[r * D + c];
+                    x[c] += v;
+                }
                 __syncthreads();
             }
             const float *lnf = lw0 + (int64_t)L * LAYER_FLOATS;
