@@ -489,9 +489,14 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
                     __syncthreads();
                     if (lane == 0) red[512 + 8 + warp] = ssum;
                     // output dimension d = tid % 32 over positions t = tid / 32, tid / 32 + 8, ...
+                    // (unrolled over the whole context so the value loads are issued together)
                     const int d = tid & 31, tg0 = tid >> 5;
                     float o_acc = 0.0f;
-                    for (int t = tg0; t <= pos; t += THREADS / 32) o_acc = fmaf(red[t], vr_base[t * D + d], o_acc);
+#pragma unroll
+                    for (int i = 0; i < CTX / (THREADS / 32); ++i) {
+                        const int t = tg0 + i * (THREADS / 32);
+                        if (t <= pos) o_acc = fmaf(red[t], vr_base[t * D + d], o_acc);
+                    }
                     red[256 + tid] = o_acc;
                     __syncthreads();
                     if (tid < HD) {
