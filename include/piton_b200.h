@@ -164,6 +164,15 @@ typedef struct {
 } piton_allgather_args;
 PITON_B200_API int piton_b200_matmul_allgather_f32(const piton_matmul_args *args, const piton_allgather_args *g,
                                                    void *stream);
+/* All-gather of equal pieces without NCCL, for the other operators' shards (softmax rows, attention
+   heads, add ranges, MLP / TinyGPT batch rows): this rank's `bytes` at `src` are stored into
+   peer_c[r] + rank * bytes for every r < world (the own buffer included) with 16-byte peer stores
+   (byte stores when a pointer or `bytes` is not 16-byte aligned).  row_offset, ldc and multicast_c
+   are not used.  No counterpart in the reference (it runs on one device); it stands beside the
+   NCCL all-gather the Python path uses.  Every rank must pass a barrier after its call before the
+   output is read anywhere. */
+PITON_B200_API int piton_b200_allgather(const piton_allgather_args *g, uint64_t src, size_t bytes, void *stream);
+
 /* CUDA IPC of a cudaMalloc'd buffer (64-byte handle) for the peer pointers above. */
 PITON_B200_API int piton_b200_ipc_handle(uint64_t ptr, void *handle);
 PITON_B200_API int piton_b200_ipc_open(const void *handle, uint64_t *ptr);

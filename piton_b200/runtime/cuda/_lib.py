@@ -124,6 +124,7 @@ PROTOTYPES = {
     "piton_b200_matmul_host_workspace_size": (C.c_size_t, [C.POINTER(MatmulArgs)]),
     "piton_b200_matmul_f32_host": (C.c_int, [C.POINTER(MatmulArgs), C.c_void_p]),
     "piton_b200_matmul_allgather_f32": (C.c_int, [C.POINTER(MatmulArgs), C.POINTER(AllgatherArgs), C.c_void_p]),
+    "piton_b200_allgather": (C.c_int, [C.POINTER(AllgatherArgs), u64, C.c_size_t, C.c_void_p]),
     "piton_b200_ipc_handle": (C.c_int, [u64, C.c_void_p]),
     "piton_b200_ipc_open": (C.c_int, [C.c_void_p, C.POINTER(u64)]),
     "piton_b200_ipc_close": (C.c_int, [u64]),

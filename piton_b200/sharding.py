@@ -176,4 +176,27 @@ def matmul_allgather(a_piece, b, out, row_offset: int, ldc: int, stream=None, mu
                "matmul_allgather")
 
 
+def allgather_pieces(piece, out, stream=None):
+    """Store this rank's `piece` (a CUDA tensor) into every rank's full output `out`
+    (PeerOutput or SymmetricOutput) at byte offset rank * piece.nbytes, with the library's
+    peer-store all-gather (no NCCL).  Every rank must pass a barrier before reading `out`."""
+    import ctypes as C
+
+    import torch
+
+    from .runtime.cuda import _lib
+    lib = _lib.lib()
+    if not piece.is_contiguous():
+        raise ValueError("piece must be contiguous")
+    nbytes = piece.numel() * piece.element_size()
+    if (out.rank + 1) * nbytes > out.nbytes:
+        raise ValueError(f"output holds {out.nbytes} bytes; rank {out.rank}'s piece ends at {(out.rank + 1) * nbytes}")
+    g = _lib.AllgatherArgs()
+    for r, p in enumerate(out.peer_ptrs):
+        g.peer_c[r] = p
+    g.world, g.rank = out.world, out.rank
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(lib.piton_b200_allgather(C.byref(g), piece.data_ptr(), nbytes, C.c_void_p(s.cuda_stream)), "allgather")
+
+
 _WS = {}

@@ -78,3 +78,47 @@ def test_fused_allgather_matmul_two_gpus(kind):
     for rank, (err, status) in res.items():
         assert status == 0, rank
         assert err <= 4e-6, (rank, err)
+
+
+def _allgather_worker(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    from piton_b200 import sharding
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    out = None
+    try:
+        ok = True
+        for n in (4096, 1001):                       # 16-byte pieces, and byte stores
+            out = sharding.PeerOutput(dist, world * n * 4)
+            piece = torch.arange(n, device="cuda", dtype=torch.float32) + 1000.0 * (rank + 1)
+            sharding.allgather_pieces(piece, out)
+            torch.cuda.synchronize()
+            dist.barrier()
+            full = out.read(0, world * n * 4).view(np.float32).reshape(world, n)
+            want = np.arange(n, dtype=np.float32)[None, :] + 1000.0 * (np.arange(world, dtype=np.float32)[:, None] + 1)
+            ok = ok and bool(np.array_equal(full, want))
+            dist.barrier()
+            out.close()
+            out = None
+        results[rank] = ok
+        dist.barrier()
+    finally:
+        if out is not None:
+            out.close()
+        dist.destroy_process_group()
+
+
+def test_library_allgather_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_allgather_worker, args=(2, _port(), results), nprocs=2, join=True)
+        res = dict(results)
+    assert res == {0: True, 1: True}
