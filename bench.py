@@ -439,9 +439,20 @@ def e2e_matmul(torch, D, steps):
     Cm = pinned_empty((mloc, N))
     grid = (triton.cdiv(mloc, 8) * triton.cdiv(N, 64),)
 
-    def step():
-        return matmul_kernel[grid](A, B, Cm, mloc, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
-                                   BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
+    if D.world > 1:
+        # every rank uploads its A rows and 1/N of B; B is completed over NVLink (peer stores)
+        from piton_b200 import sharding
+        hs = sharding.HostShardedMatmul(D.pg, mloc, N, K)
+
+        def step():
+            hs(A, B, Cm)
+            return {"h2d_bytes": hs.h2d_bytes(), "d2h_bytes": hs.d2h_bytes()}
+    else:
+        hs = None
+
+        def step():
+            return matmul_kernel[grid](A, B, Cm, mloc, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
+                                       BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
 
     st = step()
     D.barrier(torch)
@@ -455,6 +466,9 @@ def e2e_matmul(torch, D, steps):
     e1.synchronize()
     sec = D.max(torch, max(e0.elapsed_time(e1) / 1e3, 0.0) / steps)
     _ = t0
+    if hs is not None:
+        D.barrier(torch)
+        hs.close()
     return {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"], "flops": 2.0 * M * N * K}
 
 
@@ -661,7 +675,11 @@ def main():
     if e2e:
         line["e2e"] = {"value": e2e["flops"] / e2e["sec"] / 1e12, "unit": "TFLOP/s",
                        "h2d_bytes_per_step": e2e["h2d"], "d2h_bytes_per_step": e2e["d2h"],
-                       "ms_per_step": 1e3 * e2e["sec"], "path": "kernel[grid](numpy pinned host arrays)"}
+                       "ms_per_step": 1e3 * e2e["sec"],
+                       "path": ("kernel[grid](numpy pinned host arrays): H2D of A and B, GEMM, D2H of C, pipelined "
+                                "by row blocks" if D.world == 1 else
+                                "sharding.HostShardedMatmul (pinned host arrays): each rank uploads its A rows and "
+                                "1/N of B's rows, B completed over NVLink, GEMM, D2H of its C rows; bytes per rank")}
     line["secondary"] = sec
     line["peaks"] = {"hbm_gbs": hbm, "source": peaks["source"]}
     line["clocks"] = sampler.summary()

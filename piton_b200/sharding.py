@@ -199,4 +199,75 @@ def allgather_pieces(piece, out, stream=None):
     _lib.check(lib.piton_b200_allgather(C.byref(g), piece.data_ptr(), nbytes, C.c_void_p(s.cuda_stream)), "allgather")
 
 
+class HostShardedMatmul:
+    """C = A @ B across the ranks with every operand in HOST memory: rank r holds its rows of
+    A and of C (A_r [m, K], C_r [m, N]) and all of B [K, N].  Each call uploads A_r and only
+    1/world of B's rows, completes B on every GPU with the peer-store all-gather over NVLink
+    (each GPU's PCIe link carries K/world rows of B instead of all K), runs the GEMM and copies
+    C_r back.  Host arrays should be page-locked (``runtime.cuda.pinned_empty``) for
+    asynchronous copies; the call returns after C_r is on the host."""
+
+    def __init__(self, dist, m: int, N: int, K: int):
+        import torch
+        self.dist = dist
+        self.world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+        self.rank = dist.get_rank() if self.world > 1 else 0
+        if K % self.world:
+            raise ValueError(f"K = {K} must be a multiple of the {self.world} ranks")
+        self.m, self.N, self.K = m, N, K
+        self.kslice = K // self.world
+        self.b_full = PeerOutput(dist, K * N * 4)
+        dev = torch.cuda.current_device()
+        self.b_full_t = None
+        self.b_piece = torch.empty(self.kslice * N, dtype=torch.float32, device=dev)
+        self.a = torch.empty(m * K, dtype=torch.float32, device=dev)
+        self.c = torch.empty(m * N, dtype=torch.float32, device=dev)
+        self.done = torch.zeros(1, device=dev)
+        self.copy_stream = torch.cuda.Stream(dev)
+
+    def h2d_bytes(self) -> int:
+        return 4 * (self.m * self.K + self.kslice * self.N)
+
+    def d2h_bytes(self) -> int:
+        return 4 * self.m * self.N
+
+    def __call__(self, a_host, b_host, c_host):
+        import ctypes as C
+
+        import torch
+
+        from .runtime.cuda import _lib
+        lib = _lib.lib()
+        s = torch.cuda.current_stream()
+        if self.world > 1:
+            self.dist.all_reduce(self.done)      # no rank still reads B from the previous call
+        k0 = self.rank * self.kslice
+        b_rows = torch.from_numpy(b_host.reshape(self.K, self.N)[k0:k0 + self.kslice].reshape(-1))
+        # A's rows on a copy stream, overlapping B's slice and the all-gather
+        self.copy_stream.wait_stream(s)
+        with torch.cuda.stream(self.copy_stream):
+            self.a.copy_(torch.from_numpy(a_host.reshape(-1)), non_blocking=True)
+        self.b_piece.copy_(b_rows, non_blocking=True)
+        allgather_pieces(self.b_piece, self.b_full, stream=s)
+        if self.world > 1:
+            self.dist.all_reduce(self.done)      # every rank's slice has landed in every B
+        s.wait_stream(self.copy_stream)
+        M, N, K = self.m, self.N, self.K
+        a = _lib.MatmulArgs(self.a.data_ptr(), self.b_full.ptr, self.c.data_ptr(), M, N, K, K, 1, N, 1, N, 1, 8, 64,
+                            8, 8, -(-M // 8) * -(-N // 64), 0, 0, 0, 0)
+        ws = lib.piton_b200_matmul_workspace_size(C.byref(a))
+        key = (torch.cuda.current_device(), "host_sharded_ws")
+        buf = _WS.get(key)
+        if buf is None or buf.numel() < ws:
+            buf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+            _WS[key] = buf
+        a.workspace, a.workspace_bytes = buf.data_ptr(), ws
+        _lib.check(lib.piton_b200_matmul_f32(C.byref(a), C.c_void_p(s.cuda_stream)), "matmul")
+        torch.from_numpy(c_host.reshape(-1)).copy_(self.c, non_blocking=True)
+        s.synchronize()
+
+    def close(self):
+        self.b_full.close()
+
+
 _WS = {}
