@@ -137,7 +137,9 @@ PITON_B200_API int piton_b200_matmul_f32_noalloc(const piton_matmul_args *args, 
    stride_bn == 1, stride_cm == N, stride_cn == 1), a grid that covers every tile and no flags, so that every
    element of C is written.  B is copied first, then A in row blocks on a copy stream; each block's GEMM
    starts when its rows have landed and its C rows go back on a second copy stream while the next block
-   computes.  Bit-identical to piton_b200_matmul_f32.  args->workspace: device scratch of
+   computes.  An operand already in the current device's memory is used in place (no copy), so host
+   and device operands mix (e.g. host A and C with a device-resident B).  Bit-identical to
+   piton_b200_matmul_f32.  args->workspace: device scratch of
    piton_b200_matmul_host_workspace_size() bytes (device copies of A, B, C and the split operands; 0 when the
    problem does not qualify, and the call then returns PITON_B200_ENOTSUP).  C must not overlap A or B.
    Enqueues on `stream` like every entry point: the host buffers must stay valid until it has finished.

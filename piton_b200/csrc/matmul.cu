@@ -269,9 +269,22 @@ int host_blocks(int64_t M, int64_t *start, int64_t *rows) {
 size_t align1k(size_t b) { return (b + 1023) / 1024 * 1024; }
 
 // Byte offsets of the device copies of B, A, C and the split scratch in the workspace.
+// An operand already in the current device's memory is used in place (no copy, no room).
 struct HostLayout {
     size_t b, a, c, split, total;
+    bool dev_a, dev_b, dev_c;
 };
+
+bool on_this_device(uint64_t p) {
+    cudaPointerAttributes at;
+    if (cudaPointerGetAttributes(&at, reinterpret_cast<const void *>(p)) != cudaSuccess) {
+        cudaGetLastError();   // an unknown host pointer: not device memory
+        return false;
+    }
+    int dev = -1;
+    cudaGetDevice(&dev);
+    return at.type == cudaMemoryTypeDevice && at.device == dev;
+}
 
 bool host_layout(const piton_matmul_args *a, HostLayout *L, int *n_blocks, int64_t *start, int64_t *rows) {
     if (a->flags != 0) return false;
@@ -288,10 +301,13 @@ bool host_layout(const piton_matmul_args *a, HostLayout *L, int *n_blocks, int64
         size_t need = tc_gemm_workspace_bytes(t);
         if (need > split) split = need;
     }
+    L->dev_a = on_this_device(a->a);
+    L->dev_b = on_this_device(a->b);
+    L->dev_c = on_this_device(a->c);
     L->b = 0;
-    L->a = L->b + align1k((size_t)a->K * a->N * 4);
-    L->c = L->a + align1k((size_t)a->M * a->K * 4);
-    L->split = L->c + align1k((size_t)a->M * a->N * 4);
+    L->a = L->b + (L->dev_b ? 0 : align1k((size_t)a->K * a->N * 4));
+    L->c = L->a + (L->dev_a ? 0 : align1k((size_t)a->M * a->K * 4));
+    L->split = L->c + (L->dev_c ? 0 : align1k((size_t)a->M * a->N * 4));
     L->total = L->split + split;
     *n_blocks = n;
     return true;
@@ -353,17 +369,18 @@ extern "C" int piton_b200_matmul_f32_host(const piton_matmul_args *a, void *stre
     if (!a->workspace || a->workspace_bytes < L.total)
         return set_error(PITON_B200_EWORKSPACE, "host matmul needs %zu bytes of workspace, got %llu", L.total,
                          (unsigned long long)a->workspace_bytes);
-    // C must not share host memory with A or B: its blocks go back while later A blocks are still copied in
+    // C must not share memory with A or B: its blocks go back while later A blocks are still copied in
     const uintptr_t c0 = a->c, c1 = a->c + (uintptr_t)a->M * a->N * 4;
     const uintptr_t a0 = a->a, a1 = a->a + (uintptr_t)a->M * a->K * 4;
     const uintptr_t b0 = a->b, b1 = a->b + (uintptr_t)a->K * a->N * 4;
-    PITON_REQUIRE((c1 <= a0 || a1 <= c0) && (c1 <= b0 || b1 <= c0), "C overlaps A or B in host memory");
+    PITON_REQUIRE((c1 <= a0 || a1 <= c0) && (c1 <= b0 || b1 <= c0), "C overlaps A or B");
     HostPipe *p = host_pipe(&rc);
     if (!p) return rc;
     cudaStream_t s = as_stream(stream);
     uint8_t *ws = reinterpret_cast<uint8_t *>(a->workspace);
-    float *dB = reinterpret_cast<float *>(ws + L.b), *dA = reinterpret_cast<float *>(ws + L.a);
-    float *dC = reinterpret_cast<float *>(ws + L.c);
+    float *dB = L.dev_b ? reinterpret_cast<float *>(a->b) : reinterpret_cast<float *>(ws + L.b);
+    float *dA = L.dev_a ? reinterpret_cast<float *>(a->a) : reinterpret_cast<float *>(ws + L.a);
+    float *dC = L.dev_c ? reinterpret_cast<float *>(a->c) : reinterpret_cast<float *>(ws + L.c);
     const float *hA = reinterpret_cast<const float *>(a->a), *hB = reinterpret_cast<const float *>(a->b);
     float *hC = reinterpret_cast<float *>(a->c);
 
@@ -371,11 +388,12 @@ extern "C" int piton_b200_matmul_f32_host(const piton_matmul_args *a, void *stre
     PITON_CUDA(cudaEventRecord(p->start, s));
     PITON_CUDA(cudaStreamWaitEvent(p->h2d, p->start, 0));
     PITON_CUDA(cudaStreamWaitEvent(p->d2h, p->start, 0));
-    PITON_CUDA(cudaMemcpyAsync(dB, hB, (size_t)a->K * a->N * 4, cudaMemcpyDefault, p->h2d));
+    if (!L.dev_b) PITON_CUDA(cudaMemcpyAsync(dB, hB, (size_t)a->K * a->N * 4, cudaMemcpyDefault, p->h2d));
     PITON_CUDA(cudaEventRecord(p->b_in, p->h2d));
     for (int i = 0; i < n; ++i) {
-        PITON_CUDA(cudaMemcpyAsync(dA + start[i] * a->K, hA + start[i] * a->K, (size_t)rows[i] * a->K * 4,
-                                   cudaMemcpyDefault, p->h2d));
+        if (!L.dev_a)
+            PITON_CUDA(cudaMemcpyAsync(dA + start[i] * a->K, hA + start[i] * a->K, (size_t)rows[i] * a->K * 4,
+                                       cudaMemcpyDefault, p->h2d));
         PITON_CUDA(cudaEventRecord(p->a_in[i], p->h2d));
     }
     PITON_CUDA(cudaStreamWaitEvent(s, p->b_in, 0));
@@ -390,8 +408,9 @@ extern "C" int piton_b200_matmul_f32_host(const piton_matmul_args *a, void *stre
         if ((rc = tc_gemm(t, ws + L.split, s)) != PITON_B200_OK) return rc;
         PITON_CUDA(cudaEventRecord(p->c_out[i], s));
         PITON_CUDA(cudaStreamWaitEvent(p->d2h, p->c_out[i], 0));
-        PITON_CUDA(cudaMemcpyAsync(hC + start[i] * a->N, dC + start[i] * a->N, (size_t)rows[i] * a->N * 4,
-                                   cudaMemcpyDefault, p->d2h));
+        if (!L.dev_c)
+            PITON_CUDA(cudaMemcpyAsync(hC + start[i] * a->N, dC + start[i] * a->N, (size_t)rows[i] * a->N * 4,
+                                       cudaMemcpyDefault, p->d2h));
     }
     PITON_CUDA(cudaEventRecord(p->done, p->d2h));
     PITON_CUDA(cudaStreamWaitEvent(s, p->done, 0));

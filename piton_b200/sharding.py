@@ -218,12 +218,8 @@ class HostShardedMatmul:
         self.kslice = K // self.world
         self.b_full = PeerOutput(dist, K * N * 4)
         dev = torch.cuda.current_device()
-        self.b_full_t = None
         self.b_piece = torch.empty(self.kslice * N, dtype=torch.float32, device=dev)
-        self.a = torch.empty(m * K, dtype=torch.float32, device=dev)
-        self.c = torch.empty(m * N, dtype=torch.float32, device=dev)
         self.done = torch.zeros(1, device=dev)
-        self.copy_stream = torch.cuda.Stream(dev)
 
     def h2d_bytes(self) -> int:
         return 4 * (self.m * self.K + self.kslice * self.N)
@@ -243,27 +239,24 @@ class HostShardedMatmul:
             self.dist.all_reduce(self.done)      # no rank still reads B from the previous call
         k0 = self.rank * self.kslice
         b_rows = torch.from_numpy(b_host.reshape(self.K, self.N)[k0:k0 + self.kslice].reshape(-1))
-        # A's rows on a copy stream, overlapping B's slice and the all-gather
-        self.copy_stream.wait_stream(s)
-        with torch.cuda.stream(self.copy_stream):
-            self.a.copy_(torch.from_numpy(a_host.reshape(-1)), non_blocking=True)
         self.b_piece.copy_(b_rows, non_blocking=True)
         allgather_pieces(self.b_piece, self.b_full, stream=s)
         if self.world > 1:
             self.dist.all_reduce(self.done)      # every rank's slice has landed in every B
-        s.wait_stream(self.copy_stream)
+        # host A and C, device-resident B: the library pipelines A's row blocks, the GEMM and C's
         M, N, K = self.m, self.N, self.K
-        a = _lib.MatmulArgs(self.a.data_ptr(), self.b_full.ptr, self.c.data_ptr(), M, N, K, K, 1, N, 1, N, 1, 8, 64,
-                            8, 8, -(-M // 8) * -(-N // 64), 0, 0, 0, 0)
-        ws = lib.piton_b200_matmul_workspace_size(C.byref(a))
+        a = _lib.MatmulArgs(a_host.ctypes.data, self.b_full.ptr, c_host.ctypes.data, M, N, K, K, 1, N, 1, N, 1, 8,
+                            64, 8, 8, -(-M // 8) * -(-N // 64), 0, 0, 0, 0)
+        ws = lib.piton_b200_matmul_host_workspace_size(C.byref(a))
+        if ws == 0:
+            raise ValueError("the host-buffer matmul does not take this problem")
         key = (torch.cuda.current_device(), "host_sharded_ws")
         buf = _WS.get(key)
         if buf is None or buf.numel() < ws:
-            buf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+            buf = torch.empty(ws, dtype=torch.uint8, device="cuda")
             _WS[key] = buf
         a.workspace, a.workspace_bytes = buf.data_ptr(), ws
-        _lib.check(lib.piton_b200_matmul_f32(C.byref(a), C.c_void_p(s.cuda_stream)), "matmul")
-        torch.from_numpy(c_host.reshape(-1)).copy_(self.c, non_blocking=True)
+        _lib.check(lib.piton_b200_matmul_f32_host(C.byref(a), C.c_void_p(s.cuda_stream)), "matmul")
         s.synchronize()
 
     def close(self):

@@ -112,3 +112,32 @@ def test_c_abi_rejects_overlap_and_unsupported_layouts(cuda):
     args.c = c.ctypes.data
     assert lib().piton_b200_matmul_f32_host(C.byref(args), None) == _lib.EWORKSPACE
     torch.cuda.synchronize()
+
+
+@pytest.mark.parametrize("where", ["hdh", "dhh", "hhd", "ddd"])
+def test_mixed_host_and_device_operands(cuda, where):
+    """Operands already in device memory are used in place (A, B, C = host or device in the
+    order of `where`); every mix gives the bits of the device-buffer call."""
+    torch = cuda
+    M, N, K = 2304, 640, 384
+    rng = np.random.default_rng(17)
+    a = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+    b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+    ta, tb = torch.from_numpy(a).cuda(), torch.from_numpy(b).cuda()
+    want = torch.empty(M, N, device="cuda")
+    run(ta, tb, want, M, N, K)
+    ha, hb, hc = pinned_empty((M, K)), pinned_empty((K, N)), pinned_empty((M, N))
+    ha[...], hb[...], hc[...] = a, b, np.nan
+    dc = torch.full((M, N), float("nan"), device="cuda")
+    ptr = {"a": (ha.ctypes.data, ta.data_ptr()), "b": (hb.ctypes.data, tb.data_ptr()),
+           "c": (hc.ctypes.data, dc.data_ptr())}
+    pa, pb, pc = (ptr[k][where[i] == "d"] for i, k in enumerate("abc"))
+    args = _lib.MatmulArgs(pa, pb, pc, M, N, K, K, 1, N, 1, N, 1, 8, 64, 8, 8, (M // 8) * (N // 64), 0, 0, 0, 0)
+    ws = lib().piton_b200_matmul_host_workspace_size(C.byref(args))
+    assert ws > 0
+    buf = torch.empty(ws, dtype=torch.uint8, device="cuda")
+    args.workspace, args.workspace_bytes = buf.data_ptr(), ws
+    _lib.check(lib().piton_b200_matmul_f32_host(C.byref(args), None), "matmul host")
+    torch.cuda.synchronize()
+    got = dc.cpu().numpy() if where[2] == "d" else hc
+    np.testing.assert_array_equal(got.view(np.uint32), want.cpu().numpy().view(np.uint32))
