@@ -44,6 +44,7 @@ sys.path.insert(0, REPO)
 
 METRIC = "fp32 matmul TFLOPS + softmax/attn GB/s vs roofline at 1/2/4/8 B200"
 MM = 8192
+GEMM_TRAFFIC_8192 = 5.49e9 + 267.1e6   # bytes per launch (ncu, 1 B200)
 SM_M, SM_N = 32768, 16384
 AT_B, AT_H, AT_S, AT_D = 32, 32, 4096, 64
 ADD_N = 1 << 28
@@ -664,7 +665,11 @@ def main():
                                 "l2": "inputs larger than L2 (A+B = 512 MB)",
                                 "path": "tcgen05 3xTF32" if r["tc"] else "CUDA-core fp32 FFMA"},
                      "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
-                                  "frac": ach / peak, "traffic": None,
+                                  "frac": ach / peak,
+                                  # DRAM bytes of one launch of the CTA-pair GEMM at 8192^3 measured with ncu
+                                  # (dram__bytes_read.sum + dram__bytes_write.sum, single-pass capture)
+                                  "traffic": GEMM_TRAFFIC_8192 if (D.world == 1 and MM == 8192) else None,
+                                  "traffic_unit": "bytes per launch",
                                   "peak_source": f"cuBLAS TF32 8192^3 measured in this run ({tf32:.1f} TFLOP/s) / 3",
                                   "frac_of_bf16_measured_over_6": ach / (peaks["bf16_tflops"] / 6.0)},
                      "max_norm_err_vs_f64": r["err"]})
