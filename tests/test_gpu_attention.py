@@ -181,3 +181,24 @@ def test_tensor_core_path_strided_k_and_padded_rows(cuda):
     assert stats["path"] == "tcgen05_3xtf32"
     np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, True), rtol=0, atol=ATOL)
     assert np.all(out[:, :, d:] == 0)
+
+
+@pytest.mark.parametrize("q_off", [0, 1])
+def test_tensor_core_path_unaligned_q_and_out(cuda, q_off):
+    """Q rows 65 floats apart (and, with q_off = 1, a Q base off the 16-byte grid) cannot be
+    read by TMA in place: the kernel works from a contiguous copy of Q; Out rows 65 apart take
+    the scalar stores."""
+    from piton_b200.runtime.launcher import offset_ptr
+    heads, n, d, ld = 2, 256, 64, 65
+    rng = np.random.default_rng(23 + q_off)
+    qbuf = rng.standard_normal(heads * n * ld + 8).astype(np.float32)
+    q = qbuf[q_off:q_off + heads * n * ld].reshape(heads, n, ld)
+    k, v = (rng.standard_normal((heads, n, d)).astype(np.float32) for _ in range(2))
+    out = np.full((heads, n, ld), 3.0, np.float32)
+    stats = attn_fwd_kernel[(n // 2, heads)](offset_ptr(qbuf, q_off), k, v, out, 0.125, n * ld, ld, n * d, d, 1,
+                                             n * d, d, n * ld, ld, n, HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16,
+                                             CAUSAL=False, EVEN_N=True, device="b200").last_stats
+    assert stats["path"] == "tcgen05_3xtf32"
+    assert _status() == 0
+    np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, False), rtol=0, atol=ATOL)
+    assert np.all(out[:, :, d:] == 3.0)
