@@ -189,9 +189,9 @@ class Launch:
         if nbytes == 0:
             return 0
         if self.capturing:
-            # from the graph's private pool: it stays reserved for the graph's replays
+            # allocated from the graph's private pool, which stays reserved for the graph's
+            # replays after this tensor is released
             buf = torch.empty(nbytes, dtype=torch.uint8, device=self.device or "cuda")
-            self._keep = getattr(self, "_keep", []) + [buf]
             return buf.data_ptr()
         key = torch.cuda.current_device() if self.device is None else self.device
         buf = _WORKSPACE.get(key)
