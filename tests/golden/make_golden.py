@@ -311,6 +311,74 @@ def case_attention(fp, procs, big):
             save(name, meta, heads_kept=np.arange(2), out_first_heads=out[:2])
 
 
+def case_tinygpt(fp, procs, big):
+    """TinyGPT -- a model the reference does not have -- composed from the reference's own
+    kernels on its emulator: dense_layer_kernel (RELU off) for every linear layer,
+    attn_fwd_kernel for the causal heads (head dim 32), layernorm_kernel
+    (tests/test_reroll_reduce.py) for the LayerNorms; the embeddings, the LayerNorm gain and
+    bias, GELU and the residual adds on the host in float32.  A prefill of a short prompt,
+    the logits of every position: pins the float64 host model (oracle/tinygpt_ref.py) and the
+    B200 decode to the reference's kernels at small size."""
+    from nn_kernels import dense_layer_kernel, dense_tiles
+    import attention as A
+    import piton.compiler as pc
+    from piton.runtime.launcher import run_emulator
+    sys.path.insert(0, os.path.join(_STATE["ref"], "tests"))
+    import test_reroll_reduce as RR
+    from piton_b200 import tinygpt
+    plen, seed = 5, 0
+    name = f"tinygpt_emu_p{plen}_seed{seed}"
+    if exists(name):
+        return
+    t = time.time()
+    w = tinygpt.init_weights(seed)
+    prompt = tinygpt.random_prompts(1, seed=7, length=plen)[0]
+    f32 = np.float32
+    x = (w["wte"][prompt] + w["wpe"][:plen]).astype(f32)
+
+    def ln(v, g, b):
+        rows = v.shape[0]
+        sig = {"x_ptr": "*fp32", "out_ptr": "*fp32", "n": "i32", "eps": "fp32"}
+        ck = pc.compile(RR.layernorm_kernel, sig, {"BLOCK": tinygpt.D_MODEL}, grid=(rows,), num_stages=2)
+        y = np.zeros_like(v)
+        run_emulator(ck, (rows,), dict(x_ptr=np.ascontiguousarray(v), out_ptr=y, n=tinygpt.D_MODEL, eps=1e-5))
+        return (y * g + b).astype(f32)
+
+    def dense(v, wm, b):
+        return _run_dense(pc, run_emulator, dense_layer_kernel, dense_tiles, np.ascontiguousarray(v, f32),
+                          np.ascontiguousarray(wm, f32), np.ascontiguousarray(b, f32), True, False)
+
+    def heads(m):   # [plen, 128] -> [4, plen, 32]
+        return np.ascontiguousarray(m.reshape(plen, tinygpt.N_HEAD, -1).transpose(1, 0, 2))
+
+    hd = tinygpt.D_MODEL // tinygpt.N_HEAD
+    consts = dict(HEAD_DIM=hd, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=plen % 16 == 0,
+                  **A.contiguous_strides(hd, "nd", plen))
+    asig = A.signature_for(consts)
+    for layer in range(tinygpt.N_LAYER):
+        p = {k: w[f"h{layer}.{k}"] for k, _ in tinygpt.LAYER_TENSORS}
+        h = ln(x, p["ln1_g"], p["ln1_b"])
+        qkv = dense(h, p["w_qkv"], p["b_qkv"])
+        d = tinygpt.D_MODEL
+        q, k, v = heads(qkv[:, :d]), heads(qkv[:, d:2 * d]), heads(qkv[:, 2 * d:])
+        vals = dict(Q=q, K=k, V=v, Out=np.zeros_like(q), sm_scale=float(1 / np.sqrt(hd)), N_CTX=plen,
+                    stride_qh=plen * hd, stride_kh=plen * hd, stride_vh=plen * hd, stride_oh=plen * hd)
+        vals = {key: val for key, val in vals.items() if key in asig}
+        att = run_split(A.attn_fwd_kernel, (-(-plen // 2), tinygpt.N_HEAD), asig, consts, vals, "Out", procs)
+        att = np.ascontiguousarray(att.reshape(tinygpt.N_HEAD, plen, hd).transpose(1, 0, 2).reshape(plen, d))
+        x = (x + dense(att, p["w_o"], p["b_o"])).astype(f32)
+        h2 = ln(x, p["ln2_g"], p["ln2_b"])
+        fpre = dense(h2, p["w_fc"], p["b_fc"]).astype(np.float64)
+        import math
+        gelu = (0.5 * fpre * (1.0 + np.vectorize(math.erf)(fpre / math.sqrt(2.0)))).astype(f32)
+        x = (x + dense(gelu, p["w_pr"], p["b_pr"])).astype(f32)
+    hf = ln(x, w["lnf_g"], w["lnf_b"])
+    logits = dense(hf, np.ascontiguousarray(w["wte"].T), np.zeros(tinygpt.VOCAB, f32))
+    meta = dict(op="tinygpt_prefill", prompt_len=plen, weight_seed=seed, prompt_seed=7, ref=fp,
+                emu_seconds=time.time() - t)
+    save(name, meta, prompt=prompt.astype(np.int32), logits=logits)
+
+
 def case_idiv(fp, procs, big):
     import piton
     from primitive_kernels import idiv_kernel
@@ -388,7 +456,8 @@ def main():
     ap.add_argument("--ref", default=os.environ.get("PITON_REFERENCE", ""), required=False)
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 1)
     ap.add_argument("--big", action="store_true", help="also the multi-minute configuration sizes")
-    ap.add_argument("--only", default="", help="comma list of add,softmax,matmul,dense,attention")
+    ap.add_argument("--only", default="", help="comma list of add,softmax,matmul,dense,attention,idiv,life,elem,"
+                                               "tinygpt")
     args = ap.parse_args()
     if not args.ref or not os.path.isdir(args.ref):
         sys.exit("--ref must point at a PIton checkout")
@@ -396,10 +465,11 @@ def main():
     sys.path.insert(0, os.path.join(args.ref, "examples"))
     os.environ.setdefault("PITON_PAIR", "0")      # same bits, faster compiles (tests/test_attention.py:4-8)
     fp = ref_fingerprint(args.ref)
+    _STATE["ref"] = args.ref
     only = set(filter(None, args.only.split(",")))
     for name, fn in (("add", case_add), ("softmax", case_softmax), ("matmul", case_matmul),
                      ("dense", case_dense), ("attention", case_attention), ("idiv", case_idiv), ("life", case_life),
-                     ("elem", case_elem)):
+                     ("elem", case_elem), ("tinygpt", case_tinygpt)):
         if not only or name in only:
             fn(fp, args.procs, args.big)
 

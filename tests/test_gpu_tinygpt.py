@@ -63,3 +63,19 @@ def test_batch_rows_are_independent(cuda):
     together = model.generate(prompts, 20)
     alone = np.concatenate([model.generate(prompts[i:i + 1], 20) for i in range(9)])
     np.testing.assert_array_equal(together, alone)
+
+
+def test_logits_against_reference_kernels_on_the_emulator(cuda):
+    """The B200 decode against TinyGPT composed from the reference's own kernels on its
+    emulator (tests/golden/make_golden.py case_tinygpt): the logits after every prefix of the
+    prompt within 5e-5, the same greedy token."""
+    from conftest import goldens
+    gs = goldens("tinygpt_emu_")
+    assert gs
+    for g in gs:
+        model = tinygpt.TinyGPT(tinygpt.init_weights(g.meta["weight_seed"]))
+        prompt = g["prompt"]
+        for p in range(1, len(prompt) + 1):
+            _, logits = model.generate(prompt[None, :p], 0, return_logits=True)
+            np.testing.assert_allclose(logits[0], g["logits"][p - 1], rtol=0, atol=5e-5)
+            assert int(np.argmax(logits[0])) == int(np.argmax(g["logits"][p - 1]))

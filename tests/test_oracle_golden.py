@@ -134,3 +134,22 @@ def test_elementwise_qpu(g):
     else:
         got = O.qpu_scaled_relu(x, 0.5)
     np.testing.assert_array_equal(bits(got), bits(g["out"]))
+
+
+TGPT = goldens("tinygpt_emu_")
+
+
+@pytest.mark.parametrize("g", TGPT, ids=golden_ids(TGPT))
+def test_tinygpt_host_model_against_reference_kernels(g):
+    """The float64 TinyGPT host model against the model composed from the reference's own
+    kernels on its emulator (dense_layer_kernel, attn_fwd_kernel, layernorm_kernel): the
+    logits of every prompt prefix within 2e-5 (they are O(0.5); the emulator rounds toward
+    zero), the same greedy token."""
+    from oracle import tinygpt_ref
+    from piton_b200 import tinygpt
+    w = tinygpt.init_weights(g.meta["weight_seed"])
+    prompt = g["prompt"]
+    for p in range(1, len(prompt) + 1):
+        _, logits, _ = tinygpt_ref.generate(w, prompt[None, :p], 0)
+        np.testing.assert_allclose(logits[0], g["logits"][p - 1], rtol=0, atol=2e-5)
+        assert int(np.argmax(logits[0])) == int(np.argmax(g["logits"][p - 1]))
