@@ -3,9 +3,12 @@ B200 decode).
 
 The reference has no TinyGPT (its pieces are dense_layer_kernel,
 attn_fwd_kernel, softmax_kernel and a LayerNorm test kernel), so this model
-follows the specification in piton_b200/tinygpt.py and its parity is unpinned
-by any reference test.  It recomputes with a KV cache exactly like the device
-kernel: per fed position, every layer, attention over positions 0..pos.
+follows the specification in piton_b200/tinygpt.py.  It is pinned at small size
+against the same model composed from those reference kernels on the reference's
+emulator (tests/golden/tinygpt_emu_*.npz, made by tests/golden/make_golden.py):
+the logits of every prompt prefix agree within 2e-5.  It recomputes with a KV
+cache exactly like the device kernel: per fed position, every layer, attention
+over positions 0..pos.
 
 Greedy decoding is compared token by token; when the float64 top-2 logit
 margin at some step is below `tie_margin`, the B200's fp32 arithmetic may
