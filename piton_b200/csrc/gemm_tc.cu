@@ -87,7 +87,10 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
 }
 
 // Row-major source with unit column stride and 16-byte aligned rows: the split
-// needs no transpose, so it streams float4 in and two float4 out per thread.
+// needs no transpose, so it streams float4 in and float4 out per thread.  With
+// hi == nullptr only the low halves are written: kind::tf32 MMAs ignore the low 13
+// bits of an fp32 operand (the raw value multiplies exactly as its truncated high
+// half), so the GEMM then reads the high half straight from the source.
 __global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__restrict__ src, int64_t rows,
                                                               int64_t cols, int64_t s_row, float *__restrict__ hi,
                                                               float *__restrict__ lo, int64_t ld) {
@@ -100,7 +103,7 @@ __global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__res
         float4 h = make_float4(tf32_trunc(v.x), tf32_trunc(v.y), tf32_trunc(v.z), tf32_trunc(v.w));
         float4 l = make_float4(isfinite(v.x) ? tf32_trunc(v.x - h.x) : 0.0f, isfinite(v.y) ? tf32_trunc(v.y - h.y) : 0.0f,
                                isfinite(v.z) ? tf32_trunc(v.z - h.z) : 0.0f, isfinite(v.w) ? tf32_trunc(v.w - h.w) : 0.0f);
-        *reinterpret_cast<float4 *>(hi + r * ld + c) = h;
+        if (hi) *reinterpret_cast<float4 *>(hi + r * ld + c) = h;
         *reinterpret_cast<float4 *>(lo + r * ld + c) = l;
     }
 }
@@ -860,14 +863,17 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     float *a_hi = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K));
     float *a_lo = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K) + region(s.M, s.K));
 
-    // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves
+    // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves.  A row-major A with 16-byte
+    //    aligned rows is its own high half (the tensor core ignores the low 13 bits): only A_lo
+    //    is written and the A_hi tensor map reads A in place.
+    const bool vec_a = s.sak == 1 && s.K % 4 == 0 && s.sam % 4 == 0 && s.sam >= s.K && s.sam < (1ll << 37) &&
+                       (reinterpret_cast<uintptr_t>(s.a) & 15) == 0;
     {
         dim3 ga((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.M, 32));
-        const bool vec_a = s.sak == 1 && s.K % 4 == 0 && s.sam % 4 == 0 && (reinterpret_cast<uintptr_t>(s.a) & 15) == 0;
         if (vec_a) {
             int64_t blocks = cdiv(s.M * (s.K / 4), 256);
             if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
-            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, a_hi, a_lo, ld);
+            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, nullptr, a_lo, ld);
         } else {
             int along_rows_a = llabs(s.sam) < llabs(s.sak);
             split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
@@ -884,7 +890,8 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     const int b_box = pairs ? bn / 2 : bn;   // rows of B^T one CTA loads
     CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
     int rc;
-    if ((rc = make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) || (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
+    if ((rc = vec_a ? make_map(&m_ahi, s.a, s.M, s.K, s.sam, BM) : make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) ||
+        (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
         (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, b_box)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, b_box)))
         return rc;
     GemmArgs g;
