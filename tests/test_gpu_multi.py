@@ -122,3 +122,49 @@ def test_library_allgather_two_gpus():
         mp.spawn(_allgather_worker, args=(2, _port(), results), nprocs=2, join=True)
         res = dict(results)
     assert res == {0: True, 1: True}
+
+
+def _host_sharded_worker(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    from piton_b200 import sharding
+    from piton_b200.runtime.cuda import pinned_empty
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    hs = None
+    try:
+        M, N, K = 2048, 768, 512
+        rng = np.random.default_rng(3)
+        a_full = rng.uniform(-1, 1, (M, K)).astype(np.float32)
+        b = rng.uniform(-1, 1, (K, N)).astype(np.float32)
+        r0, per = sharding.shard(M, world, rank)
+        A, B, Cm = pinned_empty((per, K)), pinned_empty((K, N)), pinned_empty((per, N))
+        A[...], B[...] = a_full[r0:r0 + per], b
+        hs = sharding.HostShardedMatmul(dist, per, N, K)
+        errs = []
+        for _ in range(2):
+            Cm[...] = np.nan
+            hs(A, B, Cm)
+            ref = a_full[r0:r0 + per].astype(np.float64) @ b.astype(np.float64)
+            errs.append(float(np.abs(Cm - ref).max() / np.abs(ref).max()))
+        results[rank] = max(errs)
+        dist.barrier()
+    finally:
+        if hs is not None:
+            hs.close()
+        dist.destroy_process_group()
+
+
+def test_host_sharded_matmul_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_host_sharded_worker, args=(2, _port(), results), nprocs=2, join=True)
+        res = dict(results)
+    assert len(res) == 2 and all(e <= 4e-6 for e in res.values()), res
