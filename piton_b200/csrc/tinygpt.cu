@@ -59,7 +59,7 @@ __device__ __forceinline__ void linear(const float *in, float *out, const float 
     for (int s = 0; s < SEQ; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (g < G) {
         const float4 *w4 = reinterpret_cast<const float4 *>(W) + q;
-#pragma unroll 8
+#pragma unroll 32
         for (int k = g * KG; k < (g + 1) * KG; ++k) {
             float4 w = __ldg(w4 + (int64_t)k * NQ);
 #pragma unroll
@@ -133,7 +133,7 @@ __device__ __forceinline__ void layernorm(const float *x, float *y, const float 
     __syncthreads();
 }
 
-__global__ void __launch_bounds__(THREADS) tinygpt_step_kernel(StepArgs a) {
+__global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
     __shared__ __align__(16) float x[SEQ * D], h[SEQ * D], qkv[SEQ * 3 * D], att[SEQ * D], f[SEQ * F];
     __shared__ float probs[SEQ * H][CTX];
     __shared__ __align__(16) float scratch[SEQ * THREADS * 4];
