@@ -13,7 +13,7 @@
 
 namespace piton {
 
-constexpr int MLP_ROWS = 32, MLP_THREADS = 256;
+constexpr int MLP_ROWS = 16, MLP_THREADS = 256;   // 16 images per CTA: 113 CTAs for 1797 images
 
 template <bool QPU>
 __device__ __forceinline__ float mac(float acc, float a, float b) {
@@ -31,9 +31,9 @@ __device__ __forceinline__ void layer(const float *in, float *out, const float *
     float acc[RPT];
 #pragma unroll
     for (int i = 0; i < RPT; ++i) acc[i] = 0.0f;
-#pragma unroll 8
+#pragma unroll 32
     for (int k = 0; k < K; ++k) {
-        float w = __ldg(W + k * N + n);
+        float w = __ldg(W + k * N + n);   // 32 weight loads in flight per thread: L2 latency, not FMA, bounds this
 #pragma unroll
         for (int i = 0; i < RPT; ++i) acc[i] = mac<QPU>(acc[i], in[(r0 + i) * K + k], w);
     }
@@ -47,7 +47,7 @@ __device__ __forceinline__ void layer(const float *in, float *out, const float *
 }
 
 template <bool QPU, bool U8>
-__global__ void __launch_bounds__(MLP_THREADS) mlp_kernel(piton_mlp_args a) {
+__global__ void __launch_bounds__(MLP_THREADS, 1) mlp_kernel(piton_mlp_args a) {
     __shared__ float x[MLP_ROWS * 64];
     __shared__ float h1[MLP_ROWS * 128];
     __shared__ float h2[MLP_ROWS * 64];
