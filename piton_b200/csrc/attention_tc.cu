@@ -1,5 +1,6 @@
-// Flash-attention forward on the 5th-generation tensor cores with the 3xTF32
-// split (examples/attention.py:33-113; the semantics are those of
+// Flash-attention forward on the 5th-generation tensor cores with a 3xTF32-class
+// split: tf32 products of the high halves (and hi x lo stacked beside them), bf16
+// products for the lo x hi cross terms (examples/attention.py:33-113; the semantics are those of
 // attention.cu's header: key_end, causal mask, row_end, base-2 online softmax).
 //
 // Per call:
@@ -85,25 +86,6 @@ constexpr int TMEM_COLS = 512;
 constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_O = 384;
 static_assert(KSTAGES == VSTAGES, "the producers share one ring depth");
 constexpr float BF16_MAX = 3.3895313892515355e38f;       // largest finite bf16
-
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-    return (1u << 4)                       // D format f32
-           | (1u << 7)                     // A format bf16
-           | (1u << 10)                    // B format bf16
-           | ((uint32_t)(N >> 3) << 17)    // N / 8
-           | ((uint32_t)(M >> 4) << 24);   // M / 16
-}
-
-// D[tmem] += A[tmem] * B[smem]^T, kind::f16 with bf16 operands: A is M=128 lanes x K=16,
-// two bf16 per 32-bit column (even k in the low half), 8 columns from a_tmem.
-__device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "setp.ne.b32 p, 1, 0;\n\t"
-        "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
-        "r"(a_tmem), "l"(b_desc), "r"(idesc)
-        : "memory");
-}
 
 // two floats -> bf16 pair (round to nearest), `lo_k` in the low half
 __device__ __forceinline__ uint32_t pack_bf16(float lo_k, float hi_k) {

@@ -1,21 +1,36 @@
-// fp32 GEMM on the 5th-generation tensor cores with the 3xTF32 split
+// fp32 GEMM on the 5th-generation tensor cores from a split of each operand
 // (tutorial matmul, examples/kernels.py:18-57, default rounding mode).
 //
-// fp32 accuracy from TF32 tensor cores: each operand x is split into
+// fp32 accuracy from TF32 / BF16 tensor cores: each operand x is split into
 // x_hi = x with the low 13 mantissa bits cleared (exactly representable in
-// TF32) and x_lo = tf32(x - x_hi), and C = A_hi B_hi + A_hi B_lo + A_lo B_hi,
-// accumulated in fp32 in tensor memory.  The dropped A_lo B_lo term and the
-// truncation of x_lo are below 2^-21 relative to each product.
+// TF32) and x_lo = x - x_hi (exact in fp32, at most 2^-10 |x|), and
+//   C = A_hi B_hi + (A_lo B + A B_lo)
+// where A_hi B_hi is a kind::tf32 product (exact products) and the bracket is
+// one kind::f16 product of bf16 operands, concatenated along k: per group of 8
+// k-values the A operand holds [bf16(A_lo), bf16(A)] and the B operand
+// [bf16(B), bf16(B_lo)], so one 16-deep bf16 MMA adds A_lo B + A B_lo over the
+// same 8 k-values a tf32 MMA covers.  A B_lo + A_lo B = A_hi B_lo + A_lo B_hi +
+// 2 A_lo B_lo; with A_lo B_lo below 2^-20 of the product, the bracket carries
+// the two cross terms of the classic 3xTF32 split (and the lo x lo term once
+// more, which is below the rounding of the bf16 operands).  The bf16 rounding
+// of a cross operand (8-bit mantissa) costs at most 2^-9 of a term that is
+// itself at most 2^-10 of the product: ~2^-19 per product in the worst case,
+// with unbiased (round-to-nearest) signs.  A bf16 MMA of depth 16 issues as
+// fast as a tf32 MMA of depth 8, so each 8-deep k-step takes two MMAs instead
+// of 3xTF32's three, from the same shared-memory bytes.
 //
 // Two kernels per call:
 //  1. split: reads A and B with their (arbitrary) element strides and writes
-//     A_hi, A_lo as [M, ld] and B_hi, B_lo transposed as [N, ld] (K-major,
-//     ld = K rounded up to 4) into the caller's workspace.  HBM-bound.
+//     A_hi as [M, ld] fp32 (ld = K rounded up to 4) and the cross operand A_x
+//     as [M, ldx] bf16 (ldx = 2 x K rounded up to 16), and B_hi, B_x
+//     transposed as [N, ld] / [N, ldx] (K-major), into the caller's workspace.
+//     HBM-bound.  A row-major A is its own A_hi (see below).
 //  2. gemm: persistent, one CTA per SM (320 threads): warp 0 issues TMA tile
-//     loads (128x16 A tiles, 256x16 B tiles, 64-byte swizzle, 4-stage
-//     mbarrier ring), warp 1 owns 512 TMEM columns (two 128x256 fp32
-//     accumulators) and issues tcgen05.mma kind::tf32 128x256x8 from one
-//     thread, warps 2-9 drain finished accumulators with tcgen05.ld.
+//     loads (128x16 A tiles, 256x16 B tiles (fp32) and the bf16 tiles of the
+//     same 16 k-values, 64-byte swizzle, 4-stage mbarrier ring), warp 1 owns
+//     512 TMEM columns (two 128x256 fp32 accumulators) and issues, from one
+//     thread, tcgen05.mma kind::tf32 128x256x8 and kind::f16 128x256x16,
+//     warps 2-9 drain finished accumulators with tcgen05.ld.
 //
 // The tensor cores add into the TMEM accumulator with truncation, and that
 // bias grows with the number of accumulation steps (at K = 8192 it is ~30x
@@ -29,6 +44,8 @@
 // returns.
 #include <algorithm>
 #include <vector>
+
+#include <cuda_bf16.h>
 
 #include "attention.cuh"
 #include "common.cuh"
@@ -47,9 +64,10 @@ constexpr int BM = 128, BK = 16, STAGES = 4;
 constexpr int THREADS = 320;
 constexpr int EPI_WARPS = 8;
 constexpr int KC_BLOCKS = 16;   // k-blocks of BK per accumulation chunk (KC = 256)
-constexpr uint32_t A_TILE_BYTES = BM * BK * 4;   // 8 KB
+constexpr uint32_t A_TILE_BYTES = BM * BK * 4;   // 8 KB: 128 rows x 16 fp32, or x 32 bf16 (cross operand)
 // BN (tile width along N) is 256, or 224 where that packs the tiles into fewer
-// rounds over the SMs (tile_width()); a B tile is BN x 16 fp32 (14 or 16 KB)
+// rounds over the SMs (tile_width()); a B tile is BN x 16 fp32 (14 or 16 KB), and
+// its cross tile BN x 32 bf16 as many bytes
 __host__ __device__ constexpr uint32_t b_tile_bytes(int bn) { return (uint32_t)bn * BK * 4; }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_TILE_BYTES + 2 * b_tile_bytes(bn); }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) { return STAGES * stage_bytes(bn) + 1024 /*barriers*/ + 1024 /*alignment*/; }
@@ -58,11 +76,28 @@ constexpr int GROUP_M = 16;
 
 __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
-// dst_hi/lo[r * ld + c] from src[r * s_row + c * s_col], r < rows, c < cols, through
-// 32 x 32 shared-memory tiles so that both the strided read and the write coalesce.
+// Cross operand of value v (at k) in a row of the bf16 array x: per group of 8
+// k-values, positions [16 g, 16 g + 8) hold the first part and [16 g + 8, 16 g + 16)
+// the second.  A side: (bf16(lo), bf16(v)); B side: (bf16(v), bf16(lo)), so that one
+// 16-deep product of the two adds A_lo B + A B_lo.  Non-finite values contribute 0
+// (their high half carries them), finite ones are clamped to the bf16 range.
+__device__ __forceinline__ __nv_bfloat16 bf16_of(float v) {
+    constexpr float BF16_MAX = 3.3895313892515355e38f;
+    return __float2bfloat16_rn(isfinite(v) ? fminf(fmaxf(v, -BF16_MAX), BF16_MAX) : 0.0f);
+}
+__device__ __forceinline__ void put_cross(__nv_bfloat16 *xrow, int64_t c, float v, float lo, bool a_side) {
+    const int64_t p = 16 * (c >> 3) + (c & 7);
+    xrow[p] = a_side ? bf16_of(lo) : bf16_of(v);
+    xrow[p + 8] = a_side ? bf16_of(v) : bf16_of(lo);
+}
+
+// hi[r * ld + c] (if hi) and the cross operand x[r * ldx + ...] from src[r * s_row + c * s_col],
+// r < rows, c < cols, through 32 x 32 shared-memory tiles so that both the strided read and the
+// write coalesce; k-values from cols up to the next multiple of 8 are written as zeros.
 __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
                                                     int64_t s_row, int64_t s_col, float *__restrict__ hi,
-                                                    float *__restrict__ lo, int64_t ld, int lanes_along_rows) {
+                                                    __nv_bfloat16 *__restrict__ x, int64_t ld, int64_t ldx,
+                                                    int lanes_along_rows, int a_side) {
     __shared__ float tile[32][33];
     const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
     const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;    // 32 x 8
@@ -74,37 +109,43 @@ __global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ sr
         else tile[j][tx] = v;
     }
     __syncthreads();
+    const int64_t cols8 = (cols + 7) / 8 * 8;
     for (int j = ty; j < 32; j += 8) {
         int64_t r = r0 + j, c = c0 + tx;
-        if (r < rows && c < cols) {
-            float v = tile[j][tx];
-            float h = tf32_trunc(v);
-            float l = isfinite(v) ? tf32_trunc(v - h) : 0.0f;
-            hi[r * ld + c] = h;
-            lo[r * ld + c] = l;
+        if (r < rows && c < cols8) {
+            const float v = c < cols ? tile[j][tx] : 0.0f;
+            const float h = tf32_trunc(v);
+            if (hi && c < cols) hi[r * ld + c] = h;
+            put_cross(x + r * ldx, c, v, isfinite(v) ? v - h : 0.0f, a_side != 0);
         }
     }
 }
 
-// Row-major source with unit column stride and 16-byte aligned rows: the split
-// needs no transpose, so it streams float4 in and float4 out per thread.  With
-// hi == nullptr only the low halves are written: kind::tf32 MMAs ignore the low 13
-// bits of an fp32 operand (the raw value multiplies exactly as its truncated high
-// half), so the GEMM then reads the high half straight from the source.
+// Row-major A with unit column stride and 16-byte aligned rows: kind::tf32 MMAs ignore
+// the low 13 bits of an fp32 operand (the raw value multiplies exactly as its truncated
+// high half), so the GEMM reads A_hi straight from the source and only the cross operand
+// is written: per thread 4 k-values in (one float4), 4 + 4 bf16 out (two 8-byte stores).
 __global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__restrict__ src, int64_t rows,
-                                                              int64_t cols, int64_t s_row, float *__restrict__ hi,
-                                                              float *__restrict__ lo, int64_t ld) {
-    const int64_t q_per_row = cols / 4;
+                                                              int64_t cols, int64_t s_row,
+                                                              __nv_bfloat16 *__restrict__ x, int64_t ldx) {
+    const int64_t q_per_row = (cols + 7) / 8 * 2;   // cols % 4 == 0: whole float4s, up to the 8-group
     const int64_t total = rows * q_per_row;
     for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int64_t r = i / q_per_row, c = 4 * (i % q_per_row);
-        float4 v = __ldcs(reinterpret_cast<const float4 *>(src + r * s_row + c));
-        float4 h = make_float4(tf32_trunc(v.x), tf32_trunc(v.y), tf32_trunc(v.z), tf32_trunc(v.w));
-        float4 l = make_float4(isfinite(v.x) ? tf32_trunc(v.x - h.x) : 0.0f, isfinite(v.y) ? tf32_trunc(v.y - h.y) : 0.0f,
-                               isfinite(v.z) ? tf32_trunc(v.z - h.z) : 0.0f, isfinite(v.w) ? tf32_trunc(v.w - h.w) : 0.0f);
-        if (hi) *reinterpret_cast<float4 *>(hi + r * ld + c) = h;
-        *reinterpret_cast<float4 *>(lo + r * ld + c) = l;
+        const float4 v = c < cols ? __ldcs(reinterpret_cast<const float4 *>(src + r * s_row + c))
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        __align__(8) __nv_bfloat16 lo[4], full[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const float h = tf32_trunc(vv[e]);
+            lo[e] = bf16_of(isfinite(vv[e]) ? vv[e] - h : 0.0f);
+            full[e] = bf16_of(vv[e]);
+        }
+        __nv_bfloat16 *p = x + r * ldx + 16 * (c >> 3) + (c & 7);
+        *reinterpret_cast<uint2 *>(p) = *reinterpret_cast<const uint2 *>(lo);
+        *reinterpret_cast<uint2 *>(p + 8) = *reinterpret_cast<const uint2 *>(full);
     }
 }
 
@@ -174,8 +215,8 @@ __device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int64_t
 
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
-                       const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_ax,
+                       const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_bx,
                        GemmArgs args) {
     constexpr uint32_t B_TILE_BYTES = b_tile_bytes(BN);
     constexpr uint32_t STAGE_BYTES = stage_bytes(BN);
@@ -206,9 +247,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         fence_mbarrier_init();
         prefetch_tmap(&tm_ahi);
-        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_ax);
         prefetch_tmap(&tm_bhi);
-        prefetch_tmap(&tm_blo);
+        prefetch_tmap(&tm_bx);
     }
     if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_holder);
     tc_fence_before();
@@ -233,11 +274,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     uint8_t *st = smem + s * STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                    int kx = kb * BK;
+                    const int kx = kb * BK, kxx = 2 * kb * BK;   // fp32 and bf16 (cross) columns
                     tma_load_2d(st, &tm_ahi, &full[s], kx, tm * BM);
-                    tma_load_2d(st + A_TILE_BYTES, &tm_alo, &full[s], kx, tm * BM);
+                    tma_load_2d(st + A_TILE_BYTES, &tm_ax, &full[s], kxx, tm * BM);
                     tma_load_2d(st + 2 * A_TILE_BYTES, &tm_bhi, &full[s], kx, tn * BN);
-                    tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_blo, &full[s], kx, tn * BN);
+                    tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_bx, &full[s], kxx, tn * BN);
                 }
             }
             // drain: every copy this thread issued has landed before the CTA may exit
@@ -248,7 +289,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_tf32(BM, BN);
+            constexpr uint32_t IDESC = idesc_tf32(BM, BN), IDESC_X = idesc_bf16(BM, BN);
             uint32_t it = 0, chunk = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < args.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -274,19 +315,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         tc_fence_after();
                         uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-                        uint32_t a_hi = base, a_lo = base + A_TILE_BYTES;
-                        uint32_t b_hi = base + 2 * A_TILE_BYTES, b_lo = b_hi + B_TILE_BYTES;
+                        uint32_t a_hi = base, a_x = base + A_TILE_BYTES;
+                        uint32_t b_hi = base + 2 * A_TILE_BYTES, b_x = b_hi + B_TILE_BYTES;
 #pragma unroll
                         for (int ks = 0; ks < BK / 8; ++ks) {
-                            uint32_t off = ks * 32;   // 8 tf32 = 32 bytes along K inside the swizzled row
+                            // 8 tf32, or the 16 bf16 of the same 8 k-values: 32 bytes along K in the row
+                            uint32_t off = ks * 32;
                             uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dax = smem_desc_kmajor(a_x + off, 64, LAYOUT_SWIZZLE_64B);
                             uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dbx = smem_desc_kmajor(b_x + off, 64, LAYOUT_SWIZZLE_64B);
                             uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
-                            mma_tf32(d_tmem, dal, dbh, IDESC, first);   // A_lo B_hi
-                            mma_tf32(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
-                            mma_tf32(d_tmem, dah, dbh, IDESC, 1u);      // A_hi B_hi
+                            mma_bf16(d_tmem, dax, dbx, IDESC_X, first);   // A_lo B + A B_lo
+                            mma_tf32(d_tmem, dah, dbh, IDESC, 1u);        // A_hi B_hi
                         }
                         mma_commit(&empty[s]);   // stage s free once these MMAs have read it
                     }
@@ -482,6 +523,13 @@ __device__ __forceinline__ void mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b
         "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u)
         : "memory");
 }
+__device__ __forceinline__ void mma_bf16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u)
+        : "memory");
+}
 // arrives on `bar` in both CTAs of the pair once this thread's MMAs have completed
 __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
     asm volatile(
@@ -493,8 +541,8 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
 
 template <int BNP>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_3xtf32_2sm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_alo,
-                           const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_blo,
+    gemm_3xtf32_2sm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_ax,
+                           const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_bx,
                            GemmArgs args) {
     constexpr uint32_t B_TILE = b2_tile_bytes(BNP), STAGE = stage2_bytes(BNP);
     constexpr int HALF = BNP / 2;   // accumulator columns per epilogue warpgroup, and B rows per CTA
@@ -528,9 +576,9 @@ __global__ void __launch_bounds__(THREADS, 1)
         *abort_flag = 0;
         fence_mbarrier_init();
         prefetch_tmap(&tm_ahi);
-        prefetch_tmap(&tm_alo);
+        prefetch_tmap(&tm_ax);
         prefetch_tmap(&tm_bhi);
-        prefetch_tmap(&tm_blo);
+        prefetch_tmap(&tm_bx);
     }
     if (warp == 1) {   // the same warp of both CTAs allocates the pair's TMEM
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -563,11 +611,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint8_t *st = smem + s * STAGE;
                     const uint32_t bar = cluster_addr_rank0(&full[s]);
                     if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE);   // both CTAs' bytes
-                    const int kx = kb * BK;
+                    const int kx = kb * BK, kxx = 2 * kb * BK;   // fp32 and bf16 (cross) columns
                     tma_load_2d_pair(st, &tm_ahi, bar, kx, arow);
-                    tma_load_2d_pair(st + A2_TILE_BYTES, &tm_alo, bar, kx, arow);
+                    tma_load_2d_pair(st + A2_TILE_BYTES, &tm_ax, bar, kxx, arow);
                     tma_load_2d_pair(st + 2 * A2_TILE_BYTES, &tm_bhi, bar, kx, brow);
-                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES + B_TILE, &tm_blo, bar, kx, brow);
+                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES + B_TILE, &tm_bx, bar, kxx, brow);
                 }
             }
             // drain: every copy of both CTAs completes on the even CTA's stage barriers
@@ -580,7 +628,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (even CTA) ----------------
         if (lane == 0 && leader) {
-            constexpr uint32_t IDESC = idesc_tf32(2 * BM, BNP);
+            constexpr uint32_t IDESC = idesc_tf32(2 * BM, BNP), IDESC_X = idesc_bf16(2 * BM, BNP);
             uint32_t it = 0, chunk = 0;
             bool ok = true;
             for (int t = pair; ok && t < args.num_tiles && !*abort_flag; t += npairs) {
@@ -602,19 +650,18 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         tc_fence_after();
                         const uint32_t base = smem_u32(smem + s * STAGE);
-                        const uint32_t a_hi = base, a_lo = base + A2_TILE_BYTES;
-                        const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_lo = b_hi + B_TILE;
+                        const uint32_t a_hi = base, a_x = base + A2_TILE_BYTES;
+                        const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_x = b_hi + B_TILE;
 #pragma unroll
                         for (int ks = 0; ks < BK / 8; ++ks) {
                             const uint32_t off = ks * 32;
                             const uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dax = smem_desc_kmajor(a_x + off, 64, LAYOUT_SWIZZLE_64B);
                             const uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dbx = smem_desc_kmajor(b_x + off, 64, LAYOUT_SWIZZLE_64B);
                             const uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
-                            mma_tf32_pair(d_tmem, dal, dbh, IDESC, first);   // A_lo B_hi
-                            mma_tf32_pair(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
-                            mma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);      // A_hi B_hi
+                            mma_bf16_pair(d_tmem, dax, dbx, IDESC_X, first);   // A_lo B + A B_lo
+                            mma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);        // A_hi B_hi
                         }
                         mma_commit_pair(&empty[s]);   // stage s free in both CTAs
                     }
@@ -789,7 +836,24 @@ int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, in
     return PITON_B200_OK;
 }
 
+// bf16 cross operand [rows, ldx]: 16 bf16 (32 bytes) per group of 8 k-values; box [box_rows, 2 * BK]
+// (the same 64 bytes per row as an fp32 box of BK), 64-byte swizzle.
+int make_map_x(CUtensorMap *map, const __nv_bfloat16 *base, int64_t rows, int64_t ldx, int box_rows) {
+    EncodeTiled enc = encode_fn();
+    if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {(cuuint64_t)ldx, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ldx * 2)};
+    cuuint32_t box[2] = {(cuuint32_t)(2 * BK), (cuuint32_t)box_rows};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16 *>(base), dims, strides, box,
+                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
+    return PITON_B200_OK;
+}
+
 int64_t ld_of(int64_t K) { return (K + 3) / 4 * 4; }
+int64_t ldx_of(int64_t K) { return (K + 7) / 8 * 16; }
 
 // CTA pairs (2-SM MMAs) for problems with at least two 256-row tiles; tile width along N
 // chosen as for one CTA, over the pairs.
@@ -802,7 +866,7 @@ int pair_tile_width(int64_t M, int64_t N) {
 }
 
 template <int BNP>
-int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtensorMap &b_hi, const CUtensorMap &b_lo,
+int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_x, const CUtensorMap &b_hi, const CUtensorMap &b_x,
                  GemmArgs g, cudaStream_t stream) {
     static bool attr[64] = {};
     int dev = 0;
@@ -825,7 +889,7 @@ int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtenso
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_3xtf32_2sm_kernel<BNP>, a_hi, a_lo, b_hi, b_lo, g));
+    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_3xtf32_2sm_kernel<BNP>, a_hi, a_x, b_hi, b_x, g));
     return PITON_B200_OK;
 }
 
@@ -840,6 +904,7 @@ int tile_width(int64_t M, int64_t N) {
     return cost224 < cost256 ? 224 : 256;
 }
 size_t region(int64_t rows, int64_t K) { return ((size_t)rows * ld_of(K) * 4 + 1023) / 1024 * 1024; }
+size_t xregion(int64_t rows, int64_t K) { return ((size_t)rows * ldx_of(K) * 2 + 1023) / 1024 * 1024; }
 
 }  // namespace
 
@@ -853,46 +918,49 @@ bool tc_gemm_supported(const TcGemmShape &s) {
     return encode_fn() != nullptr;
 }
 
-size_t tc_gemm_workspace_bytes(const TcGemmShape &s) { return 2 * region(s.M, s.K) + 2 * region(s.N, s.K); }
+size_t tc_gemm_workspace_bytes(const TcGemmShape &s) {
+    return region(s.M, s.K) + xregion(s.M, s.K) + region(s.N, s.K) + xregion(s.N, s.K);
+}
 
 int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
-    const int64_t ld = ld_of(s.K);
+    const int64_t ld = ld_of(s.K), ldx = ldx_of(s.K);
     uint8_t *ws = static_cast<uint8_t *>(workspace);
+    const size_t nb = region(s.N, s.K) + xregion(s.N, s.K);   // B's operands first: their place does not depend on M
     float *b_hi = reinterpret_cast<float *>(ws);
-    float *b_lo = reinterpret_cast<float *>(ws + region(s.N, s.K));
-    float *a_hi = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K));
-    float *a_lo = reinterpret_cast<float *>(ws + 2 * region(s.N, s.K) + region(s.M, s.K));
+    __nv_bfloat16 *b_x = reinterpret_cast<__nv_bfloat16 *>(ws + region(s.N, s.K));
+    float *a_hi = reinterpret_cast<float *>(ws + nb);
+    __nv_bfloat16 *a_x = reinterpret_cast<__nv_bfloat16 *>(ws + nb + region(s.M, s.K));
 
-    // 1. split A [M, K] and B^T [N, K] into tf32 hi/lo halves.  A row-major A with 16-byte
-    //    aligned rows is its own high half (the tensor core ignores the low 13 bits): only A_lo
-    //    is written and the A_hi tensor map reads A in place.
+    // 1. split A [M, K] and B^T [N, K] into the tf32 high halves and the bf16 cross operands.
+    //    A row-major A with 16-byte aligned rows is its own high half (the tensor core ignores the
+    //    low 13 bits): only A_x is written and the A_hi tensor map reads A in place.
     const bool vec_a = s.sak == 1 && s.K % 4 == 0 && s.sam % 4 == 0 && s.sam >= s.K && s.sam < (1ll << 37) &&
                        (reinterpret_cast<uintptr_t>(s.a) & 15) == 0;
     {
         dim3 ga((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.M, 32));
         if (vec_a) {
-            int64_t blocks = cdiv(s.M * (s.K / 4), 256);
+            int64_t blocks = cdiv(s.M * (ldx / 8), 256);
             if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
-            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, nullptr, a_lo, ld);
+            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, a_x, ldx);
         } else {
             int along_rows_a = llabs(s.sam) < llabs(s.sak);
-            split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_lo, ld, along_rows_a);
+            split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_x, ld, ldx, along_rows_a, 1);
         }
         if (s.split_b) {
             dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
             int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
-            split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_lo, ld, along_rows_b);
+            split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_x, ld, ldx, along_rows_b, 0);
         }
     }
     // 2. persistent tcgen05 GEMM
     const bool pairs = use_pairs(s.M, s.N);
     const int bn = pairs ? pair_tile_width(s.M, s.N) : tile_width(s.M, s.N);
     const int b_box = pairs ? bn / 2 : bn;   // rows of B^T one CTA loads
-    CUtensorMap m_ahi, m_alo, m_bhi, m_blo;
+    CUtensorMap m_ahi, m_ax, m_bhi, m_bx;
     int rc;
     if ((rc = vec_a ? make_map(&m_ahi, s.a, s.M, s.K, s.sam, BM) : make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) ||
-        (rc = make_map(&m_alo, a_lo, s.M, s.K, ld, BM)) ||
-        (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, b_box)) || (rc = make_map(&m_blo, b_lo, s.N, s.K, ld, b_box)))
+        (rc = make_map_x(&m_ax, a_x, s.M, ldx, BM)) || (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, b_box)) ||
+        (rc = make_map_x(&m_bx, b_x, s.N, ldx, b_box)))
         return rc;
     GemmArgs g;
     g.c = s.c;
@@ -909,8 +977,8 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
         g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
         g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
         g.num_tiles = g.tiles_m * g.tiles_n;
-        rc = bn == 224 ? launch_pairs<224>(m_ahi, m_alo, m_bhi, m_blo, g, stream)
-                       : launch_pairs<256>(m_ahi, m_alo, m_bhi, m_blo, g, stream);
+        rc = bn == 224 ? launch_pairs<224>(m_ahi, m_ax, m_bhi, m_bx, g, stream)
+                       : launch_pairs<256>(m_ahi, m_ax, m_bhi, m_bx, g, stream);
         if (rc) return rc;
         return check_launch("gemm_3xtf32_2sm", s.split_b ? 3 : 2);
     }
@@ -932,9 +1000,9 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.num_tiles = g.tiles_m * g.tiles_n;
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     if (bn == 224)
-        gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
+        gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_ax, m_bhi, m_bx, g);
     else
-        gemm_3xtf32_kernel<256><<<grid, THREADS, smem_bytes(256), stream>>>(m_ahi, m_alo, m_bhi, m_blo, g);
+        gemm_3xtf32_kernel<256><<<grid, THREADS, smem_bytes(256), stream>>>(m_ahi, m_ax, m_bhi, m_bx, g);
     return check_launch("gemm_3xtf32", s.split_b ? 3 : 2);
 }
 

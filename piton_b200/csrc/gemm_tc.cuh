@@ -19,9 +19,9 @@ struct TcGemmShape {
     int64_t row_offset = 0, ldc_peer = 0;
     float *peer_c[MAX_PEERS] = {};
     float *multicast_c = nullptr;   // non-null: multimem stores through the NVSwitch instead of peer copies
-    // false: B's hi/lo halves are already in the workspace from an earlier call
-    // with the same B, N and K (the workspace holds B's halves first, so their
-    // place does not depend on M)
+    // false: B's split operands (high half and bf16 cross operand) are already in
+    // the workspace from an earlier call with the same B, N and K (the workspace
+    // holds B's operands first, so their place does not depend on M)
     bool split_b = true;
 };
 

@@ -1,6 +1,7 @@
 // Entry points of the tutorial matmul (examples/kernels.py:18-57) and the dense
 // layer (examples/nn_kernels.py:23-74): argument checks and the choice between
-// the tcgen05 3xTF32 path (gemm_tc.cu) and the CUDA-core path (gemm_simt.cu).
+// the tcgen05 split-operand path (gemm_tc.cu: tf32 high halves + bf16 cross terms) and the
+// CUDA-core path (gemm_simt.cu).
 #include "common.cuh"
 #include "gemm_simt.cuh"
 #include "gemm_tc.cuh"
