@@ -44,7 +44,7 @@ sys.path.insert(0, REPO)
 
 METRIC = "fp32 matmul TFLOPS + softmax/attn GB/s vs roofline at 1/2/4/8 B200"
 MM = 8192
-GEMM_TRAFFIC_8192 = 5.49e9 + 267.1e6   # bytes per launch (ncu, 1 B200)
+GEMM_TRAFFIC_8192 = 6.849e9 + 268.0e6   # bytes per launch (ncu, 1 B200)
 SM_M, SM_N = 32768, 16384
 AT_B, AT_H, AT_S, AT_D = 32, 32, 4096, 64
 ADD_N = 1 << 28

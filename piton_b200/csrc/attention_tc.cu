@@ -52,6 +52,7 @@
 #include "attention.cuh"
 #include "common.cuh"
 #include "sm100.cuh"
+#include "split.cuh"
 
 namespace piton {
 
@@ -130,6 +131,31 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float *__restrict
             ll[r * ld + c] = fin ? tf32_trunc(v - x) : 0.0f;
             bb[r * ldb + c] = __float2bfloat16_rn(fin ? fminf(fmaxf(v, -BF16_MAX), BF16_MAX) : 0.0f);
         }
+    }
+}
+
+// K rows with unit d stride and 16-byte aligned rows: no transpose, float4 in; lo (tf32 of the
+// rest) and bf (bf16 of the value) out, and hi (the tf32 high half) unless the kernel reads K in
+// place (hi == nullptr).  One thread per 4 d-values; grid-stride over heads x n_ctx x 16.
+__global__ void __launch_bounds__(256) attn_split_rows_kernel(const float *__restrict__ src, int64_t n_ctx,
+                                                              int64_t heads, int64_t s_h, int64_t s_r,
+                                                              float *__restrict__ hi, float *__restrict__ lo,
+                                                              __nv_bfloat16 *__restrict__ bf) {
+    const int64_t total = heads * n_ctx * (HD / 4);
+    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t q = i % (HD / 4), row = i / (HD / 4), h = row / n_ctx, r = row % n_ctx;
+        const float4 v = __ldcs(reinterpret_cast<const float4 *>(src + h * s_h + r * s_r + 4 * q));
+        const float vv[4] = {v.x, v.y, v.z, v.w};
+        float vh[4], vl[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            vh[e] = tf32_trunc(vv[e]);
+            vl[e] = isfinite(vv[e]) ? tf32_trunc(vv[e] - vh[e]) : 0.0f;
+        }
+        const int64_t o = row * HD + 4 * q;
+        if (hi) *reinterpret_cast<float4 *>(hi + o) = make_float4(vh[0], vh[1], vh[2], vh[3]);
+        *reinterpret_cast<float4 *>(lo + o) = make_float4(vl[0], vl[1], vl[2], vl[3]);
+        *reinterpret_cast<uint2 *>(bf + o) = make_uint2(split_bf16_pair(vv[0], vv[1]), split_bf16_pair(vv[2], vv[3]));
     }
 }
 
@@ -625,6 +651,20 @@ __global__ void __launch_bounds__(256) attn_q_copy_kernel(const float *__restric
         dst[h * n_ctx * HD + i] = src[h * s_h + (i / HD) * s_r + i % HD];
 }
 
+// K split without a transpose: unit d stride, 16-byte aligned rows and heads
+bool k_rows_vec(const AttnParams &p) {
+    return p.skk == 1 && p.skn % 4 == 0 && p.skh % 4 == 0 && (reinterpret_cast<uintptr_t>(p.k) & 15) == 0;
+}
+// K read in place as its own tf32 high half (the tensor core ignores the low 13 bits): the rows
+// of all heads one stride apart, as the 2-D tensor map [heads * n_ctx, HD] needs
+bool k_in_place(const AttnParams &p) {
+    return k_rows_vec(p) && p.skn >= HD && p.skh == p.n_ctx * p.skn && p.skn < (1ll << 37);
+}
+// V^T by the 64 x 64-tile transposing split: d contiguous (always), keys and heads 16-byte aligned
+bool v_vec(const AttnParams &p) {
+    return p.svn % 4 == 0 && p.svh % 4 == 0 && (reinterpret_cast<uintptr_t>(p.v) & 15) == 0;
+}
+
 int64_t v_ld(int64_t n_ctx) { return (n_ctx + 3) / 4 * 4; }
 int64_t v_ldb(int64_t n_ctx) { return (n_ctx + 7) / 8 * 8; }   // bf16 rows: 16-byte multiple
 size_t k_region(const AttnParams &p) { return ((size_t)p.heads * p.n_ctx * HD * 4 + 1023) / 1024 * 1024; }
@@ -660,14 +700,24 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     __nv_bfloat16 *v_bf = reinterpret_cast<__nv_bfloat16 *>(ws + 2 * k_region(p) + 2 * v_region(p) + kb_region(p));
     const int64_t ldv = v_ld(p.n_ctx), ldvb = v_ldb(p.n_ctx);
     // K [n_ctx, D] per head (strides skn, skk) -> [heads * n_ctx, D]
-    {
+    const bool k_direct = k_in_place(p);
+    if (k_rows_vec(p)) {
+        const int64_t total = p.heads * p.n_ctx * (HD / 4);
+        const int64_t blocks = std::min<int64_t>(cdiv(total, (int64_t)256), (int64_t)num_sms() * 16);
+        attn_split_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p.k, p.n_ctx, p.heads, p.skh, p.skn,
+                                                                     k_direct ? nullptr : k_hi, k_lo, k_bf);
+    } else {
         dim3 g((unsigned)cdiv(HD, 32), (unsigned)cdiv(p.n_ctx, 32), (unsigned)p.heads);
         int along_rows = llabs(p.skn) < llabs(p.skk);
         attn_split_kernel<<<g, 256, 0, stream>>>(p.k, p.n_ctx, HD, p.skh, p.skn, p.skk, k_hi, k_lo, HD, k_bf, HD,
                                                  along_rows);
     }
     // V [n_ctx, D] per head (strides svn, 1) -> V^T [heads * D, ldv]
-    {
+    if (v_vec(p)) {
+        dim3 g((unsigned)cdiv(p.n_ctx, 64), 1, (unsigned)p.heads);
+        split_transpose_kernel<SPLIT_T_ATTN_V><<<g, 256, 0, stream>>>(p.v, HD, p.n_ctx, p.svn, p.svh, v_hi, v_lo, v_bf,
+                                                                       ldv, ldvb);
+    } else {
         dim3 g((unsigned)cdiv(p.n_ctx, 32), (unsigned)cdiv(HD, 32), (unsigned)p.heads);
         attn_split_kernel<<<g, 256, 0, stream>>>(p.v, HD, p.n_ctx, p.svh, 1, p.svn, v_hi, v_lo, ldv, v_bf, ldvb, 1);
     }
@@ -686,7 +736,8 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     CUtensorMap mq, mkh, mkl, mkb, mvh, mvl, mvb;
     int rc;
     if ((rc = make_map_q(&mq, q, p.n_ctx, p.heads, sqm, sqh)) ||
-        (rc = make_map(&mkh, k_hi, p.heads * p.n_ctx, HD, HD)) || (rc = make_map(&mkl, k_lo, p.heads * p.n_ctx, HD, HD)) ||
+        (rc = k_direct ? make_map(&mkh, p.k, p.heads * p.n_ctx, HD, p.skn) : make_map(&mkh, k_hi, p.heads * p.n_ctx, HD, HD)) ||
+        (rc = make_map(&mkl, k_lo, p.heads * p.n_ctx, HD, HD)) ||
         (rc = make_map_bf16(&mkb, k_bf, p.heads * p.n_ctx, HD, HD)) ||
         (rc = make_map(&mvh, v_hi, p.heads * HD, p.n_ctx, ldv)) || (rc = make_map(&mvl, v_lo, p.heads * HD, p.n_ctx, ldv)) ||
         (rc = make_map_bf16(&mvb, v_bf, p.heads * HD, p.n_ctx, ldvb)))

@@ -51,6 +51,7 @@
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "sm100.cuh"
+#include "split.cuh"
 
 namespace piton {
 
@@ -947,9 +948,17 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
             split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_x, ld, ldx, along_rows_a, 1);
         }
         if (s.split_b) {
-            dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
-            int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
-            split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_x, ld, ldx, along_rows_b, 0);
+            // row-major B (unit n stride, 16-byte aligned rows): 64 x 64-tile transpose with 16-byte stores
+            const bool vec_b = s.sbn == 1 && s.N % 4 == 0 && s.sbk % 4 == 0 && (reinterpret_cast<uintptr_t>(s.b) & 15) == 0;
+            if (vec_b) {
+                dim3 gb((unsigned)cdiv(s.K, 64), (unsigned)cdiv(s.N, 64));
+                split_transpose_kernel<SPLIT_T_GEMM_B><<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbk, 0, b_hi, nullptr,
+                                                                                b_x, ld, ldx);
+            } else {
+                dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
+                int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
+                split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_x, ld, ldx, along_rows_b, 0);
+            }
         }
     }
     // 2. persistent tcgen05 GEMM

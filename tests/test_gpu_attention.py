@@ -202,3 +202,29 @@ def test_tensor_core_path_unaligned_q_and_out(cuda, q_off):
     assert _status() == 0
     np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, False), rtol=0, atol=ATOL)
     assert np.all(out[:, :, d:] == 3.0)
+
+
+@pytest.mark.parametrize("k_ld,k_gap,v_ld", [(68, 0, 68), (65, 0, 65), (64, 4, 64), (64, 0, 72)])
+def test_tensor_core_path_k_and_v_layouts(cuda, k_ld, k_gap, v_ld):
+    """K rows k_ld floats apart with k_gap extra floats between heads, V rows v_ld apart: K read in
+    place as its own high half (rows one stride apart across heads, 16-byte multiples), the
+    vectorised K split (16-byte rows, heads not one stride apart), or the strided one (odd row
+    stride); V through the 64 x 64-tile transposing split (16-byte rows) or the strided one."""
+    heads, n, d = 2, 200, 64
+    rng = np.random.default_rng(k_ld + 10 * k_gap + v_ld)
+    q = rng.standard_normal((heads, n, d)).astype(np.float32)
+    k = rng.standard_normal((heads, n, d)).astype(np.float32)
+    v = rng.standard_normal((heads, n, d)).astype(np.float32)
+    skh, svh = n * k_ld + k_gap, n * v_ld
+    kbuf = np.full(heads * skh, np.nan, np.float32)
+    vbuf = np.full(heads * svh, np.nan, np.float32)
+    for h in range(heads):
+        kbuf[h * skh:h * skh + n * k_ld].reshape(n, k_ld)[:, :d] = k[h]
+        vbuf[h * svh:h * svh + n * v_ld].reshape(n, v_ld)[:, :d] = v[h]
+    out = np.zeros_like(q)
+    stats = attn_fwd_kernel[(n // 2, heads)](q, kbuf, vbuf, out, 0.125, n * d, d, skh, k_ld, 1, svh, v_ld, n * d, d, n,
+                                             HEAD_DIM=d, BLOCK_M=2, BLOCK_N=8, CAUSAL=True, EVEN_N=True,
+                                             device="b200").last_stats
+    assert stats["path"] == "tcgen05_3xtf32"
+    assert _status() == 0
+    np.testing.assert_allclose(out, O.attention_f64(q, k, v, True), rtol=0, atol=ATOL)
