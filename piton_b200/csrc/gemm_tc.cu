@@ -12,10 +12,10 @@
 // same 8 k-values a tf32 MMA covers.  A B_lo + A_lo B = A_hi B_lo + A_lo B_hi +
 // 2 A_lo B_lo; with A_lo B_lo below 2^-20 of the product, the bracket carries
 // the two cross terms of the classic 3xTF32 split (and the lo x lo term once
-// more, which is below the rounding of the bf16 operands).  The bf16 rounding
-// of a cross operand (8-bit mantissa) costs at most 2^-9 of a term that is
-// itself at most 2^-10 of the product: ~2^-19 per product in the worst case,
-// with unbiased (round-to-nearest) signs.  A bf16 MMA of depth 16 issues as
+// more, at most 2^-20 of the product).  Rounding both operands of a cross term
+// to bf16 (8-bit mantissas) costs at most 2^-8 of a term that is itself at most
+// 2^-10 of the product: at most 2^-17 + 2^-20 per product, ~2^-19.6 rms, with
+// unbiased (round-to-nearest) signs.  A bf16 MMA of depth 16 issues as
 // fast as a tf32 MMA of depth 8, so each 8-deep k-step takes two MMAs instead
 // of 3xTF32's three, from the same shared-memory bytes.
 //
