@@ -203,3 +203,23 @@ def test_tensor_core_k_edges(cuda, K):
     err = float((C[:M].double() - ref).abs().max() / ref.abs().max())
     assert err <= fp32_bound(K), (err, st)
     assert bool((C[M:] == 3.0).all())
+
+
+@pytest.mark.parametrize("K", [257, 1004])
+def test_tensor_core_transposed_operands_odd_k(cuda, K):
+    """A and B given as transposes (unit stride along M and along K): both operands go through the
+    32 x 32-tile strided split, whose cross operand is zero-filled up to the next multiple of 8
+    k-values; C written through a transposed view."""
+    torch = cuda
+    M, N = 384, 256
+    A = (torch.rand(K, M, device="cuda") * 2 - 1).t()     # stride_am = 1, stride_ak = M
+    B = (torch.rand(N, K, device="cuda") * 2 - 1).t()     # stride_bk = 1, stride_bn = K
+    C = torch.zeros(N, M, device="cuda").t()              # stride_cm = 1, stride_cn = M
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, A.stride(0), A.stride(1), B.stride(0), B.stride(1), C.stride(0), C.stride(1),
+        BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
+    assert st["path"] == "tcgen05_3xtf32"
+    assert device_status() == 0
+    ref = A.double() @ B.double()
+    err = float((C.double() - ref).abs().max() / ref.abs().max())
+    assert err <= fp32_bound(K), err
