@@ -1,13 +1,17 @@
 // Flash-attention forward on the 5th-generation tensor cores with a 3xTF32-class
 // split: tf32 products of the high halves (and hi x lo stacked beside them), bf16
-// products for the lo x hi cross terms (examples/attention.py:33-113; the semantics are those of
-// attention.cu's header: key_end, causal mask, row_end, base-2 online softmax).
+// products for the lo x hi cross terms (examples/attention.py:33-113; the
+// semantics are those of attention.cu's header: key_end, causal mask, row_end,
+// base-2 online softmax).
 //
 // Per call:
-//  1. split: K -> K_hi, K_lo as [heads * n_ctx, D] and V -> V^T_hi, V^T_lo as
-//     [heads * D, ld] (ld = n_ctx rounded up to 4), tf32 hi/lo halves, plus
-//     bf16 copies K_bf [heads * n_ctx, D] and V^T_bf [heads * D, ldb] (ldb =
-//     n_ctx rounded up to 8), into the workspace.
+//  1. split (HBM-bound): K -> K_lo (tf32 of the rest) and K_bf (bf16) as
+//     [heads * n_ctx, D], and K_hi unless K itself can serve (the tensor core
+//     ignores the low 13 bits of an fp32 operand: K is read in place when its
+//     rows are one 16-byte-multiple stride apart across heads); V -> V^T_hi,
+//     V^T_lo as [heads * D, ld] (ld = n_ctx rounded up to 4) and V^T_bf as
+//     [heads * D, ldb] (ldb = n_ctx rounded up to 8), through 64 x 64 tiles
+//     with 16-byte stores (split.cuh) when V's rows are 16-byte aligned.
 //  2. persistent CTAs walk (head, 128-query block) items, 352 threads:
 //     * warps 2-9, two per TMEM lane quarter (one thread per query row =
 //       TMEM lane in each), each warp of a pair on half of the columns: they
@@ -31,20 +35,21 @@
 //       Q_lo against K_bf (N = 64, added to columns 0-63); likewise P_hi
 //       [V_hi; V_lo] and P_lo V_bf for P.V.  The softmax warps add the two
 //       halves in fp32 registers (round to nearest), so the hi/lo sums are not
-//       truncated by the tensor core.  The lo x hi cross term is ~2^-10 of
-//       the product, so its bf16 operands (8-bit mantissas) still leave it
-//       correct to ~2^-19 of the product, while a bf16 MMA covers twice the k
-//       range of a tf32 one in the same issue time: 12 MMAs per 64-key block
-//       for S and 12 for P.V instead of 16 each.
+//       truncated by the tensor core.  The lo x hi cross term is at most
+//       2^-10 of the product, so rounding both of its operands to bf16 (8-bit
+//       mantissas) leaves it correct to at most 2^-18 of the product, while a
+//       bf16 MMA covers twice the k range of a tf32 one in the same issue
+//       time: 12 MMAs per 64-key block for S and 12 for P.V instead of 16 each.
 //     A block's P.V lands in its own TMEM accumulator that the softmax warps
 //     add into registers, so the tensor core's truncating accumulation never
 //     spans more than one 64-key block.
 // The scores of block j+1 are computed while the softmax warps work on block
 // j (two S/P buffers), and a block's P.V accumulator is folded into the
 // registers after the next block's P is written, so the tensor core and the
-// softmax warps overlap.  TMEM columns: Q_hi [0,64) Q_lo [64,96)
-// S/P x2 [128,384) (128 each) O_blk [384,512) (512 allocated).  All waits are bounded (2 s): on expiry
-// the kernel records a status, drains its copies and MMAs, frees TMEM, returns.
+// softmax warps overlap.  TMEM columns: Q_hi [0,64) Q_lo [64,96), S/P x2
+// [128,384) (128 each), O_blk [384,512) (512 allocated).  All waits are
+// bounded (2 s): on expiry the kernel records a status, drains its copies and
+// MMAs, frees TMEM and returns.
 #include <algorithm>
 
 #include <cuda_bf16.h>
@@ -86,7 +91,6 @@ constexpr int TMEM_COLS = 512;
 // 128-column O_blk (P_hi.V_hi (+ P_lo.V_bf) in 0-63, P_hi.V_lo in 64-127)
 constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_O = 384;
 static_assert(KSTAGES == VSTAGES, "the producers share one ring depth");
-constexpr float BF16_MAX = 3.3895313892515355e38f;       // largest finite bf16
 
 // two floats -> bf16 pair (round to nearest), `lo_k` in the low half
 __device__ __forceinline__ uint32_t pack_bf16(float lo_k, float hi_k) {
@@ -129,7 +133,7 @@ __global__ void __launch_bounds__(256) attn_split_kernel(const float *__restrict
             const bool fin = isfinite(v);
             hh[r * ld + c] = x;
             ll[r * ld + c] = fin ? tf32_trunc(v - x) : 0.0f;
-            bb[r * ldb + c] = __float2bfloat16_rn(fin ? fminf(fmaxf(v, -BF16_MAX), BF16_MAX) : 0.0f);
+            bb[r * ldb + c] = split_bf16_of(v);
         }
     }
 }

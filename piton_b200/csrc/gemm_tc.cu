@@ -82,14 +82,10 @@ __device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__
 // the second.  A side: (bf16(lo), bf16(v)); B side: (bf16(v), bf16(lo)), so that one
 // 16-deep product of the two adds A_lo B + A B_lo.  Non-finite values contribute 0
 // (their high half carries them), finite ones are clamped to the bf16 range.
-__device__ __forceinline__ __nv_bfloat16 bf16_of(float v) {
-    constexpr float BF16_MAX = 3.3895313892515355e38f;
-    return __float2bfloat16_rn(isfinite(v) ? fminf(fmaxf(v, -BF16_MAX), BF16_MAX) : 0.0f);
-}
 __device__ __forceinline__ void put_cross(__nv_bfloat16 *xrow, int64_t c, float v, float lo, bool a_side) {
     const int64_t p = 16 * (c >> 3) + (c & 7);
-    xrow[p] = a_side ? bf16_of(lo) : bf16_of(v);
-    xrow[p + 8] = a_side ? bf16_of(v) : bf16_of(lo);
+    xrow[p] = a_side ? split_bf16_of(lo) : split_bf16_of(v);
+    xrow[p + 8] = a_side ? split_bf16_of(v) : split_bf16_of(lo);
 }
 
 // hi[r * ld + c] (if hi) and the cross operand x[r * ldx + ...] from src[r * s_row + c * s_col],
@@ -141,8 +137,8 @@ __global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__res
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
             const float h = tf32_trunc(vv[e]);
-            lo[e] = bf16_of(isfinite(vv[e]) ? vv[e] - h : 0.0f);
-            full[e] = bf16_of(vv[e]);
+            lo[e] = split_bf16_of(isfinite(vv[e]) ? vv[e] - h : 0.0f);
+            full[e] = split_bf16_of(vv[e]);
         }
         __nv_bfloat16 *p = x + r * ldx + 16 * (c >> 3) + (c & 7);
         *reinterpret_cast<uint2 *>(p) = *reinterpret_cast<const uint2 *>(lo);
