@@ -419,6 +419,59 @@ def bench_mlp(torch, D, args, lib_calls):
     return out
 
 
+def run_sweep(args):
+    """The HBM-bound operators over the sizes of the B200 sweep (one GPU): add n = 2^20 ... 2^28 and
+    softmax 32768 x N, N = 256 ... 16384.  Each launch is timed alone with CUDA events after a
+    256 MB write has evicted the 126 MB L2 (the smaller inputs would otherwise be served from
+    it); the median of 10 launches.  One JSON line."""
+    import ctypes as C
+    import statistics
+
+    import torch
+    from piton_b200.runtime.cuda import _lib
+    from piton_b200.runtime.cuda._lib import lib
+    peaks = load_peaks()
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+
+    def median_seconds(fn):
+        for _ in range(3):
+            fn()
+        ts = []
+        for _ in range(10):
+            flush.zero_()
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1) / 1e3)
+        return statistics.median(ts)
+
+    out = {"add": [], "softmax": []}
+    for lg in (20, 22, 24, 26, 28):
+        n = 1 << lg
+        x, y = torch.rand(n, device="cuda"), torch.rand(n, device="cuda")
+        z = torch.empty_like(x)
+        a = _lib.AddArgs(x.data_ptr(), y.data_ptr(), z.data_ptr(), n, 1024, (n + 1023) // 1024, 0, 0)
+        t = median_seconds(lambda: _lib.check(lib().piton_b200_add_f32(C.byref(a), stream), "add"))
+        out["add"].append({"n": n, "us": 1e6 * t, "gbs": 12.0 * n / t / 1e9,
+                           "frac_of_copy": 12.0 * n / t / 1e9 / peaks["hbm_gbs"]})
+        del x, y, z
+    M = 32768
+    for N in (256, 1024, 4096, 16384):
+        x = torch.randn(M, N, device="cuda") * 4
+        y = torch.empty_like(x)
+        a = _lib.SoftmaxArgs(y.data_ptr(), x.data_ptr(), N, N, N, N, M, 0, 0)
+        t = median_seconds(lambda: _lib.check(lib().piton_b200_softmax_f32(C.byref(a), stream), "softmax"))
+        out["softmax"].append({"M": M, "N": N, "us": 1e6 * t, "gbs": 8.0 * M * N / t / 1e9,
+                               "frac_of_copy": 8.0 * M * N / t / 1e9 / peaks["hbm_gbs"]})
+        del x, y
+    print(json.dumps({"sweep": out, "timing": "median of 10 launches, L2 evicted before each",
+                      "peaks": {"hbm_gbs": peaks["hbm_gbs"], "source": peaks["source"]}}))
+    return 0
+
+
 def tf32_peak(torch):
     """cuBLAS TF32 GEMM throughput at 8192^3 (the denominator of the tensor-core GEMM roofline)."""
     prev = torch.backends.cuda.matmul.allow_tf32
@@ -593,6 +646,8 @@ def main():
     ap.add_argument("--allgather", default="peer", choices=["peer", "multicast"],
                     help="matmul all-gather at N > 1: peer stores, or multimem stores to an NVSwitch multicast address")
     ap.add_argument("--attn-bh", type=int, default=AT_B * AT_H, help="attention batch x heads (profiling runs use fewer)")
+    ap.add_argument("--sweep", action="store_true",
+                    help="instead of the benchmark line: add and softmax over the sweep sizes (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     MM = args.mm_size
@@ -600,6 +655,8 @@ def main():
     ATTN_BH = args.attn_bh
     if args.impl == "reference":
         return run_reference(args)
+    if args.sweep:
+        return run_sweep(args)
 
     import torch
     D = Dist()
