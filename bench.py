@@ -289,7 +289,10 @@ def bench_attention(torch, D, args, lib_calls):
     h0, hloc = shard(BH, D.world, D.rank)
     q, k, v = (torch.randn(hloc, AT_S, AT_D, device="cuda") for _ in range(3))
     o = torch.empty_like(q)
-    ofull = torch.empty(BH, AT_S, AT_D, device="cuda") if D.world > 1 else o
+    # at N > 1 (peer all-gather) the kernel stores each finished block of rows into every rank's full
+    # output itself: a gather warp trails the softmax warps with NVLink peer stores
+    fused = D.world > 1 and args.allgather == "peer"
+    ofull = torch.empty(BH, AT_S, AT_D, device="cuda") if (D.world > 1 and not fused) else o
     sd = AT_S * AT_D
     a = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), 1.0 / np.sqrt(AT_D), sd, AT_D, sd,
                            AT_D, 1, sd, AT_D, sd, AT_D, AT_S, AT_D, 64, 64, AT_S // 64, hloc, 1, 1, 0, 0, 0, 0)
@@ -301,9 +304,24 @@ def bench_attention(torch, D, args, lib_calls):
     def kernel_only():
         _lib.check(lib().piton_b200_attention_f32(C.byref(a), stream), "attention")
 
-    def step():
-        kernel_only()
-        D.allgather(torch, ofull, o)
+    peer = None
+    if fused:
+        from piton_b200 import sharding
+        peer = sharding.PeerOutput(D.pg, BH * sd * 4)
+        gargs = _lib.AllgatherArgs()
+        for r, p in enumerate(peer.peer_ptrs):
+            gargs.peer_c[r] = p
+        gargs.world, gargs.rank, gargs.row_offset = D.world, D.rank, h0
+        done = torch.zeros(1, device="cuda")
+        fa = lib().piton_b200_attention_allgather_f32
+
+        def step():
+            _lib.check(fa(C.byref(a), C.byref(gargs), stream), "attention_allgather")
+            D.pg.all_reduce(done)   # completion barrier: every rank's stores have landed
+    else:
+        def step():
+            kernel_only()
+            D.allgather(torch, ofull, o)
 
     steps = max(1, args.steps // 4)
     n0 = lib().piton_b200_launch_count()
@@ -319,9 +337,24 @@ def bench_attention(torch, D, args, lib_calls):
     s = s.masked_fill(torch.ones(64, AT_S, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
     ref = torch.softmax(s, 1) @ vs
     err = float((o[0, :64].double() - ref).abs().max())
+    if peer is not None:
+        # the fused all-gather's output: this rank's first rows in its own full output, and the next
+        # rank's first rows as that rank's gather warp stored them here, against that rank's own copy
+        torch.cuda.synchronize()
+        D.pg.barrier()
+        mine = peer.read(h0 * sd * 4, 64 * AT_D * 4).view(np.float32).reshape(64, AT_D)
+        err = max(err, float(np.abs(mine - ref.cpu().numpy()).max()))
+        sums = [None] * D.world
+        D.pg.all_gather_object(sums, float(np.abs(mine.astype(np.float64)).sum()))
+        nxt = (D.rank + 1) % D.world
+        theirs = peer.read(nxt * hloc * sd * 4, 64 * AT_D * 4).view(np.float32)
+        if float(np.abs(theirs.astype(np.float64)).sum()) != sums[nxt]:
+            err = float("inf")
+        D.pg.barrier()
+        peer.close()
     flops = 4.0 * BH * AT_S * AT_S * AT_D * 0.5
     return {"flops": flops, "bytes": 16.0 * BH * AT_S * AT_D, "t_step": t_step, "t_kernel": t_kernel, "err": err,
-            "local_flops": flops * hloc / BH, "tc": ws > 0}
+            "local_flops": flops * hloc / BH, "tc": ws > 0, "fused": fused}
 
 
 def bench_add(torch, D, args, lib_calls):
@@ -707,6 +740,9 @@ def main():
                             "kernel_tflops_per_gpu": r["local_flops"] / r["t_kernel"] / 1e12,
                             "path": "tcgen05 split (tf32 high halves + bf16 cross terms)" if r.get("tc")
                                     else "CUDA-core fp32",
+                            "allgather": ("fused: the kernel's gather warp stores finished rows to every rank "
+                                          "(NVLink peer stores)" if r.get("fused") else
+                                          "NCCL all_gather_into_tensor after the kernel") if D.world > 1 else None,
                             "ms_per_step": 1e3 * r["t_step"], "max_abs_err_vs_f64": r["err"]}
         if D.world > 1:
             sec["attention"]["value_without_allgather"] = r["flops"] / r["t_kernel"] / 1e12

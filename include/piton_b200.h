@@ -227,6 +227,20 @@ typedef struct {
 PITON_B200_API size_t piton_b200_attention_workspace_size(const piton_attention_args *args);
 PITON_B200_API int piton_b200_attention_f32(const piton_attention_args *args, void *stream);
 
+/* ---- attention sharded by heads with the output all-gather fused into the kernel ----
+   No counterpart in the reference (it runs on one device); the north star's "attention by
+   batch x head + all-gather of Out" as one kernel: this rank computes heads
+   [row_offset, row_offset + args->grid_y) of the full output (args->out is ignored; q, k, v
+   hold this rank's heads), and every finished 128-row block of a head is stored into each
+   rank's full output peer_c[r] (head h at peer_c[r] + h * stride_oh, rows stride_om apart,
+   the same strides on every rank, multiples of 4 elements): into the own one by the softmax
+   warps, into the others by a gather warp that trails them (NVLink peer stores, overlapped
+   with the next blocks' math).  Tensor-core path only (ENOTSUP otherwise); ldc is not used and
+   a nonzero multicast_c is rejected with ENOTSUP.  Every rank must pass a barrier after its
+   call before the output is read anywhere. */
+PITON_B200_API int piton_b200_attention_allgather_f32(const piton_attention_args *args,
+                                                      const piton_allgather_args *g, void *stream);
+
 /* ---- row LayerNorm without affine: tests/test_reroll_reduce.py:199-208 layernorm_kernel ---- */
 typedef struct {
     uint64_t x, y;        /* float* */

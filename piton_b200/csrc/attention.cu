@@ -235,3 +235,34 @@ extern "C" int piton_b200_attention_f32(const piton_attention_args *a, void *str
     }
     return attention_simt(p, as_stream(stream));
 }
+
+extern "C" int piton_b200_attention_allgather_f32(const piton_attention_args *a, const piton_allgather_args *g,
+                                                  void *stream) {
+    AttnParams p;
+    int rc = attn_params(a, p);
+    if (rc) return rc;
+    PITON_REQUIRE(g != nullptr, "allgather args is NULL");
+    PITON_REQUIRE(g->world >= 1 && g->world <= MAX_PEERS && g->rank >= 0 && g->rank < g->world,
+                  "world %d / rank %d outside 1..%d", g->world, g->rank, MAX_PEERS);
+    PITON_REQUIRE(g->row_offset >= 0, "bad first head %lld", (long long)g->row_offset);
+    if (g->multicast_c)
+        return set_error(PITON_B200_ENOTSUP, "the all-gather attention stores to peers only (no multicast output)");
+    PITON_REQUIRE(a->stride_oh % 4 == 0 && a->stride_om % 4 == 0, "output strides must be multiples of 4 elements");
+    for (int i = 0; i < g->world; ++i)
+        PITON_REQUIRE(g->peer_c[i] != 0 && (g->peer_c[i] & 15) == 0, "peer output %d is NULL or misaligned", i);
+    if (p.row_end <= 0 || p.heads == 0) return PITON_B200_OK;
+    PITON_REQUIRE(p.heads < 65536, "too many heads for one launch");
+    PITON_REQUIRE(a->q && a->k && a->v, "NULL pointer");
+    if (!use_tc(a, p))
+        return set_error(PITON_B200_ENOTSUP, "the all-gather attention runs on the tensor-core path only "
+                                             "(HEAD_DIM 64, n_ctx >= 64)");
+    size_t need = attention_tc_workspace_bytes(p);
+    if (a->workspace_bytes < need || !a->workspace)
+        return set_error(PITON_B200_EWORKSPACE, "attention needs %zu bytes of workspace, got %llu", need,
+                         (unsigned long long)a->workspace_bytes);
+    p.world = g->world;
+    p.rank = g->rank;
+    for (int i = 0; i < g->world; ++i) p.peer_o[i] = reinterpret_cast<float *>(g->peer_c[i]) + g->row_offset * a->stride_oh;
+    p.o = p.peer_o[g->rank];
+    return attention_tc(p, reinterpret_cast<void *>(a->workspace), as_stream(stream));
+}

@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "gemm_tc.cuh"   // MAX_PEERS
+
 namespace piton {
 
 struct AttnParams {
@@ -14,6 +16,10 @@ struct AttnParams {
     int64_t row_end;   // query rows >= row_end are not written
     float qk_scale;    // sm_scale * log2(e)
     int causal;
+    // all-gather (world > 1, tensor-core path): o = peer_o[rank]; every row is also stored at the
+    // same offset from each other rank's peer_o (full outputs, offset to this rank's first head)
+    int world = 0, rank = 0;
+    float *peer_o[MAX_PEERS] = {};
 };
 
 int attention_simt(const AttnParams &p, cudaStream_t s);

@@ -72,6 +72,8 @@ using namespace sm100;
 
 constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 2, VSTAGES = 2, THREADS = 352;
 constexpr int SOFTMAX_WARPS = 8;                          // warps 2-9: two per TMEM lane quarter
+constexpr int GATHER_WARP = 11;                           // copies finished rows to the peers (world > 1)
+constexpr int GATHER_THREADS = THREADS + 32;              // launch with the gather warp
 constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes (32 fp32 or 64 bf16)
 // K stage: for each 32-wide box b of d the hi box and the lo box are adjacent,
 // [K_hi b0][K_lo b0][K_hi b1][K_lo b1][K_bf], so one 128-row B operand covers hi rows
@@ -171,6 +173,17 @@ struct TcAttnArgs {
     int causal;
 };
 
+// The all-gather launch: o is this rank's part of its own full output, and every finished row
+// is also stored at the same offset from peer_o[r] (rank r's full output, offset to this rank's
+// first head) for every other rank r.  (A separate type keeps the plain kernel's parameters,
+// and with them its register allocation, as they are.)
+struct TcAttnGatherArgs : TcAttnArgs {
+    int world, rank;
+    float *peer_o[MAX_PEERS];
+};
+template <int NTHREADS> struct AttnArgsOf { using type = TcAttnArgs; };
+template <> struct AttnArgsOf<GATHER_THREADS> { using type = TcAttnGatherArgs; };
+
 __device__ __forceinline__ bool warp_wait(uint64_t *bar, uint32_t parity) {
     bool ok = mbar_wait(bar, parity);
     return __all_sync(0xffffffffu, ok);
@@ -201,11 +214,12 @@ __device__ __forceinline__ Item item_of(const TcAttnArgs &a, int64_t it) {
     return r;
 }
 
-__global__ void __launch_bounds__(THREADS, 1)
+template <int NTHREADS>   // THREADS, or GATHER_THREADS for the all-gather
+__global__ void __launch_bounds__(NTHREADS, 1)
     attn_3xtf32_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constant__ CUtensorMap m_khi,
                        const __grid_constant__ CUtensorMap m_klo, const __grid_constant__ CUtensorMap m_kbf,
                        const __grid_constant__ CUtensorMap m_vhi, const __grid_constant__ CUtensorMap m_vlo,
-                       const __grid_constant__ CUtensorMap m_vbf, TcAttnArgs a) {
+                       const __grid_constant__ CUtensorMap m_vbf, const typename AttnArgsOf<NTHREADS>::type a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *kst = smem;                                          // K stages
@@ -229,6 +243,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint64_t *sum_bar = max_bar + 8;          // [4 quarters], 64 arrivals
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sum_bar + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
+    volatile int *rows_stored = abort_flag + 1;   // softmax-warp item stores done (8 per item)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -254,6 +269,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int b = 0; b < 8; ++b) mbar_init(&max_bar[b], 64);
         for (int b = 0; b < 4; ++b) mbar_init(&sum_bar[b], 64);
         *abort_flag = 0;
+        if constexpr (NTHREADS > THREADS) *rows_stored = 0;
         fence_mbarrier_init();
         prefetch_tmap(&m_q);
         prefetch_tmap(&m_khi);
@@ -387,6 +403,54 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             mma_commit(drain);
             if (!mbar_wait(drain, 0)) record_status(STATUS_TIMEOUT_DRAIN);
+        }
+    } else if (NTHREADS > THREADS && warp == GATHER_WARP) {
+        // ---------------- all-gather (world > 1): each item's stored rows to every other rank ----------------
+        // The rows are read back from this rank's own output (L2) once all eight softmax warps
+        // have stored them, so the NVLink stores never hold up the softmax warps; this warp
+        // trails them by up to the items still in flight and finishes the kernel's last ones.
+        if constexpr (NTHREADS > THREADS) {
+            int need = 0;
+            for (int64_t it = blockIdx.x; it < a.items; it += gridDim.x) {
+                need += SOFTMAX_WARPS;
+                int go = 1;
+                if (lane == 0 && *rows_stored < need) {
+                    const uint64_t t0 = globaltimer();
+                    while (*rows_stored < need) {
+                        if (*abort_flag || globaltimer() - t0 > 2000000000ull) {
+                            go = 0;
+                            break;
+                        }
+                        __nanosleep(200);
+                    }
+                }
+                if (!__shfl_sync(0xffffffffu, go, 0)) {
+                    if (lane == 0 && !*abort_flag) record_status(STATUS_TIMEOUT_EPILOGUE);
+                    break;
+                }
+                __threadfence();   // pairs with the softmax warps' fence before their count
+                const Item w = item_of(a, it);
+                const int64_t r_end = w.q0 + BM < a.row_end ? w.q0 + BM : a.row_end;
+                const int n4 = (int)(r_end - w.q0) * (HD / 4);
+                const int64_t base = w.head * a.soh + w.q0 * a.som;
+                constexpr int U = 8;   // float4 loads in flight per lane
+                for (int i0 = 0; i0 < n4; i0 += 32 * U) {
+                    float4 v[U];
+                    int64_t off[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int i = i0 + u * 32 + lane;
+                        off[u] = base + (int64_t)(i >> 4) * a.som + 4 * (i & 15);
+                        if (i < n4) v[u] = __ldcg(reinterpret_cast<const float4 *>(a.o + off[u]));
+                    }
+                    for (int p = 1; p < a.world; ++p) {
+                        float *dst = a.peer_o[(a.rank + p) % a.world];
+#pragma unroll
+                        for (int u = 0; u < U; ++u)
+                            if (i0 + u * 32 + lane < n4) *reinterpret_cast<float4 *>(dst + off[u]) = v[u];
+                    }
+                }
+            }
         }
     } else {
         // ---------------- softmax / accumulate / store (warps 2-9) ----------------
@@ -563,6 +627,11 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int d = 0; d < HH; ++d) orow[d] = acc[d] * inv;
                 }
+            }
+            if constexpr (NTHREADS > THREADS) {   // the item's rows are in this rank's output: hand them to the gather warp
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(const_cast<int *>(rows_stored), 1);
             }
         }
         if (!ok) {
@@ -746,12 +815,18 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
         (rc = make_map(&mvh, v_hi, p.heads * HD, p.n_ctx, ldv)) || (rc = make_map(&mvl, v_lo, p.heads * HD, p.n_ctx, ldv)) ||
         (rc = make_map_bf16(&mvb, v_bf, p.heads * HD, p.n_ctx, ldvb)))
         return rc;
-    static bool attr[64] = {false};
+    static bool attr[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
-    if (dev < 64 && !attr[dev]) {
-        PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-        attr[dev] = true;
+    const bool gather = p.world > 1;
+    if (dev < 64 && !attr[dev][gather]) {
+        if (gather)
+            PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel<GATHER_THREADS>,
+                                            cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+        else
+            PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel<THREADS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                            SMEM_BYTES));
+        attr[dev][gather] = true;
     }
     TcAttnArgs a;
     a.o = p.o;
@@ -763,7 +838,16 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     a.causal = p.causal;
     // persistent: one CTA per SM walks the items (head-major, heavy query blocks first)
     const int64_t grid = std::min<int64_t>(a.items, (int64_t)num_sms());
-    if (grid > 0) attn_3xtf32_kernel<<<(unsigned)grid, THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mkb, mvh, mvl, mvb, a);
+    if (grid > 0 && gather) {
+        TcAttnGatherArgs ga;
+        static_cast<TcAttnArgs &>(ga) = a;
+        ga.world = p.world;
+        ga.rank = p.rank;
+        for (int i = 0; i < MAX_PEERS; ++i) ga.peer_o[i] = p.peer_o[i];
+        attn_3xtf32_kernel<GATHER_THREADS>
+            <<<(unsigned)grid, GATHER_THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mkb, mvh, mvl, mvb, ga);
+    } else if (grid > 0)
+        attn_3xtf32_kernel<THREADS><<<(unsigned)grid, THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mkb, mvh, mvl, mvb, a);
     return check_launch("attention_3xtf32", launches);
 }
 

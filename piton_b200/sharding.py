@@ -5,8 +5,9 @@ C with B replicated; softmax: rows; attention: batch x head; add: element
 ranges; MLP / TinyGPT: batch rows), so a rank computes its piece with no
 exchange, and the only collective is the final all-gather of the output
 pieces over NVLink, which leaves the whole output on every rank: NCCL for most
-operators, and for matmul stores from the GEMM epilogue itself (NVSwitch
-multicast or peer stores).
+operators, for matmul stores from the GEMM epilogue itself (NVSwitch multicast
+or peer stores), and for attention peer stores from a gather warp of the
+attention kernel.
 
 Functions here are backend-agnostic (``torch.distributed`` with ``nccl`` on
 GPUs or ``gloo`` on CPU), so the host-side logic is tested on CPU.
@@ -174,6 +175,43 @@ def matmul_allgather(a_piece, b, out, row_offset: int, ldc: int, stream=None, mu
     s = stream if stream is not None else torch.cuda.current_stream()
     _lib.check(lib.piton_b200_matmul_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
                "matmul_allgather")
+
+
+def attention_allgather(q, k, v, peer_ptrs, rank: int, head_offset: int, causal: bool = True, sm_scale=None,
+                        stream=None):
+    """This rank's heads of causal (or full) attention, q, k, v [heads, n_ctx, 64] contiguous
+    CUDA float32 tensors, stored by the fused all-gather kernel into every rank's full output
+    ([all heads, n_ctx, 64] float32) at heads [head_offset, head_offset + heads).  `peer_ptrs`:
+    one device pointer per rank, valid in this process (PeerOutput.peer_ptrs), this rank's own
+    output at index `rank`.  Every rank must pass a barrier before reading the outputs."""
+    import ctypes as C
+
+    import torch
+
+    from .runtime.cuda import _lib
+    lib = _lib.lib()
+    heads, n, d = q.shape
+    for t in (q, k, v):
+        if not t.is_contiguous() or t.shape != (heads, n, d):
+            raise ValueError("q, k, v must be contiguous [heads, n_ctx, head_dim] tensors")
+    scale = float(sm_scale) if sm_scale is not None else 1.0 / float(d) ** 0.5
+    sd = n * d
+    a = _lib.AttentionArgs(q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, scale, sd, d, sd, d, 1, sd, d, sd, d, n, d,
+                           64, 64, -(-n // 64), heads, 1 if causal else 0, 1 if n % 64 == 0 else 0, 0, 0, 0, 0)
+    ws = lib.piton_b200_attention_workspace_size(C.byref(a))
+    key = (torch.cuda.current_device(), "attn_allgather_ws")
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < ws:
+        buf = torch.empty(max(ws, 1), dtype=torch.uint8, device="cuda")
+        _WS[key] = buf
+    a.workspace, a.workspace_bytes = buf.data_ptr(), ws
+    g = _lib.AllgatherArgs()
+    for r, p in enumerate(peer_ptrs):
+        g.peer_c[r] = p
+    g.world, g.rank, g.row_offset = len(peer_ptrs), rank, head_offset
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(lib.piton_b200_attention_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
+               "attention_allgather")
 
 
 def allgather_pieces(piece, out, stream=None):

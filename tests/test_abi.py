@@ -98,6 +98,39 @@ def test_argument_errors_need_no_gpu():
     assert lib.piton_b200_add_f32(C.byref(z), None) == _lib.OK
 
 
+def _attention_args(heads=2, n=128, stride_om=64):
+    sd = n * 64
+    return _lib.AttentionArgs(0, 0, 0, 0, 0.125, sd, 64, sd, 64, 1, sd, 64, sd, stride_om, n, 64, 64, 64, -(-n // 64),
+                              heads, 1, 1, 0, 0, 0, 0)
+
+
+def test_attention_allgather_argument_errors_need_no_gpu():
+    lib = _lib.lib()
+    f = lib.piton_b200_attention_allgather_f32
+    g = _lib.AllgatherArgs()
+    g.peer_c[0], g.peer_c[1] = 4096, 8192
+    g.world, g.rank = 2, 0
+    a = _attention_args()
+    assert f(C.byref(a), None, None) == _lib.EINVAL
+    g.world = 0
+    assert f(C.byref(a), C.byref(g), None) == _lib.EINVAL
+    g.world, g.rank = 2, 2
+    assert f(C.byref(a), C.byref(g), None) == _lib.EINVAL
+    g.rank, g.row_offset = 1, -1
+    assert f(C.byref(a), C.byref(g), None) == _lib.EINVAL
+    g.row_offset = 0
+    g.multicast_c = 4096                       # the attention all-gather has no multicast form
+    assert f(C.byref(a), C.byref(g), None) == _lib.ENOTSUP
+    g.multicast_c = 0
+    g.peer_c[1] = 8200                         # not 16-byte aligned
+    assert f(C.byref(a), C.byref(g), None) == _lib.EINVAL
+    g.peer_c[1] = 8192
+    odd = _attention_args(stride_om=66)         # rows must stay 16-byte aligned on every rank
+    assert f(C.byref(odd), C.byref(g), None) == _lib.EINVAL
+    none = _attention_args(heads=0)            # no heads: nothing to do
+    assert f(C.byref(none), C.byref(g), None) == _lib.OK
+
+
 def test_check_maps_status_codes():
     with pytest.raises(ValueError):
         _lib.check(_lib.lib().piton_b200_add_f32(None, None))

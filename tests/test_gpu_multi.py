@@ -168,3 +168,56 @@ def test_host_sharded_matmul_two_gpus():
         mp.spawn(_host_sharded_worker, args=(2, _port(), results), nprocs=2, join=True)
         res = dict(results)
     assert len(res) == 2 and all(e <= 4e-6 for e in res.values()), res
+
+
+def _attention_worker(rank, world, port, results):
+    import datetime
+
+    import torch.distributed as dist
+
+    from oracle import oracle as O
+    from piton_b200 import sharding
+    from piton_b200.runtime.cuda import _lib
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    out = None
+    try:
+        heads, n = 3, 320                              # per rank; the same seed on every rank
+        g = torch.Generator(device="cuda").manual_seed(11)
+        q, k, v = (torch.randn(world * heads, n, 64, device="cuda", generator=g) for _ in range(3))
+        h0 = rank * heads
+        out = sharding.PeerOutput(dist, world * heads * n * 64 * 4)
+        for _ in range(2):
+            sharding.attention_allgather(q[h0:h0 + heads].contiguous(), k[h0:h0 + heads].contiguous(),
+                                         v[h0:h0 + heads].contiguous(), out.peer_ptrs, rank, h0, causal=True)
+            torch.cuda.synchronize()
+            dist.barrier()
+        full = out.read(0, world * heads * n * 64 * 4).view(np.float32).reshape(world * heads, n, 64)
+        ref = O.attention_f64(q.cpu().numpy(), k.cpu().numpy(), v.cpu().numpy(), True)
+        import ctypes as C
+        st = C.c_int(-1)
+        _lib.lib().piton_b200_device_status(C.byref(st))
+        results[rank] = (float(np.abs(full - ref).max()), st.value)
+        dist.barrier()
+    finally:
+        if out is not None:
+            out.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allgather_attention_two_gpus():
+    """Every rank ends with all heads: its own stored by the softmax warps, the other rank's by
+    that rank's gather warp over NVLink."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_attention_worker, args=(2, _port(), results), nprocs=2, join=True)
+        res = dict(results)
+    assert len(res) == 2
+    for rank, (err, status) in res.items():
+        assert status == 0, rank
+        assert err <= 2e-5, (rank, err)
