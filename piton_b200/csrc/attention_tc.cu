@@ -29,6 +29,9 @@
 //     * warp 0 streams Q and the K tiles, warp 10 the V^T tiles, with TMA
 //       (128-byte swizzle; separate two-stage rings, since a K tile is free
 //       after S and a V tile only after P.V);
+//     * warp 11, only in the all-gather launch (384 threads), copies each item's
+//       stored rows from this rank's output to every other rank's (NVLink peer
+//       stores), one item behind the softmax warps;
 //     * warp 1 issues, from one thread, per 8-wide k-step one tf32 MMA of Q_hi
 //       against the stacked [K_hi; K_lo] tile (N = 128: Q_hi K_hi in columns
 //       0-63, Q_hi K_lo in 64-127), and per 16-wide k-step one bf16 MMA of
