@@ -345,7 +345,7 @@ def bench_attention(torch, D, args, lib_calls):
         mine = peer.read(h0 * sd * 4, 64 * AT_D * 4).view(np.float32).reshape(64, AT_D)
         err = max(err, float(np.abs(mine - ref.cpu().numpy()).max()))
         sums = [None] * D.world
-        D.pg.all_gather_object(sums, float(np.abs(mine.astype(np.float64)).sum()))
+        D.pg.all_gather_object(sums, float(np.abs(mine.ravel().astype(np.float64)).sum()))
         nxt = (D.rank + 1) % D.world
         theirs = peer.read(nxt * hloc * sd * 4, 64 * AT_D * 4).view(np.float32)
         if float(np.abs(theirs.astype(np.float64)).sum()) != sums[nxt]:
