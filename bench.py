@@ -587,6 +587,13 @@ def cpu_baseline_matmul(rows: int, threads: int):
     return 2.0 * rows * MM * MM / sec / 1e12, sec
 
 
+def sample_rows(seconds: float, rate_tflops: float, threads: int) -> int:
+    """Rows of the 8192^3 product that take about `seconds` at `rate_tflops`, a whole number per
+    thread (at least one, at most all 8192)."""
+    rows = int(seconds * rate_tflops * 1e12 / (2.0 * MM * MM)) // threads * threads
+    return max(threads, min(MM, rows))
+
+
 def cpu_baselines_secondary(threads: int) -> dict:
     """The oracle's restatements of the reference's CPU path for the other operators, each on a
     bounded sample of its benchmark workload (a few seconds in all), reported beside the B200
@@ -640,10 +647,11 @@ def run_reference(args):
     if D.rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    # calibrate on a 2-row sample, then size each step to ~min(10 s, 120 s / steps)
-    rate, _ = cpu_baseline_matmul(2, threads)
+    # calibrate on one row per thread (the oracle splits rows over threads), then size each step to
+    # ~min(10 s, 120 s / steps) in whole rows per thread
+    rate, _ = cpu_baseline_matmul(threads, threads)
     per_step = min(10.0, 120.0 / max(1, args.steps))
-    rows = max(1, min(MM, int(per_step * rate * 1e12 / (2.0 * MM * MM))))
+    rows = sample_rows(per_step, rate, threads)
     for _ in range(max(0, min(args.warmup, 1))):
         cpu_baseline_matmul(max(1, rows // 4), threads)
     vals, t_all = [], 0.0
@@ -817,8 +825,8 @@ def main():
     line["clocks"] = sampler.summary()
     if "matmul" in ops and D.world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
-        rate, _ = cpu_baseline_matmul(2, threads)
-        rows = max(1, min(MM, int(15.0 * rate * 1e12 / (2.0 * MM * MM))))
+        rate, _ = cpu_baseline_matmul(threads, threads)   # one row per thread: the calibration
+        rows = sample_rows(15.0, rate, threads)
         v, s = cpu_baseline_matmul(rows, threads)
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                 "sample": f"{rows} of {MM} rows of the {MM}^3 product ({s:.1f} s): the oracle's "
