@@ -124,9 +124,12 @@ PITON_B200_API int piton_b200_matmul_f32(const piton_matmul_args *args, void *st
    by another allocator's pool).  It has no counterpart in the reference.  The tensor-core path's scratch comes from one static device
    array of PITON_B200_NOALLOC_SCRATCH_BYTES inside this library (held by every GPU that loads
    it, until exit) instead of args->workspace, which is ignored; the call allocates nothing.
-   Problems whose scratch would exceed that size are rejected with PITON_B200_EINVAL.  The first
-   call on a device looks the array's address up (cudaGetSymbolAddress), so make it before any
-   stream capture.  All calls share the array: calls that overlap on the GPU race. */
+   Only tensor-core-path problems whose scratch would exceed that size are rejected, with
+   PITON_B200_EINVAL; problems that take the CUDA-core path (QPU rounding, FORCE_SIMT, a partial
+   grid, M or N below 128) need no scratch and run at any size.  The first call in a CUDA context
+   on a device looks the array's address up (cudaGetSymbolAddress; again after cudaDeviceReset),
+   so make it before any stream capture.  All calls share the array: calls that overlap on the
+   GPU race. */
 #define PITON_B200_NOALLOC_SCRATCH_BYTES (32u << 20)
 PITON_B200_API int piton_b200_matmul_f32_noalloc(const piton_matmul_args *args, void *stream);
 

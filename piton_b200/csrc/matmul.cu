@@ -104,22 +104,34 @@ extern "C" int piton_b200_dense_f32(const piton_dense_args *a, void *stream) {
 // every GPU that loads this library keeps it until the process exits.
 //
 // In host code `g_matmul_scratch` names a host-side stand-in, not a device
-// address, so the device address is looked up with cudaGetSymbolAddress once
-// per device (with that device current) on the first call there, and cached.
-// That first call should therefore come before any stream capture.  Every
-// call shares the array and it keeps the last call's contents; nothing in it
-// needs to start at zero (the split kernel writes every element the GEMM
-// reads).  Calls that overlap on the GPU (other streams, other host threads
-// on the same device) race on it and must be serialised by the caller.
+// address, so the device address is looked up with cudaGetSymbolAddress (with
+// the device current) the first time a call runs in a CUDA context, and cached
+// under that context's process-unique id (cuCtxGetId).  A later call in a new
+// context on the same device (after cudaDeviceReset, or with another context
+// made current) sees a different id and looks the address up again, so no
+// stale address is ever used.  A call that does the look-up should come before
+// any stream capture.  Every call shares the array and it keeps the last
+// call's contents; nothing in it needs to start at zero (the split kernel
+// writes every element the GEMM reads).  Calls that overlap on the GPU (other
+// streams, other host threads on the same device) race on it and must be
+// serialised by the caller.
 // ---------------------------------------------------------------------------
 
+#include <cuda.h>
 #include <mutex>
 
 static __device__ __align__(256) uint8_t g_matmul_scratch[PITON_B200_NOALLOC_SCRATCH_BYTES];
 
+static bool current_context_id(unsigned long long *id) {
+    CUcontext ctx = nullptr;
+    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+    return cuCtxGetId(ctx, id) == CUDA_SUCCESS;
+}
+
 static void *noalloc_scratch(int *rc) {
     static std::mutex mu;
     static void *ptrs[64] = {nullptr};
+    static unsigned long long ctx_ids[64] = {0};
     int dev = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) {
@@ -131,14 +143,21 @@ static void *noalloc_scratch(int *rc) {
         return nullptr;
     }
     std::lock_guard<std::mutex> lock(mu);
-    if (!ptrs[dev]) {
+    unsigned long long id = 0;
+    bool have_id = current_context_id(&id);   // false before the runtime has made a context current
+    if (!have_id || !ptrs[dev] || ctx_ids[dev] != id) {
         void *p = nullptr;
-        err = cudaGetSymbolAddress(&p, g_matmul_scratch);
+        err = cudaGetSymbolAddress(&p, g_matmul_scratch);   // also makes the primary context current
         if (err != cudaSuccess) {
             *rc = set_error(PITON_B200_ECUDA, "cudaGetSymbolAddress(scratch): %s", cudaGetErrorString(err));
             return nullptr;
         }
+        if (!current_context_id(&id)) {
+            *rc = set_error(PITON_B200_ECUDA, "no current CUDA context after cudaGetSymbolAddress");
+            return nullptr;
+        }
         ptrs[dev] = p;
+        ctx_ids[dev] = id;
     }
     *rc = PITON_B200_OK;
     return ptrs[dev];

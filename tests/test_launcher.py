@@ -1,6 +1,6 @@
 """The launch surface without a GPU: binding rules (piton/runtime/launcher.py:25-63),
 device dispatch (:238-244), the registry, the accessed-extent checks and the
-reference's own JITFunction objects (when a reference checkout is present)."""
+reference's own JITFunction objects (when PITON_REFERENCE names a reference checkout)."""
 
 import os
 import sys
@@ -77,16 +77,21 @@ def test_extent():
     assert cuda.extent((0, 5)) == (0, -1)
 
 
-@pytest.mark.skipif(not os.path.isdir("/root/reference/examples"), reason="reference checkout not present")
+REF = os.environ.get("PITON_REFERENCE", "")
+
+
+@pytest.mark.skipif(not (REF and os.path.isdir(os.path.join(REF, "examples"))),
+                    reason="PITON_REFERENCE (a reference checkout) is not set")
 def test_reference_jit_functions_match_the_registry():
-    sys.path.insert(0, "/root/reference")
-    sys.path.insert(0, "/root/reference/examples")
+    examples = os.path.join(REF, "examples")
+    sys.path.insert(0, REF)
+    sys.path.insert(0, examples)
     try:
         import kernels as ref_kernels
         import nn_kernels as ref_nn
     finally:
-        sys.path.remove("/root/reference/examples")
-        sys.path.remove("/root/reference")
+        sys.path.remove(examples)
+        sys.path.remove(REF)
     reg = dict.fromkeys(cuda.registered())
     for k in (ref_kernels.add_kernel, ref_kernels.matmul_kernel, ref_kernels.softmax_kernel,
               ref_nn.dense_layer_kernel):

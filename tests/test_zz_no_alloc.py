@@ -4,10 +4,13 @@ Callers that cannot allocate device memory (fixed-budget hosts, plugin hosts
 that own every allocation) get the tensor-core matmul with its scratch taken
 from a static device array inside the library.  This test calls it through
 the C-ABI and checks it against the ordinary entry point (which takes a
-caller-provided workspace) on two calls in a row, within the tolerance the
-matmul tests use; both run the same kernels, so the results are expected to
-be identical bit for bit.  It also checks that problems too large for the
-static array are refused with an error instead of running.
+caller-provided workspace) on three calls in a row (the last smaller than
+the one before it, so leftovers in the shared array would show), within the
+tolerance the matmul tests use; both run the same kernels, so the results are
+expected to be identical bit for bit.  It also runs the CUDA-core branch
+(which needs no scratch) through the same entry point, and checks that
+problems too large for the static array are refused with an error instead of
+running.
 
 The file is named to be collected last, so a run that stops at the first
 failure has already run every other test.
@@ -40,7 +43,9 @@ def test_noalloc_matches_workspace_entry_point(cuda):
     from piton_b200.runtime.cuda import _lib
     lib = _lib.lib()
     stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
-    for call, (M, N, K) in enumerate([(1024, 768, 1000), (1100, 1300, 1024)]):
+    # the third call is smaller than the second: bytes the larger call left in the shared array
+    # must never reach C
+    for call, (M, N, K) in enumerate([(1024, 768, 1000), (1100, 1300, 1024), (256, 384, 512)]):
         g = torch.Generator(device="cuda").manual_seed(77 + call)
         A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
         B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
@@ -75,3 +80,32 @@ def test_noalloc_refuses_problems_beyond_its_scratch(cuda):
     assert b"scratch" in lib.piton_b200_last_error()
     torch.cuda.synchronize()
     assert bool((out == 5.0).all())
+
+
+@pytest.mark.parametrize("shape,flags", [((40, 70, 36), 0), ((256, 256, 256), "FORCE_SIMT")])
+def test_noalloc_cuda_core_branch_matches(cuda, shape, flags):
+    """Shapes under 128 and the FORCE_SIMT flag take the CUDA-core path, which uses no scratch: the
+    no-alloc entry point hands them to the ordinary one with the workspace cleared, so a garbage
+    workspace pointer in the caller's args is never used and the result is the same bits."""
+    torch = cuda
+    from piton_b200.runtime.cuda import _lib
+    lib = _lib.lib()
+    M, N, K = shape
+    fl = getattr(_lib, flags) if flags else 0
+    stream = C.c_void_p(torch.cuda.current_stream().cuda_stream)
+    g = torch.Generator(device="cuda").manual_seed(5)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    ref_c = torch.empty(M, N, device="cuda")
+    ra = _args(_lib, A, B, ref_c, M, N, K)
+    ra.flags = fl
+    assert lib.piton_b200_matmul_workspace_size(C.byref(ra)) == 0
+    _lib.check(lib.piton_b200_matmul_f32(C.byref(ra), stream))
+    out = torch.full((M, N), float("nan"), device="cuda")
+    na = _args(_lib, A, B, out, M, N, K)
+    na.flags = fl
+    na.workspace, na.workspace_bytes = 0xDEAD0000, 1 << 40     # never dereferenced
+    _lib.check(lib.piton_b200_matmul_f32_noalloc(C.byref(na), stream))
+    torch.cuda.synchronize()
+    assert _status(lib) == 0
+    assert torch.equal(out, ref_c)
