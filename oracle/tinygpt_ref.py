@@ -38,8 +38,23 @@ def _gelu(x):
 
 def generate(weights: dict, prompts: np.ndarray, new_tokens: int, tie_margin: float = 1e-4):
     """Returns (tokens [B, P+new], last logits [B, 65], first_near_tie_step [B] (-1: none))."""
+    return _decode(weights, np.asarray(prompts), new_tokens, tie_margin, None)
+
+
+def teacher_forced_logits(weights: dict, tokens: np.ndarray, prompt_len: int) -> np.ndarray:
+    """The logits this model gives for every generated step when it is fed `tokens` [B, T]
+    (tokens a decode produced, the prompt in [:, :prompt_len]) instead of its own choices:
+    [B, T - prompt_len, 65], entry t being the logits at position prompt_len - 1 + t, the ones
+    that chose tokens[:, prompt_len + t].  Judges every step of another implementation's greedy
+    decode, also after a near tie where the two decodes may part."""
+    tokens = np.asarray(tokens)
+    steps = []
+    _decode(weights, tokens[:, :prompt_len], tokens.shape[1] - prompt_len, 0.0, tokens, steps)
+    return np.stack(steps, 1) if steps else np.zeros((tokens.shape[0], 0, VOCAB))
+
+
+def _decode(weights, prompts, new_tokens, tie_margin, forced, step_logits=None):
     W = {k: np.asarray(v, np.float64) for k, v in weights.items()}
-    prompts = np.asarray(prompts)
     B, P = prompts.shape
     toks = np.zeros((B, P + new_tokens), np.int64)
     toks[:, :P] = prompts
@@ -73,5 +88,7 @@ def generate(weights: dict, prompts: np.ndarray, new_tokens: int, tie_margin: fl
             top2 = np.sort(logits, 1)[:, -2:]
             tie = (top2[:, 1] - top2[:, 0]) < tie_margin
             near = np.where((near < 0) & tie, pos + 1, near)
-            toks[:, pos + 1] = np.argmax(logits, 1)
+            toks[:, pos + 1] = np.argmax(logits, 1) if forced is None else forced[:, pos + 1]
+            if step_logits is not None:
+                step_logits.append(logits)
     return toks.astype(np.int32), logits, near

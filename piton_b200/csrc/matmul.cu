@@ -122,10 +122,27 @@ extern "C" int piton_b200_dense_f32(const piton_dense_args *a, void *stream) {
 
 static __device__ __align__(256) uint8_t g_matmul_scratch[PITON_B200_NOALLOC_SCRATCH_BYTES];
 
+// The driver functions are reached through cudaGetDriverEntryPoint, so the library keeps no
+// link-time dependency on libcuda (it must load on machines without a driver, for its CPU tests).
 static bool current_context_id(unsigned long long *id) {
+    typedef CUresult (*get_current_t)(CUcontext *);
+    typedef CUresult (*get_id_t)(CUcontext, unsigned long long *);
+    static get_current_t get_current = nullptr;
+    static get_id_t get_id = nullptr;
+    if (!get_current || !get_id) {
+        void *p1 = nullptr, *p2 = nullptr;
+        cudaDriverEntryPointQueryResult q1, q2;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p1, cudaEnableDefault, &q1) != cudaSuccess ||
+            q1 != cudaDriverEntryPointSuccess ||
+            cudaGetDriverEntryPoint("cuCtxGetId", &p2, cudaEnableDefault, &q2) != cudaSuccess ||
+            q2 != cudaDriverEntryPointSuccess)
+            return false;
+        get_current = reinterpret_cast<get_current_t>(p1);
+        get_id = reinterpret_cast<get_id_t>(p2);
+    }
     CUcontext ctx = nullptr;
-    if (cuCtxGetCurrent(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
-    return cuCtxGetId(ctx, id) == CUDA_SUCCESS;
+    if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return false;
+    return get_id(ctx, id) == CUDA_SUCCESS;
 }
 
 static void *noalloc_scratch(int *rc) {

@@ -35,6 +35,41 @@ def gather(dist, out, piece):
     return out
 
 
+def batch_piece(batch, world: int, rank: int):
+    """This rank's rows of a batch (numpy [n, ...]): the equal piece of ceil(n / world) rows
+    starting at rank * ceil(n / world), with zero rows past the end of the batch (a zero image, a
+    prompt of token 0), so that every rank runs the same shape.  Returns (piece, start)."""
+    import numpy as np
+    batch = np.asarray(batch)
+    start, per = shard(batch.shape[0], world, rank)
+    piece = np.zeros((per,) + batch.shape[1:], batch.dtype)
+    mine = batch[start:start + per]
+    piece[:len(mine)] = mine
+    return piece, start
+
+
+def run_batch_sharded(dist, fn, batch):
+    """Data parallelism over independent batch rows, the sharding of the digits MLP's predict
+    (examples/digits_model.py:137-139 runs every image through the same forward) and of
+    batched TinyGPT decoding: each rank runs ``fn(piece)`` -> a torch tensor with one row per
+    piece row on its own rows, the pieces are all-gathered and the first n rows (the whole
+    batch's result, in batch order) are returned on every rank."""
+    import torch
+    world = dist.get_world_size() if dist is not None and dist.is_initialized() else 1
+    rank = dist.get_rank() if world > 1 else 0
+    n = len(batch)
+    piece, _ = batch_piece(batch, world, rank)
+    res = fn(piece)
+    if not isinstance(res, torch.Tensor):
+        res = torch.as_tensor(res)
+    if res.shape[0] != piece.shape[0]:
+        raise ValueError(f"fn returned {res.shape[0]} rows for a piece of {piece.shape[0]}")
+    res = res.contiguous()
+    out = torch.empty((res.shape[0] * world,) + tuple(res.shape[1:]), dtype=res.dtype, device=res.device)
+    gather(dist, out, res)
+    return out[:n]
+
+
 def max_over_ranks(dist, value: float, device=None) -> float:
     """The maximum of a per-rank float (a timing) over all ranks."""
     if dist is None or not dist.is_initialized() or dist.get_world_size() == 1:

@@ -379,6 +379,95 @@ def case_tinygpt(fp, procs, big):
     save(name, meta, prompt=prompt.astype(np.int32), logits=logits)
 
 
+def case_tinygpt_decode(fp, procs, big):
+    """TinyGPT greedy decoding composed from the reference's own kernels on its emulator, the
+    way the B200 decode runs it: a prefill of a 16-token prompt, then 4 greedy steps that each
+    feed one new token through every layer (dense_layer_kernel on that row only; the K and V
+    rows of earlier positions are the emulator's own outputs from earlier steps, a KV cache)
+    with attn_fwd_kernel over all positions so far, of which the new row is kept.  The
+    embeddings, LayerNorm gain and bias, GELU, residual adds and the argmax run on the host in
+    float32.  Records the prompt, the 4 greedy tokens and the logits that chose each of them;
+    pins the float64 host model and the B200 decode beyond the prefill."""
+    from nn_kernels import dense_layer_kernel, dense_tiles
+    import attention as A
+    import math
+    import piton.compiler as pc
+    from piton.runtime.launcher import run_emulator
+    sys.path.insert(0, os.path.join(_STATE["ref"], "tests"))
+    import test_reroll_reduce as RR
+    from piton_b200 import tinygpt
+    plen, steps, seed = 16, 4, 0
+    name = f"tinygpt_emu_decode_p{plen}_n{steps}_seed{seed}"
+    if exists(name):
+        return
+    t = time.time()
+    w = tinygpt.init_weights(seed)
+    prompt = tinygpt.random_prompts(1, seed=7, length=plen)[0]
+    f32 = np.float32
+    d, nh = tinygpt.D_MODEL, tinygpt.N_HEAD
+    hd = d // nh
+
+    def ln(v, g, b):
+        rows = v.shape[0]
+        sig = {"x_ptr": "*fp32", "out_ptr": "*fp32", "n": "i32", "eps": "fp32"}
+        ck = pc.compile(RR.layernorm_kernel, sig, {"BLOCK": d}, grid=(rows,), num_stages=2)
+        y = np.zeros_like(v)
+        run_emulator(ck, (rows,), dict(x_ptr=np.ascontiguousarray(v), out_ptr=y, n=d, eps=1e-5))
+        return (y * g + b).astype(f32)
+
+    def dense(v, wm, b):
+        return _run_dense(pc, run_emulator, dense_layer_kernel, dense_tiles, np.ascontiguousarray(v, f32),
+                          np.ascontiguousarray(wm, f32), np.ascontiguousarray(b, f32), True, False)
+
+    def heads(m):   # [S, 128] -> [4, S, 32]
+        return np.ascontiguousarray(m.reshape(m.shape[0], nh, -1).transpose(1, 0, 2))
+
+    def attend(q, k, v):   # all positions so far, [S, 128] each -> [S, 128]
+        n = q.shape[0]
+        consts = dict(HEAD_DIM=hd, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=n % 16 == 0,
+                      **A.contiguous_strides(hd, "nd", n))
+        asig = A.signature_for(consts)
+        qh, kh, vh = heads(q), heads(k), heads(v)
+        vals = dict(Q=qh, K=kh, V=vh, Out=np.zeros_like(qh), sm_scale=float(1 / np.sqrt(hd)), N_CTX=n,
+                    stride_qh=n * hd, stride_kh=n * hd, stride_vh=n * hd, stride_oh=n * hd)
+        vals = {key: val for key, val in vals.items() if key in asig}
+        att = run_split(A.attn_fwd_kernel, (-(-n // 2), nh), asig, consts, vals, "Out", procs)
+        return np.ascontiguousarray(att.reshape(nh, n, hd).transpose(1, 0, 2).reshape(n, d))
+
+    cache = [{"q": np.zeros((0, d), f32), "k": np.zeros((0, d), f32), "v": np.zeros((0, d), f32)}
+             for _ in range(tinygpt.N_LAYER)]
+
+    def feed(tokens, start):
+        """Feed `tokens` at positions start.. through every layer; the logits of the last one."""
+        x = (w["wte"][tokens] + w["wpe"][start:start + len(tokens)]).astype(f32)
+        for layer in range(tinygpt.N_LAYER):
+            p = {k: w[f"h{layer}.{k}"] for k, _ in tinygpt.LAYER_TENSORS}
+            c = cache[layer]
+            qkv = dense(ln(x, p["ln1_g"], p["ln1_b"]), p["w_qkv"], p["b_qkv"])
+            c["q"] = np.concatenate([c["q"], qkv[:, :d]])
+            c["k"] = np.concatenate([c["k"], qkv[:, d:2 * d]])
+            c["v"] = np.concatenate([c["v"], qkv[:, 2 * d:]])
+            att = attend(c["q"], c["k"], c["v"])[start:]
+            x = (x + dense(att, p["w_o"], p["b_o"])).astype(f32)
+            fpre = dense(ln(x, p["ln2_g"], p["ln2_b"]), p["w_fc"], p["b_fc"]).astype(np.float64)
+            gelu = (0.5 * fpre * (1.0 + np.vectorize(math.erf)(fpre / math.sqrt(2.0)))).astype(f32)
+            x = (x + dense(gelu, p["w_pr"], p["b_pr"])).astype(f32)
+        hf = ln(x[-1:], w["lnf_g"], w["lnf_b"])
+        return dense(hf, np.ascontiguousarray(w["wte"].T), np.zeros(tinygpt.VOCAB, f32))[0]
+
+    logits = [feed(prompt, 0)]
+    tokens = []
+    for step in range(steps):
+        tokens.append(int(np.argmax(logits[-1])))          # first maximum, like the decode
+        if step + 1 < steps:
+            logits.append(feed(np.array([tokens[-1]]), plen + step))
+    logits = np.stack(logits).astype(f32)
+    top2 = np.sort(logits, 1)[:, -2:]
+    meta = dict(op="tinygpt_decode", prompt_len=plen, new_tokens=steps, weight_seed=seed, prompt_seed=7, ref=fp,
+                min_top2_margin=float((top2[:, 1] - top2[:, 0]).min()), emu_seconds=time.time() - t)
+    save(name, meta, prompt=prompt.astype(np.int32), tokens=np.array(tokens, np.int32), logits=logits)
+
+
 def case_idiv(fp, procs, big):
     import piton
     from primitive_kernels import idiv_kernel
@@ -457,7 +546,7 @@ def main():
     ap.add_argument("--procs", type=int, default=os.cpu_count() or 1)
     ap.add_argument("--big", action="store_true", help="also the multi-minute configuration sizes")
     ap.add_argument("--only", default="", help="comma list of add,softmax,matmul,dense,attention,idiv,life,elem,"
-                                               "tinygpt")
+                                               "tinygpt,tinygpt_decode")
     args = ap.parse_args()
     if not args.ref or not os.path.isdir(args.ref):
         sys.exit("--ref must point at a PIton checkout")
@@ -469,7 +558,8 @@ def main():
     only = set(filter(None, args.only.split(",")))
     for name, fn in (("add", case_add), ("softmax", case_softmax), ("matmul", case_matmul),
                      ("dense", case_dense), ("attention", case_attention), ("idiv", case_idiv), ("life", case_life),
-                     ("elem", case_elem), ("tinygpt", case_tinygpt)):
+                     ("elem", case_elem), ("tinygpt", case_tinygpt),
+                     ("tinygpt_decode", case_tinygpt_decode)):
         if not only or name in only:
             fn(fp, args.procs, args.big)
 

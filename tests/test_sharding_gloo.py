@@ -119,3 +119,57 @@ def test_attention_allgather_rejects_mismatched_shards():
         sharding.attention_allgather(q, torch.zeros(3, 64, 64), q, [0, 0], 0, 0)
     with pytest.raises(ValueError):
         sharding.attention_allgather(q, q.transpose(1, 2), q, [0, 0], 0, 0)
+
+
+def _batch_worker(rank, world, port, results):
+    """Each rank classifies / decodes only its piece of the batch with the oracle's host models
+    and the gathered result must be the single-process one, row for row."""
+    from oracle import oracle as O
+    from oracle import tinygpt_ref
+    from piton_b200 import tinygpt, workloads as W
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        images, model = W.digits_images(1797, 0), W.digits_model(0)
+        pred = sharding.run_batch_sharded(
+            dist, lambda piece: torch.from_numpy(np.argmax(O.qpu_mlp(piece, model)[:, :10], 1)), images)
+        w = tinygpt.init_weights(0)
+        prompts = tinygpt.random_prompts(256, seed=100)
+        toks = sharding.run_batch_sharded(
+            dist, lambda piece: torch.from_numpy(tinygpt_ref.generate(w, piece, tinygpt.NEW_TOKENS)[0]), prompts)
+        results[rank] = (pred.numpy().tolist(), toks.numpy().tolist())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_gloo_batch_sharding_of_mlp_and_tinygpt():
+    """The digits predict (1797 images, the last rank's piece padded with zero images) and a
+    256-sequence TinyGPT greedy decode, sharded by batch over two gloo ranks: the gathered
+    argmax and tokens equal the single-process result exactly, on both ranks."""
+    from oracle import oracle as O
+    from oracle import tinygpt_ref
+    from piton_b200 import tinygpt, workloads as W
+    images, model = W.digits_images(1797, 0), W.digits_model(0)
+    want_pred = np.argmax(O.qpu_mlp(images, model)[:, :10], 1)
+    w = tinygpt.init_weights(0)
+    want_toks = tinygpt_ref.generate(w, tinygpt.random_prompts(256, seed=100), tinygpt.NEW_TOKENS)[0]
+    world = 2
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_batch_worker, args=(world, _free_port(), results), nprocs=world, join=True)
+        res = dict(results)
+    assert sorted(res) == [0, 1]
+    for rank, (pred, toks) in res.items():
+        np.testing.assert_array_equal(np.array(pred), want_pred, err_msg=f"rank {rank}")
+        np.testing.assert_array_equal(np.array(toks), want_toks, err_msg=f"rank {rank}")
+
+
+def test_batch_piece_pads_the_last_rank():
+    batch = np.arange(10 * 3).reshape(10, 3)
+    p0, s0 = sharding.batch_piece(batch, 4, 0)
+    p3, s3 = sharding.batch_piece(batch, 4, 3)
+    assert (s0, s3) == (0, 9) and p0.shape == p3.shape == (3, 3)
+    np.testing.assert_array_equal(p3[0], batch[9])
+    assert not p3[1:].any()
+    one, _ = sharding.batch_piece(batch, 1, 0)
+    np.testing.assert_array_equal(one, batch)
