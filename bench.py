@@ -44,11 +44,64 @@ sys.path.insert(0, REPO)
 
 METRIC = "fp32 matmul TFLOPS + softmax/attn GB/s vs roofline at 1/2/4/8 B200"
 MM = 8192
-GEMM_TRAFFIC_8192 = 6.849e9 + 268.0e6   # bytes per launch (ncu, 1 B200)
 SM_M, SM_N = 32768, 16384
 AT_B, AT_H, AT_S, AT_D = 32, 32, 4096, 64
 ADD_N = 1 << 28
 ATTN_BH = AT_B * AT_H
+
+
+def profiled_traffic(name: str):
+    """DRAM bytes of one launch (dram__bytes_read.sum + dram__bytes_write.sum) from the single-pass
+    ncu capture summarised in profiles/<name>.md, whose line 'traffic per launch: <bytes> bytes
+    (<units> ...)' gives the bytes and the units the captured launch processed: (bytes, units), or
+    None when the summary is absent.  The capture is of an earlier run of the same kernel, not of
+    this run; the bench line says so."""
+    import re
+    try:
+        with open(os.path.join(REPO, "profiles", name + ".md")) as f:
+            for line in f:
+                m = re.match(r"traffic per launch: ([0-9.eE+]+) bytes \(([0-9.eE+]+) ", line.strip())
+                if m:
+                    return float(m.group(1)), float(m.group(2))
+    except OSError:
+        pass
+    return None
+
+
+def traffic_for(name: str, units: float):
+    """The profiled DRAM bytes per launch of `name`, scaled to a launch of `units` (traffic of these
+    streaming kernels grows in proportion to the units processed)."""
+    t = profiled_traffic(name)
+    if t is None:
+        return None, None
+    b, u = t
+    return b * units / u, f"ncu capture in profiles/{name}.md ({u:g} units; scaled to {units:g})" if u != units \
+        else f"ncu capture in profiles/{name}.md"
+
+
+def roofline(bound: str, achieved: float, peak: float, unit: str, traffic=None, traffic_source=None, **extra):
+    r = {"bound": bound, "achieved": achieved, "peak": peak, "unit": unit, "frac": achieved / peak if peak else None,
+         "traffic": traffic}
+    if traffic_source:
+        r["traffic_source"] = traffic_source
+    r.update(extra)
+    return r
+
+
+def timed_e2e(torch, D, step, steps, warmup=1):
+    """Seconds per step (max over ranks) of `step`, a call through the public API with host
+    buffers; it returns the launch stats ({'h2d_bytes', 'd2h_bytes'})."""
+    for _ in range(warmup):
+        st = step()
+    D.barrier(torch)
+    s = torch.cuda.current_stream()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(s)
+    for _ in range(steps):
+        st = step()
+    e1.record(s)
+    e1.synchronize()
+    return D.max(torch, e0.elapsed_time(e1) / 1e3 / steps), st
 
 
 def load_peaks():
@@ -254,7 +307,7 @@ def bench_matmul(torch, D, args, lib_calls):
 def bench_softmax(torch, D, args, lib_calls):
     from piton_b200.kernels import softmax_kernel
     r0, mloc = shard(SM_M, D.world, D.rank)
-    x = torch.randn(mloc, SM_N, device="cuda") * 4
+    x = softmax_rows(torch, mloc, SM_N, 7 + D.rank)
     y = torch.empty_like(x)
     yfull = torch.empty(SM_M, SM_N, device="cuda") if D.world > 1 else y
     from piton_b200.runtime.cuda import _lib
@@ -276,9 +329,31 @@ def bench_softmax(torch, D, args, lib_calls):
     lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     ref = torch.softmax(x[:8].double(), 1)
     err = float(((y[:8].double() - ref).abs() / ref.abs().clamp_min(1e-37)).max())
-    _ = softmax_kernel
+    del x, y, yfull
+    e2e = None
+    if not args.no_e2e:
+        # the public launch with pinned host arrays: the rank's rows in, its rows out
+        from piton_b200.runtime.cuda import pinned_empty
+        xh, yh = pinned_empty((mloc, SM_N)), pinned_empty((mloc, SM_N))
+        torch.from_numpy(xh).copy_(softmax_rows(torch, mloc, SM_N, 7 + D.rank))
+        launch = softmax_kernel[(mloc,)]
+        sec, st = timed_e2e(torch, D, lambda: launch(yh, xh, SM_N, SM_N, SM_N, BLOCK_SIZE=SM_N,
+                                                     device="b200").last_stats, max(2, args.steps // 10))
+        lib_calls["launches"] += max(2, args.steps // 10) + 1
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        del xh, yh
     return {"bytes": 8.0 * SM_M * SM_N, "t_step": t_step, "t_kernel": t_kernel, "err": err,
-            "local_bytes": 8.0 * mloc * SM_N}
+            "local_bytes": 8.0 * mloc * SM_N, "e2e": e2e}
+
+
+def softmax_rows(torch, rows, cols, seed):
+    """normal(0, 1) * 4 with 1 % of each row's entries set to -inf (never a whole row), the
+    configuration's value distribution, generated on the device."""
+    g = torch.Generator(device="cuda").manual_seed(seed)
+    x = torch.randn(rows, cols, device="cuda", generator=g) * 4
+    mask = torch.rand(rows, cols, device="cuda", generator=g) < 0.01
+    mask[:, 0] = False
+    return x.masked_fill_(mask, float("-inf"))
 
 
 def bench_attention(torch, D, args, lib_calls):
@@ -353,8 +428,25 @@ def bench_attention(torch, D, args, lib_calls):
         D.pg.barrier()
         peer.close()
     flops = 4.0 * BH * AT_S * AT_S * AT_D * 0.5
+    e2e = None
+    if not args.no_e2e:
+        # the public launch with pinned host arrays: the rank's heads of Q, K, V in, of O out
+        from piton_b200.kernels import attn_fwd_kernel
+        from piton_b200.runtime.cuda import pinned_empty
+        hq, hk, hv, ho = (pinned_empty((hloc, AT_S, AT_D)) for _ in range(4))
+        for h_, d_ in ((hq, q), (hk, k), (hv, v)):
+            torch.from_numpy(h_).copy_(d_)
+        del q, k, v, o, ofull, wbuf
+        launch = attn_fwd_kernel[(AT_S // 2, hloc)]
+        sm = float(1.0 / np.sqrt(AT_D))
+        sec, st = timed_e2e(torch, D, lambda: launch(hq, hk, hv, ho, sm, sd, AT_D, sd, AT_D, 1, sd, AT_D, sd, AT_D, AT_S,
+                                                     HEAD_DIM=AT_D, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=True,
+                                                     device="b200").last_stats, 2)
+        lib_calls["launches"] += 3 * per_call
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        del hq, hk, hv, ho
     return {"flops": flops, "bytes": 16.0 * BH * AT_S * AT_D, "t_step": t_step, "t_kernel": t_kernel, "err": err,
-            "local_flops": flops * hloc / BH, "tc": ws > 0, "fused": fused}
+            "local_flops": flops * hloc / BH, "tc": ws > 0, "fused": fused, "e2e": e2e, "heads_local": hloc}
 
 
 def bench_add(torch, D, args, lib_calls):
@@ -362,7 +454,9 @@ def bench_add(torch, D, args, lib_calls):
     from piton_b200.runtime.cuda import _lib
     from piton_b200.runtime.cuda._lib import lib
     n0, nloc = shard(ADD_N, D.world, D.rank)
-    x, y = torch.rand(nloc, device="cuda"), torch.rand(nloc, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(11 + D.rank)
+    x = torch.rand(nloc, device="cuda", generator=g) * 2 - 1          # U[-1, 1], the configuration's inputs
+    y = torch.rand(nloc, device="cuda", generator=g) * 2 - 1
     out = torch.empty_like(x)
     ofull = torch.empty(ADD_N, device="cuda") if D.world > 1 else out
     a = _lib.AddArgs(x.data_ptr(), y.data_ptr(), out.data_ptr(), nloc, 1024, (nloc + 1023) // 1024, 0, 0)
@@ -380,14 +474,35 @@ def bench_add(torch, D, args, lib_calls):
     t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
     lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     err = float((out[:1 << 20] - (x[:1 << 20] + y[:1 << 20])).abs().max())
-    return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc}
+    e2e = None
+    if not args.no_e2e:
+        from piton_b200.kernels import add_kernel
+        from piton_b200.runtime.cuda import pinned_empty
+        xh, yh, oh = pinned_empty((nloc,)), pinned_empty((nloc,)), pinned_empty((nloc,))
+        torch.from_numpy(xh).copy_(x)
+        torch.from_numpy(yh).copy_(y)
+        del x, y, out, ofull
+        launch = add_kernel[((nloc + 1023) // 1024,)]
+        k = max(2, args.steps // 10)
+        sec, st = timed_e2e(torch, D, lambda: launch(xh, yh, oh, nloc, BLOCK_SIZE=1024, device="b200").last_stats, k)
+        lib_calls["launches"] += k + 1
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        del xh, yh, oh
+    return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc,
+            "e2e": e2e}
 
 
 def bench_tinygpt(torch, D, args, lib_calls, batch):
-    from piton_b200 import tinygpt
+    """Greedy decode of `batch` sequences sharded by batch (sharding.batch_piece: each rank decodes
+    its ceil(batch / N) prompts of one fixed seeded batch).  A batch smaller than N (batch 1)
+    cannot shard: there every rank decodes its own single sequence (weak scaling, labelled so)."""
+    from piton_b200 import sharding, tinygpt
     model = tinygpt.TinyGPT(tinygpt.init_weights(0))
-    per = max(1, batch // D.world)
-    prompts = tinygpt.random_prompts(per, seed=100 + D.rank)
+    if batch >= D.world:
+        prompts, _ = sharding.batch_piece(tinygpt.random_prompts(batch, seed=100), D.world, D.rank)
+    else:
+        prompts = tinygpt.random_prompts(1, seed=100 + D.rank)
+    per = len(prompts)
     buf = np.zeros((per, tinygpt.CTX), np.int32)
     buf[:, :tinygpt.PROMPT_LEN] = prompts
     base = torch.from_numpy(buf).cuda()
@@ -409,18 +524,24 @@ def bench_tinygpt(torch, D, args, lib_calls, batch):
     n0 = lib().piton_b200_launch_count()
     model.generate_device(toks, tinygpt.PROMPT_LEN, tinygpt.NEW_TOKENS)
     torch.cuda.synchronize()
-    lib_calls["launches"] += 2 * steps * (lib().piton_b200_launch_count() - n0)
-    return {"tokens": per * D.world * tinygpt.NEW_TOKENS, "t_step": t, "t_eager": t_eager}
+    per_decode = lib().piton_b200_launch_count() - n0
+    lib_calls["launches"] += 2 * steps * per_decode
+    e2e = None
+    if not args.no_e2e:
+        # the public call with host prompts in and host tokens out (TinyGPT.generate)
+        k = max(2, args.steps // 10)
+        sec, _ = timed_e2e(torch, D, lambda: (model.generate(prompts), {})[1], k)
+        lib_calls["launches"] += (k + 1) * per_decode
+        e2e = {"sec": sec, "h2d": int(buf.nbytes), "d2h": int(buf.nbytes)}
+    return {"tokens": per * D.world * tinygpt.NEW_TOKENS, "t_step": t, "t_eager": t_eager, "e2e": e2e,
+            "batch": per * D.world, "per_rank": per, "weak": batch < D.world}
 
 
 def bench_mlp(torch, D, args, lib_calls):
-    from piton_b200 import digits, workloads as W
+    from piton_b200 import digits, sharding, workloads as W
     rows = 1797
-    per = -(-rows // D.world)
-    imgs = np.zeros((per, 64), np.uint8)
-    lo = D.rank * per
-    mine = W.digits_images(rows, 0)[lo:lo + per]
-    imgs[:len(mine)] = mine
+    imgs, _ = sharding.batch_piece(W.digits_images(rows, 0), D.world, D.rank)
+    per = len(imgs)
     model = digits.DigitsMLP(W.digits_model(0))
     x = torch.from_numpy(imgs).cuda()
     logits = torch.empty(per, 16, device="cuda")
@@ -449,6 +570,11 @@ def bench_mlp(torch, D, args, lib_calls):
         out["t_step"] = timed(torch, D, g.replay, args.steps, args.warmup)
         lib_calls["launches"] += args.steps
         del g
+    if not args.no_e2e:
+        # the public call: host uint8 images in, host logits and predictions out
+        sec, _ = timed_e2e(torch, D, lambda: (model(imgs, return_pred=True), {})[1], args.steps)
+        lib_calls["launches"] += args.steps + 1
+        out["e2e"] = {"sec": sec, "h2d": int(imgs.nbytes), "d2h": per * (16 * 4 + 4)}
     return out
 
 
@@ -587,6 +713,27 @@ def cpu_baseline_matmul(rows: int, threads: int):
     return 2.0 * rows * MM * MM / sec / 1e12, sec
 
 
+def cpu_baseline_blas(threads: int) -> dict:
+    """numpy float32 A @ B at the full 8192^3 size on the host's BLAS (OpenBLAS sgemm, all host
+    threads): a plain fp32 CPU product beside the reference-semantics port, not the reference."""
+    rng = np.random.default_rng(1)
+    a = rng.uniform(-1, 1, (MM, MM)).astype(np.float32)
+    b = rng.uniform(-1, 1, (MM, MM)).astype(np.float32)
+    a[:64] @ b                                        # warm the BLAS threads
+    t0 = time.perf_counter()
+    a @ b
+    sec = time.perf_counter() - t0
+    try:
+        import threadpoolctl
+        info = [p for p in threadpoolctl.threadpool_info() if p.get("user_api") == "blas"]
+        blas = f"{info[0]['internal_api']} {info[0]['version']}, {info[0]['num_threads']} threads" if info else "BLAS"
+        cores = info[0]["num_threads"] if info else threads
+    except Exception:   # threadpoolctl is optional: report the host's thread count
+        blas, cores = "BLAS", threads
+    return {"value": 2.0 * MM ** 3 / sec / 1e12, "unit": "TFLOP/s", "cores": cores, "kind": "numpy",
+            "sample": f"one full {MM}^3 numpy float32 A @ B ({sec:.2f} s, {blas}); not the reference's arithmetic"}
+
+
 def sample_rows(seconds: float, rate_tflops: float, threads: int) -> int:
     """Rows of the 8192^3 product that take about `seconds` at `rate_tflops`, a whole number per
     thread (at least one, at most all 8192)."""
@@ -639,6 +786,13 @@ def cpu_baselines_secondary(threads: int) -> dict:
     sec = time.perf_counter() - t0
     out["tinygpt_b1"] = {"value": new / sec, "unit": "tokens/s", "cores": 1, "kind": "port",
                          "sample": f"batch 1, {new} of the 64 greedy tokens, float64 numpy host model"}
+    prompts = tinygpt.random_prompts(256, seed=100)
+    t0 = time.perf_counter()
+    tinygpt_ref.generate(w, prompts, new)
+    sec = time.perf_counter() - t0
+    out["tinygpt_b256"] = {"value": 256 * new / sec, "unit": "tokens/s", "cores": threads, "kind": "port",
+                           "sample": f"batch 256, {new} of the 64 greedy tokens (the first steps, the cheapest "
+                                     f"per token), float64 numpy host model with a KV cache, BLAS threads"}
     return out
 
 
@@ -674,7 +828,7 @@ def run_reference(args):
 
 
 def main():
-    global MM
+    global MM, ATTN_BH, ADD_N, SM_M
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
@@ -687,13 +841,14 @@ def main():
     ap.add_argument("--allgather", default="peer", choices=["peer", "multicast"],
                     help="matmul all-gather at N > 1: peer stores, or multimem stores to an NVSwitch multicast address")
     ap.add_argument("--attn-bh", type=int, default=AT_B * AT_H, help="attention batch x heads (profiling runs use fewer)")
+    ap.add_argument("--add-n", type=int, default=1 << 28, help="vector add elements (profiling runs use fewer)")
+    ap.add_argument("--softmax-m", type=int, default=32768, help="softmax rows (profiling runs use fewer)")
     ap.add_argument("--sweep", action="store_true",
                     help="instead of the benchmark line: add and softmax over the sweep sizes (1 GPU)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     MM = args.mm_size
-    global ATTN_BH
-    ATTN_BH = args.attn_bh
+    ATTN_BH, ADD_N, SM_M = args.attn_bh, args.add_n, args.softmax_m
     if args.impl == "reference":
         return run_reference(args)
     if args.sweep:
@@ -725,52 +880,124 @@ def main():
     finally:
         sampler.stop()
     e2e = e2e_matmul(torch, D, max(2, args.steps // 5)) if "matmul" in ops and not args.no_e2e else None
-    tf32 = tf32_peak(torch) if "matmul" in ops else None
+    tf32 = tf32_peak(torch) if ("matmul" in ops or "attention" in ops) else None
     D.close()
     if D.rank != 0:
         return 0
 
+    from piton_b200 import tinygpt
     hbm = peaks["hbm_gbs"]
+    tf32_src = f"cuBLAS TF32 8192^3 measured in this run ({tf32:.1f} TFLOP/s)" if tf32 else None
+
+    def e2e_entry(r, units, unit, scale):
+        e = r.get("e2e")
+        if not e:
+            return None
+        return {"value": units / e["sec"] / scale, "unit": unit, "h2d_bytes_per_step": e["h2d"],
+                "d2h_bytes_per_step": e["d2h"], "ms_per_step": 1e3 * e["sec"],
+                "path": "the public call with pinned host buffers (copy in, launch, copy back every step)"
+                        + ("; per rank: its own shard in and out, max over ranks" if D.world > 1 else "")}
+
     sec = {}
-    for name in ("softmax", "add"):
+    for name, kernel, cfg in (("softmax", "softmax_reg_kernel", f"{SM_M} x {SM_N}"),
+                              ("add", "add_vec4_kernel", f"n = {ADD_N}")):
         if name in res:
             r = res[name]
             ach = r["local_bytes"] / r["t_kernel"] / 1e9
-            sec[name] = {"value": r["bytes"] / r["t_step"] / 1e9, "unit": "GB/s",
-                         "kernel_gbs_per_gpu": ach, "roofline_frac": ach / hbm,
-                         "ms_per_step": 1e3 * r["t_step"], "max_rel_err" if name == "softmax" else "max_abs_err": r["err"]}
+            units = SM_M * SM_N if name == "softmax" else ADD_N
+            trf, trf_src = traffic_for(name + "_dram", units / D.world) if D.world == 1 else (None, None)
+            sec[name] = {"value": r["bytes"] / r["t_step"] / 1e9, "unit": "GB/s", "workload": cfg,
+                         "kernel_gbs_per_gpu": ach,
+                         "roofline": roofline("hbm", ach, hbm, "GB/s", trf, trf_src, kernel=kernel,
+                                              algorithmic_bytes_per_launch=r["local_bytes"],
+                                              peak_source=f"MEASURED_PEAKS.json hbm_gbs ({peaks['source']})"),
+                         "ms_per_step": 1e3 * r["t_step"],
+                         "max_rel_err" if name == "softmax" else "max_abs_err": r["err"]}
+            e = e2e_entry(r, r["local_bytes"] * D.world, "GB/s", 1e9)
+            if e:
+                sec[name]["e2e"] = e
             if D.world > 1:
                 sec[name]["value_without_allgather"] = r["bytes"] / r["t_kernel"] / 1e9
     if "attention" in res:
         r = res["attention"]
+        ach = r["local_flops"] / r["t_kernel"] / 1e12
+        peak = tf32 / 3.0 if tf32 else None
+        trf, trf_src = traffic_for("attention_dram", r["heads_local"]) if D.world == 1 else (None, None)
         sec["attention"] = {"value": r["flops"] / r["t_step"] / 1e12, "unit": "TFLOP/s",
+                            "workload": f"B={AT_B} H={AT_H} S={AT_S} D={AT_D} causal (B x H = {ATTN_BH})",
                             "gbs": r["bytes"] / r["t_step"] / 1e9,
-                            "kernel_tflops_per_gpu": r["local_flops"] / r["t_kernel"] / 1e12,
+                            "kernel_tflops_per_gpu": ach,
+                            "roofline": roofline("tensor", ach, peak, "TFLOP/s", trf, trf_src,
+                                                 kernel="attn_3xtf32_kernel",
+                                                 peak_source=(tf32_src + " / 3: per useful 8-deep product the "
+                                                              "kernel issues one N=128 tf32 MMA (hi.[hi;lo], two "
+                                                              "TF32 units) and one 16-deep bf16 MMA (lo.hi, one "
+                                                              "unit), the unit count of classic 3xTF32, the "
+                                                              "bound the north star names") if tf32 else None,
+                                                 gbs_over_4BHSD4=r["bytes"] / r["t_kernel"] / 1e9 / D.world
+                                                 if D.world > 1 else r["bytes"] / r["t_kernel"] / 1e9),
                             "path": "tcgen05 split (tf32 high halves + bf16 cross terms)" if r.get("tc")
                                     else "CUDA-core fp32",
                             "allgather": ("fused: the kernel's gather warp stores finished rows to every rank "
                                           "(NVLink peer stores)" if r.get("fused") else
                                           "NCCL all_gather_into_tensor after the kernel") if D.world > 1 else None,
                             "ms_per_step": 1e3 * r["t_step"], "max_abs_err_vs_f64": r["err"]}
+        e = e2e_entry(r, r["local_flops"] * D.world, "TFLOP/s", 1e12)
+        if e:
+            sec["attention"]["e2e"] = e
         if D.world > 1:
             sec["attention"]["value_without_allgather"] = r["flops"] / r["t_kernel"] / 1e12
     if "mlp" in res:
         r = res["mlp"]
+        flops = 2.0 * r["images"] * (64 * 128 + 128 * 64 + 64 * 16)
+        ffma = 148 * 128 * 2 * 1.965e9 / 1e12
         sec["mlp_digits_1797"] = {"value": r["images"] / r["t_step"], "unit": "images/s",
                                   "ms_per_step": 1e3 * r["t_step"], "eager_value": r["images"] / r["t_eager"],
+                                  "roofline": roofline("latency", flops / D.world / r["t_step"] / 1e12, ffma,
+                                                       "TFLOP/s", kernel="mlp_kernel",
+                                                       us_per_forward=1e6 * r["t_step"],
+                                                       peak_source="fp32 FFMA nominal: 148 SMs x 128 lanes x 2 x "
+                                                                   "1.965 GHz; 62.6 MFLOP per forward is far below "
+                                                                   "any throughput roof, the time is launch and L2 "
+                                                                   "latency"),
                                   "workload": "1797 images through 64-128-64-16 in one launch; value: the launch "
                                               "replayed from a CUDA graph (N = 1), eager_value: one library call "
                                               "per step from Python"}
+        e = e2e_entry(r, r["images"], "images/s", 1.0)
+        if e:
+            sec["mlp_digits_1797"]["e2e"] = e
     for key in ("tinygpt_b1", "tinygpt_b256"):
         if key in res:
             r = res[key]
-            sec[key] = {"value": r["tokens"] / r["t_step"], "unit": "tokens/s", "ms_per_step": 1e3 * r["t_step"],
-                        "eager_value": r["tokens"] / r["t_eager"],
-                        "workload": "greedy decode of 64 tokens after 16-token prompts; batches up to the "
-                                    "number of 16-CTA clusters that fit (9 on 148 SMs) run as one cluster launch "
-                                    "per decode with the weights in shared memory, larger ones as 79 launches "
-                                    "of one position each; value: replayed from a CUDA graph, eager_value: "
-                                    "launched directly"}
+            pos = tinygpt.PROMPT_LEN + tinygpt.NEW_TOKENS - 1
+            ent = {"value": r["tokens"] / r["t_step"], "unit": "tokens/s", "ms_per_step": 1e3 * r["t_step"],
+                   "eager_value": r["tokens"] / r["t_eager"], "batch": r["batch"],
+                   "workload": "greedy decode of 64 tokens after 16-token prompts; batches up to the "
+                               "number of 16-CTA clusters that fit (9 on 148 SMs) run as one cluster launch "
+                               "per decode with the weights in shared memory, larger ones as 79 launches "
+                               "of one position each; value: replayed from a CUDA graph, eager_value: "
+                               "launched directly"}
+            if r["weak"]:
+                ent["scaling"] = "weak"
+                ent["workload"] += f"; at N = {D.world} every GPU decodes its own single sequence (batch 1 " \
+                                   f"cannot shard): {r['batch']} sequences in all"
+            if key == "tinygpt_b256":
+                # algorithmic bytes of one decode: the weights once per fed position plus, per sequence
+                # and position p, the K and V rows 0..p of every layer read and row p written
+                wbytes = 4.0 * tinygpt.pack(tinygpt.init_weights(0)).size
+                kv = 2 * tinygpt.N_LAYER * tinygpt.D_MODEL * 4.0
+                per_seq = sum(kv * (p + 1) + kv for p in range(pos))
+                byts = pos * wbytes + r["per_rank"] * per_seq
+                ent["roofline"] = roofline("hbm", byts / r["t_step"] / 1e9, hbm, "GB/s", kernel="tinygpt_step_kernel",
+                                           algorithmic_bytes_per_decode=byts,
+                                           note="KV cache (134 MB at batch 256) and weights mostly L2-resident")
+            else:
+                ent["roofline"] = roofline("latency", 1e6 * r["t_step"] / pos, None, "us per fed position",
+                                           kernel="tinygpt_cluster_kernel")
+            e = e2e_entry(r, r["tokens"], "tokens/s", 1.0)
+            if e:
+                ent["e2e"] = e
+            sec[key] = ent
     line = {"metric": METRIC, "n_gpus": D.world, "steps": args.steps, "warmup": args.warmup,
             "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
             "data": "synthetic (seeded torch.rand / randn on device)"}
@@ -782,6 +1009,10 @@ def main():
         # depth 16 (the cross terms), and bf16 runs at twice the tf32 rate: the instruction mix's peak
         # is the measured TF32 throughput / 2 (bf16 / 4); classic 3xTF32 would be TF32 / 3
         peak = tf32 / 2.0
+        gemm_traffic = (profiled_traffic("gemm_dram_8192") or (None, None))[0] if (D.world == 1 and MM == 8192) \
+            else None
+        gemm_traffic = (gemm_traffic, "ncu capture of an earlier run of this kernel, profiles/gemm_dram_8192.md"
+                        if gemm_traffic else None)
         line.update({"value": value, "unit": "TFLOP/s", "ms_per_step": 1e3 * r["t_step"],
                      "config": {"workload": f"matmul C=A@B fp32 {MM}x{MM}x{MM}, A,B ~ U[-1,1], sharded by M-tiles, "
                                             f"all-gather of C each step" + (
@@ -795,9 +1026,9 @@ def main():
                                         if r["tc"] else "CUDA-core fp32 FFMA"},
                      "roofline": {"bound": "tensor", "achieved": ach, "peak": peak, "unit": "TFLOP/s",
                                   "frac": ach / peak,
-                                  # DRAM bytes of one launch of the CTA-pair GEMM at 8192^3 measured with ncu
-                                  # (dram__bytes_read.sum + dram__bytes_write.sum, single-pass capture)
-                                  "traffic": GEMM_TRAFFIC_8192 if (D.world == 1 and MM == 8192) else None,
+                                  # DRAM bytes of one launch of the CTA-pair GEMM at 8192^3 from the committed
+                                  # single-pass ncu capture (dram__bytes_read.sum + dram__bytes_write.sum)
+                                  "traffic": gemm_traffic[0], "traffic_source": gemm_traffic[1],
                                   "traffic_unit": "bytes per launch",
                                   "peak_source": f"cuBLAS TF32 8192^3 measured in this run ({tf32:.1f} TFLOP/s) / 2 "
                                                  "(one tf32 + one double-depth bf16 MMA per 8-deep k-step)",
@@ -831,6 +1062,7 @@ def main():
         line["cpu_baseline"] = {"value": v, "unit": "TFLOP/s", "cores": threads, "kind": "port",
                                 "sample": f"{rows} of {MM} rows of the {MM}^3 product ({s:.1f} s): the oracle's "
                                           f"restatement of the emulator's sequential-k round-toward-zero dot"}
+        line["cpu_baseline_blas"] = cpu_baseline_blas(threads)
     if D.world == 1 and not args.no_cpu_baseline and line.get("secondary"):
         # the reference's CPU path for the other operators, beside their B200 figures
         for key, cb in cpu_baselines_secondary(os.cpu_count() or 1).items():

@@ -84,7 +84,7 @@ def test_logits_against_reference_kernels_on_the_emulator(cuda):
     emulator (tests/golden/make_golden.py case_tinygpt): the logits after every prefix of the
     prompt within 5e-5, the same greedy token."""
     from conftest import goldens
-    gs = goldens("tinygpt_emu_")
+    gs = goldens("tinygpt_emu_p")
     assert gs
     for g in gs:
         model = tinygpt.TinyGPT(tinygpt.init_weights(g.meta["weight_seed"]))
@@ -93,3 +93,21 @@ def test_logits_against_reference_kernels_on_the_emulator(cuda):
             _, logits = model.generate(prompt[None, :p], 0, return_logits=True)
             np.testing.assert_allclose(logits[0], g["logits"][p - 1], rtol=0, atol=5e-5)
             assert int(np.argmax(logits[0])) == int(np.argmax(g["logits"][p - 1]))
+
+
+def test_decode_against_reference_kernels_on_the_emulator(cuda):
+    """The B200 greedy decode (KV cache, one position per step) against the same decode composed
+    from the reference's kernels on its emulator (tests/golden/make_golden.py
+    case_tinygpt_decode): a 16-token prompt and 4 greedy steps give the same tokens, and the logits
+    that chose each token agree within LOGIT_ATOL."""
+    from conftest import goldens
+    gs = goldens("tinygpt_emu_decode_")
+    assert gs
+    for g in gs:
+        model = tinygpt.TinyGPT(tinygpt.init_weights(g.meta["weight_seed"]))
+        plen, new = g.meta["prompt_len"], g.meta["new_tokens"]
+        toks = model.generate(g["prompt"][None], new)
+        np.testing.assert_array_equal(toks[0, plen:], g["tokens"])
+        for k in range(1, new + 1):
+            _, logits = model.generate(g["prompt"][None], k, return_logits=True)
+            np.testing.assert_allclose(logits[0], g["logits"][k - 1], rtol=0, atol=LOGIT_ATOL)

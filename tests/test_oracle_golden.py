@@ -136,7 +136,7 @@ def test_elementwise_qpu(g):
     np.testing.assert_array_equal(bits(got), bits(g["out"]))
 
 
-TGPT = goldens("tinygpt_emu_")
+TGPT = goldens("tinygpt_emu_p")
 
 
 @pytest.mark.parametrize("g", TGPT, ids=golden_ids(TGPT))
