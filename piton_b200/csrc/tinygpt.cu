@@ -18,6 +18,10 @@
 //              ln2_g[D] ln2_b[D] w_fc[D,4D] b_fc[4D] w_pr[4D,D] b_pr[D]
 //   lnf_g[D] lnf_b[D]
 // KV cache: fp32 [L][2][B][CTX][D] (keys, then values).
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
 #include "common.cuh"
 
 namespace piton {
@@ -569,6 +573,322 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
     cl_sync();   // no CTA leaves while another may still store into its shared memory
 }
 
+// ---------------------------------------------------------------------------
+// Larger batches: one cluster of H = 4 CTAs per group of up to GS sequences, one launch per
+// decode.  CTA r of a cluster owns attention head r and hidden units [128 r, 128 r + 128) of
+// the MLP.  Per layer it computes, for every sequence of its group, the head's 96 q, k and v
+// columns of W_qkv (appending k and v to the KV cache), the head's causal attention, the
+// head's share of the output projection (its 32 outputs times the head's 32 rows of W_o), its
+// 128 GELU hidden units (W_fc columns) and their share of the MLP projection (the matching 128
+// rows of W_pr).  The two 128-wide partial products per layer go to all four CTAs' shared
+// memory (st.shared::cluster) and one cluster barrier each publishes them; every CTA adds the
+// four partials in rank order, so all four keep the same residual stream without further
+// exchange.  Each CTA reads a quarter of the weights from L2 per position (the step kernel's
+// CTAs read all of them), and the whole decode is one launch with 9 cluster barriers per
+// position.
+// ---------------------------------------------------------------------------
+
+constexpr int HC = H;                 // CTAs per cluster, one per head (portable cluster size)
+constexpr int GS = 8;                 // sequences per group at most
+constexpr int HT = 256;               // threads per CTA
+constexpr int KGRP = 8;               // k-groups of the split-k linears
+constexpr int FH = F / HC;            // hidden units per CTA (128)
+constexpr int V_R = (V + HC - 1) / HC;   // vocabulary rows per CTA (17)
+constexpr int LG_LD = V + 3;
+
+struct HeadsSmem {
+    float x[GS][D];                   // residual stream (the same in all four CTAs)
+    float h[GS][D];                   // LayerNorm output
+    float q[GS][HD];                  // this head's queries
+    float att[GS][HD];                // this head's attention outputs
+    float f[GS][FH];                  // this CTA's GELU hidden units
+    float part[2][HC][GS][D];         // partial products from every CTA, two slots used in turn
+    float red[KGRP][GS][D];           // split-k partial sums
+    float probs[GS][CTX];
+    float lg[GS][LG_LD];              // logits, every CTA's vocabulary rows
+    int tok[GS];
+};
+
+struct HeadsArgs {
+    const float *w;
+    float *kv;
+    int32_t *tokens;
+    float *logits;
+    int64_t batch;
+    int prompt_len, end, steps;
+    int group;                        // sequences per group (1..GS)
+};
+
+__device__ __forceinline__ void st_cluster4(float *local, uint32_t rank, float4 v) {
+    uint32_t a = (uint32_t)__cvta_generic_to_shared(local), r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(r), "f"(v.x), "f"(v.y), "f"(v.z),
+                 "f"(v.w)
+                 : "memory");
+}
+
+// Split-k product of the group's rows in[s][0..K) (shared memory, row stride K) with NQ quads of
+// weight columns: quad j is columns col0(j) .. col0(j) + 3 of W (row stride ldw, rows krow0 ..
+// krow0 + K).  Thread (j, g) sums k-group g for all GS rows with 16-byte weight loads; the KGRP
+// partial sums meet in red, and epi(s, j, float4) receives each finished quad once.
+template <int K, int NQ, typename ColFn, typename Epi>
+__device__ __forceinline__ void group_linear(const float *in, const float *__restrict__ W, int ldw, int krow0,
+                                             ColFn col0, float (*red)[GS][D], Epi epi) {
+    constexpr int KG = K / KGRP;
+    static_assert(K % KGRP == 0 && NQ * KGRP <= HT && NQ * 4 <= D, "group_linear tiling");
+    const int tid = threadIdx.x;
+    const int j = tid % NQ, g = tid / NQ;
+    if (g < KGRP) {
+        float4 acc[GS];
+#pragma unroll
+        for (int s = 0; s < GS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+        const float *wp = W + (int64_t)(krow0 + g * KG) * ldw + col0(j);
+#pragma unroll
+        for (int k = 0; k < KG; ++k) {
+            const float4 w = __ldg(reinterpret_cast<const float4 *>(wp + (int64_t)k * ldw));
+#pragma unroll
+            for (int s = 0; s < GS; ++s) {
+                const float xv = in[s * K + g * KG + k];
+                acc[s].x = fmaf(xv, w.x, acc[s].x);
+                acc[s].y = fmaf(xv, w.y, acc[s].y);
+                acc[s].z = fmaf(xv, w.z, acc[s].z);
+                acc[s].w = fmaf(xv, w.w, acc[s].w);
+            }
+        }
+#pragma unroll
+        for (int s = 0; s < GS; ++s) *reinterpret_cast<float4 *>(&red[g][s][4 * j]) = acc[s];
+    }
+    __syncthreads();
+    for (int i = tid; i < GS * NQ; i += HT) {
+        const int s = i / NQ, jj = i % NQ;
+        float4 v = *reinterpret_cast<const float4 *>(&red[0][s][4 * jj]);
+#pragma unroll
+        for (int gg = 1; gg < KGRP; ++gg) {
+            const float4 p = *reinterpret_cast<const float4 *>(&red[gg][s][4 * jj]);
+            v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+        }
+        epi(s, jj, v);
+    }
+    __syncthreads();
+}
+
+// LayerNorm of the group's rows of x into h, a warp per sequence (biased variance, eps 1e-5).
+__device__ __forceinline__ void group_ln(const float (*x)[D], float (*h)[D], const float *__restrict__ g,
+                                         const float *__restrict__ b) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int s = warp; s < GS; s += HT / 32) {
+        float v[D / 32], sum = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            v[i] = x[s][lane + 32 * i];
+            sum += v[i];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        const float mean = sum * (1.0f / D);
+        float q = 0.0f;
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            v[i] -= mean;
+            q += v[i] * v[i];
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+        const float r = rsqrtf(q * (1.0f / D) + 1e-5f);
+#pragma unroll
+        for (int i = 0; i < D / 32; ++i) {
+            const int c = lane + 32 * i;
+            h[s][c] = v[i] * r * __ldg(g + c) + __ldg(b + c);
+        }
+    }
+    __syncthreads();
+}
+
+// this CTA's partial product part[s][4 j ..] to slot `slot` of every CTA of the cluster
+__device__ __forceinline__ void send_part(HeadsSmem &S, int slot, uint32_t rank, int s, int j, float4 v) {
+#pragma unroll
+    for (uint32_t r = 0; r < HC; ++r) st_cluster4(&S.part[slot][rank][s][4 * j], r, v);
+}
+
+// x[s][c] += bias[c] + the four CTAs' partials of `slot`, added in rank order
+__device__ __forceinline__ void add_parts(HeadsSmem &S, int slot, const float *__restrict__ bias) {
+    for (int i = threadIdx.x; i < GS * D; i += HT) {
+        const int s = i / D, c = i % D;
+        float v = __ldg(bias + c);
+#pragma unroll
+        for (int r = 0; r < HC; ++r) v += S.part[slot][r][s][c];
+        S.x[s][c] += v;
+    }
+    __syncthreads();
+}
+
+__global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
+    extern __shared__ __align__(16) unsigned char heads_smem[];
+    HeadsSmem &S = *reinterpret_cast<HeadsSmem *>(heads_smem);
+    const uint32_t rank = cl_rank();
+    const int hh = (int)rank;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const float *wte = a.w, *wpe = a.w + V * D;
+    const float *lw0 = a.w + V * D + CTX * D;
+    const int64_t groups = cdiv_dev(a.batch, a.group);
+    int slot = 0;
+    cl_sync();   // every CTA of the cluster is running before any stores into its shared memory
+
+    for (int64_t grp = cl_id(); grp < groups; grp += cl_count()) {
+        const int64_t b0 = grp * a.group;
+        const int gs = (int)min((int64_t)a.group, a.batch - b0);
+        if (tid < GS) S.tok[tid] = tid < gs ? a.tokens[(b0 + tid) * CTX] : 0;
+        __syncthreads();
+        for (int pos = 0; pos < a.steps; ++pos) {
+            if (tid < gs && pos < a.prompt_len) S.tok[tid] = a.tokens[(b0 + tid) * CTX + pos];
+            __syncthreads();
+            for (int i = tid; i < GS * D; i += HT) {
+                const int s = i / D, c = i % D;
+                int t = S.tok[s];
+                t = t < 0 ? 0 : (t >= V ? V - 1 : t);
+                S.x[s][c] = s < gs ? __ldg(wte + t * D + c) + __ldg(wpe + pos * D + c) : 0.0f;
+            }
+            __syncthreads();
+            for (int l = 0; l < L; ++l) {
+                const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
+                const float *ln1_g = lw, *ln1_b = ln1_g + D, *w_qkv = ln1_b + D, *b_qkv = w_qkv + D * 3 * D;
+                const float *w_o = b_qkv + 3 * D, *b_o = w_o + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
+                const float *w_fc = ln2_b + D, *b_fc = w_fc + D * F, *w_pr = b_fc + F, *b_pr = w_pr + F * D;
+                float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
+                float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
+
+                // 1. this head's q, k, v: quads 0-7 q, 8-15 k, 16-23 v
+                group_ln(S.x, S.h, ln1_g, ln1_b);
+                group_linear<D, 24>(
+                    &S.h[0][0], w_qkv, 3 * D, 0, [&](int j) { return (j >> 3) * D + hh * HD + 4 * (j & 7); }, S.red,
+                    [&](int s, int j, float4 v) {
+                        const int c = (j >> 3) * D + hh * HD + 4 * (j & 7);
+                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(b_qkv + c));
+                        v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
+                        if (j < 8) {
+                            *reinterpret_cast<float4 *>(&S.q[s][4 * j]) = v;
+                        } else if (s < gs) {
+                            float *cache = j < 16 ? kc : vc;
+                            *reinterpret_cast<float4 *>(cache + ((b0 + s) * CTX + pos) * D + hh * HD +
+                                                        4 * (j & 7)) = v;
+                        }
+                    });
+                // 2. causal attention of head hh over positions 0..pos, a warp per sequence
+                for (int s = warp; s < gs; s += HT / 32) {
+                    const float *kr = kc + ((b0 + s) * CTX) * D + hh * HD;
+                    const float *vr = vc + ((b0 + s) * CTX) * D + hh * HD;
+                    const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
+                    float sc[CTX / 32];
+                    float mx = -INFINITY;
+#pragma unroll
+                    for (int jt = 0; jt < CTX / 32; ++jt) {
+                        const int t = lane + 32 * jt;
+                        float dot = -INFINITY;
+                        if (t <= pos) {
+                            float acc = 0.0f;
+#pragma unroll
+                            for (int d = 0; d < HD; d += 4) {
+                                const float4 k4 = *reinterpret_cast<const float4 *>(kr + (int64_t)t * D + d);
+                                acc = fmaf(S.q[s][d], k4.x, acc);
+                                acc = fmaf(S.q[s][d + 1], k4.y, acc);
+                                acc = fmaf(S.q[s][d + 2], k4.z, acc);
+                                acc = fmaf(S.q[s][d + 3], k4.w, acc);
+                            }
+                            dot = acc * scale;
+                        }
+                        sc[jt] = dot;
+                        mx = fmaxf(mx, dot);
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    float sum = 0.0f;
+#pragma unroll
+                    for (int jt = 0; jt < CTX / 32; ++jt) {
+                        const int t = lane + 32 * jt;
+                        const float p = t <= pos ? expf(sc[jt] - mx) : 0.0f;
+                        S.probs[s][t] = p;
+                        sum += p;
+                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                    __syncwarp();
+                    // lane = output dimension; eight positions' values requested at a time
+                    float o0 = 0.0f, o1 = 0.0f;
+                    int t = 0;
+                    for (; t + 8 <= pos + 1; t += 8) {
+                        float vv[8];
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) vv[u] = vr[(int64_t)(t + u) * D + lane];
+#pragma unroll
+                        for (int u = 0; u < 8; u += 2) {
+                            o0 = fmaf(S.probs[s][t + u], vv[u], o0);
+                            o1 = fmaf(S.probs[s][t + u + 1], vv[u + 1], o1);
+                        }
+                    }
+                    for (; t <= pos; ++t) o0 = fmaf(S.probs[s][t], vr[(int64_t)t * D + lane], o0);
+                    S.att[s][lane] = (o0 + o1) / sum;
+                }
+                for (int i = tid; i < (GS - gs) * HD; i += HT) S.att[gs + i / HD][i % HD] = 0.0f;
+                __syncthreads();
+                // 3. the head's share of the output projection, to every CTA; x += b_o + the four shares
+                group_linear<HD, D / 4>(
+                    &S.att[0][0], w_o, D, hh * HD, [](int j) { return 4 * j; }, S.red,
+                    [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
+                cl_sync();
+                add_parts(S, slot, b_o);
+                slot ^= 1;
+                // 4. this CTA's 128 hidden units, then their share of the MLP projection
+                group_ln(S.x, S.h, ln2_g, ln2_b);
+                group_linear<D, FH / 4>(
+                    &S.h[0][0], w_fc, F, 0, [&](int j) { return (int)rank * FH + 4 * j; }, S.red,
+                    [&](int s, int j, float4 v) {
+                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(b_fc + rank * FH + 4 * j));
+                        float r4[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) r4[e] = 0.5f * r4[e] * (1.0f + erff(r4[e] * 0.70710678118654752f));
+                        *reinterpret_cast<float4 *>(&S.f[s][4 * j]) = make_float4(r4[0], r4[1], r4[2], r4[3]);
+                    });
+                group_linear<FH, D / 4>(
+                    &S.f[0][0], w_pr, D, (int)rank * FH, [](int j) { return 4 * j; }, S.red,
+                    [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
+                cl_sync();
+                add_parts(S, slot, b_pr);
+                slot ^= 1;
+            }
+            const bool next_from_model = pos + 1 >= a.prompt_len && pos + 1 < a.end;
+            const bool want_logits = a.logits && pos == a.steps - 1;
+            if (!next_from_model && !want_logits) continue;
+            // final LayerNorm and the tied head: this CTA's vocabulary rows, a warp per (sequence, row)
+            const float *lnf = lw0 + (int64_t)L * LAYER_FLOATS;
+            group_ln(S.x, S.h, lnf, lnf + D);
+            const int v0 = (int)rank * V_R, nv = min(V_R, V - v0);
+            for (int pv = warp; pv < gs * nv; pv += HT / 32) {
+                const int s = pv / nv, v = v0 + pv % nv;
+                float acc = 0.0f;
+#pragma unroll
+                for (int i = 0; i < D / 32; ++i) acc = fmaf(S.h[s][lane + 32 * i], __ldg(wte + v * D + lane + 32 * i), acc);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane < HC) st_cluster(&S.lg[s][v], lane, acc);
+            }
+            cl_sync();
+            if (tid < gs) {
+                int best = 0;
+                for (int v = 1; v < V; ++v)
+                    if (S.lg[tid][v] > S.lg[tid][best]) best = v;     // first maximum, as numpy.argmax
+                if (next_from_model) {
+                    S.tok[tid] = best;
+                    if (rank == 0) a.tokens[(b0 + tid) * CTX + pos + 1] = best;
+                }
+            }
+            if (want_logits && rank == 0)
+                for (int i = tid; i < gs * V; i += HT) a.logits[(b0 + i / V) * V + i % V] = S.lg[i / V][i % V];
+            __syncthreads();
+        }
+    }
+    cl_sync();   // no CTA leaves while another may still store into its shared memory
+}
+
 }  // namespace tg
 }  // namespace piton
 
@@ -629,6 +949,64 @@ void launch_cluster(const tg::ClusterArgs &c, int clusters, cudaStream_t q) {
     cfg.attrs = at;
     cfg.numAttrs = 1;
     cudaLaunchKernelEx(&cfg, tg::tinygpt_cluster_kernel, c);
+}
+
+// Clusters of 4 CTAs with the heads kernel's shared memory that fit on the current device at
+// once (0: that path is unavailable), looked up once per device.
+int heads_capacity() {
+    static int cache[64];
+    static bool known[64];
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+    if (known[dev]) return cache[dev];
+    int n = 0;
+    if (cudaFuncSetAttribute(tg::tinygpt_heads_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)sizeof(tg::HeadsSmem)) == cudaSuccess) {
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(tg::HC);
+        cfg.blockDim = dim3(tg::HT);
+        cfg.dynamicSmemBytes = sizeof(tg::HeadsSmem);
+        cudaLaunchAttribute at[1];
+        at[0].id = cudaLaunchAttributeClusterDimension;
+        at[0].val.clusterDim.x = tg::HC;
+        at[0].val.clusterDim.y = 1;
+        at[0].val.clusterDim.z = 1;
+        cfg.attrs = at;
+        cfg.numAttrs = 1;
+        if (cudaOccupancyMaxActiveClusters(&n, tg::tinygpt_heads_kernel, &cfg) != cudaSuccess) n = 0;
+    }
+    cudaGetLastError();   // a refused attribute or query only disables this path
+    cache[dev] = n;
+    known[dev] = true;
+    return n;
+}
+
+void launch_heads(const tg::HeadsArgs &h, int clusters, cudaStream_t q) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(clusters * tg::HC));
+    cfg.blockDim = dim3(tg::HT);
+    cfg.dynamicSmemBytes = sizeof(tg::HeadsSmem);
+    cfg.stream = q;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeClusterDimension;
+    at[0].val.clusterDim.x = tg::HC;
+    at[0].val.clusterDim.y = 1;
+    at[0].val.clusterDim.z = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, tg::tinygpt_heads_kernel, h);
+}
+
+// PITON_B200_TINYGPT_KERNEL=cluster|heads|step picks a decode kernel for comparisons; by default
+// batches up to the number of 16-CTA clusters that fit use the cluster kernel, larger ones the
+// heads kernel, and the per-position step kernel serves when neither cluster launch is possible.
+int forced_kernel() {
+    const char *e = getenv("PITON_B200_TINYGPT_KERNEL");
+    if (!e || !*e) return 0;
+    if (!strcmp(e, "cluster")) return 1;
+    if (!strcmp(e, "heads")) return 2;
+    if (!strcmp(e, "step")) return 3;
+    return -1;
 }
 
 }  // namespace
@@ -718,11 +1096,44 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     if (a->new_tokens == 0 && a->logits) steps = (int)a->prompt_len;
     const unsigned grid = (unsigned)cdiv(a->batch, SEQ);
     cudaStream_t st = as_stream(stream);
-    // small batches: one 16-CTA cluster per sequence, weights resident in shared memory, one launch
+    // small batches: one 16-CTA cluster per sequence, weights resident in shared memory, one launch;
+    // larger ones: one 4-CTA cluster (a CTA per head) per group of up to 8 sequences, one launch
+    const int forced = forced_kernel();
+    PITON_REQUIRE(forced >= 0, "PITON_B200_TINYGPT_KERNEL must be cluster, heads or step");
     const int clusters = cluster_capacity();
-    const bool use_cluster = clusters > 0 && a->batch <= clusters;
-    const int launches = use_cluster ? 1 : steps;
+    const int hcap = heads_capacity();
+    bool use_cluster = clusters > 0 && a->batch <= clusters;
+    bool use_heads = !use_cluster && hcap > 0;
+    if (forced == 1) {
+        PITON_REQUIRE(clusters > 0 && a->batch <= clusters, "the cluster kernel takes at most %d sequences", clusters);
+        use_cluster = true, use_heads = false;
+    } else if (forced == 2) {
+        PITON_REQUIRE(hcap > 0, "the heads kernel cannot be launched on this device");
+        use_cluster = false, use_heads = true;
+    } else if (forced == 3) {
+        use_cluster = use_heads = false;
+    }
+    int group = 0, hclusters = 0;
+    if (use_heads) {
+        group = (int)std::min<int64_t>(GS, std::max<int64_t>(1, cdiv(a->batch, hcap)));
+        hclusters = (int)std::min<int64_t>(hcap, cdiv(a->batch, group));
+    }
+    const int launches = (use_cluster || use_heads) ? 1 : steps;
     auto enqueue = [&](cudaStream_t q) {
+        if (use_heads) {
+            HeadsArgs h;
+            h.w = s.w;
+            h.kv = s.kv;
+            h.tokens = s.tokens;
+            h.logits = reinterpret_cast<float *>(a->logits);
+            h.batch = a->batch;
+            h.prompt_len = s.prompt_len;
+            h.end = s.end;
+            h.steps = steps;
+            h.group = group;
+            launch_heads(h, hclusters, q);
+            return;
+        }
         if (use_cluster) {
             ClusterArgs c;
             c.w = s.w;

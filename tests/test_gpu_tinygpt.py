@@ -111,3 +111,21 @@ def test_decode_against_reference_kernels_on_the_emulator(cuda):
         for k in range(1, new + 1):
             _, logits = model.generate(g["prompt"][None], k, return_logits=True)
             np.testing.assert_allclose(logits[0], g["logits"][k - 1], rtol=0, atol=LOGIT_ATOL)
+
+
+@pytest.mark.parametrize("kernel,batch", [("heads", 1), ("heads", 7), ("heads", 37), ("step", 12), ("cluster", 3)])
+def test_every_decode_kernel_matches_host_model(cuda, monkeypatch, kernel, batch):
+    """Each decode kernel, forced with PITON_B200_TINYGPT_KERNEL, judged step by step against the
+    host model: the 16-CTA cluster kernel (small batches), the 4-CTA heads kernel (groups of up
+    to 8 sequences per cluster, ragged last group) and the per-position step kernel."""
+    monkeypatch.setenv("PITON_B200_TINYGPT_KERNEL", kernel)
+    w = tinygpt.init_weights(1)
+    model = tinygpt.TinyGPT(w)
+    check(model, w, tinygpt.random_prompts(batch, seed=40 + batch), 24)
+
+
+def test_unknown_decode_kernel_is_rejected(cuda, monkeypatch):
+    monkeypatch.setenv("PITON_B200_TINYGPT_KERNEL", "bogus")
+    model = tinygpt.TinyGPT(tinygpt.init_weights(0))
+    with pytest.raises(ValueError):
+        model.generate(tinygpt.random_prompts(2), 2)
