@@ -319,9 +319,27 @@ def bench_softmax(torch, D, args, lib_calls):
     def kernel_only():
         _lib.check(lib().piton_b200_softmax_f32(C.byref(a), stream), "softmax")
 
-    def step():
-        kernel_only()
-        D.allgather(torch, yfull, y)
+    peer = None
+    if D.world > 1 and args.allgather == "peer":
+        # the all-gather fused into the kernel: every finished row is stored into each rank's full
+        # output over NVLink; a 1-element NCCL all-reduce after it is the completion barrier
+        from piton_b200 import sharding
+        del yfull
+        peer = sharding.PeerOutput(D.pg, SM_M * SM_N * 4)
+        gargs = _lib.AllgatherArgs()
+        for r, p in enumerate(peer.peer_ptrs):
+            gargs.peer_c[r] = p
+        gargs.world, gargs.rank, gargs.row_offset, gargs.ldc = D.world, D.rank, r0, SM_N
+        done = torch.zeros(1, device="cuda")
+        fs = lib().piton_b200_softmax_allgather_f32
+
+        def step():
+            _lib.check(fs(C.byref(a), C.byref(gargs), stream), "softmax_allgather")
+            D.pg.all_reduce(done)
+    else:
+        def step():
+            kernel_only()
+            D.allgather(torch, yfull, y)
 
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
     # at N = 1 the step is the kernel-only call itself: one measurement serves both
@@ -329,6 +347,18 @@ def bench_softmax(torch, D, args, lib_calls):
     lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     ref = torch.softmax(x[:8].double(), 1)
     err = float(((y[:8].double() - ref).abs() / ref.abs().clamp_min(1e-37)).max())
+    if peer is not None:
+        # this rank's first rows as every rank stored them into this rank's full output
+        torch.cuda.synchronize()
+        D.pg.barrier()
+        firsts = [None] * D.world
+        D.pg.all_gather_object(firsts, ref[0].cpu().numpy())
+        for r in range(D.world):
+            got = peer.read(r * mloc * SM_N * 4, SM_N * 4).view(np.float32).astype(np.float64)
+            err = max(err, float((np.abs(got - firsts[r]) / np.maximum(np.abs(firsts[r]), 1e-37)).max()))
+        D.pg.barrier()
+        peer.close()
+        yfull = None
     del x, y, yfull
     e2e = None
     if not args.no_e2e:
@@ -465,15 +495,48 @@ def bench_add(torch, D, args, lib_calls):
     def kernel_only():
         _lib.check(lib().piton_b200_add_f32(C.byref(a), stream), "add")
 
-    def step():
-        kernel_only()
-        D.allgather(torch, ofull, out)
+    peer = None
+    if D.world > 1 and args.allgather == "peer":
+        # the all-gather fused into the kernel (NVLink peer stores of every result element), a
+        # 1-element NCCL all-reduce after it as the completion barrier
+        from piton_b200 import sharding
+        del ofull
+        ofull = None
+        peer = sharding.PeerOutput(D.pg, nloc * D.world * 4)
+        gargs = _lib.AllgatherArgs()
+        for r, p in enumerate(peer.peer_ptrs):
+            gargs.peer_c[r] = p
+        gargs.world, gargs.rank, gargs.row_offset = D.world, D.rank, n0
+        done = torch.zeros(1, device="cuda")
+        fa = lib().piton_b200_add_allgather_f32
+
+        def step():
+            _lib.check(fa(C.byref(a), C.byref(gargs), stream), "add_allgather")
+            D.pg.all_reduce(done)
+    else:
+        def step():
+            kernel_only()
+            D.allgather(torch, ofull, out)
 
     t_kernel = timed(torch, D, kernel_only, args.steps, args.warmup)
     # at N = 1 the step is the kernel-only call itself: one measurement serves both
     t_step = timed(torch, D, step, args.steps, args.warmup) if D.world > 1 else t_kernel
     lib_calls["launches"] += args.steps * (2 if D.world > 1 else 1)
     err = float((out[:1 << 20] - (x[:1 << 20] + y[:1 << 20])).abs().max())
+    if peer is not None:
+        # this rank's range in its own full output, and a checksum of every rank's range there
+        torch.cuda.synchronize()
+        D.pg.barrier()
+        got = torch.from_numpy(peer.read(n0 * 4, (1 << 20) * 4).view(np.float32)).cuda()
+        err = max(err, float((got - (x[:1 << 20] + y[:1 << 20])).abs().max()))
+        sums = [None] * D.world
+        D.pg.all_gather_object(sums, float((x + y).double().sum()))
+        for r in range(D.world):
+            theirs = peer.read(r * nloc * 4, nloc * 4).view(np.float32).astype(np.float64).sum()
+            if abs(theirs - sums[r]) > 1e-6 * max(1.0, abs(sums[r])):
+                err = float("inf")
+        D.pg.barrier()
+        peer.close()
     e2e = None
     if not args.no_e2e:
         from piton_b200.kernels import add_kernel

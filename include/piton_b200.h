@@ -178,6 +178,21 @@ PITON_B200_API int piton_b200_matmul_allgather_f32(const piton_matmul_args *args
    output is read anywhere. */
 PITON_B200_API int piton_b200_allgather(const piton_allgather_args *g, uint64_t src, size_t bytes, void *stream);
 
+/* Softmax sharded by rows and vector add sharded by element ranges, each with the output all-gather
+   fused into the kernel (the north star's "softmax by rows / add by elements + all-gather" as one
+   kernel per rank).  No counterpart in the reference (it runs on one device).  Softmax: this rank
+   computes rows [row_offset, row_offset + args->grid_x) of the full output and stores each finished
+   row into row row_offset + r (row stride ldc) of every rank's full output peer_c[*]; rows
+   16-byte aligned, n_cols a multiple of 4 up to 32768.  Add: this rank computes elements
+   [row_offset, row_offset + n) (n = min(n_elements, grid_x * BLOCK_SIZE)) and stores them at the
+   same offsets of every rank's full output; IEEE rounding, 16-byte aligned inputs, n and row_offset
+   multiples of 4.  args->out is not used; multicast_c is not used.  Every rank must pass a barrier
+   after its call before the output is read anywhere. */
+PITON_B200_API int piton_b200_softmax_allgather_f32(const piton_softmax_args *args, const piton_allgather_args *g,
+                                                    void *stream);
+PITON_B200_API int piton_b200_add_allgather_f32(const piton_add_args *args, const piton_allgather_args *g,
+                                                void *stream);
+
 /* CUDA IPC of a cudaMalloc'd buffer (64-byte handle) for the peer pointers above. */
 PITON_B200_API int piton_b200_ipc_handle(uint64_t ptr, void *handle);
 PITON_B200_API int piton_b200_ipc_open(const void *handle, uint64_t *ptr);

@@ -13,6 +13,7 @@
 //   * longer rows: a CTA per row with an online max/sum pass and a second
 //     read for the scaled write (12 bytes per element).
 #include "common.cuh"
+#include "gemm_tc.cuh"
 
 namespace piton {
 
@@ -58,13 +59,24 @@ struct VecT<4> {
 __device__ __forceinline__ float &el(float &v, int) { return v; }
 __device__ __forceinline__ float &el(float4 &v, int i) { return (&v.x)[i]; }
 
+// Destinations of the fused all-gather: row `row` of this rank's shard goes to row row0 + row
+// (row stride ld) of every rank's full output p[0 .. world), starting with the next rank's, so
+// that the ranks' NVLink stores spread over the peers.
+struct GatherOut {
+    float *p[MAX_PEERS];
+    int world, rank;
+    int64_t row0, ld;
+};
+
 // Each row group of TPR threads owns a row; thread t holds, for item i, the VEC
-// columns starting at VEC * (t + i * TPR).
-template <int TPR, int ITEMS, int VEC>
+// columns starting at VEC * (t + i * TPR).  With GATHER the row is stored into every
+// rank's full output instead of `out` (VEC == 4 only).
+template <int TPR, int ITEMS, int VEC, bool GATHER = false>
 __global__ void __launch_bounds__(TPR > 32 ? TPR : 256) softmax_reg_kernel(float *__restrict__ out,
                                                                            const float *__restrict__ in,
                                                                            int64_t in_stride, int64_t out_stride,
-                                                                           int64_t n, int64_t rows) {
+                                                                           int64_t n, int64_t rows,
+                                                                           GatherOut g = GatherOut{}) {
     using V = typename VecT<VEC>::T;
     __shared__ float red[32];
     int64_t row;
@@ -113,7 +125,19 @@ __global__ void __launch_bounds__(TPR > 32 ? TPR : 256) softmax_reg_kernel(float
         if (c < nv) {
 #pragma unroll
             for (int j = 0; j < VEC; ++j) el(x[i], j) *= r;
-            __stcs(dst + c, x[i]);
+            if constexpr (!GATHER) __stcs(dst + c, x[i]);
+        }
+    }
+    if constexpr (GATHER) {
+        for (int d = 0; d < g.world; ++d) {
+            int dr = g.rank + 1 + d;
+            dr = dr >= g.world ? dr - g.world : dr;
+            V *gd = reinterpret_cast<V *>(g.p[dr] + (g.row0 + row) * g.ld);
+#pragma unroll
+            for (int i = 0; i < ITEMS; ++i) {
+                int64_t c = t + (int64_t)i * TPR;
+                if (c < nv) __stcs(gd + c, x[i]);
+            }
         }
     }
 }
@@ -143,32 +167,32 @@ __global__ void __launch_bounds__(1024) softmax_long_kernel(float *__restrict__ 
     for (int64_t c = threadIdx.x; c < n; c += blockDim.x) dst[c] = expf(src[c] - gm) * r;
 }
 
-template <int TPR, int ITEMS, int VEC>
-static void launch_reg(const piton_softmax_args *a, int64_t n, cudaStream_t s) {
+template <int TPR, int ITEMS, int VEC, bool GATHER>
+static void launch_reg(const piton_softmax_args *a, int64_t n, cudaStream_t s, const GatherOut &g) {
     float *out = reinterpret_cast<float *>(a->out);
     const float *in = reinterpret_cast<const float *>(a->in);
     if constexpr (TPR == 32) {
         int64_t blocks = cdiv(a->grid_x, 8);
-        softmax_reg_kernel<32, ITEMS, VEC><<<(unsigned)blocks, 256, 0, s>>>(out, in, a->in_row_stride,
-                                                                            a->out_row_stride, n, a->grid_x);
+        softmax_reg_kernel<32, ITEMS, VEC, GATHER><<<(unsigned)blocks, 256, 0, s>>>(out, in, a->in_row_stride,
+                                                                                    a->out_row_stride, n, a->grid_x, g);
     } else {
-        softmax_reg_kernel<TPR, ITEMS, VEC><<<(unsigned)a->grid_x, TPR, 0, s>>>(out, in, a->in_row_stride,
-                                                                                a->out_row_stride, n, a->grid_x);
+        softmax_reg_kernel<TPR, ITEMS, VEC, GATHER><<<(unsigned)a->grid_x, TPR, 0, s>>>(
+            out, in, a->in_row_stride, a->out_row_stride, n, a->grid_x, g);
     }
 }
 
-template <int VEC>
-static bool dispatch_reg(const piton_softmax_args *a, int64_t n, cudaStream_t s) {
+template <int VEC, bool GATHER = false>
+static bool dispatch_reg(const piton_softmax_args *a, int64_t n, cudaStream_t s, const GatherOut &g = GatherOut{}) {
     int64_t per = cdiv(n, VEC);   // vectors per row
-    if (per <= 32) launch_reg<32, 1, VEC>(a, n, s);
-    else if (per <= 64) launch_reg<32, 2, VEC>(a, n, s);
-    else if (per <= 128) launch_reg<32, 4, VEC>(a, n, s);
-    else if (per <= 256) launch_reg<32, 8, VEC>(a, n, s);
-    else if (per <= 512) launch_reg<256, 2, VEC>(a, n, s);
-    else if (per <= 1024) launch_reg<256, 4, VEC>(a, n, s);
-    else if (per <= 2048) launch_reg<256, 8, VEC>(a, n, s);
-    else if (per <= 4096) launch_reg<512, 8, VEC>(a, n, s);
-    else if (per <= 8192) launch_reg<1024, 8, VEC>(a, n, s);
+    if (per <= 32) launch_reg<32, 1, VEC, GATHER>(a, n, s, g);
+    else if (per <= 64) launch_reg<32, 2, VEC, GATHER>(a, n, s, g);
+    else if (per <= 128) launch_reg<32, 4, VEC, GATHER>(a, n, s, g);
+    else if (per <= 256) launch_reg<32, 8, VEC, GATHER>(a, n, s, g);
+    else if (per <= 512) launch_reg<256, 2, VEC, GATHER>(a, n, s, g);
+    else if (per <= 1024) launch_reg<256, 4, VEC, GATHER>(a, n, s, g);
+    else if (per <= 2048) launch_reg<256, 8, VEC, GATHER>(a, n, s, g);
+    else if (per <= 4096) launch_reg<512, 8, VEC, GATHER>(a, n, s, g);
+    else if (per <= 8192) launch_reg<1024, 8, VEC, GATHER>(a, n, s, g);
     else return false;
     return true;
 }
@@ -194,4 +218,36 @@ extern "C" int piton_b200_softmax_f32(const piton_softmax_args *a, void *stream)
                                                                  reinterpret_cast<const float *>(a->in),
                                                                  a->in_row_stride, a->out_row_stride, n);
     return check_launch("softmax");
+}
+
+// Softmax over this rank's rows with the output all-gather fused into the kernel: row r of the
+// shard (rows [row_offset, row_offset + grid_x) of the full output) is stored into row
+// row_offset + r of every rank's full output through NVLink peer stores, so no separate
+// all-gather runs.  The caller orders completion across ranks (a barrier on every rank after
+// the call) before reading the output.
+extern "C" int piton_b200_softmax_allgather_f32(const piton_softmax_args *a, const piton_allgather_args *g,
+                                                void *stream) {
+    PITON_REQUIRE(a != nullptr && g != nullptr, "args is NULL");
+    PITON_REQUIRE(a->grid_x >= 0 && a->n_cols >= 0 && a->block_size > 0, "bad shape: rows %lld cols %lld BLOCK %lld",
+                  (long long)a->grid_x, (long long)a->n_cols, (long long)a->block_size);
+    PITON_REQUIRE(a->flags == 0, "unknown flags 0x%x", a->flags);
+    PITON_REQUIRE(a->grid_x < (1ll << 31), "too many rows");
+    PITON_REQUIRE(g->world >= 1 && g->world <= MAX_PEERS && g->rank >= 0 && g->rank < g->world,
+                  "world %d / rank %d outside 1..%d", g->world, g->rank, MAX_PEERS);
+    int64_t n = a->n_cols < a->block_size ? a->n_cols : a->block_size;
+    PITON_REQUIRE(g->row_offset >= 0 && g->ldc >= n && g->ldc % 4 == 0, "bad row_offset / ldc");
+    for (int i = 0; i < g->world; ++i)
+        PITON_REQUIRE(g->peer_c[i] != 0 && (g->peer_c[i] & 15) == 0, "peer output %d is NULL or misaligned", i);
+    if (n == 0 || a->grid_x == 0) return PITON_B200_OK;
+    PITON_REQUIRE(a->in, "NULL pointer");
+    PITON_REQUIRE((a->in & 15u) == 0 && a->in_row_stride % 4 == 0 && n % 4 == 0 && n <= 4 * 8192,
+                  "the all-gather softmax needs 16-byte aligned rows, n_cols %% 4 == 0 and n_cols <= 32768");
+    GatherOut go{};
+    for (int i = 0; i < g->world; ++i) go.p[i] = reinterpret_cast<float *>(g->peer_c[i]);
+    go.world = g->world;
+    go.rank = g->rank;
+    go.row0 = g->row_offset;
+    go.ld = g->ldc;
+    dispatch_reg<4, true>(a, n, as_stream(stream), go);
+    return check_launch("softmax_allgather");
 }

@@ -132,6 +132,8 @@ PROTOTYPES = {
     "piton_b200_mlp_f32": (C.c_int, [C.POINTER(MlpArgs), C.c_void_p]),
     "piton_b200_attention_workspace_size": (C.c_size_t, [C.POINTER(AttentionArgs)]),
     "piton_b200_attention_f32": (C.c_int, [C.POINTER(AttentionArgs), C.c_void_p]),
+    "piton_b200_softmax_allgather_f32": (C.c_int, [C.POINTER(SoftmaxArgs), C.POINTER(AllgatherArgs), C.c_void_p]),
+    "piton_b200_add_allgather_f32": (C.c_int, [C.POINTER(AddArgs), C.POINTER(AllgatherArgs), C.c_void_p]),
     "piton_b200_attention_allgather_f32": (C.c_int, [C.POINTER(AttentionArgs), C.POINTER(AllgatherArgs),
                                                      C.c_void_p]),
     "piton_b200_layernorm_f32": (C.c_int, [C.POINTER(LayernormArgs), C.c_void_p]),

@@ -249,6 +249,52 @@ def attention_allgather(q, k, v, peer_ptrs, rank: int, head_offset: int, causal:
                "attention_allgather")
 
 
+def softmax_allgather(x, peer_ptrs, rank: int, row_offset: int, ld: int, stream=None):
+    """Row softmax of this rank's rows x ([rows, n] contiguous CUDA float32, n % 4 == 0, n <= 32768),
+    stored by the fused all-gather kernel into rows [row_offset, row_offset + rows) (row stride `ld`
+    floats) of every rank's full output.  `peer_ptrs`: one device pointer per rank valid in this
+    process, this rank's own output at index `rank`.  Every rank must pass a barrier before
+    reading the outputs."""
+    import ctypes as C
+
+    import torch
+
+    from .runtime.cuda import _lib
+    if x.dim() != 2 or not x.is_contiguous() or x.dtype != torch.float32:
+        raise ValueError("x must be a contiguous float32 [rows, n_cols] tensor")
+    rows, n = x.shape
+    a = _lib.SoftmaxArgs(0, x.data_ptr(), n, n, n, n, rows, 0, 0)
+    g = _lib.AllgatherArgs()
+    for r, p in enumerate(peer_ptrs):
+        g.peer_c[r] = p
+    g.world, g.rank, g.row_offset, g.ldc = len(peer_ptrs), rank, row_offset, ld
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(_lib.lib().piton_b200_softmax_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
+               "softmax_allgather")
+
+
+def add_allgather(x, y, peer_ptrs, rank: int, offset: int, stream=None):
+    """x + y for this rank's elements (contiguous CUDA float32 vectors of a multiple of 4 elements),
+    stored by the fused all-gather kernel into elements [offset, offset + n) of every rank's full
+    output.  Every rank must pass a barrier before reading the outputs."""
+    import ctypes as C
+
+    import torch
+
+    from .runtime.cuda import _lib
+    if x.shape != y.shape or x.dim() != 1 or not (x.is_contiguous() and y.is_contiguous()):
+        raise ValueError("x and y must be contiguous float32 vectors of one length")
+    n = x.numel()
+    a = _lib.AddArgs(x.data_ptr(), y.data_ptr(), 0, n, 1024, -(-n // 1024), 0, 0)
+    g = _lib.AllgatherArgs()
+    for r, p in enumerate(peer_ptrs):
+        g.peer_c[r] = p
+    g.world, g.rank, g.row_offset = len(peer_ptrs), rank, offset
+    s = stream if stream is not None else torch.cuda.current_stream()
+    _lib.check(_lib.lib().piton_b200_add_allgather_f32(C.byref(a), C.byref(g), C.c_void_p(s.cuda_stream)),
+               "add_allgather")
+
+
 def allgather_pieces(piece, out, stream=None):
     """Store this rank's `piece` (a CUDA tensor) into every rank's full output `out`
     (PeerOutput or SymmetricOutput) at byte offset rank * piece.nbytes, with the library's

@@ -221,3 +221,61 @@ def test_fused_allgather_attention_two_gpus():
     for rank, (err, status) in res.items():
         assert status == 0, rank
         assert err <= 2e-5, (rank, err)
+
+
+def _hbm_worker(rank, world, port, results):
+    """Softmax by rows and add by elements, each rank storing its piece into every rank's full
+    output from inside the kernel (NVLink peer stores); every rank must end with the whole."""
+    import datetime
+
+    import torch.distributed as dist
+
+    from piton_b200 import sharding
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    outs = []
+    try:
+        rows, n = 256, 4096
+        g = torch.Generator(device="cuda").manual_seed(9)
+        x = torch.randn(rows, n, device="cuda", generator=g) * 4      # same on every rank (same seed)
+        r0, per = sharding.shard(rows, world, rank)
+        sm = sharding.PeerOutput(dist, rows * n * 4)
+        outs.append(sm)
+        ne = 1 << 20
+        u = torch.rand(ne, device="cuda", generator=g) * 2 - 1
+        v = torch.rand(ne, device="cuda", generator=g) * 2 - 1
+        e0, eper = sharding.shard(ne, world, rank, multiple=4)
+        ad = sharding.PeerOutput(dist, ne * 4)
+        outs.append(ad)
+        for _ in range(2):
+            sharding.softmax_allgather(x[r0:r0 + per], sm.peer_ptrs, rank, r0, n)
+            sharding.add_allgather(u[e0:e0 + eper], v[e0:e0 + eper], ad.peer_ptrs, rank, e0)
+            torch.cuda.synchronize()
+            dist.barrier()
+        got_sm = sm.read(0, rows * n * 4).view(np.float32).reshape(rows, n)
+        ref = torch.softmax(x.double(), 1).cpu().numpy()
+        err_sm = float((np.abs(got_sm - ref) / np.maximum(np.abs(ref), 1e-37)).max())
+        got_add = ad.read(0, ne * 4).view(np.float32)
+        exact_add = bool(np.array_equal(got_add, (u + v).cpu().numpy()))
+        results[rank] = (err_sm, exact_add)
+        dist.barrier()
+    finally:
+        for o in outs:
+            o.close()
+        dist.destroy_process_group()
+
+
+def test_fused_allgather_softmax_and_add_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    with mp.Manager() as manager:
+        results = manager.dict()
+        mp.spawn(_hbm_worker, args=(2, _port(), results), nprocs=2, join=True)
+        res = dict(results)
+    assert len(res) == 2
+    for rank, (err_sm, exact_add) in res.items():
+        assert err_sm <= 1e-5, (rank, err_sm)
+        assert exact_add, rank
