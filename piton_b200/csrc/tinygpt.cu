@@ -583,9 +583,14 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
 // rows of W_pr).  The two 128-wide partial products per layer go to all four CTAs' shared
 // memory (st.shared::cluster) and one cluster barrier each publishes them; every CTA adds the
 // four partials in rank order, so all four keep the same residual stream without further
-// exchange.  Each CTA reads a quarter of the weights from L2 per position (the step kernel's
-// CTAs read all of them), and the whole decode is one launch with 9 cluster barriers per
-// position.
+// exchange.  Each CTA reads a quarter of the weights per position (the step kernel's CTAs read
+// all of them), and the whole decode is one launch with 9 cluster barriers per position.
+//
+// The decode is a chain of short dependent phases, so every global read is taken off it:
+// each phase's weight slice (and its biases / LayerNorm parameters) is copied into one of two
+// shared-memory buffers with cp.async while the previous phase computes; the CTA's vocabulary
+// rows stay in shared memory for the whole decode; the attention issues all of a sequence's
+// key and value loads at once (lanes over positions) and sums P.V with a reduce-scatter.
 // ---------------------------------------------------------------------------
 
 constexpr int HC = H;                 // CTAs per cluster, one per head (portable cluster size)
@@ -595,8 +600,14 @@ constexpr int KGRP = 8;               // k-groups of the split-k linears
 constexpr int FH = F / HC;            // hidden units per CTA (128)
 constexpr int V_R = (V + HC - 1) / HC;   // vocabulary rows per CTA (17)
 constexpr int LG_LD = V + 3;
+// weight-slice buffer: up to 128 x 128 floats plus the phase's small parameters
+constexpr int WB_MAT = D * FH, WB_PAR = 2 * D + FH;   // 16384 + 384 floats
+constexpr int WB = WB_MAT + WB_PAR;
+// the four phases of a layer, in order
+enum Phase { PH_QKV = 0, PH_O = 1, PH_FC = 2, PH_PR = 3 };
 
 struct HeadsSmem {
+    float wbuf[2][WB];                // weight slices, double-buffered
     float x[GS][D];                   // residual stream (the same in all four CTAs)
     float h[GS][D];                   // LayerNorm output
     float q[GS][HD];                  // this head's queries
@@ -604,8 +615,9 @@ struct HeadsSmem {
     float f[GS][FH];                  // this CTA's GELU hidden units
     float part[2][HC][GS][D];         // partial products from every CTA, two slots used in turn
     float red[KGRP][GS][D];           // split-k partial sums
-    float probs[GS][CTX];
     float lg[GS][LG_LD];              // logits, every CTA's vocabulary rows
+    float wte_s[V_R][D];              // this CTA's vocabulary rows of the tied embedding
+    float lnf[2 * D];                 // final LayerNorm gain and bias
     int tok[GS];
 };
 
@@ -627,13 +639,66 @@ __device__ __forceinline__ void st_cluster4(float *local, uint32_t rank, float4 
                  : "memory");
 }
 
-// Split-k product of the group's rows in[s][0..K) (shared memory, row stride K) with NQ quads of
-// weight columns: quad j is columns col0(j) .. col0(j) + 3 of W (row stride ldw, rows krow0 ..
-// krow0 + K).  Thread (j, g) sums k-group g for all GS rows with 16-byte weight loads; the KGRP
-// partial sums meet in red, and epi(s, j, float4) receives each finished quad once.
-template <int K, int NQ, typename ColFn, typename Epi>
-__device__ __forceinline__ void group_linear(const float *in, const float *__restrict__ W, int ldw, int krow0,
-                                             ColFn col0, float (*red)[GS][D], Epi epi) {
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+                 "l"(gmem)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Starts the copies of phase `ph` of layer `l` into buffer `buf` (one commit group per call):
+//   QKV: the head's 96 columns of W_qkv [128 x 96], then ln1 gain, bias, the 96 q/k/v biases;
+//   O:   the head's 32 rows of W_o [32 x 128], then b_o;
+//   FC:  the CTA's 128 columns of W_fc [128 x 128], then ln2 gain, bias, the 128 biases;
+//   PR:  the CTA's 128 rows of W_pr [128 x 128], then b_pr.
+__device__ __forceinline__ void prefetch_phase(float *buf, const float *__restrict__ w, int l, int ph, int rank) {
+    const float *lw = w + V * D + CTX * D + (int64_t)l * LAYER_FLOATS;
+    const float *ln1_g = lw, *ln1_b = ln1_g + D, *w_qkv = ln1_b + D, *b_qkv = w_qkv + D * 3 * D;
+    const float *w_o = b_qkv + 3 * D, *b_o = w_o + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
+    const float *w_fc = ln2_b + D, *b_fc = w_fc + D * F, *w_pr = b_fc + F, *b_pr = w_pr + F * D;
+    float *par = buf + WB_MAT;
+    const int tid = threadIdx.x;
+    if (ph == PH_QKV) {
+        for (int i = tid; i < D * 24; i += HT) {       // 24 quads per row: q, k, v sections of 8 quads
+            const int k = i / 24, j = i % 24;
+            cp_async16(buf + k * 96 + 4 * j, w_qkv + (int64_t)k * 3 * D + (j >> 3) * D + rank * HD + 4 * (j & 7));
+        }
+        for (int i = tid; i < 2 * D / 4 + 24; i += HT) {
+            if (i < D / 4) cp_async16(par + 4 * i, ln1_g + 4 * i);
+            else if (i < D / 2) cp_async16(par + 4 * i, ln1_b + 4 * (i - D / 4));
+            else {
+                const int j = i - D / 2;
+                cp_async16(par + 2 * D + 4 * j, b_qkv + (j >> 3) * D + rank * HD + 4 * (j & 7));
+            }
+        }
+    } else if (ph == PH_O) {
+        for (int i = tid; i < HD * D / 4; i += HT) cp_async16(buf + 4 * i, w_o + (int64_t)rank * HD * D + 4 * i);
+        for (int i = tid; i < D / 4; i += HT) cp_async16(par + 4 * i, b_o + 4 * i);
+    } else if (ph == PH_FC) {
+        for (int i = tid; i < D * FH / 4; i += HT) {
+            const int k = i / (FH / 4), j = i % (FH / 4);
+            cp_async16(buf + k * FH + 4 * j, w_fc + (int64_t)k * F + rank * FH + 4 * j);
+        }
+        for (int i = tid; i < (2 * D + FH) / 4; i += HT) {
+            if (i < D / 4) cp_async16(par + 4 * i, ln2_g + 4 * i);
+            else if (i < D / 2) cp_async16(par + 4 * i, ln2_b + 4 * (i - D / 4));
+            else cp_async16(par + 4 * i, b_fc + rank * FH + 4 * (i - D / 2));
+        }
+    } else {
+        for (int i = tid; i < FH * D / 4; i += HT) cp_async16(buf + 4 * i, w_pr + (int64_t)rank * FH * D + 4 * i);
+        for (int i = tid; i < D / 4; i += HT) cp_async16(par + 4 * i, b_pr + 4 * i);
+    }
+    cp_async_commit();
+}
+
+// Split-k product of the group's rows in[s][0..K) (shared memory, row stride K) with the NQ quads
+// of columns of a weight slice in shared memory (row-major, row stride 4 NQ).  Thread (j, g) sums
+// k-group g for all GS rows; the KGRP partial sums meet in red, and epi(s, j, float4) receives each
+// finished quad once.
+template <int K, int NQ, typename Epi>
+__device__ __forceinline__ void group_linear(const float *in, const float *ws, float (*red)[GS][D], Epi epi) {
     constexpr int KG = K / KGRP;
     static_assert(K % KGRP == 0 && NQ * KGRP <= HT && NQ * 4 <= D, "group_linear tiling");
     const int tid = threadIdx.x;
@@ -642,10 +707,10 @@ __device__ __forceinline__ void group_linear(const float *in, const float *__res
         float4 acc[GS];
 #pragma unroll
         for (int s = 0; s < GS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
-        const float *wp = W + (int64_t)(krow0 + g * KG) * ldw + col0(j);
+        const float *wp = ws + (g * KG) * (4 * NQ) + 4 * j;
 #pragma unroll
         for (int k = 0; k < KG; ++k) {
-            const float4 w = __ldg(reinterpret_cast<const float4 *>(wp + (int64_t)k * ldw));
+            const float4 w = *reinterpret_cast<const float4 *>(wp + k * (4 * NQ));
 #pragma unroll
             for (int s = 0; s < GS; ++s) {
                 const float xv = in[s * K + g * KG + k];
@@ -672,9 +737,9 @@ __device__ __forceinline__ void group_linear(const float *in, const float *__res
     __syncthreads();
 }
 
-// LayerNorm of the group's rows of x into h, a warp per sequence (biased variance, eps 1e-5).
-__device__ __forceinline__ void group_ln(const float (*x)[D], float (*h)[D], const float *__restrict__ g,
-                                         const float *__restrict__ b) {
+// LayerNorm of the group's rows of x into h, a warp per sequence (biased variance, eps 1e-5);
+// gain and bias in shared memory.
+__device__ __forceinline__ void group_ln(const float (*x)[D], float (*h)[D], const float *g, const float *b) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int s = warp; s < GS; s += HT / 32) {
         float v[D / 32], sum = 0.0f;
@@ -698,7 +763,7 @@ __device__ __forceinline__ void group_ln(const float (*x)[D], float (*h)[D], con
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) {
             const int c = lane + 32 * i;
-            h[s][c] = v[i] * r * __ldg(g + c) + __ldg(b + c);
+            h[s][c] = v[i] * r * g[c] + b[c];
         }
     }
     __syncthreads();
@@ -711,15 +776,82 @@ __device__ __forceinline__ void send_part(HeadsSmem &S, int slot, uint32_t rank,
 }
 
 // x[s][c] += bias[c] + the four CTAs' partials of `slot`, added in rank order
-__device__ __forceinline__ void add_parts(HeadsSmem &S, int slot, const float *__restrict__ bias) {
+__device__ __forceinline__ void add_parts(HeadsSmem &S, int slot, const float *bias) {
     for (int i = threadIdx.x; i < GS * D; i += HT) {
         const int s = i / D, c = i % D;
-        float v = __ldg(bias + c);
+        float v = bias[c];
 #pragma unroll
         for (int r = 0; r < HC; ++r) v += S.part[slot][r][s][c];
         S.x[s][c] += v;
     }
     __syncthreads();
+}
+
+// Causal attention of one sequence's head over positions 0..pos, by one warp: lanes over
+// positions t = lane + 32 j; every key and value row the warp needs is requested at once.
+// q: the head's 32 queries (shared memory); kr / vr: the head's cached rows (row stride D).
+// Returns this lane's output dimension (lane) of softmax(q.K^T / sqrt(32)) V.
+__device__ __forceinline__ float head_attention(const float *q, const float *kr, const float *vr, int pos,
+                                                int lane) {
+    constexpr int NJ = CTX / 32;
+    const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
+    float sc[NJ];
+    float mx = -INFINITY;
+    // positions past pos read row pos instead (written, finite) and are masked afterwards, so
+    // that the loads carry no branch and all of them are in flight together
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const int t = lane + 32 * j;
+        const float4 *k4 = reinterpret_cast<const float4 *>(kr + (int64_t)min(t, pos) * D);
+        float acc = 0.0f;
+#pragma unroll
+        for (int d = 0; d < HD / 4; ++d) {
+            const float4 kv = k4[d];
+            const float4 qv = reinterpret_cast<const float4 *>(q)[d];
+            acc = fmaf(qv.x, kv.x, acc);
+            acc = fmaf(qv.y, kv.y, acc);
+            acc = fmaf(qv.z, kv.z, acc);
+            acc = fmaf(qv.w, kv.w, acc);
+        }
+        sc[j] = t <= pos ? acc * scale : -INFINITY;
+        mx = fmaxf(mx, sc[j]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float sum = 0.0f;
+    float acc[HD];
+#pragma unroll
+    for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const int t = lane + 32 * j;
+        const float p = t <= pos ? expf(sc[j] - mx) : 0.0f;
+        sum += p;
+        const float4 *v4 = reinterpret_cast<const float4 *>(vr + (int64_t)min(t, pos) * D);
+#pragma unroll
+        for (int d = 0; d < HD / 4; ++d) {
+            const float4 vv = v4[d];
+            acc[4 * d] = fmaf(p, vv.x, acc[4 * d]);
+            acc[4 * d + 1] = fmaf(p, vv.y, acc[4 * d + 1]);
+            acc[4 * d + 2] = fmaf(p, vv.z, acc[4 * d + 2]);
+            acc[4 * d + 3] = fmaf(p, vv.w, acc[4 * d + 3]);
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+    // reduce-scatter: after the stage of width w, lane L holds the partial sums of the w dims whose
+    // index agrees with L in the bits above w; at the end lane L holds dimension L
+#pragma unroll
+    for (int w = HD / 2; w >= 1; w >>= 1) {
+        const bool upper = (lane & w) != 0;
+#pragma unroll
+        for (int i = 0; i < w; ++i) {
+            const float give = upper ? acc[i] : acc[i + w];
+            const float keep = upper ? acc[i + w] : acc[i];
+            acc[i] = keep + __shfl_xor_sync(0xffffffffu, give, w);
+        }
+    }
+    return acc[0] / sum;
 }
 
 __global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
@@ -731,7 +863,12 @@ __global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
     const float *wte = a.w, *wpe = a.w + V * D;
     const float *lw0 = a.w + V * D + CTX * D;
     const int64_t groups = cdiv_dev(a.batch, a.group);
-    int slot = 0;
+    const int v0 = (int)rank * V_R, nv = min(V_R, V - v0);
+    // the CTA's vocabulary rows and the final LayerNorm, for the whole decode
+    for (int i = tid; i < V_R * D; i += HT) S.wte_s[i / D][i % D] = i / D < nv ? __ldg(wte + (v0 + i / D) * D + i % D) : 0.f;
+    for (int i = tid; i < 2 * D; i += HT) S.lnf[i] = __ldg(lw0 + (int64_t)L * LAYER_FLOATS + i);
+    int slot = 0, buf = 0;
+    prefetch_phase(S.wbuf[0], a.w, 0, PH_QKV, (int)rank);   // the first phase's slice
     cl_sync();   // every CTA of the cluster is running before any stores into its shared memory
 
     for (int64_t grp = cl_id(); grp < groups; grp += cl_count()) {
@@ -750,20 +887,18 @@ __global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
             }
             __syncthreads();
             for (int l = 0; l < L; ++l) {
-                const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
-                const float *ln1_g = lw, *ln1_b = ln1_g + D, *w_qkv = ln1_b + D, *b_qkv = w_qkv + D * 3 * D;
-                const float *w_o = b_qkv + 3 * D, *b_o = w_o + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
-                const float *w_fc = ln2_b + D, *b_fc = w_fc + D * F, *w_pr = b_fc + F, *b_pr = w_pr + F * D;
                 float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
                 float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
-
-                // 1. this head's q, k, v: quads 0-7 q, 8-15 k, 16-23 v
-                group_ln(S.x, S.h, ln1_g, ln1_b);
-                group_linear<D, 24>(
-                    &S.h[0][0], w_qkv, 3 * D, 0, [&](int j) { return (j >> 3) * D + hh * HD + 4 * (j & 7); }, S.red,
-                    [&](int s, int j, float4 v) {
-                        const int c = (j >> 3) * D + hh * HD + 4 * (j & 7);
-                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(b_qkv + c));
+                // each phase: start the next phase's copies, wait for this phase's, compute
+                // 1. LayerNorm and this head's q, k, v: quads 0-7 q, 8-15 k, 16-23 v
+                prefetch_phase(S.wbuf[buf ^ 1], a.w, l, PH_O, (int)rank);
+                cp_async_wait<1>();
+                __syncthreads();
+                {
+                    const float *wq = S.wbuf[buf], *par = wq + WB_MAT;
+                    group_ln(S.x, S.h, par, par + D);
+                    group_linear<D, 24>(&S.h[0][0], wq, S.red, [&](int s, int j, float4 v) {
+                        const float4 bb = *reinterpret_cast<const float4 *>(par + 2 * D + 4 * j);
                         v.x += bb.x; v.y += bb.y; v.z += bb.z; v.w += bb.w;
                         if (j < 8) {
                             *reinterpret_cast<float4 *>(&S.q[s][4 * j]) = v;
@@ -773,103 +908,77 @@ __global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
                                                         4 * (j & 7)) = v;
                         }
                     });
-                // 2. causal attention of head hh over positions 0..pos, a warp per sequence
-                for (int s = warp; s < gs; s += HT / 32) {
-                    const float *kr = kc + ((b0 + s) * CTX) * D + hh * HD;
-                    const float *vr = vc + ((b0 + s) * CTX) * D + hh * HD;
-                    const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
-                    float sc[CTX / 32];
-                    float mx = -INFINITY;
-#pragma unroll
-                    for (int jt = 0; jt < CTX / 32; ++jt) {
-                        const int t = lane + 32 * jt;
-                        float dot = -INFINITY;
-                        if (t <= pos) {
-                            float acc = 0.0f;
-#pragma unroll
-                            for (int d = 0; d < HD; d += 4) {
-                                const float4 k4 = *reinterpret_cast<const float4 *>(kr + (int64_t)t * D + d);
-                                acc = fmaf(S.q[s][d], k4.x, acc);
-                                acc = fmaf(S.q[s][d + 1], k4.y, acc);
-                                acc = fmaf(S.q[s][d + 2], k4.z, acc);
-                                acc = fmaf(S.q[s][d + 3], k4.w, acc);
-                            }
-                            dot = acc * scale;
-                        }
-                        sc[jt] = dot;
-                        mx = fmaxf(mx, dot);
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                    float sum = 0.0f;
-#pragma unroll
-                    for (int jt = 0; jt < CTX / 32; ++jt) {
-                        const int t = lane + 32 * jt;
-                        const float p = t <= pos ? expf(sc[jt] - mx) : 0.0f;
-                        S.probs[s][t] = p;
-                        sum += p;
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                    __syncwarp();
-                    // lane = output dimension; eight positions' values requested at a time
-                    float o0 = 0.0f, o1 = 0.0f;
-                    int t = 0;
-                    for (; t + 8 <= pos + 1; t += 8) {
-                        float vv[8];
-#pragma unroll
-                        for (int u = 0; u < 8; ++u) vv[u] = vr[(int64_t)(t + u) * D + lane];
-#pragma unroll
-                        for (int u = 0; u < 8; u += 2) {
-                            o0 = fmaf(S.probs[s][t + u], vv[u], o0);
-                            o1 = fmaf(S.probs[s][t + u + 1], vv[u + 1], o1);
-                        }
-                    }
-                    for (; t <= pos; ++t) o0 = fmaf(S.probs[s][t], vr[(int64_t)t * D + lane], o0);
-                    S.att[s][lane] = (o0 + o1) / sum;
                 }
-                for (int i = tid; i < (GS - gs) * HD; i += HT) S.att[gs + i / HD][i % HD] = 0.0f;
+                buf ^= 1;
+                // 2. causal attention of head hh, a warp per sequence
+                prefetch_phase(S.wbuf[buf ^ 1], a.w, l, PH_FC, (int)rank);
+                for (int s = warp; s < GS; s += HT / 32) {
+                    if (s < gs) {
+                        const float o = head_attention(S.q[s], kc + ((b0 + s) * CTX) * D + hh * HD,
+                                                       vc + ((b0 + s) * CTX) * D + hh * HD, pos, lane);
+                        S.att[s][lane] = o;
+                    } else {
+                        S.att[s][lane] = 0.0f;
+                    }
+                }
+                cp_async_wait<1>();
                 __syncthreads();
                 // 3. the head's share of the output projection, to every CTA; x += b_o + the four shares
-                group_linear<HD, D / 4>(
-                    &S.att[0][0], w_o, D, hh * HD, [](int j) { return 4 * j; }, S.red,
-                    [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
-                cl_sync();
-                add_parts(S, slot, b_o);
-                slot ^= 1;
-                // 4. this CTA's 128 hidden units, then their share of the MLP projection
-                group_ln(S.x, S.h, ln2_g, ln2_b);
-                group_linear<D, FH / 4>(
-                    &S.h[0][0], w_fc, F, 0, [&](int j) { return (int)rank * FH + 4 * j; }, S.red,
-                    [&](int s, int j, float4 v) {
-                        const float4 bb = __ldg(reinterpret_cast<const float4 *>(b_fc + rank * FH + 4 * j));
+                {
+                    const float *wo = S.wbuf[buf];
+                    group_linear<HD, D / 4>(&S.att[0][0], wo, S.red,
+                                            [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
+                    cl_sync();
+                    add_parts(S, slot, wo + WB_MAT);
+                    slot ^= 1;
+                }
+                buf ^= 1;
+                // 4. LayerNorm and this CTA's 128 GELU hidden units
+                prefetch_phase(S.wbuf[buf ^ 1], a.w, l, PH_PR, (int)rank);
+                cp_async_wait<1>();
+                __syncthreads();
+                {
+                    const float *wf = S.wbuf[buf], *par = wf + WB_MAT;
+                    group_ln(S.x, S.h, par, par + D);
+                    group_linear<D, FH / 4>(&S.h[0][0], wf, S.red, [&](int s, int j, float4 v) {
+                        const float4 bb = *reinterpret_cast<const float4 *>(par + 2 * D + 4 * j);
                         float r4[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) r4[e] = 0.5f * r4[e] * (1.0f + erff(r4[e] * 0.70710678118654752f));
                         *reinterpret_cast<float4 *>(&S.f[s][4 * j]) = make_float4(r4[0], r4[1], r4[2], r4[3]);
                     });
-                group_linear<FH, D / 4>(
-                    &S.f[0][0], w_pr, D, (int)rank * FH, [](int j) { return 4 * j; }, S.red,
-                    [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
-                cl_sync();
-                add_parts(S, slot, b_pr);
-                slot ^= 1;
+                }
+                buf ^= 1;
+                // 5. their share of the MLP projection, to every CTA; x += b_pr + the four shares
+                {
+                    const int nl = l + 1 < L ? l + 1 : 0;   // the next phase: the next layer's (or position's) QKV
+                    prefetch_phase(S.wbuf[buf ^ 1], a.w, nl, PH_QKV, (int)rank);
+                }
+                cp_async_wait<1>();
+                __syncthreads();
+                {
+                    const float *wp = S.wbuf[buf];
+                    group_linear<FH, D / 4>(&S.f[0][0], wp, S.red,
+                                            [&](int s, int j, float4 v) { send_part(S, slot, rank, s, j, v); });
+                    cl_sync();
+                    add_parts(S, slot, wp + WB_MAT);
+                    slot ^= 1;
+                }
+                buf ^= 1;
             }
             const bool next_from_model = pos + 1 >= a.prompt_len && pos + 1 < a.end;
             const bool want_logits = a.logits && pos == a.steps - 1;
             if (!next_from_model && !want_logits) continue;
             // final LayerNorm and the tied head: this CTA's vocabulary rows, a warp per (sequence, row)
-            const float *lnf = lw0 + (int64_t)L * LAYER_FLOATS;
-            group_ln(S.x, S.h, lnf, lnf + D);
-            const int v0 = (int)rank * V_R, nv = min(V_R, V - v0);
+            group_ln(S.x, S.h, S.lnf, S.lnf + D);
             for (int pv = warp; pv < gs * nv; pv += HT / 32) {
-                const int s = pv / nv, v = v0 + pv % nv;
+                const int s = pv / nv, v = pv % nv;
                 float acc = 0.0f;
 #pragma unroll
-                for (int i = 0; i < D / 32; ++i) acc = fmaf(S.h[s][lane + 32 * i], __ldg(wte + v * D + lane + 32 * i), acc);
+                for (int i = 0; i < D / 32; ++i) acc = fmaf(S.h[s][lane + 32 * i], S.wte_s[v][lane + 32 * i], acc);
 #pragma unroll
                 for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                if (lane < HC) st_cluster(&S.lg[s][v], lane, acc);
+                if (lane < HC) st_cluster(&S.lg[s][v0 + v], lane, acc);
             }
             cl_sync();
             if (tid < gs) {
@@ -886,7 +995,8 @@ __global__ void __launch_bounds__(HT, 1) tinygpt_heads_kernel(HeadsArgs a) {
             __syncthreads();
         }
     }
-    cl_sync();   // no CTA leaves while another may still store into its shared memory
+    cp_async_wait<0>();   // the last, unused prefetch lands before the CTA's shared memory goes
+    cl_sync();            // no CTA leaves while another may still store into its shared memory
 }
 
 }  // namespace tg
