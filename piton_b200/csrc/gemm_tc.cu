@@ -1,57 +1,48 @@
-// fp32 GEMM on the 5th-generation tensor cores from a split of each operand
+// fp32 GEMM on the 5th-generation tensor cores from an fp16 split of each operand
 // (tutorial matmul, examples/kernels.py:18-57, default rounding mode).
 //
-// fp32 accuracy from TF32 / BF16 tensor cores: each operand x is split into
-// x_hi = x with the low 13 mantissa bits cleared (exactly representable in
-// TF32) and x_lo = x - x_hi (exact in fp32, at most 2^-10 |x|), and
-//   C = A_hi B_hi + (A_lo B + A B_lo)
-// where A_hi B_hi is a kind::tf32 product (exact products) and the bracket is
-// one kind::f16 product of bf16 operands, concatenated along k: per group of 8
-// k-values the A operand holds [bf16(A_lo), bf16(A)] and the B operand
-// [bf16(B), bf16(B_lo)], so one 16-deep bf16 MMA adds A_lo B + A B_lo over the
-// same 8 k-values a tf32 MMA covers.  A B_lo + A_lo B = A_hi B_lo + A_lo B_hi +
-// 2 A_lo B_lo; with A_lo B_lo below 2^-20 of the product, the bracket carries
-// the two cross terms of the classic 3xTF32 split (and the lo x lo term once
-// more, at most 2^-20 of the product).  Rounding both operands of a cross term
-// to bf16 (8-bit mantissas) costs at most 2^-8 of a term that is itself at most
-// 2^-10 of the product: at most 2^-17 + 2^-20 per product, ~2^-19.6 rms, with
-// unbiased (round-to-nearest) signs.  A bf16 MMA of depth 16 issues as
-// fast as a tf32 MMA of depth 8, so each 8-deep k-step takes two MMAs instead
-// of 3xTF32's three, from the same shared-memory bytes.
+// fp32 accuracy from FP16 tensor cores: every 256-deep chunk of a row of A (and of a
+// column of B) is scaled by a power of two 2^e that brings its largest finite magnitude
+// into [2^14, 2^15), and each scaled value s is split into s_hi = fp16(s) and
+// s_lo = fp16(s - s_hi) (s - s_hi is exact in fp32), 22 significant bits in all.  Then
+//   C = sum over chunks of 2^-(e_A + e_B) (A_hi B_hi + A_hi B_lo + A_lo B_hi)
+// with three kind::f16 MMAs per 16 k-values (fp16 products are exact in the fp32
+// accumulator); the dropped A_lo B_lo and the rounding of the low halves cost about
+// 2^-21 of a product, against ~2^-17 for a tf32 high half with bf16 cross terms, and the
+// operands take 4 bytes per element (hi + lo) instead of 8.  A value too small for fp16's
+// subnormals after scaling (below 2^-25 of its chunk's largest) contributes ~nothing.  A
+// chunk holding an inf or nan is marked (exponent NONFINITE): split products cannot keep
+// IEEE semantics there (inf x a zero low half is nan), so a small kernel after the GEMM
+// recomputes that row (or column) of C with fp32 FMAs from A and B.
 //
 // Two kernels per call:
-//  1. split: reads A and B with their (arbitrary) element strides and writes
-//     A_hi as [M, ld] fp32 (ld = K rounded up to 4) and the cross operand A_x
-//     as [M, ldx] bf16 (ldx = 2 x K rounded up to 16), and B_hi, B_x
-//     transposed as [N, ld] / [N, ldx] (K-major), into the caller's workspace.
-//     HBM-bound.  A row-major A is its own A_hi (see below).
-//  2. gemm: persistent, one CTA per SM (320 threads): warp 0 issues TMA tile
-//     loads (128x16 A tiles, 256x16 B tiles (fp32) and the bf16 tiles of the
-//     same 16 k-values, 64-byte swizzle, 4-stage mbarrier ring), warp 1 owns
-//     512 TMEM columns (two 128x256 fp32 accumulators) and issues, from one
-//     thread, tcgen05.mma kind::tf32 128x256x8 and kind::f16 128x256x16,
-//     warps 2-9 drain finished accumulators with tcgen05.ld.
+//  1. split: reads A and B with their (arbitrary) element strides and writes A_hi, A_lo
+//     as [M, ldh] fp16 and B_hi, B_lo transposed as [N, ldh] (K-major, ldh = K rounded up
+//     to 8) and the chunk exponents e as int8 [chunks, M] / [chunks, N], into the
+//     caller's workspace.  HBM-bound.
+//  2. gemm: persistent, one CTA per SM (320 threads): warp 0 issues TMA tile loads
+//     (128x32 A_hi / A_lo tiles and BNx32 B_hi / B_lo tiles, 64-byte swizzle, 4-stage
+//     mbarrier ring), warp 1 owns 512 TMEM columns (two 128xBN fp32 accumulators) and
+//     issues, from one thread, three tcgen05.mma kind::f16 128xBNx16 per 16 k-values,
+//     warps 2-9 drain finished accumulators with tcgen05.ld and apply the chunk scales.
 //
-// The tensor cores add into the TMEM accumulator with truncation, and that
-// bias grows with the number of accumulation steps (at K = 8192 it is ~30x
-// the error of an fp32 FFMA loop).  So an accumulator only ever holds a chunk
-// of KC = 256 k-values: the MMA warp alternates between the two TMEM
-// buffers per chunk, and the epilogue warps add every finished chunk into an
-// fp32 register sum (round to nearest), then store the tile with C's element
-// strides.  The error is then at the level of an fp32 FFMA loop.
-// Every mbarrier wait is bounded (2 s of global time): on expiry the kernel
-// records a status word, drains its own TMA copies and MMAs, frees TMEM and
-// returns.
+// The tensor cores add into the TMEM accumulator with truncation, and that bias grows
+// with the number of accumulation steps (at K = 8192 it is ~30x the error of an fp32
+// FFMA loop).  So an accumulator only ever holds a chunk of KC = 256 k-values (one
+// scaling chunk): the MMA warp alternates between the two TMEM buffers per chunk, and
+// the epilogue warps multiply every finished chunk by its 2^-(e_A + e_B) and add it into
+// an fp32 register sum (round to nearest), then store the tile with C's element strides.
+// Every mbarrier wait is bounded (2 s of global time): on expiry the kernel records a
+// status word, drains its own TMA copies and MMAs, frees TMEM and returns.
 #include <algorithm>
 #include <vector>
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "attention.cuh"
 #include "common.cuh"
 #include "gemm_tc.cuh"
 #include "sm100.cuh"
-#include "split.cuh"
 
 namespace piton {
 
@@ -61,88 +52,144 @@ __device__ int g_tc_status = 0;
 
 namespace {
 
-constexpr int BM = 128, BK = 16, STAGES = 4;
+constexpr int BM = 128, BK = 32, STAGES = 4;   // BK: fp16 k-values per stage (64-byte rows)
 constexpr int THREADS = 320;
 constexpr int EPI_WARPS = 8;
-constexpr int KC_BLOCKS = 16;   // k-blocks of BK per accumulation chunk (KC = 256)
-constexpr uint32_t A_TILE_BYTES = BM * BK * 4;   // 8 KB: 128 rows x 16 fp32, or x 32 bf16 (cross operand)
+constexpr int KC = 256;                         // k-values per accumulation and scaling chunk
+constexpr int KC_BLOCKS = KC / BK;              // k-blocks per chunk
+constexpr uint32_t A_TILE_BYTES = BM * BK * 2;   // 8 KB: 128 rows x 32 fp16 (A_hi, or A_lo)
 // BN (tile width along N) is 256, or 224 where that packs the tiles into fewer
-// rounds over the SMs (tile_width()); a B tile is BN x 16 fp32 (14 or 16 KB), and
-// its cross tile BN x 32 bf16 as many bytes
-__host__ __device__ constexpr uint32_t b_tile_bytes(int bn) { return (uint32_t)bn * BK * 4; }
+// rounds over the SMs (tile_width()); a B tile is BN x 32 fp16 (14 or 16 KB), hi and lo
+__host__ __device__ constexpr uint32_t b_tile_bytes(int bn) { return (uint32_t)bn * BK * 2; }
 __host__ __device__ constexpr uint32_t stage_bytes(int bn) { return 2 * A_TILE_BYTES + 2 * b_tile_bytes(bn); }
 __host__ __device__ constexpr uint32_t smem_bytes(int bn) { return STAGES * stage_bytes(bn) + 1024 /*barriers*/ + 1024 /*alignment*/; }
 constexpr int TMEM_COLS = 512;
 constexpr int GROUP_M = 16;
 
-__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
+// Marker exponent of a chunk that holds an inf or a nan (outside the clamp range below).
+constexpr int NONFINITE = -128;
 
-// Cross operand of value v (at k) in a row of the bf16 array x: per group of 8
-// k-values, positions [16 g, 16 g + 8) hold the first part and [16 g + 8, 16 g + 16)
-// the second.  A side: (bf16(lo), bf16(v)); B side: (bf16(v), bf16(lo)), so that one
-// 16-deep product of the two adds A_lo B + A B_lo.  Non-finite values contribute 0
-// (their high half carries them), finite ones are clamped to the bf16 range.
-__device__ __forceinline__ void put_cross(__nv_bfloat16 *xrow, int64_t c, float v, float lo, bool a_side) {
-    const int64_t p = 16 * (c >> 3) + (c & 7);
-    xrow[p] = a_side ? split_bf16_of(lo) : split_bf16_of(v);
-    xrow[p + 8] = a_side ? split_bf16_of(v) : split_bf16_of(lo);
+// Exponent e of a chunk's scale 2^e: its largest finite magnitude m goes into [2^14, 2^15);
+// 0 for a chunk without a finite non-zero value; clamped to [-112, 112] (2^e and 2^-e normal).
+__device__ __forceinline__ int chunk_exponent(float m) {
+    if (!(m > 0.0f)) return 0;
+    int E;
+    frexpf(m, &E);   // m = f 2^E, f in [0.5, 1)
+    return max(-112, min(112, 15 - E));
 }
 
-// hi[r * ld + c] (if hi) and the cross operand x[r * ldx + ...] from src[r * s_row + c * s_col],
-// r < rows, c < cols, through 32 x 32 shared-memory tiles so that both the strided read and the
-// write coalesce; k-values from cols up to the next multiple of 8 are written as zeros.
-__global__ void __launch_bounds__(256) split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                    int64_t s_row, int64_t s_col, float *__restrict__ hi,
-                                                    __nv_bfloat16 *__restrict__ x, int64_t ld, int64_t ldx,
-                                                    int lanes_along_rows, int a_side) {
-    __shared__ float tile[32][33];
-    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;    // 32 x 8
-    for (int j = ty; j < 32; j += 8) {
-        int64_t r = lanes_along_rows ? r0 + tx : r0 + j;
-        int64_t c = lanes_along_rows ? c0 + j : c0 + tx;
-        float v = (r < rows && c < cols) ? src[r * s_row + c * s_col] : 0.0f;
-        if (lanes_along_rows) tile[tx][j] = v;
-        else tile[j][tx] = v;
+// s = v 2^e split into fp16 halves: hi = fp16(s), lo = fp16(s - hi); non-finite s keeps its
+// high half and a zero low half.
+__device__ __forceinline__ void split_half(float v, float sc, __half &hi, __half &lo) {
+    const float s = v * sc;
+    hi = __float2half_rn(s);
+    lo = __float2half_rn(isfinite(s) ? s - __half2float(hi) : 0.0f);
+}
+
+__device__ __forceinline__ float finite_abs(float v) { return isfinite(v) ? fabsf(v) : 0.0f; }
+
+// Rows with unit stride along k (row-major A, or B stored column-major): one warp per
+// (row, 256-deep chunk), 8 consecutive k-values per lane (two 16-byte loads when `vec`),
+// the chunk's maximum by shuffles, 16-byte stores of both halves.  k-values from K up to
+// ldh (K rounded up to 8) are written as zeros; the exponent goes to ex[chunk * ld_ex + row].
+__global__ void __launch_bounds__(256) split16_rows_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
+                                                           int64_t s_row, __half *__restrict__ hi,
+                                                           __half *__restrict__ lo, int8_t *__restrict__ ex,
+                                                           int64_t ldh, int64_t ld_ex, int chunks, int vec) {
+    const int lane = threadIdx.x & 31;
+    const int64_t w = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+    if (w >= rows * chunks) return;
+    const int64_t r = w / chunks;
+    const int c = (int)(w % chunks);
+    const int64_t k0 = (int64_t)c * KC + 8 * lane;
+    const float *row = src + r * s_row;
+    float v[8];
+    if (vec && k0 + 8 <= K) {
+        const float4 p = __ldcs(reinterpret_cast<const float4 *>(row + k0));
+        const float4 q = __ldcs(reinterpret_cast<const float4 *>(row + k0 + 4));
+        v[0] = p.x; v[1] = p.y; v[2] = p.z; v[3] = p.w; v[4] = q.x; v[5] = q.y; v[6] = q.z; v[7] = q.w;
+    } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] = k0 + e < K ? row[k0 + e] : 0.0f;
+    }
+    float m = 0.0f;
+    bool bad = false;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        m = fmaxf(m, finite_abs(v[e]));
+        bad |= !isfinite(v[e]);
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    bad = __any_sync(0xffffffffu, bad);
+    const int ee = chunk_exponent(m);
+    const float sc = ldexpf(1.0f, ee);
+    __align__(16) __half h[8], l[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) split_half(v[e], sc, h[e], l[e]);
+    if (k0 < ldh) {
+        *reinterpret_cast<uint4 *>(hi + r * ldh + k0) = *reinterpret_cast<const uint4 *>(h);
+        *reinterpret_cast<uint4 *>(lo + r * ldh + k0) = *reinterpret_cast<const uint4 *>(l);
+    }
+    if (lane == 0) ex[(int64_t)c * ld_ex + r] = (int8_t)(bad ? NONFINITE : ee);
+}
+
+// Any strides (row-major B transposed into K-major rows, transposed or strided A): a CTA
+// stages a 32-row x 256-k tile in shared memory, reading with the lanes along whichever of
+// rows and k has the unit (smaller) stride so that the loads coalesce, then each warp splits
+// four rows: a half2 of consecutive k-values per lane, 128-byte stores per warp.
+__global__ void __launch_bounds__(256) split16_tile_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
+                                                           int64_t s_row, int64_t s_col, __half *__restrict__ hi,
+                                                           __half *__restrict__ lo, int8_t *__restrict__ ex,
+                                                           int64_t ldh, int64_t ld_ex, int lanes_along_rows) {
+    __shared__ float tile[32][KC + 1];
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int c = blockIdx.x;
+    const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)c * KC;
+    if (lanes_along_rows) {
+        const int64_t r = r0 + lane;
+        for (int kk = warp; kk < KC; kk += 8) {
+            const int64_t k = k0 + kk;
+            tile[lane][kk] = (r < rows && k < K) ? src[r * s_row + k * s_col] : 0.0f;
+        }
+    } else {
+        for (int rr = warp; rr < 32; rr += 8) {
+            const int64_t r = r0 + rr;
+            for (int kk = lane; kk < KC; kk += 32) {
+                const int64_t k = k0 + kk;
+                tile[rr][kk] = (r < rows && k < K) ? src[r * s_row + k * s_col] : 0.0f;
+            }
+        }
     }
     __syncthreads();
-    const int64_t cols8 = (cols + 7) / 8 * 8;
-    for (int j = ty; j < 32; j += 8) {
-        int64_t r = r0 + j, c = c0 + tx;
-        if (r < rows && c < cols8) {
-            const float v = c < cols ? tile[j][tx] : 0.0f;
-            const float h = tf32_trunc(v);
-            if (hi && c < cols) hi[r * ld + c] = h;
-            put_cross(x + r * ldx, c, v, isfinite(v) ? v - h : 0.0f, a_side != 0);
-        }
-    }
-}
-
-// Row-major A with unit column stride and 16-byte aligned rows: kind::tf32 MMAs ignore
-// the low 13 bits of an fp32 operand (the raw value multiplies exactly as its truncated
-// high half), so the GEMM reads A_hi straight from the source and only the cross operand
-// is written: per thread 4 k-values in (one float4), 4 + 4 bf16 out (two 8-byte stores).
-__global__ void __launch_bounds__(256) split_rows_vec4_kernel(const float *__restrict__ src, int64_t rows,
-                                                              int64_t cols, int64_t s_row,
-                                                              __nv_bfloat16 *__restrict__ x, int64_t ldx) {
-    const int64_t q_per_row = (cols + 7) / 8 * 2;   // cols % 4 == 0: whole float4s, up to the 8-group
-    const int64_t total = rows * q_per_row;
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total;
-         i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t r = i / q_per_row, c = 4 * (i % q_per_row);
-        const float4 v = c < cols ? __ldcs(reinterpret_cast<const float4 *>(src + r * s_row + c))
-                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-        __align__(8) __nv_bfloat16 lo[4], full[4];
+    for (int rr = warp; rr < 32; rr += 8) {
+        const int64_t r = r0 + rr;
+        if (r >= rows) break;
+        float m = 0.0f;
+        bool bad = false;
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            const float h = tf32_trunc(vv[e]);
-            lo[e] = split_bf16_of(isfinite(vv[e]) ? vv[e] - h : 0.0f);
-            full[e] = split_bf16_of(vv[e]);
+        for (int e = 0; e < KC / 64; ++e) {
+            const float v0 = tile[rr][2 * lane + 64 * e], v1 = tile[rr][2 * lane + 64 * e + 1];
+            m = fmaxf(m, fmaxf(finite_abs(v0), finite_abs(v1)));
+            bad |= !isfinite(v0) || !isfinite(v1);
         }
-        __nv_bfloat16 *p = x + r * ldx + 16 * (c >> 3) + (c & 7);
-        *reinterpret_cast<uint2 *>(p) = *reinterpret_cast<const uint2 *>(lo);
-        *reinterpret_cast<uint2 *>(p + 8) = *reinterpret_cast<const uint2 *>(full);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+        bad = __any_sync(0xffffffffu, bad);
+        const int ee = chunk_exponent(m);
+        const float sc = ldexpf(1.0f, ee);
+#pragma unroll
+        for (int e = 0; e < KC / 64; ++e) {
+            const int64_t k = k0 + 2 * lane + 64 * e;
+            if (k < ldh) {
+                __half h0, l0, h1, l1;
+                split_half(tile[rr][2 * lane + 64 * e], sc, h0, l0);
+                split_half(tile[rr][2 * lane + 64 * e + 1], sc, h1, l1);
+                *reinterpret_cast<__half2 *>(hi + r * ldh + k) = __halves2half2(h0, h1);
+                *reinterpret_cast<__half2 *>(lo + r * ldh + k) = __halves2half2(l0, l1);
+            }
+        }
+        if (lane == 0) ex[(int64_t)c * ld_ex + r] = (int8_t)(bad ? NONFINITE : ee);
     }
 }
 
@@ -155,7 +202,48 @@ struct GemmArgs {
     int64_t row_offset, ldc_peer;
     float *peer_c[MAX_PEERS];
     float *mc_c;                     // multicast all-gather: one multimem store reaches every rank
+    const int8_t *ea, *eb;           // chunk exponents of A [chunks, ld_ea] and of B [chunks, ld_eb]
+    int64_t ld_ea, ld_eb;
+    const float *a, *b;              // the fp32 operands (chunks marked NONFINITE are recomputed from them)
+    int64_t sam, sak, sbk, sbn;
 };
+
+// The contribution of a finished chunk product `acc` to C: acc 2^-(ea + eb) (exponent bits
+// directly when the scale is a normal float, exp2f otherwise; a zero stays zero even where the
+// scale overflows).  Rows and columns with a chunk marked NONFINITE get garbage here and are
+// rewritten by nonfinite_fixup_kernel after the GEMM.
+__device__ __forceinline__ float chunk_value(float acc, int ea, int eb) {
+    const int et = 127 - ea - eb;
+    const float sc = (unsigned)(et - 1) < 254u ? __int_as_float(et << 23) : exp2f((float)(et - 127));
+    return acc == 0.0f ? 0.0f : acc * sc;
+}
+
+// After the GEMM: every row of A and every column of B with a chunk marked NONFINITE (an inf or
+// a nan, which split products cannot carry with IEEE semantics: inf times a zero low half is nan)
+// has its row / column of C recomputed with fp32 FMAs over the whole K, a warp per row or column.
+// Without such values each warp only reads its row's or column's chunk exponents.
+__global__ void __launch_bounds__(256) nonfinite_fixup_kernel(GemmArgs g, int chunks) {
+    const int lane = threadIdx.x & 31;
+    const int64_t idx = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+    const bool is_row = idx < g.M;
+    if (idx >= g.M + g.N) return;
+    const int64_t i = is_row ? idx : idx - g.M;
+    bool bad = false;
+    for (int c = lane; c < chunks; c += 32)
+        bad |= (is_row ? g.ea[(int64_t)c * g.ld_ea + i] : g.eb[(int64_t)c * g.ld_eb + i]) == NONFINITE;
+    if (!__any_sync(0xffffffffu, bad)) return;
+    const int64_t n_out = is_row ? g.N : g.M;
+    for (int64_t o = lane; o < n_out; o += 32) {
+        const int64_t row = is_row ? i : o, col = is_row ? o : i;
+        float s = 0.0f;
+        for (int64_t k = 0; k < g.K; ++k) s = fmaf(g.a[row * g.sam + k * g.sak], g.b[k * g.sbk + col * g.sbn], s);
+        if (g.world > 0) {
+            for (int r = 0; r < g.world; ++r) g.peer_c[r][(g.row_offset + row) * g.ldc_peer + col] = s;
+        } else {
+            g.c[row * g.scm + col * g.scn] = s;
+        }
+    }
+}
 
 // multimem stores: the NVSwitch writes the value into the memory of every GPU bound
 // to the multicast address (relaxed, system scope; the kernel ends with a system fence)
@@ -212,9 +300,9 @@ __device__ __forceinline__ void copy_rows_to_peers(const GemmArgs &args, int64_t
 
 template <int BN>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_3xtf32_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_ax,
-                       const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_bx,
-                       GemmArgs args) {
+    gemm_f16x3_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
+                      const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
+                      GemmArgs args) {
     constexpr uint32_t B_TILE_BYTES = b_tile_bytes(BN);
     constexpr uint32_t STAGE_BYTES = stage_bytes(BN);
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -243,10 +331,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(epi_bar, EPI_WARPS);
         *abort_flag = 0;
         fence_mbarrier_init();
-        prefetch_tmap(&tm_ahi);
-        prefetch_tmap(&tm_ax);
-        prefetch_tmap(&tm_bhi);
-        prefetch_tmap(&tm_bx);
+        prefetch_tmap(&tm_ah);
+        prefetch_tmap(&tm_al);
+        prefetch_tmap(&tm_bh);
+        prefetch_tmap(&tm_bl);
     }
     if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_holder);
     tc_fence_before();
@@ -271,11 +359,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     uint8_t *st = smem + s * STAGE_BYTES;
                     mbar_arrive_expect_tx(&full[s], STAGE_BYTES);
-                    const int kx = kb * BK, kxx = 2 * kb * BK;   // fp32 and bf16 (cross) columns
-                    tma_load_2d(st, &tm_ahi, &full[s], kx, tm * BM);
-                    tma_load_2d(st + A_TILE_BYTES, &tm_ax, &full[s], kxx, tm * BM);
-                    tma_load_2d(st + 2 * A_TILE_BYTES, &tm_bhi, &full[s], kx, tn * BN);
-                    tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_bx, &full[s], kxx, tn * BN);
+                    const int kx = kb * BK;
+                    tma_load_2d(st, &tm_ah, &full[s], kx, tm * BM);
+                    tma_load_2d(st + A_TILE_BYTES, &tm_al, &full[s], kx, tm * BM);
+                    tma_load_2d(st + 2 * A_TILE_BYTES, &tm_bh, &full[s], kx, tn * BN);
+                    tma_load_2d(st + 2 * A_TILE_BYTES + B_TILE_BYTES, &tm_bl, &full[s], kx, tn * BN);
                 }
             }
             // drain: every copy this thread issued has landed before the CTA may exit
@@ -286,7 +374,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer ----------------
         if (lane == 0) {
-            constexpr uint32_t IDESC = idesc_tf32(BM, BN), IDESC_X = idesc_bf16(BM, BN);
+            constexpr uint32_t IDESC = idesc_f16(BM, BN);
             uint32_t it = 0, chunk = 0;
             bool ok = true;
             for (int t = blockIdx.x; ok && t < args.num_tiles && !*abort_flag; t += gridDim.x) {
@@ -312,19 +400,20 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         tc_fence_after();
                         uint32_t base = smem_u32(smem + s * STAGE_BYTES);
-                        uint32_t a_hi = base, a_x = base + A_TILE_BYTES;
-                        uint32_t b_hi = base + 2 * A_TILE_BYTES, b_x = b_hi + B_TILE_BYTES;
+                        uint32_t a_hi = base, a_lo = base + A_TILE_BYTES;
+                        uint32_t b_hi = base + 2 * A_TILE_BYTES, b_lo = b_hi + B_TILE_BYTES;
 #pragma unroll
-                        for (int ks = 0; ks < BK / 8; ++ks) {
-                            // 8 tf32, or the 16 bf16 of the same 8 k-values: 32 bytes along K in the row
+                        for (int ks = 0; ks < BK / 16; ++ks) {
+                            // 16 fp16 k-values: 32 bytes along K in the row
                             uint32_t off = ks * 32;
                             uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            uint64_t dax = smem_desc_kmajor(a_x + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
                             uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            uint64_t dbx = smem_desc_kmajor(b_x + off, 64, LAYOUT_SWIZZLE_64B);
+                            uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
                             uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
-                            mma_bf16(d_tmem, dax, dbx, IDESC_X, first);   // A_lo B + A B_lo
-                            mma_tf32(d_tmem, dah, dbh, IDESC, 1u);        // A_hi B_hi
+                            mma_f16(d_tmem, dah, dbh, IDESC, first);   // A_hi B_hi
+                            mma_f16(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
+                            mma_f16(d_tmem, dal, dbh, IDESC, 1u);      // A_lo B_hi
                         }
                         mma_commit(&empty[s]);   // stage s free once these MMAs have read it
                     }
@@ -349,6 +438,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         int pend_tm = -1, pend_tn = -1;                       // finished tile still to be sent to peers
         uint32_t tiles_done = 0;
         for (int t = blockIdx.x; ok && t < args.num_tiles; t += gridDim.x) {
+            int tm, tn;
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
+            const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
+            const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
             for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk, ++ci) {
                 const int acc = chunk & 1;
                 const uint32_t use = chunk >> 1;
@@ -365,13 +458,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < BN / 2; ++j) sum[j] = 0.0f;
                 }
+                const int ea = row < args.M ? (int)args.ea[(int64_t)ci * args.ld_ea + row] : 0;
+                const int8_t *ebc = args.eb + (int64_t)ci * args.ld_eb;
 #pragma unroll
                 for (int part = 0; part < BN / 2 / 16; ++part) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(taddr + part * 16, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) sum[part * 16 + j] += __uint_as_float(r[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        const int64_t col = col0 + part * 16 + j;
+                        const int eb = col < args.N ? (int)ebc[col] : 0;
+                        sum[part * 16 + j] += chunk_value(__uint_as_float(r[j]), ea, eb);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -381,11 +480,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                                        min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
-            int tm, tn;
-            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
-            const int64_t row = (int64_t)tm * BM + quarter * 32 + lane;
             if (row < args.M) {
-                const int64_t col0 = (int64_t)tn * BN + half * (BN / 2);
                 if (args.mc_c) {
                     // multicast all-gather: one store per element, replicated to every rank by the switch
                     float *mrow = args.mc_c + (args.row_offset + row) * args.ldc_peer;
@@ -483,8 +578,8 @@ __global__ void __launch_bounds__(THREADS, 1)
 // cluster barriers (after set-up, before TMEM is freed) are reached unconditionally.
 
 constexpr int STAGES2 = 6;
-constexpr uint32_t A2_TILE_BYTES = BM * BK * 4;   // 8 KB: this CTA's 128 rows
-__host__ __device__ constexpr uint32_t b2_tile_bytes(int bnp) { return (uint32_t)(bnp / 2) * BK * 4; }
+constexpr uint32_t A2_TILE_BYTES = BM * BK * 2;   // 8 KB: this CTA's 128 rows x 32 fp16
+__host__ __device__ constexpr uint32_t b2_tile_bytes(int bnp) { return (uint32_t)(bnp / 2) * BK * 2; }
 __host__ __device__ constexpr uint32_t stage2_bytes(int bnp) { return 2 * A2_TILE_BYTES + 2 * b2_tile_bytes(bnp); }
 __host__ __device__ constexpr uint32_t smem2_bytes(int bnp) { return STAGES2 * stage2_bytes(bnp) + 1024 + 1024; }
 
@@ -513,14 +608,7 @@ __device__ __forceinline__ void tma_load_2d_pair(void *dst, const CUtensorMap *m
         "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster), "r"(x), "r"(y)
         : "memory");
 }
-__device__ __forceinline__ void mma_tf32_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
-    asm volatile(
-        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-        "tcgen05.mma.cta_group::2.kind::tf32 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d),
-        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u)
-        : "memory");
-}
-__device__ __forceinline__ void mma_bf16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+__device__ __forceinline__ void mma_f16_pair(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
     asm volatile(
         "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
         "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d),
@@ -538,9 +626,9 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
 
 template <int BNP>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_3xtf32_2sm_kernel(const __grid_constant__ CUtensorMap tm_ahi, const __grid_constant__ CUtensorMap tm_ax,
-                           const __grid_constant__ CUtensorMap tm_bhi, const __grid_constant__ CUtensorMap tm_bx,
-                           GemmArgs args) {
+    gemm_f16x3_2sm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
+                          const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
+                          GemmArgs args) {
     constexpr uint32_t B_TILE = b2_tile_bytes(BNP), STAGE = stage2_bytes(BNP);
     constexpr int HALF = BNP / 2;   // accumulator columns per epilogue warpgroup, and B rows per CTA
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -572,10 +660,10 @@ __global__ void __launch_bounds__(THREADS, 1)
         mbar_init(epi_bar, EPI_WARPS);
         *abort_flag = 0;
         fence_mbarrier_init();
-        prefetch_tmap(&tm_ahi);
-        prefetch_tmap(&tm_ax);
-        prefetch_tmap(&tm_bhi);
-        prefetch_tmap(&tm_bx);
+        prefetch_tmap(&tm_ah);
+        prefetch_tmap(&tm_al);
+        prefetch_tmap(&tm_bh);
+        prefetch_tmap(&tm_bl);
     }
     if (warp == 1) {   // the same warp of both CTAs allocates the pair's TMEM
         asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_holder)),
@@ -608,11 +696,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint8_t *st = smem + s * STAGE;
                     const uint32_t bar = cluster_addr_rank0(&full[s]);
                     if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE);   // both CTAs' bytes
-                    const int kx = kb * BK, kxx = 2 * kb * BK;   // fp32 and bf16 (cross) columns
-                    tma_load_2d_pair(st, &tm_ahi, bar, kx, arow);
-                    tma_load_2d_pair(st + A2_TILE_BYTES, &tm_ax, bar, kxx, arow);
-                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES, &tm_bhi, bar, kx, brow);
-                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES + B_TILE, &tm_bx, bar, kxx, brow);
+                    const int kx = kb * BK;
+                    tma_load_2d_pair(st, &tm_ah, bar, kx, arow);
+                    tma_load_2d_pair(st + A2_TILE_BYTES, &tm_al, bar, kx, arow);
+                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES, &tm_bh, bar, kx, brow);
+                    tma_load_2d_pair(st + 2 * A2_TILE_BYTES + B_TILE, &tm_bl, bar, kx, brow);
                 }
             }
             // drain: every copy of both CTAs completes on the even CTA's stage barriers
@@ -625,7 +713,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer (even CTA) ----------------
         if (lane == 0 && leader) {
-            constexpr uint32_t IDESC = idesc_tf32(2 * BM, BNP), IDESC_X = idesc_bf16(2 * BM, BNP);
+            constexpr uint32_t IDESC = idesc_f16(2 * BM, BNP);
             uint32_t it = 0, chunk = 0;
             bool ok = true;
             for (int t = pair; ok && t < args.num_tiles && !*abort_flag; t += npairs) {
@@ -647,18 +735,19 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                         tc_fence_after();
                         const uint32_t base = smem_u32(smem + s * STAGE);
-                        const uint32_t a_hi = base, a_x = base + A2_TILE_BYTES;
-                        const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_x = b_hi + B_TILE;
+                        const uint32_t a_hi = base, a_lo = base + A2_TILE_BYTES;
+                        const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_lo = b_hi + B_TILE;
 #pragma unroll
-                        for (int ks = 0; ks < BK / 8; ++ks) {
-                            const uint32_t off = ks * 32;
+                        for (int ks = 0; ks < BK / 16; ++ks) {
+                            const uint32_t off = ks * 32;   // 16 fp16 k-values
                             const uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dax = smem_desc_kmajor(a_x + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
                             const uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dbx = smem_desc_kmajor(b_x + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
                             const uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
-                            mma_bf16_pair(d_tmem, dax, dbx, IDESC_X, first);   // A_lo B + A B_lo
-                            mma_tf32_pair(d_tmem, dah, dbh, IDESC, 1u);        // A_hi B_hi
+                            mma_f16_pair(d_tmem, dah, dbh, IDESC, first);   // A_hi B_hi
+                            mma_f16_pair(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
+                            mma_f16_pair(d_tmem, dal, dbh, IDESC, 1u);      // A_lo B_hi
                         }
                         mma_commit_pair(&empty[s]);   // stage s free in both CTAs
                     }
@@ -690,6 +779,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         int64_t pend_row = -1;
         uint32_t tiles_done = 0;
         for (int t = pair; ok && t < args.num_tiles; t += npairs) {
+            int tm, tn;
+            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
+            const int64_t row_base = (int64_t)tm * 2 * BM + (int64_t)rank * BM;
+            const int64_t row = row_base + quarter * 32 + lane;
+            const int64_t col0 = (int64_t)tn * BNP + half * HALF;
             for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk, ++ci) {
                 const int acc = chunk & 1;
                 const uint32_t use = chunk >> 1;
@@ -706,13 +800,19 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                     for (int j = 0; j < HALF; ++j) sum[j] = 0.0f;
                 }
+                const int ea = row < args.M ? (int)args.ea[(int64_t)ci * args.ld_ea + row] : 0;
+                const int8_t *ebc = args.eb + (int64_t)ci * args.ld_eb;
 #pragma unroll
                 for (int part = 0; part < HALF / 16; ++part) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(taddr + part * 16, r);
                     tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < 16; ++j) sum[part * 16 + j] += __uint_as_float(r[j]);
+                    for (int j = 0; j < 16; ++j) {
+                        const int64_t col = col0 + part * 16 + j;
+                        const int eb = col < args.N ? (int)ebc[col] : 0;
+                        sum[part * 16 + j] += chunk_value(__uint_as_float(r[j]), ea, eb);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
@@ -722,13 +822,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                             min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
-            int tm, tn;
-            tile_coords(t, args.tiles_m, args.tiles_n, args.group, tm, tn);
-            const int64_t row_base = (int64_t)tm * 2 * BM + (int64_t)rank * BM;
-            const int64_t row = row_base + quarter * 32 + lane;
             if (row < args.M && args.mc_c) {
                 // multicast all-gather: one store per element, replicated to every rank by the switch
-                const int64_t col0 = (int64_t)tn * BNP + half * HALF;
                 float *mrow = args.mc_c + (args.row_offset + row) * args.ldc_peer;
 #pragma unroll
                 for (int j = 0; j < HALF; j += 4) {
@@ -741,7 +836,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                 }
             } else if (row < args.M) {
-                const int64_t col0 = (int64_t)tn * BNP + half * HALF;
                 float *crow;
                 bool vec;
                 int64_t scn;
@@ -818,39 +912,24 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// Row-major [rows, ld] fp32 (inner extent `cols`), box [box_rows, BK], 64-byte swizzle.
-int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld, int box_rows) {
+// Row-major [rows, ldh] fp16, box [box_rows, BK] (64 bytes per row), 64-byte swizzle.
+int make_map16(CUtensorMap *map, const __half *base, int64_t rows, int64_t ldh, int box_rows) {
     EncodeTiled enc = encode_fn();
     if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
+    cuuint64_t dims[2] = {(cuuint64_t)ldh, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)(ldh * 2)};
     cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
+    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (fp16) failed (%d)", (int)r);
     return PITON_B200_OK;
 }
 
-// bf16 cross operand [rows, ldx]: 16 bf16 (32 bytes) per group of 8 k-values; box [box_rows, 2 * BK]
-// (the same 64 bytes per row as an fp32 box of BK), 64-byte swizzle.
-int make_map_x(CUtensorMap *map, const __nv_bfloat16 *base, int64_t rows, int64_t ldx, int box_rows) {
-    EncodeTiled enc = encode_fn();
-    if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)ldx, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ldx * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)(2 * BK), (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16 *>(base), dims, strides, box,
-                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
-    return PITON_B200_OK;
-}
-
-int64_t ld_of(int64_t K) { return (K + 3) / 4 * 4; }
-int64_t ldx_of(int64_t K) { return (K + 7) / 8 * 16; }
+int64_t ldh_of(int64_t K) { return (K + 7) / 8 * 8; }        // fp16 row: 16-byte multiple
+int64_t chunks_of(int64_t K) { return (K + KC - 1) / KC; }
+int64_t lde_of(int64_t rows) { return (rows + 15) / 16 * 16; }   // exponent row per chunk
 
 // CTA pairs (2-SM MMAs) for problems with at least two 256-row tiles; tile width along N
 // chosen as for one CTA, over the pairs.
@@ -863,13 +942,13 @@ int pair_tile_width(int64_t M, int64_t N) {
 }
 
 template <int BNP>
-int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_x, const CUtensorMap &b_hi, const CUtensorMap &b_x,
+int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtensorMap &b_hi, const CUtensorMap &b_lo,
                  GemmArgs g, cudaStream_t stream) {
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_2sm_kernel<BNP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        PITON_CUDA(cudaFuncSetAttribute(gemm_f16x3_2sm_kernel<BNP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         smem2_bytes(BNP)));
         attr[dev] = true;
     }
@@ -886,7 +965,7 @@ int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_x, const CUtensor
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_3xtf32_2sm_kernel<BNP>, a_hi, a_x, b_hi, b_x, g));
+    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16x3_2sm_kernel<BNP>, a_hi, a_lo, b_hi, b_lo, g));
     return PITON_B200_OK;
 }
 
@@ -900,8 +979,10 @@ int tile_width(int64_t M, int64_t N) {
     const int64_t cost224 = cdiv(tm * cdiv(N, (int64_t)224), sms) * 224;
     return cost224 < cost256 ? 224 : 256;
 }
-size_t region(int64_t rows, int64_t K) { return ((size_t)rows * ld_of(K) * 4 + 1023) / 1024 * 1024; }
-size_t xregion(int64_t rows, int64_t K) { return ((size_t)rows * ldx_of(K) * 2 + 1023) / 1024 * 1024; }
+size_t hregion(int64_t rows, int64_t K) { return ((size_t)rows * ldh_of(K) * 2 + 1023) / 1024 * 1024; }
+size_t eregion(int64_t rows, int64_t K) { return ((size_t)chunks_of(K) * lde_of(rows) + 1023) / 1024 * 1024; }
+// one operand's split: hi and lo [rows, ldh] fp16, then the chunk exponents [chunks, lde] int8
+size_t oregion(int64_t rows, int64_t K) { return 2 * hregion(rows, K) + eregion(rows, K); }
 
 }  // namespace
 
@@ -915,57 +996,59 @@ bool tc_gemm_supported(const TcGemmShape &s) {
     return encode_fn() != nullptr;
 }
 
-size_t tc_gemm_workspace_bytes(const TcGemmShape &s) {
-    return region(s.M, s.K) + xregion(s.M, s.K) + region(s.N, s.K) + xregion(s.N, s.K);
+size_t tc_gemm_workspace_bytes(const TcGemmShape &s) { return oregion(s.N, s.K) + oregion(s.M, s.K); }
+
+namespace {
+
+// hi, lo and exponents of one operand from its workspace region
+struct Split16 {
+    __half *hi, *lo;
+    int8_t *ex;
+};
+Split16 split_at(uint8_t *base, int64_t rows, int64_t K) {
+    Split16 p;
+    p.hi = reinterpret_cast<__half *>(base);
+    p.lo = reinterpret_cast<__half *>(base + hregion(rows, K));
+    p.ex = reinterpret_cast<int8_t *>(base + 2 * hregion(rows, K));
+    return p;
 }
 
-int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
-    const int64_t ld = ld_of(s.K), ldx = ldx_of(s.K);
-    uint8_t *ws = static_cast<uint8_t *>(workspace);
-    const size_t nb = region(s.N, s.K) + xregion(s.N, s.K);   // B's operands first: their place does not depend on M
-    float *b_hi = reinterpret_cast<float *>(ws);
-    __nv_bfloat16 *b_x = reinterpret_cast<__nv_bfloat16 *>(ws + region(s.N, s.K));
-    float *a_hi = reinterpret_cast<float *>(ws + nb);
-    __nv_bfloat16 *a_x = reinterpret_cast<__nv_bfloat16 *>(ws + nb + region(s.M, s.K));
-
-    // 1. split A [M, K] and B^T [N, K] into the tf32 high halves and the bf16 cross operands.
-    //    A row-major A with 16-byte aligned rows is its own high half (the tensor core ignores the
-    //    low 13 bits): only A_x is written and the A_hi tensor map reads A in place.
-    const bool vec_a = s.sak == 1 && s.K % 4 == 0 && s.sam % 4 == 0 && s.sam >= s.K && s.sam < (1ll << 37) &&
-                       (reinterpret_cast<uintptr_t>(s.a) & 15) == 0;
-    {
-        dim3 ga((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.M, 32));
-        if (vec_a) {
-            int64_t blocks = cdiv(s.M * (ldx / 8), 256);
-            if (blocks > (int64_t)num_sms() * 16) blocks = (int64_t)num_sms() * 16;
-            split_rows_vec4_kernel<<<(unsigned)blocks, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, a_x, ldx);
-        } else {
-            int along_rows_a = llabs(s.sam) < llabs(s.sak);
-            split_kernel<<<ga, 256, 0, stream>>>(s.a, s.M, s.K, s.sam, s.sak, a_hi, a_x, ld, ldx, along_rows_a, 1);
-        }
-        if (s.split_b) {
-            // row-major B (unit n stride, 16-byte aligned rows): 64 x 64-tile transpose with 16-byte stores
-            const bool vec_b = s.sbn == 1 && s.N % 4 == 0 && s.sbk % 4 == 0 && (reinterpret_cast<uintptr_t>(s.b) & 15) == 0;
-            if (vec_b) {
-                dim3 gb((unsigned)cdiv(s.K, 64), (unsigned)cdiv(s.N, 64));
-                split_transpose_kernel<SPLIT_T_GEMM_B><<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbk, 0, b_hi, nullptr,
-                                                                                b_x, ld, ldx);
-            } else {
-                dim3 gb((unsigned)cdiv(s.K, 32), (unsigned)cdiv(s.N, 32));
-                int along_rows_b = llabs(s.sbn) < llabs(s.sbk);
-                split_kernel<<<gb, 256, 0, stream>>>(s.b, s.N, s.K, s.sbn, s.sbk, b_hi, b_x, ld, ldx, along_rows_b, 0);
-            }
-        }
+// src[r * s_row + k * s_col] (r < rows, k < K) into the fp16 halves and chunk exponents
+void split16(const float *src, int64_t rows, int64_t K, int64_t s_row, int64_t s_col, const Split16 &d,
+             cudaStream_t stream) {
+    const int64_t ldh = ldh_of(K), chunks = chunks_of(K), lde = lde_of(rows);
+    if (s_col == 1) {
+        const int vec = s_row % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
+        const int64_t warps = rows * chunks;
+        split16_rows_kernel<<<(unsigned)cdiv(warps, 8), 256, 0, stream>>>(src, rows, K, s_row, d.hi, d.lo, d.ex, ldh,
+                                                                            lde, (int)chunks, vec);
+    } else {
+        dim3 g((unsigned)chunks, (unsigned)cdiv(rows, 32));
+        split16_tile_kernel<<<g, 256, 0, stream>>>(src, rows, K, s_row, s_col, d.hi, d.lo, d.ex, ldh, lde,
+                                                   llabs(s_row) < llabs(s_col));
     }
+}
+
+}  // namespace
+
+int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
+    const int64_t ldh = ldh_of(s.K);
+    uint8_t *ws = static_cast<uint8_t *>(workspace);
+    // B's operands first: their place does not depend on M
+    const Split16 B = split_at(ws, s.N, s.K);
+    const Split16 A = split_at(ws + oregion(s.N, s.K), s.M, s.K);
+
+    // 1. split A [M, K] and B^T [N, K] (row n of B^T is column n of B) into scaled fp16 halves
+    split16(s.a, s.M, s.K, s.sam, s.sak, A, stream);
+    if (s.split_b) split16(s.b, s.N, s.K, s.sbn, s.sbk, B, stream);
     // 2. persistent tcgen05 GEMM
     const bool pairs = use_pairs(s.M, s.N);
     const int bn = pairs ? pair_tile_width(s.M, s.N) : tile_width(s.M, s.N);
     const int b_box = pairs ? bn / 2 : bn;   // rows of B^T one CTA loads
-    CUtensorMap m_ahi, m_ax, m_bhi, m_bx;
+    CUtensorMap m_ah, m_al, m_bh, m_bl;
     int rc;
-    if ((rc = vec_a ? make_map(&m_ahi, s.a, s.M, s.K, s.sam, BM) : make_map(&m_ahi, a_hi, s.M, s.K, ld, BM)) ||
-        (rc = make_map_x(&m_ax, a_x, s.M, ldx, BM)) || (rc = make_map(&m_bhi, b_hi, s.N, s.K, ld, b_box)) ||
-        (rc = make_map_x(&m_bx, b_x, s.N, ldx, b_box)))
+    if ((rc = make_map16(&m_ah, A.hi, s.M, ldh, BM)) || (rc = make_map16(&m_al, A.lo, s.M, ldh, BM)) ||
+        (rc = make_map16(&m_bh, B.hi, s.N, ldh, b_box)) || (rc = make_map16(&m_bl, B.lo, s.N, ldh, b_box)))
         return rc;
     GemmArgs g;
     g.c = s.c;
@@ -977,25 +1060,33 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.ldc_peer = s.ldc_peer;
     for (int i = 0; i < MAX_PEERS; ++i) g.peer_c[i] = s.peer_c[i];
     g.mc_c = s.multicast_c;
+    g.ea = A.ex;
+    g.eb = B.ex;
+    g.ld_ea = lde_of(s.M);
+    g.ld_eb = lde_of(s.N);
+    g.a = s.a;
+    g.b = s.b;
+    g.sam = s.sam; g.sak = s.sak; g.sbk = s.sbk; g.sbn = s.sbn;
     if (pairs) {
         g.tiles_m = (int)cdiv(s.M, (int64_t)(2 * BM));
         g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
         g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
         g.num_tiles = g.tiles_m * g.tiles_n;
-        rc = bn == 224 ? launch_pairs<224>(m_ahi, m_ax, m_bhi, m_bx, g, stream)
-                       : launch_pairs<256>(m_ahi, m_ax, m_bhi, m_bx, g, stream);
+        rc = bn == 224 ? launch_pairs<224>(m_ah, m_al, m_bh, m_bl, g, stream)
+                       : launch_pairs<256>(m_ah, m_al, m_bh, m_bl, g, stream);
         if (rc) return rc;
-        return check_launch("gemm_3xtf32_2sm", s.split_b ? 3 : 2);
+        nonfinite_fixup_kernel<<<(unsigned)cdiv(s.M + s.N, 8), 256, 0, stream>>>(g, (int)chunks_of(s.K));
+        return check_launch("gemm_f16x3_2sm", s.split_b ? 4 : 3);
     }
     static bool attr[64][2] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev][bn == 224]) {
         if (bn == 224)
-            PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<224>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            PITON_CUDA(cudaFuncSetAttribute(gemm_f16x3_kernel<224>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             smem_bytes(224)));
         else
-            PITON_CUDA(cudaFuncSetAttribute(gemm_3xtf32_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            PITON_CUDA(cudaFuncSetAttribute(gemm_f16x3_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             smem_bytes(256)));
         attr[dev][bn == 224] = true;
     }
@@ -1005,10 +1096,11 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.num_tiles = g.tiles_m * g.tiles_n;
     int grid = g.num_tiles < num_sms() ? g.num_tiles : num_sms();
     if (bn == 224)
-        gemm_3xtf32_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ahi, m_ax, m_bhi, m_bx, g);
+        gemm_f16x3_kernel<224><<<grid, THREADS, smem_bytes(224), stream>>>(m_ah, m_al, m_bh, m_bl, g);
     else
-        gemm_3xtf32_kernel<256><<<grid, THREADS, smem_bytes(256), stream>>>(m_ahi, m_ax, m_bhi, m_bx, g);
-    return check_launch("gemm_3xtf32", s.split_b ? 3 : 2);
+        gemm_f16x3_kernel<256><<<grid, THREADS, smem_bytes(256), stream>>>(m_ah, m_al, m_bh, m_bl, g);
+    nonfinite_fixup_kernel<<<(unsigned)cdiv(s.M + s.N, 8), 256, 0, stream>>>(g, (int)chunks_of(s.K));
+    return check_launch("gemm_f16x3", s.split_b ? 4 : 3);
 }
 
 int tc_status_read_and_clear(int *status) {

@@ -165,6 +165,13 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
         : "memory");
 }
 
+// The same instruction with fp16 operands: kind::f16 takes its element type from the
+// instruction descriptor (idesc_f16 / idesc_bf16).
+__device__ __forceinline__ void mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                        uint32_t accumulate) {
+    mma_bf16(d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+
 // D[tmem] += A[tmem] * B[smem]^T, kind::f16 with bf16 operands: A is M=128 lanes x K=16,
 // two bf16 per 32-bit column (even k in the low half), 8 columns from a_tmem.
 __device__ __forceinline__ void mma_bf16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc) {
@@ -250,6 +257,15 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
     return (1u << 4)                       // D format f32
            | (1u << 7)                     // A format bf16
            | (1u << 10)                    // B format bf16
+           | ((uint32_t)(N >> 3) << 17)    // N / 8
+           | ((uint32_t)(M >> 4) << 24);   // M / 16
+}
+
+// Instruction descriptor: D f32, A/B fp16, both K-major, M x N (kind::f16, format 0).
+__host__ __device__ constexpr uint32_t idesc_f16(int M, int N) {
+    return (1u << 4)                       // D format f32
+           | (0u << 7)                     // A format f16
+           | (0u << 10)                    // B format f16
            | ((uint32_t)(N >> 3) << 17)    // N / 8
            | ((uint32_t)(M >> 4) << 24);   // M / 16
 }

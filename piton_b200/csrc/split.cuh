@@ -1,6 +1,5 @@
-// Transposing split of an fp32 matrix into tensor-core operands, shared by the GEMM
-// (B -> B^T high half + bf16 cross operand) and the attention (V -> V^T high / low
-// halves + bf16 copy).  Each translation unit instantiates its own mode.
+// Transposing split of an fp32 matrix into tensor-core operands for the attention
+// (V -> V^T tf32 high / low halves + bf16 copy).
 #pragma once
 #include <cuda_bf16.h>
 #include <stdint.h>
@@ -20,7 +19,7 @@ __device__ __forceinline__ uint32_t split_bf16_pair(float a, float b) {
     return (uint32_t)__bfloat16_as_ushort(split_bf16_of(a)) | ((uint32_t)__bfloat16_as_ushort(split_bf16_of(b)) << 16);
 }
 
-enum : int { SPLIT_T_GEMM_B = 0, SPLIT_T_ATTN_V = 1 };
+enum : int { SPLIT_T_ATTN_V = 1 };
 
 // Destination row r (r < rows) of head h holds the source elements src[h * s_h + c * s_col + r],
 // c < cols: the transpose of a source whose elements along r are contiguous (rows % 4 == 0,
@@ -28,9 +27,6 @@ enum : int { SPLIT_T_GEMM_B = 0, SPLIT_T_ATTN_V = 1 };
 // 16-byte loads along r, and per thread 8 consecutive c of one destination row out, in 16-byte
 // stores (eight neighbouring threads cover 64 consecutive c of a row, so a warp writes 4 runs of
 // 256 contiguous bytes).  Grid (cdiv(cols, 64), cdiv(rows, 64), heads), 256 threads.
-//  SPLIT_T_GEMM_B: hi[r * ld + c] = tf32 high half (c < cols); x[r * ldx + 16 (c / 8) + ...] = the
-//    bf16 cross operand of the B side, (bf16(v), bf16(v - hi)) per group of 8 c, zeros for c from
-//    cols up to the next multiple of 8.
 //  SPLIT_T_ATTN_V: hi, lo[r * ld + c] = tf32 high half and tf32 of the rest, x[r * ldx + c] = bf16(v).
 // Per head the destinations advance by rows * ld (hi, lo) and rows * ldx (x).
 template <int MODE>
@@ -55,9 +51,10 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__res
         tile[cc][4 * q + 3] = v.w;
     }
     __syncthreads();
-    const int64_t c_end = MODE == SPLIT_T_GEMM_B ? (cols + 7) / 8 * 8 : cols;
+    static_assert(MODE == SPLIT_T_ATTN_V, "the attention's V is the only transposing split");
+    const int64_t c_end = cols;
     float *hh = hi + h * rows * ld;
-    float *ll = MODE == SPLIT_T_ATTN_V ? lo + h * rows * ld : nullptr;
+    float *ll = lo + h * rows * ld;
     __nv_bfloat16 *xx = x + h * rows * ldx;
 #pragma unroll
     for (int i = t; i < 64 * 8; i += 256) {
@@ -81,14 +78,7 @@ __global__ void __launch_bounds__(256) split_transpose_kernel(const float *__res
             for (int e = 0; e < 8; ++e)
                 if (c + e < cols) hrow[e] = vh[e];
         }
-        if (MODE == SPLIT_T_GEMM_B) {
-            // (bf16(v), bf16(lo)) for the 8 c of the group: 32 bytes at 16 (c / 8) = 2 c
-            uint4 *dst = reinterpret_cast<uint4 *>(xx + r * ldx + 2 * c);
-            dst[0] = make_uint4(split_bf16_pair(v[0], v[1]), split_bf16_pair(v[2], v[3]), split_bf16_pair(v[4], v[5]),
-                                split_bf16_pair(v[6], v[7]));
-            dst[1] = make_uint4(split_bf16_pair(vl[0], vl[1]), split_bf16_pair(vl[2], vl[3]),
-                                split_bf16_pair(vl[4], vl[5]), split_bf16_pair(vl[6], vl[7]));
-        } else {
+        {
             float *lrow = ll + r * ld + c;
 #pragma unroll
             for (int e = 0; e < 8; ++e) vl[e] = split_tf32_trunc(vl[e]);

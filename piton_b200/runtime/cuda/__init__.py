@@ -286,7 +286,7 @@ def _matmul(L: Launch, grid):
     dense_c = s["stride_cm"] == N and s["stride_cn"] == 1 and full_grid
     if full_grid and M > 0 and N > 0 and not L.capturing and _matmul_on_host_buffers(L, M, N, K, s, bm, bn, bk, g,
                                                                                      grid):
-        return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K, "path": "tcgen05_3xtf32_host_pipelined"}
+        return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K, "path": "tcgen05_f16x3_host_pipelined"}
     A, B, Cb = L.ptr("a_ptr"), L.ptr("b_ptr"), L.ptr("c_ptr", written=True, covers=M * N if dense_c else -1)
     if M > 0 and N > 0 and grid[0] > 0:
         A.require(*extent((M, s["stride_am"]), (K, s["stride_ak"])))
@@ -299,7 +299,7 @@ def _matmul(L: Launch, grid):
     a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_matmul_f32", a, "matmul_kernel")
     return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K,
-            "path": "tcgen05_3xtf32" if ws else "cuda_core"}
+            "path": "tcgen05_f16x3" if ws else "cuda_core"}
 
 
 def _matmul_on_host_buffers(L: Launch, M, N, K, s, bm, bn, bk, g, grid) -> bool:

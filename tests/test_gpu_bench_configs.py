@@ -59,7 +59,7 @@ def test_matmul_8192_cubed(cuda):
     st = matmul_kernel[(triton.cdiv(M, 8) * triton.cdiv(N, 64),)](
         A, B, Cd, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
         device="b200").last_stats
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     rows = pair_tile_rows(M)
     assert len(rows) == 64
     c = Cd[torch.from_numpy(rows).cuda()].cpu().numpy()

@@ -2,7 +2,7 @@
 
 * QPU rounding mode (CUDA cores, sequential k, round-toward-zero): bit-exact
   with the oracle and the emulator goldens, negative C row stride included.
-* Default mode (tcgen05 3xTF32 where the layout allows, CUDA cores else):
+* Default mode (tcgen05 fp16 split with per-chunk scaling where the layout allows, CUDA cores else):
   normalised error max|C - C_oracle| / max|C_oracle| <= 2e-5 * sqrt(K), the
   hot-path tolerance; the float64 product is also checked at fp32 level,
   <= max(4e-6, 1e-7 * sqrt(K)) normalised -- the error of an fp32 FFMA loop is
@@ -124,7 +124,7 @@ def test_tensor_core_path_large(cuda, M, N, K):
     ref = A.double() @ B.double()
     err = float((C.double() - ref).abs().max() / ref.abs().max())
     assert err <= fp32_bound(K), (err, st)
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     assert device_status() == 0
 
 
@@ -157,7 +157,7 @@ def test_tensor_core_pairs_strided_c(cuda, M, N, K, neg):
             A, B, Ct, M, N, K, K, 1, N, 1, Ct.stride(0), Ct.stride(1), BLOCK_SIZE_M=8, BLOCK_SIZE_N=64,
             BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
         got = Ct
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     ref = A.double() @ B.double()
     err = float((got.double() - ref).abs().max() / ref.abs().max())
     assert err <= fp32_bound(K), err
@@ -178,7 +178,7 @@ def test_tensor_core_224_wide_tiles_ragged_n(cuda, M, N, K):
     st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
         A, B, Cp, M, N, K, K, 1, N, 1, ldc, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
         device="b200").last_stats
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     ref = A.double() @ B.double()
     err = float((Cp[:, :N].double() - ref).abs().max() / ref.abs().max())
     assert err <= fp32_bound(K), err
@@ -198,7 +198,7 @@ def test_tensor_core_k_edges(cuda, K):
         A, B, C, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
         device="b200").last_stats
     ref = A.double() @ B.double()
-    if st["path"] == "tcgen05_3xtf32":
+    if st["path"] == "tcgen05_f16x3":
         assert device_status() == 0
     err = float((C[:M].double() - ref).abs().max() / ref.abs().max())
     assert err <= fp32_bound(K), (err, st)
@@ -207,9 +207,9 @@ def test_tensor_core_k_edges(cuda, K):
 
 @pytest.mark.parametrize("K", [257, 1004])
 def test_tensor_core_transposed_operands_odd_k(cuda, K):
-    """A and B given as transposes (unit stride along M and along K): both operands go through the
-    32 x 32-tile strided split, whose cross operand is zero-filled up to the next multiple of 8
-    k-values; C written through a transposed view."""
+    """A and B given as transposes (unit stride along M and along K): A goes through the
+    strided (tile) split and B through the row split (B^T rows are contiguous), both
+    zero-filled up to the next multiple of 8 k-values; C written through a transposed view."""
     torch = cuda
     M, N = 384, 256
     A = (torch.rand(K, M, device="cuda") * 2 - 1).t()     # stride_am = 1, stride_ak = M
@@ -218,8 +218,63 @@ def test_tensor_core_transposed_operands_odd_k(cuda, K):
     st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
         A, B, C, M, N, K, A.stride(0), A.stride(1), B.stride(0), B.stride(1), C.stride(0), C.stride(1),
         BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     assert device_status() == 0
     ref = A.double() @ B.double()
     err = float((C.double() - ref).abs().max() / ref.abs().max())
+    assert err <= fp32_bound(K), err
+
+
+def test_tensor_core_wide_dynamic_range(cuda):
+    """Rows of A and columns of B spread over 2^-60 .. 2^60, far outside fp16's range: the
+    per-chunk power-of-two scaling keeps every element at fp32 level relative to its own row's
+    and column's magnitude (a single scale per matrix would flush the small ones to zero)."""
+    torch = cuda
+    M, N, K = 640, 768, 700
+    g = torch.Generator(device="cuda").manual_seed(60)
+    ra = torch.exp2(torch.randint(-60, 61, (M, 1), device="cuda", generator=g).float())
+    cb = torch.exp2(torch.randint(-60, 61, (1, N), device="cuda", generator=g).float())
+    A = (torch.rand(M, K, device="cuda", generator=g) * 2 - 1) * ra
+    B = (torch.rand(K, N, device="cuda", generator=g) * 2 - 1) * cb
+    C = torch.empty(M, N, device="cuda")
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
+        device="b200").last_stats
+    assert st["path"] == "tcgen05_f16x3"
+    assert device_status() == 0
+    exact = A.double() @ B.double()
+    scale = A.abs().amax(1, keepdim=True).double() * B.abs().amax(0, keepdim=True).double()
+    err = float(((C.double() - exact).abs() / scale).max())
+    assert err <= fp32_bound(K), err
+
+
+def test_tensor_core_non_finite_operands(cuda):
+    """inf and nan inputs keep IEEE semantics on the tensor-core path: rows of A and columns of B
+    whose chunks hold one are recomputed in fp32 after the GEMM (a split product would give nan
+    for inf times an exactly representable value), every other element is unaffected."""
+    torch = cuda
+    M, N, K = 512, 384, 1000
+    g = torch.Generator(device="cuda").manual_seed(61)
+    A = torch.rand(M, K, device="cuda", generator=g) * 2 - 1
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    B[5, :] = 1.0                                   # exactly representable: its low halves are zero
+    A[3, 5] = float("inf")
+    A[100, 999] = float("-inf")
+    A[200, 7] = float("inf")
+    A[200, 8] = float("-inf")                        # inf + -inf: nan
+    B[300, 7] = float("nan")
+    C = torch.empty(M, N, device="cuda")
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, K, 1, N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8,
+        device="b200").last_stats
+    assert st["path"] == "tcgen05_f16x3"
+    assert device_status() == 0
+    exact = (A.double() @ B.double()).cpu().numpy()
+    got = C.double().cpu().numpy()
+    np.testing.assert_array_equal(np.isnan(got), np.isnan(exact))
+    np.testing.assert_array_equal(np.isposinf(got), np.isposinf(exact))
+    np.testing.assert_array_equal(np.isneginf(got), np.isneginf(exact))
+    fin = np.isfinite(exact)
+    assert fin.sum() > 0.9 * fin.size
+    err = float(np.abs(got[fin] - exact[fin]).max() / np.abs(exact[fin]).max())
     assert err <= fp32_bound(K), err

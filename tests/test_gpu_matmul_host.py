@@ -37,12 +37,12 @@ def test_host_path_same_bits_as_device_path(cuda, M, N, K, pinned):
         c = np.empty((M, N), np.float32)
     c[...] = np.nan
     st = run(a, b, c, M, N, K)
-    assert st["path"] == "tcgen05_3xtf32_host_pipelined"
+    assert st["path"] == "tcgen05_f16x3_host_pipelined"
     assert st["h2d_bytes"] == 4 * (M * K + K * N) and st["d2h_bytes"] == 4 * M * N
     ta, tb = torch.from_numpy(np.array(a)).cuda(), torch.from_numpy(np.array(b)).cuda()
     tc = torch.full((M, N), float("nan"), device="cuda")
     st2 = run(ta, tb, tc, M, N, K)
-    assert st2["path"] == "tcgen05_3xtf32"
+    assert st2["path"] == "tcgen05_f16x3"
     np.testing.assert_array_equal(c.view(np.uint32), tc.cpu().numpy().view(np.uint32))
     ref = a.astype(np.float64) @ b.astype(np.float64)
     assert np.abs(c - ref).max() / np.abs(ref).max() <= max(4e-6, 1e-7 * np.sqrt(K))
@@ -78,7 +78,7 @@ def test_strided_or_aliased_launches_take_the_generic_path(cuda):
     grid = (triton.cdiv(M, 8) * triton.cdiv(N, 64),)
     st = matmul_kernel[grid](a, bt, c, M, N, K, K, 1, 1, K, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8,
                              GROUP_SIZE_M=8, device="b200").last_stats
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     ref = a.astype(np.float64) @ bt.T.astype(np.float64)
     assert np.abs(c - ref).max() / np.abs(ref).max() <= 4e-6
     # C is A (in-place square product): the generic path, which copies each array in first
@@ -86,7 +86,7 @@ def test_strided_or_aliased_launches_take_the_generic_path(cuda):
     y = rng.uniform(-1, 1, (M, M)).astype(np.float32)
     want = x.astype(np.float64) @ y.astype(np.float64)
     st = run(x, y, x, M, M, M)
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     assert np.abs(x - want).max() / np.abs(want).max() <= 4e-6
 
 
