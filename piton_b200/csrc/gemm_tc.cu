@@ -208,14 +208,15 @@ struct GemmArgs {
     int64_t sam, sak, sbk, sbn;
 };
 
-// The contribution of a finished chunk product `acc` to C: acc 2^-(ea + eb) (exponent bits
-// directly when the scale is a normal float, exp2f otherwise; a zero stays zero even where the
-// scale overflows).  Rows and columns with a chunk marked NONFINITE get garbage here and are
-// rewritten by nonfinite_fixup_kernel after the GEMM.
+// The contribution of a finished chunk product `acc` to C: acc 2^-(ea + eb), applied as two
+// factors 2^-t1 and 2^-t2 with t1 + t2 = ea + eb, each built from its exponent bits and always
+// a normal float (|t1|, |t2| <= 112), so the result is exact wherever it is a normal float (an
+// intermediate over- or underflows only when the result does too).  Rows and columns with a
+// chunk marked NONFINITE get garbage here and are rewritten by nonfinite_fixup_kernel after
+// the GEMM.
 __device__ __forceinline__ float chunk_value(float acc, int ea, int eb) {
-    const int et = 127 - ea - eb;
-    const float sc = (unsigned)(et - 1) < 254u ? __int_as_float(et << 23) : exp2f((float)(et - 127));
-    return acc == 0.0f ? 0.0f : acc * sc;
+    const int t = ea + eb, t1 = t >> 1, t2 = t - t1;
+    return acc * __int_as_float((127 - t1) << 23) * __int_as_float((127 - t2) << 23);
 }
 
 // After the GEMM: every row of A and every column of B with a chunk marked NONFINITE (an inf or
@@ -464,11 +465,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int part = 0; part < BN / 2 / 16; ++part) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(taddr + part * 16, r);
+                    // the 16 columns' exponents in one load (rows of ld_eb, a multiple of 16, zero padded)
+                    const int64_t c16 = col0 + part * 16;
+                    uint4 e16 = make_uint4(0u, 0u, 0u, 0u);
+                    if (c16 < args.ld_eb) e16 = __ldg(reinterpret_cast<const uint4 *>(ebc + c16));
+                    const uint32_t ew[4] = {e16.x, e16.y, e16.z, e16.w};
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int64_t col = col0 + part * 16 + j;
-                        const int eb = col < args.N ? (int)ebc[col] : 0;
+                        const int eb = (int)(int8_t)(ew[j >> 2] >> (8 * (j & 3)));
                         sum[part * 16 + j] += chunk_value(__uint_as_float(r[j]), ea, eb);
                     }
                 }
@@ -806,11 +811,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                 for (int part = 0; part < HALF / 16; ++part) {
                     uint32_t r[16];
                     tmem_ld_32x32b_x16(taddr + part * 16, r);
+                    // the 16 columns' exponents in one load (rows of ld_eb, a multiple of 16, zero padded)
+                    const int64_t c16 = col0 + part * 16;
+                    uint4 e16 = make_uint4(0u, 0u, 0u, 0u);
+                    if (c16 < args.ld_eb) e16 = __ldg(reinterpret_cast<const uint4 *>(ebc + c16));
+                    const uint32_t ew[4] = {e16.x, e16.y, e16.z, e16.w};
                     tmem_ld_wait();
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
-                        const int64_t col = col0 + part * 16 + j;
-                        const int eb = col < args.N ? (int)ebc[col] : 0;
+                        const int eb = (int)(int8_t)(ew[j >> 2] >> (8 * (j & 3)));
                         sum[part * 16 + j] += chunk_value(__uint_as_float(r[j]), ea, eb);
                     }
                 }

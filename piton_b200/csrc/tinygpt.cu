@@ -703,21 +703,29 @@ __device__ __forceinline__ void group_linear(const float *in, const float *ws, f
     static_assert(K % KGRP == 0 && NQ * KGRP <= HT && NQ * 4 <= D, "group_linear tiling");
     const int tid = threadIdx.x;
     const int j = tid % NQ, g = tid / NQ;
+    static_assert(KG % 4 == 0, "k-groups of whole float4s");
     if (g < KGRP) {
         float4 acc[GS];
 #pragma unroll
         for (int s = 0; s < GS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
         const float *wp = ws + (g * KG) * (4 * NQ) + 4 * j;
+        // four k-values at a time: per row one 16-byte load of the inputs, per k one of the weights
 #pragma unroll
-        for (int k = 0; k < KG; ++k) {
-            const float4 w = *reinterpret_cast<const float4 *>(wp + k * (4 * NQ));
+        for (int k4 = 0; k4 < KG; k4 += 4) {
+            float4 w[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) w[u] = *reinterpret_cast<const float4 *>(wp + (k4 + u) * (4 * NQ));
 #pragma unroll
             for (int s = 0; s < GS; ++s) {
-                const float xv = in[s * K + g * KG + k];
-                acc[s].x = fmaf(xv, w.x, acc[s].x);
-                acc[s].y = fmaf(xv, w.y, acc[s].y);
-                acc[s].z = fmaf(xv, w.z, acc[s].z);
-                acc[s].w = fmaf(xv, w.w, acc[s].w);
+                const float4 x4 = *reinterpret_cast<const float4 *>(in + s * K + g * KG + k4);
+                const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    acc[s].x = fmaf(xv[u], w[u].x, acc[s].x);
+                    acc[s].y = fmaf(xv[u], w[u].y, acc[s].y);
+                    acc[s].z = fmaf(xv[u], w[u].z, acc[s].z);
+                    acc[s].w = fmaf(xv[u], w[u].w, acc[s].w);
+                }
             }
         }
 #pragma unroll
