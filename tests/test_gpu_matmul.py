@@ -228,7 +228,9 @@ def test_tensor_core_transposed_operands_odd_k(cuda, K):
 def test_tensor_core_wide_dynamic_range(cuda):
     """Rows of A and columns of B spread over 2^-60 .. 2^60, far outside fp16's range: the
     per-chunk power-of-two scaling keeps every element at fp32 level relative to its own row's
-    and column's magnitude (a single scale per matrix would flush the small ones to zero)."""
+    and column's magnitude (a single scale per matrix would flush the small ones to zero).
+    Dividing C by the row and column powers of two (exact) gives the product of the unscaled
+    U[-1, 1] operands, checked at the usual fp32-level normalised error."""
     torch = cuda
     M, N, K = 640, 768, 700
     g = torch.Generator(device="cuda").manual_seed(60)
@@ -242,9 +244,9 @@ def test_tensor_core_wide_dynamic_range(cuda):
         device="b200").last_stats
     assert st["path"] == "tcgen05_f16x3"
     assert device_status() == 0
-    exact = A.double() @ B.double()
-    scale = A.abs().amax(1, keepdim=True).double() * B.abs().amax(0, keepdim=True).double()
-    err = float(((C.double() - exact).abs() / scale).max())
+    exact = (A / ra).double() @ (B / cb).double()
+    got = C.double() / (ra.double() * cb.double())
+    err = float((got - exact).abs().max() / exact.abs().max())
     assert err <= fp32_bound(K), err
 
 
