@@ -984,19 +984,20 @@ def main():
     if "attention" in res:
         r = res["attention"]
         ach = r["local_flops"] / r["t_kernel"] / 1e12
-        peak = tf32 / 3.0 if tf32 else None
+        peak = peaks["bf16_tflops"] / 3.0
         trf, trf_src = traffic_for("attention_dram", r["heads_local"]) if D.world == 1 else (None, None)
         sec["attention"] = {"value": r["flops"] / r["t_step"] / 1e12, "unit": "TFLOP/s",
                             "workload": f"B={AT_B} H={AT_H} S={AT_S} D={AT_D} causal (B x H = {ATTN_BH})",
                             "gbs": r["bytes"] / r["t_step"] / 1e9,
                             "kernel_tflops_per_gpu": ach,
                             "roofline": roofline("tensor", ach, peak, "TFLOP/s", trf, trf_src,
-                                                 kernel="attn_3xtf32_kernel",
-                                                 peak_source=(tf32_src + " / 3: per useful 8-deep product the "
-                                                              "kernel issues one N=128 tf32 MMA (hi.[hi;lo], two "
-                                                              "TF32 units) and one 16-deep bf16 MMA (lo.hi, one "
-                                                              "unit), the unit count of classic 3xTF32, the "
-                                                              "bound the north star names") if tf32 else None,
+                                                 kernel="attn_f16x3_kernel",
+                                                 peak_source=f"MEASURED_PEAKS.json bf16_tflops "
+                                                             f"({peaks['bf16_tflops']:.1f}, {peaks['source']}) / 3: per "
+                                                             "useful 16-deep product the kernel issues one N=128 fp16 "
+                                                             "MMA (hi.[hi;lo], two units) and one N=64 (lo.hi, one "
+                                                             "unit)",
+                                                 frac_of_tf32_over_3=(ach / (tf32 / 3.0)) if tf32 else None,
                                                  gbs_over_4BHSD4=r["bytes"] / r["t_kernel"] / 1e9 / D.world
                                                  if D.world > 1 else r["bytes"] / r["t_kernel"] / 1e9),
                             "path": "tcgen05 split (tf32 high halves + bf16 cross terms)" if r.get("tc")

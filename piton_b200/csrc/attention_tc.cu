@@ -1,66 +1,56 @@
-// Flash-attention forward on the 5th-generation tensor cores with a 3xTF32-class
-// split: tf32 products of the high halves (and hi x lo stacked beside them), bf16
-// products for the lo x hi cross terms (examples/attention.py:33-113; the
-// semantics are those of attention.cu's header: key_end, causal mask, row_end,
-// base-2 online softmax).
+// Flash-attention forward on the 5th-generation tensor cores with an fp16 split of
+// every operand (examples/attention.py:33-113; the semantics are those of attention.cu's
+// header: key_end, causal mask, row_end, base-2 online softmax).
+//
+// Each operand is scaled by a power of two and split into fp16 halves x_hi = fp16(x 2^e),
+// x_lo = fp16(x 2^e - x_hi) (22 significant bits): a Q row by its own scale (largest
+// magnitude into [2^14, 2^15)), K and V by one scale per 64-key block of a head, P (in
+// [0, 1]) by 2^14.  A product x y is then x_hi y_hi + x_hi y_lo + x_lo y_hi (the dropped
+// lo x lo term and the rounding of the low halves cost ~2^-21 of it), and the scales come
+// back out in the softmax warps' score multiplier and fold, where they cost nothing.
 //
 // Per call:
-//  1. split (HBM-bound): K -> K_lo (tf32 of the rest) and K_bf (bf16) as
-//     [heads * n_ctx, D], and K_hi unless K itself can serve (the tensor core
-//     ignores the low 13 bits of an fp32 operand: K is read in place when its
-//     rows are one 16-byte-multiple stride apart across heads); V -> V^T_hi,
-//     V^T_lo as [heads * D, ld] (ld = n_ctx rounded up to 4) and V^T_bf as
-//     [heads * D, ldb] (ldb = n_ctx rounded up to 8), through 64 x 64 tiles
-//     with 16-byte stores (split.cuh) when V's rows are 16-byte aligned.
+//  1. split (HBM-bound): K -> K_hi, K_lo as [heads * n_ctx, 64] fp16 and V -> V^T_hi,
+//     V^T_lo as [heads * 64, ldv] fp16 (ldv = n_ctx rounded up to 64), each 64-key block
+//     with its exponent in an int8 [heads, blocks] array; a CTA per (head, block).
 //  2. persistent CTAs walk (head, 128-query block) items, 352 threads:
-//     * warps 2-9, two per TMEM lane quarter (one thread per query row =
-//       TMEM lane in each), each warp of a pair on half of the columns: they
-//       load their half of the row of Q, split it and store Q_hi (tf32) and
-//       Q_lo (bf16, two per column) into TMEM; per 64-key block each reads
-//       its 32 keys' scores S from TMEM, applies scale and masks, exchanges
-//       its row maximum with the other warp through shared memory (an
-//       mbarrier per pair and block parity), updates the running max and its
-//       partial sum in registers, writes P_hi over S and P_lo (bf16) next to
-//       it in TMEM, then folds its 32 output dimensions of the block's P.V
-//       into an fp32 register accumulator (round to nearest); at the end of
-//       an item the pair adds its partial sums and each stores its half of
-//       O / l.  (One warp per row ran latency-bound at ~5 cycles per
-//       instruction, slower than the tensor core.)
-//     * warp 0 streams Q and the K tiles, warp 10 the V^T tiles, with TMA
-//       (128-byte swizzle; separate two-stage rings, since a K tile is free
-//       after S and a V tile only after P.V);
-//     * warp 11, only in the all-gather launch (384 threads), copies each item's
-//       stored rows from this rank's output to every other rank's (NVLink peer
-//       stores), one item behind the softmax warps;
-//     * warp 1 issues, from one thread, per 8-wide k-step one tf32 MMA of Q_hi
-//       against the stacked [K_hi; K_lo] tile (N = 128: Q_hi K_hi in columns
-//       0-63, Q_hi K_lo in 64-127), and per 16-wide k-step one bf16 MMA of
-//       Q_lo against K_bf (N = 64, added to columns 0-63); likewise P_hi
-//       [V_hi; V_lo] and P_lo V_bf for P.V.  The softmax warps add the two
-//       halves in fp32 registers (round to nearest), so the hi/lo sums are not
-//       truncated by the tensor core.  The lo x hi cross term is at most
-//       2^-10 of the product, so rounding both of its operands to bf16 (8-bit
-//       mantissas) leaves it correct to at most 2^-18 of the product, while a
-//       bf16 MMA covers twice the k range of a tf32 one in the same issue
-//       time: 12 MMAs per 64-key block for S and 12 for P.V instead of 16 each.
-//     A block's P.V lands in its own TMEM accumulator that the softmax warps
-//     add into registers, so the tensor core's truncating accumulation never
-//     spans more than one 64-key block.
-// The scores of block j+1 are computed while the softmax warps work on block
-// j (two S/P buffers), and a block's P.V accumulator is folded into the
-// registers after the next block's P is written, so the tensor core and the
-// softmax warps overlap.  TMEM columns: Q_hi [0,64) Q_lo [64,96), S/P x2
-// [128,384) (128 each), O_blk [384,512) (512 allocated).  All waits are
-// bounded (2 s): on expiry the kernel records a status, drains its copies and
-// MMAs, frees TMEM and returns.
+//     * warps 2-9, two per TMEM lane quarter (one thread per query row = TMEM lane in
+//       each), each warp of a pair on half of the columns: they read the raw row of Q,
+//       take its scale and store their half of Q_hi, Q_lo (fp16 pairs) into TMEM; per
+//       64-key block each reads its 32 keys' scores S from TMEM, applies the scale and the
+//       masks, exchanges its row maximum with the other warp through shared memory (an
+//       mbarrier per pair and block parity), updates the running max and its partial sum
+//       in registers, writes P_hi and P_lo (fp16 pairs) over S in TMEM, then folds its 32
+//       output dimensions of the block's P.V, unscaled, into an fp32 register accumulator
+//       (round to nearest); at the end of an item the pair adds its partial sums and each
+//       stores its half of O / l.
+//     * warp 0 streams Q and the K tiles, warp 10 the V^T tiles, with TMA (128-byte
+//       swizzle; separate rings, since a K tile is free after S and a V tile only after P.V);
+//     * warp 11, only in the all-gather launch (384 threads), copies each item's stored
+//       rows from this rank's output to every other rank's (NVLink peer stores), one item
+//       behind the softmax warps;
+//     * warp 1 issues, from one thread, per 16-wide k-step one kind::f16 MMA of Q_hi
+//       against the stacked [K_hi; K_lo] tile (N = 128: Q_hi K_hi in columns 0-63, Q_hi K_lo
+//       in 64-127) and one of Q_lo against K_hi (N = 64, added to columns 0-63); likewise
+//       P_hi [V_hi; V_lo] and P_lo V_hi for P.V: 8 MMAs per 64-key block for S and 8 for
+//       P.V.  The softmax warps add the two halves in fp32 registers (round to nearest), so
+//       the hi/lo sums are not truncated by the tensor core.
+//     A block's P.V lands in its own TMEM accumulator that the softmax warps add into
+//     registers, so the tensor core's truncating accumulation never spans more than one
+//     64-key block.
+// The scores of block j+1 are computed while the softmax warps work on block j (two S/P
+// buffers), and a block's P.V accumulator is folded into the registers after the next
+// block's P is written, so the tensor core and the softmax warps overlap.  TMEM columns:
+// Q_hi [0,32) Q_lo [32,64), S/P x2 [128,384) (128 each; P_hi in the first 32, P_lo in
+// 64-95), O_blk [384,512) (512 allocated).  All waits are bounded (2 s): on expiry the
+// kernel records a status, drains its copies and MMAs, frees TMEM and returns.
 #include <algorithm>
 
-#include <cuda_bf16.h>
+#include <cuda_fp16.h>
 
 #include "attention.cuh"
 #include "common.cuh"
 #include "sm100.cuh"
-#include "split.cuh"
 
 namespace piton {
 
@@ -73,99 +63,103 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 2, VSTAGES = 2, THREADS = 352;
+constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 3, VSTAGES = 3, THREADS = 352;
 constexpr int SOFTMAX_WARPS = 8;                          // warps 2-9: two per TMEM lane quarter
 constexpr int GATHER_WARP = 11;                           // copies finished rows to the peers (world > 1)
 constexpr int GATHER_THREADS = THREADS + 32;              // launch with the gather warp
-constexpr uint32_t BOX_BYTES = 64 * 32 * 4;               // 64 rows x 128 bytes (32 fp32 or 64 bf16)
-// K stage: for each 32-wide box b of d the hi box and the lo box are adjacent,
-// [K_hi b0][K_lo b0][K_hi b1][K_lo b1][K_bf], so one 128-row B operand covers hi rows
-// 0-63 and lo rows 64-127; then the bf16 tile (64 keys x 64 d).  V stage: the same over
-// 32-wide boxes of keys of V^T, then V^T_bf (64 d x 64 keys).
-constexpr uint32_t PAIR_BYTES = 2 * BOX_BYTES;
-constexpr uint32_t BF_OFF = 2 * PAIR_BYTES;
-constexpr uint32_t STAGE_BYTES = 2 * PAIR_BYTES + BOX_BYTES;
+constexpr uint32_t BOX_BYTES = 64 * 64 * 2;               // 64 rows x 128 bytes (64 fp16)
+// K stage: [K_hi][K_lo], so one 128-row B operand covers hi rows 0-63 and lo rows 64-127;
+// V stage: [V^T_hi][V^T_lo] (64 d x 64 keys each), the same way
+constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;
 constexpr uint32_t Q_BYTES = BM * HD * 4;                // raw Q rows of one item: two 128 x 32 boxes
 // row maxima exchanged between the two warps of a lane quarter ([block parity][half][row]) and
 // the row sums at the end of an item ([half][row])
 constexpr uint32_t XCHG_BYTES = (2 * 2 * BM + 2 * BM) * 4;
 constexpr uint32_t SMEM_BYTES = (KSTAGES + VSTAGES) * STAGE_BYTES + Q_BYTES + XCHG_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
-// TMEM: Q_hi, Q_lo (bf16 pairs), two 128-column S/P buffers (S: Q_hi.K_hi (+ Q_lo.K_bf) in
-// 0-63 and Q_hi.K_lo in 64-127; P: P_hi in 0-63, P_lo (bf16 pairs) in 64-95) and a
-// 128-column O_blk (P_hi.V_hi (+ P_lo.V_bf) in 0-63, P_hi.V_lo in 64-127)
-constexpr uint32_t COL_QHI = 0, COL_QLO = 64, COL_S0 = 128, COL_O = 384;
+// TMEM: Q_hi, Q_lo (fp16 pairs), two 128-column S/P buffers (S: Q_hi.K_hi (+ Q_lo.K_hi) in
+// 0-63 and Q_hi.K_lo in 64-127; P: P_hi (fp16 pairs) in 0-31, P_lo in 64-95) and a 128-column
+// O_blk (P_hi.V_hi (+ P_lo.V_hi) in 0-63, P_hi.V_lo in 64-127)
+constexpr uint32_t COL_QHI = 0, COL_QLO = 32, COL_S0 = 128, COL_O = 384;
+constexpr float P_SCALE = 16384.0f;                       // P in [0, 1] -> [0, 2^14]
 static_assert(KSTAGES == VSTAGES, "the producers share one ring depth");
 
-// two floats -> bf16 pair (round to nearest), `lo_k` in the low half
-__device__ __forceinline__ uint32_t pack_bf16(float lo_k, float hi_k) {
-    __nv_bfloat162 v = __floats2bfloat162_rn(lo_k, hi_k);
+// two floats -> fp16 pair (round to nearest), `lo_k` in the low half
+__device__ __forceinline__ uint32_t pack_f16(float lo_k, float hi_k) {
+    __half2 v = __floats2half2_rn(lo_k, hi_k);
     return *reinterpret_cast<uint32_t *>(&v);
 }
+// x (already scaled) -> fp16 hi and the fp16 of the rest; non-finite x keeps hi and a zero lo
+__device__ __forceinline__ void split_f16(float x, float &hi, float &lo) {
+    hi = __half2float(__float2half_rn(x));
+    lo = isfinite(x) ? x - hi : 0.0f;
+}
+// 2^e for e in [-126, 127] from its exponent bits
+__device__ __forceinline__ float pow2i(int e) { return __int_as_float((127 + e) << 23); }
+// exponent e of a block's scale 2^e: its largest finite magnitude m goes into [2^14, 2^15);
+// 0 for a block without a finite non-zero value; clamped to [-112, 112]
+__device__ __forceinline__ int block_exponent(float m) {
+    if (!(m > 0.0f)) return 0;
+    int E;
+    frexpf(m, &E);
+    return max(-112, min(112, 15 - E));
+}
+__device__ __forceinline__ float finite_abs(float v) { return isfinite(v) ? fabsf(v) : 0.0f; }
 
-__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 __device__ __forceinline__ void record_status(int code) { atomicCAS(&g_attn_status, 0, code); }
 
-// hi/lo[h][r][c] (row stride ld) and bf[h][r][c] (row stride ldb; bf16 of the value, round
-// to nearest, non-finite values as 0 and finite ones clamped to the bf16 range) from
-// src + h*s_h + r*s_r + c*s_c, r < rows, c < cols, through 32 x 32 shared-memory tiles
-// (grid.z = heads)
-__global__ void __launch_bounds__(256) attn_split_kernel(const float *__restrict__ src, int64_t rows, int64_t cols,
-                                                         int64_t s_h, int64_t s_r, int64_t s_c,
-                                                         float *__restrict__ hi, float *__restrict__ lo, int64_t ld,
-                                                         __nv_bfloat16 *__restrict__ bf, int64_t ldb,
-                                                         int lanes_along_rows) {
-    __shared__ float tile[32][33];
-    const int64_t h = blockIdx.z;
-    const int64_t r0 = (int64_t)blockIdx.y * 32, c0 = (int64_t)blockIdx.x * 32;
-    const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+// One 64-key block of one head, [keys, 64] from src + h*s_h + key*s_r + d*s_c (keys past
+// n_ctx read as zeros), scaled by the block's power of two and split into fp16 halves:
+//  TRANSPOSE == false (K): rows h * n_ctx + key of hi / lo, 64 fp16 each;
+//  TRANSPOSE == true  (V): rows h * 64 + d of hi / lo (row length ld = n_ctx rounded up to 64),
+//  keys key0 .. key0 + 63.
+// The block's exponent goes to ex[h * blocks + block].  A CTA of 256 threads per (block, head),
+// the block staged in shared memory (loads along whichever of keys and d has the smaller stride).
+template <bool TRANSPOSE>
+__global__ void __launch_bounds__(256) attn_split16_kernel(const float *__restrict__ src, int64_t n_ctx, int64_t s_h,
+                                                           int64_t s_r, int64_t s_c, __half *__restrict__ hi,
+                                                           __half *__restrict__ lo, int64_t ld,
+                                                           int8_t *__restrict__ ex, int64_t blocks) {
+    __shared__ float tile[64][65];   // [key][d]
+    __shared__ float wmax[8];
+    const int64_t blk = blockIdx.x, h = blockIdx.y, key0 = blk * 64;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
     const float *base = src + h * s_h;
-    for (int j = ty; j < 32; j += 8) {
-        int64_t r = lanes_along_rows ? r0 + tx : r0 + j;
-        int64_t c = lanes_along_rows ? c0 + j : c0 + tx;
-        float v = (r < rows && c < cols) ? base[r * s_r + c * s_c] : 0.0f;
-        if (lanes_along_rows) tile[tx][j] = v;
-        else tile[j][tx] = v;
+    const bool keys_fast = llabs(s_r) < llabs(s_c);
+    float m = 0.0f;
+    for (int i = t; i < 64 * 64; i += 256) {
+        const int key = keys_fast ? (i & 63) : (i >> 6), d = keys_fast ? (i >> 6) : (i & 63);
+        const float v = key0 + key < n_ctx ? base[(key0 + key) * s_r + (int64_t)d * s_c] : 0.0f;
+        tile[key][d] = v;
+        m = fmaxf(m, finite_abs(v));
     }
-    __syncthreads();
-    float *hh = hi + h * rows * ld, *ll = lo + h * rows * ld;
-    __nv_bfloat16 *bb = bf + h * rows * ldb;
-    for (int j = ty; j < 32; j += 8) {
-        int64_t r = r0 + j, c = c0 + tx;
-        if (r < rows && c < cols) {
-            float v = tile[j][tx];
-            float x = tf32_trunc(v);
-            const bool fin = isfinite(v);
-            hh[r * ld + c] = x;
-            ll[r * ld + c] = fin ? tf32_trunc(v - x) : 0.0f;
-            bb[r * ldb + c] = split_bf16_of(v);
-        }
-    }
-}
-
-// K rows with unit d stride and 16-byte aligned rows: no transpose, float4 in; lo (tf32 of the
-// rest) and bf (bf16 of the value) out, and hi (the tf32 high half) unless the kernel reads K in
-// place (hi == nullptr).  One thread per 4 d-values; grid-stride over heads x n_ctx x 16.
-__global__ void __launch_bounds__(256) attn_split_rows_kernel(const float *__restrict__ src, int64_t n_ctx,
-                                                              int64_t heads, int64_t s_h, int64_t s_r,
-                                                              float *__restrict__ hi, float *__restrict__ lo,
-                                                              __nv_bfloat16 *__restrict__ bf) {
-    const int64_t total = heads * n_ctx * (HD / 4);
-    for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
-        const int64_t q = i % (HD / 4), row = i / (HD / 4), h = row / n_ctx, r = row % n_ctx;
-        const float4 v = __ldcs(reinterpret_cast<const float4 *>(src + h * s_h + r * s_r + 4 * q));
-        const float vv[4] = {v.x, v.y, v.z, v.w};
-        float vh[4], vl[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-            vh[e] = tf32_trunc(vv[e]);
-            vl[e] = isfinite(vv[e]) ? tf32_trunc(vv[e] - vh[e]) : 0.0f;
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[warp] = m;
+    __syncthreads();
+    m = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, wmax[w]);
+    const int e = block_exponent(m);
+    const float sc = pow2i(e);
+    // 512 runs of 8 consecutive outputs (16-byte stores), two per thread
+    for (int c = t; c < 512; c += 256) {
+        const int a8 = c >> 3, b8 = (c & 7) * 8;   // K: key a8, d b8..; V: d a8, keys b8..
+        if (!TRANSPOSE && key0 + a8 >= n_ctx) continue;
+        __align__(16) __half hh[8], ll[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float v = (TRANSPOSE ? tile[b8 + q][a8] : tile[a8][b8 + q]) * sc;
+            float vh, vl;
+            split_f16(v, vh, vl);
+            hh[q] = __float2half_rn(vh);
+            ll[q] = __float2half_rn(vl);
         }
-        const int64_t o = row * HD + 4 * q;
-        if (hi) *reinterpret_cast<float4 *>(hi + o) = make_float4(vh[0], vh[1], vh[2], vh[3]);
-        *reinterpret_cast<float4 *>(lo + o) = make_float4(vl[0], vl[1], vl[2], vl[3]);
-        *reinterpret_cast<uint2 *>(bf + o) = make_uint2(split_bf16_pair(vv[0], vv[1]), split_bf16_pair(vv[2], vv[3]));
+        const int64_t off = TRANSPOSE ? (h * HD + a8) * ld + key0 + b8 : (h * n_ctx + key0 + a8) * HD + b8;
+        *reinterpret_cast<uint4 *>(hi + off) = *reinterpret_cast<const uint4 *>(hh);
+        *reinterpret_cast<uint4 *>(lo + off) = *reinterpret_cast<const uint4 *>(ll);
     }
+    if (t == 0) ex[h * blocks + blk] = (int8_t)e;
 }
 
 struct TcAttnArgs {
@@ -174,6 +168,8 @@ struct TcAttnArgs {
     int64_t n_ctx, key_end, row_end, heads, q_blocks, items;
     float qk_scale;
     int causal;
+    const int8_t *ek, *ev;   // exponents of the K and V blocks [heads, kv_blocks]
+    int64_t kv_blocks;
 };
 
 // The all-gather launch: o is this rank's part of its own full output, and every finished row
@@ -219,10 +215,9 @@ __device__ __forceinline__ Item item_of(const TcAttnArgs &a, int64_t it) {
 
 template <int NTHREADS>   // THREADS, or GATHER_THREADS for the all-gather
 __global__ void __launch_bounds__(NTHREADS, 1)
-    attn_3xtf32_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constant__ CUtensorMap m_khi,
-                       const __grid_constant__ CUtensorMap m_klo, const __grid_constant__ CUtensorMap m_kbf,
-                       const __grid_constant__ CUtensorMap m_vhi, const __grid_constant__ CUtensorMap m_vlo,
-                       const __grid_constant__ CUtensorMap m_vbf, const typename AttnArgsOf<NTHREADS>::type a) {
+    attn_f16x3_kernel(const __grid_constant__ CUtensorMap m_q, const __grid_constant__ CUtensorMap m_khi,
+                      const __grid_constant__ CUtensorMap m_klo, const __grid_constant__ CUtensorMap m_vhi,
+                      const __grid_constant__ CUtensorMap m_vlo, const typename AttnArgsOf<NTHREADS>::type a) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t *kst = smem;                                          // K stages
@@ -277,10 +272,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         prefetch_tmap(&m_q);
         prefetch_tmap(&m_khi);
         prefetch_tmap(&m_klo);
-        prefetch_tmap(&m_kbf);
         prefetch_tmap(&m_vhi);
         prefetch_tmap(&m_vlo);
-        prefetch_tmap(&m_vbf);
     }
     if (warp == 1) tmem_alloc<TMEM_COLS>(tmem_holder);
     tc_fence_before();
@@ -294,8 +287,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const bool is_k = warp == 0;
             uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
             uint8_t *stages = is_k ? kst : vst;
-            const CUtensorMap *m_hi = is_k ? &m_khi : &m_vhi, *m_lo = is_k ? &m_klo : &m_vlo,
-                              *m_bf = is_k ? &m_kbf : &m_vbf;
+            const CUtensorMap *m_hi = is_k ? &m_khi : &m_vhi, *m_lo = is_k ? &m_klo : &m_vlo;
             constexpr int NST = KSTAGES;   // == VSTAGES
             uint32_t g = 0, nq = 0;        // blocks and Q tiles issued
             bool ok = true;
@@ -324,11 +316,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     // K: rows = keys of this head, x = d; V^T: rows = d of this head, x = keys
                     const int row = is_k ? (int)(w.head * a.n_ctx + (int64_t)j * BN) : (int)(w.head * HD);
                     const int x0 = is_k ? 0 : j * BN;
-                    for (int box = 0; box < 2; ++box) {
-                        tma_load_2d(st + box * PAIR_BYTES, m_hi, &full[s], x0 + box * 32, row);
-                        tma_load_2d(st + box * PAIR_BYTES + BOX_BYTES, m_lo, &full[s], x0 + box * 32, row);
-                    }
-                    tma_load_2d(st + BF_OFF, m_bf, &full[s], x0, row);
+                    tma_load_2d(st, m_hi, &full[s], x0, row);
+                    tma_load_2d(st + BOX_BYTES, m_lo, &full[s], x0, row);
                     // the next item's Q, once this item's Q has left qbuf (early in this item)
                     if (is_k && next && j == (w.nblocks > 1 ? 1 : 0) && !(ok = load_q(it + gridDim.x))) break;
                 }
@@ -344,7 +333,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     } else if (warp == 1) {
         // ---------------- MMA issuer: S of block j+1 is issued before P_j V so it overlaps softmax j ----------------
         if (lane == 0) {
-            constexpr uint32_t IDESC_N128 = idesc_tf32(BM, 2 * BN), IDESC_BF = idesc_bf16(BM, BN);
+            constexpr uint32_t IDESC_N128 = idesc_f16(BM, 2 * BN), IDESC_N64 = idesc_f16(BM, BN);
             uint32_t g = 0, k = 0;   // global block counter, items done
             bool ok = true;
             auto issue_s = [&](uint32_t gg) -> bool {
@@ -354,15 +343,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 const uint32_t base = smem_u32(kst + s * STAGE_BYTES);
                 const uint32_t d = tmem + COL_S0 + (gg & 1) * 2 * BN;
 #pragma unroll
-                for (int ks = 0; ks < HD / 8; ++ks) {
-                    const uint32_t pair = base + (ks >> 2) * PAIR_BYTES + (ks & 3) * 32;
-                    const uint64_t b_pair = smem_desc_kmajor(pair, 128, LAYOUT_SWIZZLE_128B);   // K_hi; K_lo rows
-                    mma_tf32_ts(d, tmem + COL_QHI + 8 * ks, b_pair, IDESC_N128, ks > 0 ? 1u : 0u);
-                }
+                for (int kb = 0; kb < HD / 16; ++kb)   // Q_hi . [K_hi; K_lo], 16 d per MMA
+                    mma_f16_ts(d, tmem + COL_QHI + 8 * kb, smem_desc_kmajor(base + kb * 32, 128, LAYOUT_SWIZZLE_128B),
+                               IDESC_N128, kb > 0 ? 1u : 0u);
 #pragma unroll
-                for (int kb = 0; kb < HD / 16; ++kb)   // Q_lo . K_bf, 16 d per MMA
-                    mma_bf16_ts(d, tmem + COL_QLO + 8 * kb,
-                                smem_desc_kmajor(base + BF_OFF + kb * 32, 128, LAYOUT_SWIZZLE_128B), IDESC_BF);
+                for (int kb = 0; kb < HD / 16; ++kb)   // Q_lo . K_hi
+                    mma_f16_ts(d, tmem + COL_QLO + 8 * kb, smem_desc_kmajor(base + kb * 32, 128, LAYOUT_SWIZZLE_128B),
+                               IDESC_N64, 1u);
                 mma_commit(&s_full[gg & 1]);
                 mma_commit(&k_empty[s]);
                 return true;
@@ -387,15 +374,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const uint32_t base = smem_u32(vst + s * STAGE_BYTES);
                     const uint32_t pcol = tmem + COL_S0 + (g & 1) * 2 * BN;
 #pragma unroll
-                    for (int ks = 0; ks < BN / 8; ++ks) {
-                        const uint32_t pair = base + (ks >> 2) * PAIR_BYTES + (ks & 3) * 32;
-                        const uint64_t b_pair = smem_desc_kmajor(pair, 128, LAYOUT_SWIZZLE_128B);   // V^T_hi; V^T_lo
-                        mma_tf32_ts(tmem + COL_O, pcol + 8 * ks, b_pair, IDESC_N128, ks > 0 ? 1u : 0u);   // P_hi
-                    }
+                    for (int kb = 0; kb < BN / 16; ++kb)   // P_hi . [V^T_hi; V^T_lo], 16 keys per MMA
+                        mma_f16_ts(tmem + COL_O, pcol + 8 * kb,
+                                   smem_desc_kmajor(base + kb * 32, 128, LAYOUT_SWIZZLE_128B), IDESC_N128,
+                                   kb > 0 ? 1u : 0u);
 #pragma unroll
-                    for (int kb = 0; kb < BN / 16; ++kb)   // P_lo . V_bf, 16 keys per MMA
-                        mma_bf16_ts(tmem + COL_O, pcol + BN + 8 * kb,
-                                    smem_desc_kmajor(base + BF_OFF + kb * 32, 128, LAYOUT_SWIZZLE_128B), IDESC_BF);
+                    for (int kb = 0; kb < BN / 16; ++kb)   // P_lo . V^T_hi
+                        mma_f16_ts(tmem + COL_O, pcol + BN + 8 * kb,
+                                   smem_desc_kmajor(base + kb * 32, 128, LAYOUT_SWIZZLE_128B), IDESC_N64, 1u);
                     mma_commit(o_full);
                     mma_commit(&v_empty[s]);
                 }
@@ -463,28 +449,41 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         uint32_t g = 0, nq = 0, k = 0;
         bool ok = true;
-        // qbuf (raw Q rows, 128-byte swizzle, two 32-column boxes) -> tf32 hi / bf16 lo -> TMEM;
-        // this warp converts columns [32 * half, 32 * half + 32) = box `half`
+        // qbuf (raw Q rows, 128-byte swizzle, two 32-column boxes) -> the row's scale 2^eq (from
+        // the whole row, so both warps of the pair agree) -> fp16 hi / lo pairs of this warp's
+        // columns [32 * half, 32 * half + 32) (box `half`) -> TMEM
+        int eq_next = 0;   // the scale exponent of the Q rows last moved into TMEM
         auto q_to_tmem = [&]() -> bool {
             if (*abort_flag || !warp_wait(q_full, nq & 1)) return false;
-            uint32_t hi[2][16], lo[16];
+            float xv[32];
+            float m = 0.0f;
 #pragma unroll
-            for (int v4 = 0; v4 < 8; ++v4) {
-                const float4 x = *reinterpret_cast<const float4 *>(qbuf + half * (Q_BYTES / 2) + rloc * 128 +
-                                                                   ((v4 ^ (rloc & 7)) << 4));
-                const float xv[4] = {x.x, x.y, x.z, x.w};
-                float l[4];
+            for (int bx = 0; bx < 2; ++bx)
 #pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const float h = tf32_trunc(xv[e]);
-                    hi[v4 >> 2][4 * (v4 & 3) + e] = __float_as_uint(h);
-                    l[e] = isfinite(xv[e]) ? xv[e] - h : 0.0f;
+                for (int v4 = 0; v4 < 8; ++v4) {
+                    const float4 x = *reinterpret_cast<const float4 *>(qbuf + bx * (Q_BYTES / 2) + rloc * 128 +
+                                                                       ((v4 ^ (rloc & 7)) << 4));
+                    m = fmaxf(fmaxf(m, fmaxf(finite_abs(x.x), finite_abs(x.y))),
+                              fmaxf(finite_abs(x.z), finite_abs(x.w)));
+                    if (bx == half) {
+                        xv[4 * v4] = x.x;
+                        xv[4 * v4 + 1] = x.y;
+                        xv[4 * v4 + 2] = x.z;
+                        xv[4 * v4 + 3] = x.w;
+                    }
                 }
-                lo[2 * v4] = pack_bf16(l[0], l[1]);
-                lo[2 * v4 + 1] = pack_bf16(l[2], l[3]);
+            eq_next = block_exponent(m);
+            const float sc = pow2i(eq_next);
+            uint32_t hi[16], lo[16];
+#pragma unroll
+            for (int c = 0; c < 16; ++c) {
+                float h0, l0, h1, l1;
+                split_f16(xv[2 * c] * sc, h0, l0);
+                split_f16(xv[2 * c + 1] * sc, h1, l1);
+                hi[c] = pack_f16(h0, h1);
+                lo[c] = pack_f16(l0, l1);
             }
-            tmem_st_32x32b_x16(lane_base + COL_QHI + 32 * half, hi[0]);
-            tmem_st_32x32b_x16(lane_base + COL_QHI + 32 * half + 16, hi[1]);
+            tmem_st_32x32b_x16(lane_base + COL_QHI + 16 * half, hi);
             tmem_st_32x32b_x16(lane_base + COL_QLO + 16 * half, lo);
             tmem_st_wait();
             tc_fence_before();
@@ -498,8 +497,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         };
         constexpr int HH = HD / 2;
         float acc[HH];
-        // acc = acc * alpha + this warp's 32 dimensions of O_blk of global block gg
-        auto fold = [&](uint32_t gg, float alpha) -> bool {
+        // acc = acc * alpha + this warp's 32 dimensions of O_blk of global block gg, unscaled by vs
+        auto fold = [&](uint32_t gg, float alpha, float vs) -> bool {
             if (*abort_flag || !warp_wait(o_full, gg & 1)) return false;
             tc_fence_after();
             uint32_t r[2 * HH];
@@ -511,7 +510,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             tmem_ld_wait();
 #pragma unroll
             for (int c = 0; c < HH; ++c)
-                acc[c] = fmaf(acc[c], alpha, __uint_as_float(r[c]) + __uint_as_float(r[HH + c]));
+                acc[c] = fmaf(acc[c], alpha, (__uint_as_float(r[c]) + __uint_as_float(r[HH + c])) * vs);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_empty);
@@ -523,7 +522,12 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const Item w = item_of(a, it);
             const int64_t row = w.q0 + rloc;
             const bool next = it + gridDim.x < a.items;   // its Q follows this item's last P
-            float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f;
+            float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f, vs_prev = 1.0f;
+            // the score multiplier without the block's K scale, and the blocks' exponents, each
+            // loaded one block ahead of its use
+            const float fq = a.qk_scale * pow2i(-eq_next);
+            const int8_t *ekh = a.ek + w.head * a.kv_blocks, *evh = a.ev + w.head * a.kv_blocks;
+            int ek_n = __ldg(ekh), ev_n = __ldg(evh);
 #pragma unroll
             for (int d = 0; d < HH; ++d) acc[d] = 0.0f;
             for (int j = 0; j < w.nblocks; ++j, ++g) {
@@ -532,6 +536,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 tc_fence_after();
+                const int ek = ek_n, ev = ev_n;
+                if (j + 1 < w.nblocks) {
+                    ek_n = __ldg(ekh + j + 1);
+                    ev_n = __ldg(evh + j + 1);
+                }
+                const float f = fq * pow2i(-ek);                  // score scale of this block
+                const float vs = pow2i(-(ev + 14));               // P (2^14) and V block scales out
                 constexpr int KH = BN / 2;
                 const int64_t k0 = (int64_t)j * BN + KH * half;   // this warp's first key
                 const uint32_t scol = COL_S0 + (g & 1) * 2 * BN, pcol = scol + BN;
@@ -574,24 +585,24 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     ok = false;
                     break;
                 }
-                const float m_new = fmaxf(m_i, fmaxf(m_mine, xm[(half ^ 1) * BM + rloc]) * a.qk_scale);
+                const float m_new = fmaxf(m_i, fmaxf(m_mine, xm[(half ^ 1) * BM + rloc]) * f);
                 const float m_use = m_new == -INFINITY ? 0.0f : m_new;
                 const float alpha = fast_exp2(m_i - m_use);
                 float ps0 = 0.0f, ps1 = 0.0f;
-                uint32_t hi[2][16], lo[16];
+                uint32_t hi[16], lo[16];
 #pragma unroll
                 for (int e = 0; e < KH; e += 2) {
-                    const float p0 = fast_exp2(fmaf(sc[e], a.qk_scale, -m_use));
-                    const float p1 = fast_exp2(fmaf(sc[e + 1], a.qk_scale, -m_use));
+                    const float p0 = fast_exp2(fmaf(sc[e], f, -m_use));
+                    const float p1 = fast_exp2(fmaf(sc[e + 1], f, -m_use));
                     ps0 += p0;
                     ps1 += p1;
-                    const float h0 = tf32_trunc(p0), h1 = tf32_trunc(p1);
-                    hi[e >> 4][e & 15] = __float_as_uint(h0);
-                    hi[e >> 4][(e & 15) + 1] = __float_as_uint(h1);
-                    lo[e >> 1] = pack_bf16(p0 - h0, p1 - h1);   // the differences are exact
+                    float h0, l0, h1, l1;
+                    split_f16(p0 * P_SCALE, h0, l0);
+                    split_f16(p1 * P_SCALE, h1, l1);
+                    hi[e >> 1] = pack_f16(h0, h1);
+                    lo[e >> 1] = pack_f16(l0, l1);
                 }
-                tmem_st_32x32b_x16(lane_base + scol + KH * half, hi[0]);
-                tmem_st_32x32b_x16(lane_base + scol + KH * half + 16, hi[1]);
+                tmem_st_32x32b_x16(lane_base + scol + 16 * half, hi);
                 tmem_st_32x32b_x16(lane_base + pcol + 16 * half, lo);
                 l_i = l_i * alpha + (ps0 + ps1);
                 m_i = m_new;
@@ -602,13 +613,14 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 // after the item's last scores: the next item's Q (this item's S MMAs are all done)
                 if (j == w.nblocks - 1 && next && !(ok = q_to_tmem())) break;
                 // fold the previous block's P.V while this block's runs on the tensor core
-                if (j > 0 && !fold(g - 1, alpha_prev)) {
+                if (j > 0 && !fold(g - 1, alpha_prev, vs_prev)) {
                     ok = false;
                     break;
                 }
                 alpha_prev = alpha;
+                vs_prev = vs;
             }
-            if (ok && !fold(g - 1, alpha_prev)) ok = false;
+            if (ok && !fold(g - 1, alpha_prev, vs_prev)) ok = false;
             if (!ok) break;
             // the row sum: this warp's keys plus the other warp's
             xsum[half * BM + rloc] = l_i;
@@ -667,33 +679,19 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// row-major fp32 [rows, ld] with inner extent `cols`; boxes of 64 rows x 32 columns, 128-byte swizzle
-int make_map(CUtensorMap *map, const float *base, int64_t rows, int64_t cols, int64_t ld) {
-    EncodeTiled enc = encode_fn();
-    if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
-    cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)(ld * 4)};
-    cuuint32_t box[2] = {32, 64};
-    cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled failed (%d)", (int)r);
-    return PITON_B200_OK;
-}
-
-// row-major bf16 [rows, ld] with inner extent `cols`; boxes of 64 rows x 64 columns, 128-byte swizzle
-int make_map_bf16(CUtensorMap *map, const __nv_bfloat16 *base, int64_t rows, int64_t cols, int64_t ld) {
+// row-major fp16 [rows, ld] with inner extent `cols`; boxes of 64 rows x 64 columns (128 bytes),
+// 128-byte swizzle
+int make_map16(CUtensorMap *map, const __half *base, int64_t rows, int64_t cols, int64_t ld) {
     EncodeTiled enc = encode_fn();
     if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ld * 2)};
     cuuint32_t box[2] = {64, 64};
     cuuint32_t estr[2] = {1, 1};
-    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<__nv_bfloat16 *>(base), dims, strides, box,
-                     estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (bf16) failed (%d)", (int)r);
+    if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (fp16) failed (%d)", (int)r);
     return PITON_B200_OK;
 }
 
@@ -727,29 +725,13 @@ __global__ void __launch_bounds__(256) attn_q_copy_kernel(const float *__restric
         dst[h * n_ctx * HD + i] = src[h * s_h + (i / HD) * s_r + i % HD];
 }
 
-// K split without a transpose: unit d stride, 16-byte aligned rows and heads
-bool k_rows_vec(const AttnParams &p) {
-    return p.skk == 1 && p.skn % 4 == 0 && p.skh % 4 == 0 && (reinterpret_cast<uintptr_t>(p.k) & 15) == 0;
-}
-// K read in place as its own tf32 high half (the tensor core ignores the low 13 bits): the rows
-// of all heads one stride apart, as the 2-D tensor map [heads * n_ctx, HD] needs
-bool k_in_place(const AttnParams &p) {
-    return k_rows_vec(p) && p.skn >= HD && p.skh == p.n_ctx * p.skn && p.skn < (1ll << 37);
-}
-// V^T by the 64 x 64-tile transposing split: d contiguous (always), keys and heads 16-byte aligned
-bool v_vec(const AttnParams &p) {
-    return p.svn % 4 == 0 && p.svh % 4 == 0 && (reinterpret_cast<uintptr_t>(p.v) & 15) == 0;
-}
-
-int64_t v_ld(int64_t n_ctx) { return (n_ctx + 3) / 4 * 4; }
-int64_t v_ldb(int64_t n_ctx) { return (n_ctx + 7) / 8 * 8; }   // bf16 rows: 16-byte multiple
-size_t k_region(const AttnParams &p) { return ((size_t)p.heads * p.n_ctx * HD * 4 + 1023) / 1024 * 1024; }
-size_t v_region(const AttnParams &p) { return ((size_t)p.heads * HD * v_ld(p.n_ctx) * 4 + 1023) / 1024 * 1024; }
-size_t kb_region(const AttnParams &p) { return ((size_t)p.heads * p.n_ctx * HD * 2 + 1023) / 1024 * 1024; }
-size_t vb_region(const AttnParams &p) { return ((size_t)p.heads * HD * v_ldb(p.n_ctx) * 2 + 1023) / 1024 * 1024; }
-size_t q_region(const AttnParams &p) {
-    return q_in_place(p) ? 0 : ((size_t)p.heads * p.n_ctx * HD * 4 + 1023) / 1024 * 1024;
-}
+int64_t kv_blocks_of(int64_t n_ctx) { return (n_ctx + BN - 1) / BN; }
+int64_t v_ld(int64_t n_ctx) { return kv_blocks_of(n_ctx) * BN; }   // V^T row: whole 64-key blocks
+size_t align1k(size_t b) { return (b + 1023) / 1024 * 1024; }
+size_t k_region(const AttnParams &p) { return align1k((size_t)p.heads * p.n_ctx * HD * 2); }
+size_t v_region(const AttnParams &p) { return align1k((size_t)p.heads * HD * v_ld(p.n_ctx) * 2); }
+size_t e_region(const AttnParams &p) { return align1k((size_t)p.heads * kv_blocks_of(p.n_ctx)); }
+size_t q_region(const AttnParams &p) { return q_in_place(p) ? 0 : align1k((size_t)p.heads * p.n_ctx * HD * 4); }
 
 }  // namespace
 
@@ -763,60 +745,39 @@ bool attention_tc_supported(const AttnParams &p) {
 }
 
 size_t attention_tc_workspace_bytes(const AttnParams &p) {
-    return 2 * k_region(p) + 2 * v_region(p) + kb_region(p) + vb_region(p) + q_region(p);
+    return 2 * k_region(p) + 2 * v_region(p) + 2 * e_region(p) + q_region(p);
 }
 
 int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     uint8_t *ws = static_cast<uint8_t *>(workspace);
-    float *k_hi = reinterpret_cast<float *>(ws);
-    float *k_lo = reinterpret_cast<float *>(ws + k_region(p));
-    float *v_hi = reinterpret_cast<float *>(ws + 2 * k_region(p));
-    float *v_lo = reinterpret_cast<float *>(ws + 2 * k_region(p) + v_region(p));
-    __nv_bfloat16 *k_bf = reinterpret_cast<__nv_bfloat16 *>(ws + 2 * k_region(p) + 2 * v_region(p));
-    __nv_bfloat16 *v_bf = reinterpret_cast<__nv_bfloat16 *>(ws + 2 * k_region(p) + 2 * v_region(p) + kb_region(p));
-    const int64_t ldv = v_ld(p.n_ctx), ldvb = v_ldb(p.n_ctx);
-    // K [n_ctx, D] per head (strides skn, skk) -> [heads * n_ctx, D]
-    const bool k_direct = k_in_place(p);
-    if (k_rows_vec(p)) {
-        const int64_t total = p.heads * p.n_ctx * (HD / 4);
-        const int64_t blocks = std::min<int64_t>(cdiv(total, (int64_t)256), (int64_t)num_sms() * 16);
-        attn_split_rows_kernel<<<(unsigned)blocks, 256, 0, stream>>>(p.k, p.n_ctx, p.heads, p.skh, p.skn,
-                                                                     k_direct ? nullptr : k_hi, k_lo, k_bf);
-    } else {
-        dim3 g((unsigned)cdiv(HD, 32), (unsigned)cdiv(p.n_ctx, 32), (unsigned)p.heads);
-        int along_rows = llabs(p.skn) < llabs(p.skk);
-        attn_split_kernel<<<g, 256, 0, stream>>>(p.k, p.n_ctx, HD, p.skh, p.skn, p.skk, k_hi, k_lo, HD, k_bf, HD,
-                                                 along_rows);
-    }
-    // V [n_ctx, D] per head (strides svn, 1) -> V^T [heads * D, ldv]
-    if (v_vec(p)) {
-        dim3 g((unsigned)cdiv(p.n_ctx, 64), 1, (unsigned)p.heads);
-        split_transpose_kernel<SPLIT_T_ATTN_V><<<g, 256, 0, stream>>>(p.v, HD, p.n_ctx, p.svn, p.svh, v_hi, v_lo, v_bf,
-                                                                       ldv, ldvb);
-    } else {
-        dim3 g((unsigned)cdiv(p.n_ctx, 32), (unsigned)cdiv(HD, 32), (unsigned)p.heads);
-        attn_split_kernel<<<g, 256, 0, stream>>>(p.v, HD, p.n_ctx, p.svh, 1, p.svn, v_hi, v_lo, ldv, v_bf, ldvb, 1);
-    }
+    __half *k_hi = reinterpret_cast<__half *>(ws);
+    __half *k_lo = reinterpret_cast<__half *>(ws + k_region(p));
+    __half *v_hi = reinterpret_cast<__half *>(ws + 2 * k_region(p));
+    __half *v_lo = reinterpret_cast<__half *>(ws + 2 * k_region(p) + v_region(p));
+    int8_t *ek = reinterpret_cast<int8_t *>(ws + 2 * k_region(p) + 2 * v_region(p));
+    int8_t *ev = ek + e_region(p);
+    const int64_t blocks = kv_blocks_of(p.n_ctx), ldv = v_ld(p.n_ctx);
+    // K [n_ctx, D] per head (strides skn, skk) -> [heads * n_ctx, D]; V [n_ctx, D] (svn, 1) -> V^T
+    dim3 g((unsigned)blocks, (unsigned)p.heads);
+    attn_split16_kernel<false><<<g, 256, 0, stream>>>(p.k, p.n_ctx, p.skh, p.skn, p.skk, k_hi, k_lo, HD, ek, blocks);
+    attn_split16_kernel<true><<<g, 256, 0, stream>>>(p.v, p.n_ctx, p.svh, p.svn, 1, v_hi, v_lo, ldv, ev, blocks);
     int launches = 3;
     const float *q = p.q;
     int64_t sqm = p.sqm, sqh = p.sqh;
     if (!q_in_place(p)) {
-        float *qc = reinterpret_cast<float *>(ws + 2 * k_region(p) + 2 * v_region(p) + kb_region(p) + vb_region(p));
-        dim3 g((unsigned)std::min<int64_t>(cdiv(p.n_ctx * HD, (int64_t)256), 4096), (unsigned)p.heads);
-        attn_q_copy_kernel<<<g, 256, 0, stream>>>(p.q, p.n_ctx, p.sqh, p.sqm, qc);
+        float *qc = reinterpret_cast<float *>(ws + 2 * k_region(p) + 2 * v_region(p) + 2 * e_region(p));
+        dim3 gq((unsigned)std::min<int64_t>(cdiv(p.n_ctx * HD, (int64_t)256), 4096), (unsigned)p.heads);
+        attn_q_copy_kernel<<<gq, 256, 0, stream>>>(p.q, p.n_ctx, p.sqh, p.sqm, qc);
         q = qc;
         sqm = HD;
         sqh = p.n_ctx * HD;
         ++launches;
     }
-    CUtensorMap mq, mkh, mkl, mkb, mvh, mvl, mvb;
+    CUtensorMap mq, mkh, mkl, mvh, mvl;
     int rc;
     if ((rc = make_map_q(&mq, q, p.n_ctx, p.heads, sqm, sqh)) ||
-        (rc = k_direct ? make_map(&mkh, p.k, p.heads * p.n_ctx, HD, p.skn) : make_map(&mkh, k_hi, p.heads * p.n_ctx, HD, HD)) ||
-        (rc = make_map(&mkl, k_lo, p.heads * p.n_ctx, HD, HD)) ||
-        (rc = make_map_bf16(&mkb, k_bf, p.heads * p.n_ctx, HD, HD)) ||
-        (rc = make_map(&mvh, v_hi, p.heads * HD, p.n_ctx, ldv)) || (rc = make_map(&mvl, v_lo, p.heads * HD, p.n_ctx, ldv)) ||
-        (rc = make_map_bf16(&mvb, v_bf, p.heads * HD, p.n_ctx, ldvb)))
+        (rc = make_map16(&mkh, k_hi, p.heads * p.n_ctx, HD, HD)) || (rc = make_map16(&mkl, k_lo, p.heads * p.n_ctx, HD, HD)) ||
+        (rc = make_map16(&mvh, v_hi, p.heads * HD, ldv, ldv)) || (rc = make_map16(&mvl, v_lo, p.heads * HD, ldv, ldv)))
         return rc;
     static bool attr[64][2] = {};
     int dev = 0;
@@ -824,10 +785,10 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     const bool gather = p.world > 1;
     if (dev < 64 && !attr[dev][gather]) {
         if (gather)
-            PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel<GATHER_THREADS>,
+            PITON_CUDA(cudaFuncSetAttribute(attn_f16x3_kernel<GATHER_THREADS>,
                                             cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
         else
-            PITON_CUDA(cudaFuncSetAttribute(attn_3xtf32_kernel<THREADS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            PITON_CUDA(cudaFuncSetAttribute(attn_f16x3_kernel<THREADS>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             SMEM_BYTES));
         attr[dev][gather] = true;
     }
@@ -839,6 +800,9 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     a.items = a.q_blocks * p.heads;
     a.qk_scale = p.qk_scale;
     a.causal = p.causal;
+    a.ek = ek;
+    a.ev = ev;
+    a.kv_blocks = blocks;
     // persistent: one CTA per SM walks the items (head-major, heavy query blocks first)
     const int64_t grid = std::min<int64_t>(a.items, (int64_t)num_sms());
     if (grid > 0 && gather) {
@@ -847,11 +811,11 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
         ga.world = p.world;
         ga.rank = p.rank;
         for (int i = 0; i < MAX_PEERS; ++i) ga.peer_o[i] = p.peer_o[i];
-        attn_3xtf32_kernel<GATHER_THREADS>
-            <<<(unsigned)grid, GATHER_THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mkb, mvh, mvl, mvb, ga);
+        attn_f16x3_kernel<GATHER_THREADS>
+            <<<(unsigned)grid, GATHER_THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mvh, mvl, ga);
     } else if (grid > 0)
-        attn_3xtf32_kernel<THREADS><<<(unsigned)grid, THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mkb, mvh, mvl, mvb, a);
-    return check_launch("attention_3xtf32", launches);
+        attn_f16x3_kernel<THREADS><<<(unsigned)grid, THREADS, SMEM_BYTES, stream>>>(mq, mkh, mkl, mvh, mvl, a);
+    return check_launch("attention_f16x3", launches);
 }
 
 int attention_tc_status_read_and_clear(int *status) {

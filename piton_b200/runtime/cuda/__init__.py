@@ -380,7 +380,7 @@ def _attention(L: Launch, grid):
     L.call("piton_b200_attention_f32", a, "attn_fwd_kernel")
     flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
     return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops,
-            "path": "tcgen05_3xtf32" if ws else "cuda_core"}
+            "path": "tcgen05_f16x3" if ws else "cuda_core"}
 
 
 @register("layernorm_kernel", ("x_ptr", "out_ptr", "n", "eps", "BLOCK"))

@@ -158,7 +158,7 @@ def test_tensor_core_path(cuda, monkeypatch, heads, n, causal):
     stats = attn_fwd_kernel[(-(-n // 2), h)](q, k, v, out, float(1 / np.sqrt(d)), n * d, d, n * d, d, 1, n * d, d,
                                               (n + 2) * d, d, n, HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16,
                                               CAUSAL=causal, EVEN_N=n % 16 == 0, device="b200").last_stats
-    assert stats["path"] == "tcgen05_3xtf32"
+    assert stats["path"] == "tcgen05_f16x3"
     assert _status() == 0
     np.testing.assert_array_equal(out[:, n:], sentinel)
     np.testing.assert_allclose(out[:, :n], O.attention_f64(q, k, v, causal), rtol=0, atol=ATOL)
@@ -178,7 +178,7 @@ def test_tensor_core_path_strided_k_and_padded_rows(cuda):
     stats = attn_fwd_kernel[(n // 2, heads)](q, kt, v, out, 0.125, n * 80, 80, n * d, 1, n, n * d, d, n * 80, 80, n,
                                              HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=True,
                                              device="b200").last_stats
-    assert stats["path"] == "tcgen05_3xtf32"
+    assert stats["path"] == "tcgen05_f16x3"
     np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, True), rtol=0, atol=ATOL)
     assert np.all(out[:, :, d:] == 0)
 
@@ -198,7 +198,7 @@ def test_tensor_core_path_unaligned_q_and_out(cuda, q_off):
     stats = attn_fwd_kernel[(n // 2, heads)](offset_ptr(qbuf, q_off), k, v, out, 0.125, n * ld, ld, n * d, d, 1,
                                              n * d, d, n * ld, ld, n, HEAD_DIM=d, BLOCK_M=2, BLOCK_N=16,
                                              CAUSAL=False, EVEN_N=True, device="b200").last_stats
-    assert stats["path"] == "tcgen05_3xtf32"
+    assert stats["path"] == "tcgen05_f16x3"
     assert _status() == 0
     np.testing.assert_allclose(out[:, :, :d], O.attention_f64(q[:, :, :d], k, v, False), rtol=0, atol=ATOL)
     assert np.all(out[:, :, d:] == 3.0)
@@ -225,6 +225,6 @@ def test_tensor_core_path_k_and_v_layouts(cuda, k_ld, k_gap, v_ld):
     stats = attn_fwd_kernel[(n // 2, heads)](q, kbuf, vbuf, out, 0.125, n * d, d, skh, k_ld, 1, svh, v_ld, n * d, d, n,
                                              HEAD_DIM=d, BLOCK_M=2, BLOCK_N=8, CAUSAL=True, EVEN_N=True,
                                              device="b200").last_stats
-    assert stats["path"] == "tcgen05_3xtf32"
+    assert stats["path"] == "tcgen05_f16x3"
     assert _status() == 0
     np.testing.assert_allclose(out, O.attention_f64(q, k, v, True), rtol=0, atol=ATOL)

@@ -88,7 +88,7 @@ def test_attention_b32_h32_s4096_d64_causal(cuda):
     st = attn_fwd_kernel[(S // 2, BH)](q, k, v, o, 1.0 / math.sqrt(D), sd, D, sd, D, 1, sd, D, sd, D, S,
                                        HEAD_DIM=D, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=True,
                                        device="b200").last_stats
-    assert st["path"] == "tcgen05_3xtf32"
+    assert st["path"] == "tcgen05_f16x3"
     assert bool(torch.isfinite(o).all())
     for h in (0, BH // 2, 701, BH - 1):
         ref = O.attention_f64(q[h].cpu().numpy(), k[h].cpu().numpy(), v[h].cpu().numpy(), True)
