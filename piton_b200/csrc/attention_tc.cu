@@ -596,11 +596,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     const float p1 = fast_exp2(fmaf(sc[e + 1], f, -m_use));
                     ps0 += p0;
                     ps1 += p1;
-                    float h0, l0, h1, l1;
-                    split_f16(p0 * P_SCALE, h0, l0);
-                    split_f16(p1 * P_SCALE, h1, l1);
-                    hi[e >> 1] = pack_f16(h0, h1);
-                    lo[e >> 1] = pack_f16(l0, l1);
+                    // p is finite (exp2 of a finite value or of -inf): the pair's halves directly
+                    const float s0 = p0 * P_SCALE, s1 = p1 * P_SCALE;
+                    const __half2 h2 = __floats2half2_rn(s0, s1);
+                    const float2 hf = __half22float2(h2);
+                    const __half2 l2 = __floats2half2_rn(s0 - hf.x, s1 - hf.y);
+                    hi[e >> 1] = *reinterpret_cast<const uint32_t *>(&h2);
+                    lo[e >> 1] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
                 tmem_st_32x32b_x16(lane_base + scol + 16 * half, hi);
                 tmem_st_32x32b_x16(lane_base + pcol + 16 * half, lo);
