@@ -985,7 +985,7 @@ def main():
         r = res["attention"]
         ach = r["local_flops"] / r["t_kernel"] / 1e12
         peak = peaks["bf16_tflops"] / 3.0
-        trf, trf_src = traffic_for("attention_dram", r["heads_local"]) if D.world == 1 else (None, None)
+        trf, trf_src = traffic_for("attn_f16x3_bh64", r["heads_local"]) if D.world == 1 else (None, None)
         sec["attention"] = {"value": r["flops"] / r["t_step"] / 1e12, "unit": "TFLOP/s",
                             "workload": f"B={AT_B} H={AT_H} S={AT_S} D={AT_D} causal (B x H = {ATTN_BH})",
                             "gbs": r["bytes"] / r["t_step"] / 1e9,
