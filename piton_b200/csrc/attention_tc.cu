@@ -63,23 +63,18 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 3, VSTAGES = 3;
-constexpr int NPART = 4;                                  // softmax warps per TMEM lane quarter
-constexpr int KP = BN / NPART, DP = HD / NPART;           // keys of a block / dims of O per softmax warp
-constexpr int SOFTMAX_WARPS = 4 * NPART;                  // warps 2 .. 2 + SOFTMAX_WARPS - 1
-constexpr int V_WARP = 2 + SOFTMAX_WARPS;                 // streams the V^T tiles
-constexpr int GATHER_WARP = V_WARP + 1;                   // copies finished rows to the peers (world > 1)
-constexpr int THREADS = 32 * (V_WARP + 1);
+constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 3, VSTAGES = 3, THREADS = 352;
+constexpr int SOFTMAX_WARPS = 8;                          // warps 2-9: two per TMEM lane quarter
+constexpr int GATHER_WARP = 11;                           // copies finished rows to the peers (world > 1)
 constexpr int GATHER_THREADS = THREADS + 32;              // launch with the gather warp
-static_assert(KP == 16 && DP == 16, "a softmax warp takes 16 keys and 16 output dimensions");
 constexpr uint32_t BOX_BYTES = 64 * 64 * 2;               // 64 rows x 128 bytes (64 fp16)
 // K stage: [K_hi][K_lo], so one 128-row B operand covers hi rows 0-63 and lo rows 64-127;
 // V stage: [V^T_hi][V^T_lo] (64 d x 64 keys each), the same way
 constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;
 constexpr uint32_t Q_BYTES = BM * HD * 4;                // raw Q rows of one item: two 128 x 32 boxes
-// row maxima exchanged between the softmax warps of a lane quarter ([block parity][part][row]) and
-// the row sums at the end of an item ([part][row])
-constexpr uint32_t XCHG_BYTES = (2 * NPART * BM + NPART * BM) * 4;
+// row maxima exchanged between the two warps of a lane quarter ([block parity][half][row]) and
+// the row sums at the end of an item ([half][row])
+constexpr uint32_t XCHG_BYTES = (2 * 2 * BM + 2 * BM) * 4;
 constexpr uint32_t SMEM_BYTES = (KSTAGES + VSTAGES) * STAGE_BYTES + Q_BYTES + XCHG_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
 // TMEM: Q_hi, Q_lo (fp16 pairs), two 128-column S/P buffers (S: Q_hi.K_hi (+ Q_lo.K_hi) in
@@ -228,8 +223,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t *kst = smem;                                          // K stages
     uint8_t *vst = smem + KSTAGES * STAGE_BYTES;                  // V^T stages
     uint8_t *qbuf = vst + VSTAGES * STAGE_BYTES;                  // raw Q rows of the next item
-    float *xmax = reinterpret_cast<float *>(qbuf + Q_BYTES);       // [2][NPART][BM]
-    float *xsum = xmax + 2 * NPART * BM;                           // [NPART][BM]
+    float *xmax = reinterpret_cast<float *>(qbuf + Q_BYTES);       // [2][2][BM]
+    float *xsum = xmax + 2 * 2 * BM;                               // [2][BM]
     uint64_t *k_full = reinterpret_cast<uint64_t *>(qbuf + Q_BYTES + XCHG_BYTES);
     uint64_t *k_empty = k_full + KSTAGES;
     uint64_t *v_full = k_empty + KSTAGES;
@@ -242,8 +237,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t *o_full = q_ready + 1;
     uint64_t *o_empty = o_full + 1;
     uint64_t *drain = o_empty + 1;
-    uint64_t *max_bar = drain + 1;            // [4 quarters][2 block parities], 32 NPART arrivals
-    uint64_t *sum_bar = max_bar + 8;          // [4 quarters], 32 NPART arrivals
+    uint64_t *max_bar = drain + 1;            // [4 quarters][2 block parities], 64 arrivals
+    uint64_t *sum_bar = max_bar + 8;          // [4 quarters], 64 arrivals
     uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sum_bar + 4);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
     volatile int *rows_stored = abort_flag + 1;   // softmax-warp item stores done (8 per item)
@@ -269,8 +264,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(o_full, 1);
         mbar_init(o_empty, SOFTMAX_WARPS);
         mbar_init(drain, 1);
-        for (int b = 0; b < 8; ++b) mbar_init(&max_bar[b], 32 * NPART);
-        for (int b = 0; b < 4; ++b) mbar_init(&sum_bar[b], 32 * NPART);
+        for (int b = 0; b < 8; ++b) mbar_init(&max_bar[b], 64);
+        for (int b = 0; b < 4; ++b) mbar_init(&sum_bar[b], 64);
         *abort_flag = 0;
         if constexpr (NTHREADS > THREADS) *rows_stored = 0;
         fence_mbarrier_init();
@@ -286,8 +281,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     tc_fence_after();
     const uint32_t tmem = *tmem_holder;
 
-    if (warp == 0 || warp == V_WARP) {
-        // ---------------- TMA producers: warp 0 Q rows (one item ahead) and K tiles, warp V_WARP V^T tiles ----------------
+    if (warp == 0 || warp == 10) {
+        // ---------------- TMA producers: warp 0 Q rows (one item ahead) and K tiles, warp 10 V^T tiles ----------------
         if (lane == 0) {
             const bool is_k = warp == 0;
             uint64_t *full = is_k ? k_full : v_full, *empty = is_k ? k_empty : v_empty;
@@ -447,20 +442,20 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
         }
     } else {
-        // ---------------- softmax / accumulate / store (warps 2 .. 2 + SOFTMAX_WARPS - 1) ----------------
+        // ---------------- softmax / accumulate / store (warps 2-9) ----------------
         const int quarter = warp & 3;
-        const int part = (warp - 2) >> 2;    // this warp's 16 keys of a block and 16 dimensions of O
+        const int half = (warp - 2) >> 2;    // this warp's 32 keys of a block and 32 dimensions of O
         const int rloc = quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         uint32_t g = 0, nq = 0, k = 0;
         bool ok = true;
         // qbuf (raw Q rows, 128-byte swizzle, two 32-column boxes) -> the row's scale 2^eq (from
-        // the whole row, so all warps of the lane quarter agree) -> fp16 hi / lo pairs of this
-        // warp's columns [16 * part, 16 * part + 16) -> TMEM
+        // the whole row, so both warps of the pair agree) -> fp16 hi / lo pairs of this warp's
+        // columns [32 * half, 32 * half + 32) (box `half`) -> TMEM
         int eq_next = 0;   // the scale exponent of the Q rows last moved into TMEM
         auto q_to_tmem = [&]() -> bool {
             if (*abort_flag || !warp_wait(q_full, nq & 1)) return false;
-            float xv[DP];
+            float xv[32];
             float m = 0.0f;
 #pragma unroll
             for (int bx = 0; bx < 2; ++bx)
@@ -470,27 +465,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                                                                        ((v4 ^ (rloc & 7)) << 4));
                     m = fmaxf(fmaxf(m, fmaxf(finite_abs(x.x), finite_abs(x.y))),
                               fmaxf(finite_abs(x.z), finite_abs(x.w)));
-                    if (8 * bx + v4 >= 4 * part && 8 * bx + v4 < 4 * part + 4) {   // dims 16 part ..
-                        const int c = 4 * (8 * bx + v4 - 4 * part);
-                        xv[c] = x.x;
-                        xv[c + 1] = x.y;
-                        xv[c + 2] = x.z;
-                        xv[c + 3] = x.w;
+                    if (bx == half) {
+                        xv[4 * v4] = x.x;
+                        xv[4 * v4 + 1] = x.y;
+                        xv[4 * v4 + 2] = x.z;
+                        xv[4 * v4 + 3] = x.w;
                     }
                 }
             eq_next = block_exponent(m);
             const float sc = pow2i(eq_next);
-            uint32_t hi[DP / 2], lo[DP / 2];
+            uint32_t hi[16], lo[16];
 #pragma unroll
-            for (int c = 0; c < DP / 2; ++c) {
+            for (int c = 0; c < 16; ++c) {
                 float h0, l0, h1, l1;
                 split_f16(xv[2 * c] * sc, h0, l0);
                 split_f16(xv[2 * c + 1] * sc, h1, l1);
                 hi[c] = pack_f16(h0, h1);
                 lo[c] = pack_f16(l0, l1);
             }
-            tmem_st_32x32b_x8(lane_base + COL_QHI + (DP / 2) * part, hi);
-            tmem_st_32x32b_x8(lane_base + COL_QLO + (DP / 2) * part, lo);
+            tmem_st_32x32b_x16(lane_base + COL_QHI + 16 * half, hi);
+            tmem_st_32x32b_x16(lane_base + COL_QLO + 16 * half, lo);
             tmem_st_wait();
             tc_fence_before();
             __syncwarp();
@@ -501,18 +495,22 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ++nq;
             return true;
         };
-        float acc[DP];
-        // acc = acc * alpha + this warp's 16 dimensions of O_blk of global block gg, unscaled by vs
+        constexpr int HH = HD / 2;
+        float acc[HH];
+        // acc = acc * alpha + this warp's 32 dimensions of O_blk of global block gg, unscaled by vs
         auto fold = [&](uint32_t gg, float alpha, float vs) -> bool {
             if (*abort_flag || !warp_wait(o_full, gg & 1)) return false;
             tc_fence_after();
-            uint32_t r[2 * DP];
-            tmem_ld_32x32b_x16(lane_base + COL_O + DP * part, *reinterpret_cast<uint32_t(*)[16]>(r));
-            tmem_ld_32x32b_x16(lane_base + COL_O + HD + DP * part, *reinterpret_cast<uint32_t(*)[16]>(r + DP));
+            uint32_t r[2 * HH];
+#pragma unroll
+            for (int c = 0; c < HH; c += 16) {
+                tmem_ld_32x32b_x16(lane_base + COL_O + HH * half + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+                tmem_ld_32x32b_x16(lane_base + COL_O + HD + HH * half + c, *reinterpret_cast<uint32_t(*)[16]>(r + HH + c));
+            }
             tmem_ld_wait();
 #pragma unroll
-            for (int c = 0; c < DP; ++c)
-                acc[c] = fmaf(acc[c], alpha, (__uint_as_float(r[c]) + __uint_as_float(r[DP + c])) * vs);
+            for (int c = 0; c < HH; ++c)
+                acc[c] = fmaf(acc[c], alpha, (__uint_as_float(r[c]) + __uint_as_float(r[HH + c])) * vs);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(o_empty);
@@ -531,7 +529,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             const int8_t *ekh = a.ek + w.head * a.kv_blocks, *evh = a.ev + w.head * a.kv_blocks;
             int ek_n = __ldg(ekh), ev_n = __ldg(evh);
 #pragma unroll
-            for (int d = 0; d < DP; ++d) acc[d] = 0.0f;
+            for (int d = 0; d < HH; ++d) acc[d] = 0.0f;
             for (int j = 0; j < w.nblocks; ++j, ++g) {
                 if (*abort_flag || !warp_wait(&s_full[g & 1], (g >> 1) & 1)) {
                     ok = false;
@@ -545,52 +543,55 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
                 const float f = fq * pow2i(-ek);                  // score scale of this block
                 const float vs = pow2i(-(ev + 14));               // P (2^14) and V block scales out
-                const int64_t k0 = (int64_t)j * BN + KP * part;   // this warp's first key
+                constexpr int KH = BN / 2;
+                const int64_t k0 = (int64_t)j * BN + KH * half;   // this warp's first key
                 const uint32_t scol = COL_S0 + (g & 1) * 2 * BN, pcol = scol + BN;
-                float sc[KP];
+                float sc[KH];
                 {
-                    uint32_t r[2 * KP];
-                    tmem_ld_32x32b_x16(lane_base + scol + KP * part, *reinterpret_cast<uint32_t(*)[16]>(r));
-                    tmem_ld_32x32b_x16(lane_base + scol + BN + KP * part, *reinterpret_cast<uint32_t(*)[16]>(r + KP));
+                    uint32_t r[2 * KH];
+#pragma unroll
+                    for (int c = 0; c < KH; c += 16) {
+                        tmem_ld_32x32b_x16(lane_base + scol + KH * half + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
+                        tmem_ld_32x32b_x16(lane_base + scol + BN + KH * half + c,
+                                           *reinterpret_cast<uint32_t(*)[16]>(r + KH + c));
+                    }
                     tmem_ld_wait();
 #pragma unroll
-                    for (int c = 0; c < KP; ++c) sc[c] = __uint_as_float(r[c]) + __uint_as_float(r[KP + c]);
+                    for (int c = 0; c < KH; ++c) sc[c] = __uint_as_float(r[c]) + __uint_as_float(r[KH + c]);
                 }
                 // masks only on the blocks that reach past key_end or the causal diagonal
-                const bool masked = k0 + KP > a.key_end || (a.causal && k0 + KP - 1 > w.q0);
+                const bool masked = k0 + KH > a.key_end || (a.causal && k0 + KH - 1 > w.q0);
                 if (masked) {
 #pragma unroll
-                    for (int c = 0; c < KP; ++c) {
+                    for (int c = 0; c < KH; ++c) {
                         const int64_t col = k0 + c;
                         if (col >= a.key_end || (a.causal && col > row)) sc[c] = -INFINITY;
                     }
                 }
                 float m0 = sc[0], m1 = sc[1], m2 = sc[2], m3 = sc[3];
 #pragma unroll
-                for (int c = 4; c < KP; c += 4) {
+                for (int c = 4; c < KH; c += 4) {
                     m0 = fmaxf(m0, sc[c]);
                     m1 = fmaxf(m1, sc[c + 1]);
                     m2 = fmaxf(m2, sc[c + 2]);
                     m3 = fmaxf(m3, sc[c + 3]);
                 }
-                // the row maximum over the quarter's warps (f > 0, so max(s) * f = max(s * f))
-                float m_blk = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
-                float *xm = xmax + (g & 1) * NPART * BM;
-                xm[part * BM + rloc] = m_blk;
+                // the row maximum over both halves (scale > 0, so max(s) * scale = max(s * scale))
+                const float m_mine = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
+                float *xm = xmax + (g & 1) * 2 * BM;
+                xm[half * BM + rloc] = m_mine;
                 mbar_arrive(&max_bar[quarter * 2 + (g & 1)]);
                 if (!warp_wait(&max_bar[quarter * 2 + (g & 1)], (g >> 1) & 1)) {
                     ok = false;
                     break;
                 }
-#pragma unroll
-                for (int pp = 0; pp < NPART; ++pp) m_blk = fmaxf(m_blk, xm[pp * BM + rloc]);
-                const float m_new = fmaxf(m_i, m_blk * f);
+                const float m_new = fmaxf(m_i, fmaxf(m_mine, xm[(half ^ 1) * BM + rloc]) * f);
                 const float m_use = m_new == -INFINITY ? 0.0f : m_new;
                 const float alpha = fast_exp2(m_i - m_use);
                 float ps0 = 0.0f, ps1 = 0.0f;
-                uint32_t hi[KP / 2], lo[KP / 2];
+                uint32_t hi[16], lo[16];
 #pragma unroll
-                for (int e = 0; e < KP; e += 2) {
+                for (int e = 0; e < KH; e += 2) {
                     const float p0 = fast_exp2(fmaf(sc[e], f, -m_use));
                     const float p1 = fast_exp2(fmaf(sc[e + 1], f, -m_use));
                     ps0 += p0;
@@ -603,8 +604,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     hi[e >> 1] = *reinterpret_cast<const uint32_t *>(&h2);
                     lo[e >> 1] = *reinterpret_cast<const uint32_t *>(&l2);
                 }
-                tmem_st_32x32b_x8(lane_base + scol + (KP / 2) * part, hi);
-                tmem_st_32x32b_x8(lane_base + pcol + (KP / 2) * part, lo);
+                tmem_st_32x32b_x16(lane_base + scol + 16 * half, hi);
+                tmem_st_32x32b_x16(lane_base + pcol + 16 * half, lo);
                 l_i = l_i * alpha + (ps0 + ps1);
                 m_i = m_new;
                 tmem_st_wait();
@@ -623,27 +624,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             }
             if (ok && !fold(g - 1, alpha_prev, vs_prev)) ok = false;
             if (!ok) break;
-            // the row sum: the partial sums of all warps of the lane quarter
-            xsum[part * BM + rloc] = l_i;
+            // the row sum: this warp's keys plus the other warp's
+            xsum[half * BM + rloc] = l_i;
             mbar_arrive(&sum_bar[quarter]);
             if (!warp_wait(&sum_bar[quarter], k & 1)) {
                 ok = false;
                 break;
             }
-            l_i = 0.0f;
-#pragma unroll
-            for (int pp = 0; pp < NPART; ++pp) l_i += xsum[pp * BM + rloc];
+            l_i += xsum[(half ^ 1) * BM + rloc];
             if (row < a.row_end) {
                 const float inv = 1.0f / l_i;
-                float *orow = a.o + w.head * a.soh + row * a.som + DP * part;
-                if (o_vec) {   // 16-byte stores
+                float *orow = a.o + w.head * a.soh + row * a.som + HH * half;
+                if (o_vec) {   // 16-byte stores: a warp's store covers 32 rows x 16 bytes instead of 32 x 4
 #pragma unroll
-                    for (int d = 0; d < DP; d += 4)
+                    for (int d = 0; d < HH; d += 4)
                         *reinterpret_cast<float4 *>(orow + d) =
                             make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
                 } else {
 #pragma unroll
-                    for (int d = 0; d < DP; ++d) orow[d] = acc[d] * inv;
+                    for (int d = 0; d < HH; ++d) orow[d] = acc[d] * inv;
                 }
             }
             if constexpr (NTHREADS > THREADS) {   // the item's rows are in this rank's output: hand them to the gather warp

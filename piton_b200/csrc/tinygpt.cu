@@ -595,7 +595,8 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_cluster_kernel(ClusterArgs
 
 constexpr int HC = H;                 // CTAs per cluster, one per head (portable cluster size)
 constexpr int GS = 8;                 // sequences per group at most
-constexpr int HT = 256;               // threads per CTA
+constexpr int HT = 512;               // threads per CTA (16 warps: latency hidden by more warps)
+constexpr int SH = 2;                 // sequence halves of a group in the split-k linears
 constexpr int KGRP = 8;               // k-groups of the split-k linears
 constexpr int FH = F / HC;            // hidden units per CTA (128)
 constexpr int V_R = (V + HC - 1) / HC;   // vocabulary rows per CTA (17)
@@ -699,16 +700,18 @@ __device__ __forceinline__ void prefetch_phase(float *buf, const float *__restri
 // finished quad once.
 template <int K, int NQ, typename Epi>
 __device__ __forceinline__ void group_linear(const float *in, const float *ws, float (*red)[GS][D], Epi epi) {
-    constexpr int KG = K / KGRP;
-    static_assert(K % KGRP == 0 && NQ * KGRP <= HT && NQ * 4 <= D, "group_linear tiling");
+    constexpr int KG = K / KGRP, GH = GS / SH;
+    static_assert(K % KGRP == 0 && NQ * KGRP * SH <= HT && NQ * 4 <= D && GS % SH == 0, "group_linear tiling");
     const int tid = threadIdx.x;
-    const int j = tid % NQ, g = tid / NQ;
+    const int j = tid % NQ, g = (tid / NQ) % KGRP, sh = tid / (NQ * KGRP);
     static_assert(KG % 4 == 0, "k-groups of whole float4s");
-    if (g < KGRP) {
-        float4 acc[GS];
+    if (sh < SH) {
+        // thread (j, g, sh): column quad j, k-group g, rows [GH sh, GH sh + GH)
+        float4 acc[GH];
 #pragma unroll
-        for (int s = 0; s < GS; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < GH; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
         const float *wp = ws + (g * KG) * (4 * NQ) + 4 * j;
+        const float *inh = in + (GH * sh) * K;
         // four k-values at a time: per row one 16-byte load of the inputs, per k one of the weights
 #pragma unroll
         for (int k4 = 0; k4 < KG; k4 += 4) {
@@ -716,8 +719,8 @@ __device__ __forceinline__ void group_linear(const float *in, const float *ws, f
 #pragma unroll
             for (int u = 0; u < 4; ++u) w[u] = *reinterpret_cast<const float4 *>(wp + (k4 + u) * (4 * NQ));
 #pragma unroll
-            for (int s = 0; s < GS; ++s) {
-                const float4 x4 = *reinterpret_cast<const float4 *>(in + s * K + g * KG + k4);
+            for (int s = 0; s < GH; ++s) {
+                const float4 x4 = *reinterpret_cast<const float4 *>(inh + s * K + g * KG + k4);
                 const float xv[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
                 for (int u = 0; u < 4; ++u) {
@@ -729,7 +732,7 @@ __device__ __forceinline__ void group_linear(const float *in, const float *ws, f
             }
         }
 #pragma unroll
-        for (int s = 0; s < GS; ++s) *reinterpret_cast<float4 *>(&red[g][s][4 * j]) = acc[s];
+        for (int s = 0; s < GH; ++s) *reinterpret_cast<float4 *>(&red[g][GH * sh + s][4 * j]) = acc[s];
     }
     __syncthreads();
     for (int i = tid; i < GS * NQ; i += HT) {
@@ -1116,8 +1119,9 @@ void launch_heads(const tg::HeadsArgs &h, int clusters, cudaStream_t q) {
 }
 
 // PITON_B200_TINYGPT_KERNEL=cluster|heads|step picks a decode kernel for comparisons; by default
-// batches up to the number of 16-CTA clusters that fit use the cluster kernel, larger ones the
-// heads kernel, and the per-position step kernel serves when neither cluster launch is possible.
+// batches up to the number of 16-CTA clusters that fit use the cluster kernel, batches whose
+// 2-sequence CTAs fill three quarters of the SMs the per-position step kernel, the ones between
+// the heads kernel (and the step kernel when neither cluster launch is possible).
 int forced_kernel() {
     const char *e = getenv("PITON_B200_TINYGPT_KERNEL");
     if (!e || !*e) return 0;
@@ -1221,7 +1225,11 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     const int clusters = cluster_capacity();
     const int hcap = heads_capacity();
     bool use_cluster = clusters > 0 && a->batch <= clusters;
-    bool use_heads = !use_cluster && hcap > 0;
+    // the per-position step kernel (2 sequences per CTA, every CTA reading all the weights) wins
+    // once its CTAs fill three quarters of the SMs (measured: 3.79 M against 3.63 M tokens/s at
+    // batch 256); below that the heads kernel spreads even a few sequences over 4 SMs each
+    const bool step_fills = cdiv(a->batch, SEQ) * 4 >= (int64_t)num_sms() * 3;
+    bool use_heads = !use_cluster && hcap > 0 && !step_fills;
     if (forced == 1) {
         PITON_REQUIRE(clusters > 0 && a->batch <= clusters, "the cluster kernel takes at most %d sequences", clusters);
         use_cluster = true, use_heads = false;
