@@ -1054,7 +1054,7 @@ def main():
                 per_seq = sum(kv * (p + 1) + kv for p in range(pos))
                 byts = pos * wbytes + r["per_rank"] * per_seq
                 ent["roofline"] = roofline("hbm", byts / r["t_step"] / 1e9, hbm, "GB/s",
-                                           kernel="tinygpt_step_kernel" if r["per_rank"] * 2 >= 222 else
+                                           kernel="tinygpt_step_kernel" if r["per_rank"] >= 222 else
                                            "tinygpt_heads_kernel",
                                            algorithmic_bytes_per_decode=byts,
                                            note="KV cache (134 MB at batch 256) and weights mostly L2-resident")
