@@ -1000,7 +1000,8 @@ def main():
                                                  frac_of_tf32_over_3=(ach / (tf32 / 3.0)) if tf32 else None,
                                                  gbs_over_4BHSD4=r["bytes"] / r["t_kernel"] / 1e9 / D.world
                                                  if D.world > 1 else r["bytes"] / r["t_kernel"] / 1e9),
-                            "path": "tcgen05 split (tf32 high halves + bf16 cross terms)" if r.get("tc")
+                            "path": "tcgen05 fp16 split (Q per row, K and V per 64-key block, P x 2^14: "
+                                    "hi.hi + hi.lo + lo.hi)" if r.get("tc")
                                     else "CUDA-core fp32",
                             "allgather": ("fused: the kernel's gather warp stores finished rows to every rank "
                                           "(NVLink peer stores)" if r.get("fused") else

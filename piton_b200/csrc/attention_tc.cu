@@ -13,34 +13,36 @@
 //  1. split (HBM-bound): K -> K_hi, K_lo as [heads * n_ctx, 64] fp16 and V -> V^T_hi,
 //     V^T_lo as [heads * 64, ldv] fp16 (ldv = n_ctx rounded up to 64), each 64-key block
 //     with its exponent in an int8 [heads, blocks] array; a CTA per (head, block).
-//  2. persistent CTAs walk (head, 128-query block) items, 352 threads:
+//  2. persistent CTAs walk (head, 128-query block) items, 480 threads:
 //     * warps 2-9, two per TMEM lane quarter (one thread per query row = TMEM lane in
-//       each), each warp of a pair on half of the columns: they read the raw row of Q,
-//       take its scale and store their half of Q_hi, Q_lo (fp16 pairs) into TMEM; per
-//       64-key block each reads its 32 keys' scores S from TMEM, applies the scale and the
-//       masks, exchanges its row maximum with the other warp through shared memory (an
-//       mbarrier per pair and block parity), updates the running max and its partial sum
-//       in registers, writes P_hi and P_lo (fp16 pairs) over S in TMEM, then folds its 32
-//       output dimensions of the block's P.V, unscaled, into an fp32 register accumulator
-//       (round to nearest); at the end of an item the pair adds its partial sums and each
-//       stores its half of O / l.
+//       each), each warp of a pair on half of the keys: they read the raw row of Q, take
+//       its scale and store their half of Q_hi, Q_lo (fp16 pairs) into TMEM; per 64-key
+//       block each reads its 32 keys' scores S from TMEM, applies the scale and the masks,
+//       exchanges its row maximum with the other warp through shared memory (an mbarrier
+//       per pair and block parity), updates the running max and its partial sum in
+//       registers, writes P_hi and P_lo (fp16 pairs) over S in TMEM and hands the block's
+//       rescale factor (alpha per row) to the fold warp through shared memory;
+//     * warps 11-14, one per lane quarter (the FlashAttention-4 division of labour): per
+//       block they take alpha, read the block's P.V accumulator from TMEM and fold it,
+//       unscaled, into an fp32 register accumulator (round to nearest); at the end of an
+//       item they take the row sums and store O / l;
 //     * warp 0 streams Q and the K tiles, warp 10 the V^T tiles, with TMA (128-byte
 //       swizzle; separate rings, since a K tile is free after S and a V tile only after P.V);
-//     * warp 11, only in the all-gather launch (384 threads), copies each item's stored
+//     * warp 15, only in the all-gather launch (512 threads), copies each item's stored
 //       rows from this rank's output to every other rank's (NVLink peer stores), one item
-//       behind the softmax warps;
+//       behind the fold warps;
 //     * warp 1 issues, from one thread, per 16-wide k-step one kind::f16 MMA of Q_hi
 //       against the stacked [K_hi; K_lo] tile (N = 128: Q_hi K_hi in columns 0-63, Q_hi K_lo
 //       in 64-127) and one of Q_lo against K_hi (N = 64, added to columns 0-63); likewise
 //       P_hi [V_hi; V_lo] and P_lo V_hi for P.V: 8 MMAs per 64-key block for S and 8 for
-//       P.V.  The softmax warps add the two halves in fp32 registers (round to nearest), so
-//       the hi/lo sums are not truncated by the tensor core.
-//     A block's P.V lands in its own TMEM accumulator that the softmax warps add into
+//       P.V.  The softmax and fold warps add the two halves in fp32 registers (round to
+//       nearest), so the hi/lo sums are not truncated by the tensor core.
+//     A block's P.V lands in its own TMEM accumulator that the fold warps add into
 //     registers, so the tensor core's truncating accumulation never spans more than one
 //     64-key block.
 // The scores of block j+1 are computed while the softmax warps work on block j (two S/P
-// buffers), and a block's P.V accumulator is folded into the registers after the next
-// block's P is written, so the tensor core and the softmax warps overlap.  TMEM columns:
+// buffers), and the fold warps take a block's P.V while the softmax warps turn the next
+// block's S into P, so the tensor core, the softmax and the fold overlap.  TMEM columns:
 // Q_hi [0,32) Q_lo [32,64), S/P x2 [128,384) (128 each; P_hi in the first 32, P_lo in
 // 64-95), O_blk [384,512) (512 allocated).  All waits are bounded (2 s): on expiry the
 // kernel records a status, drains its copies and MMAs, frees TMEM and returns.
@@ -63,18 +65,20 @@ namespace {
 
 using namespace sm100;
 
-constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 3, VSTAGES = 3, THREADS = 352;
+constexpr int BM = 128, BN = 64, HD = 64, KSTAGES = 3, VSTAGES = 3, THREADS = 480;
 constexpr int SOFTMAX_WARPS = 8;                          // warps 2-9: two per TMEM lane quarter
-constexpr int GATHER_WARP = 11;                           // copies finished rows to the peers (world > 1)
+constexpr int FOLD_WARP0 = 11, FOLD_WARPS = 4;            // warps 11-14: one per lane quarter, all of O's columns
+constexpr int GATHER_WARP = 15;                           // copies finished rows to the peers (world > 1)
 constexpr int GATHER_THREADS = THREADS + 32;              // launch with the gather warp
 constexpr uint32_t BOX_BYTES = 64 * 64 * 2;               // 64 rows x 128 bytes (64 fp16)
 // K stage: [K_hi][K_lo], so one 128-row B operand covers hi rows 0-63 and lo rows 64-127;
 // V stage: [V^T_hi][V^T_lo] (64 d x 64 keys each), the same way
 constexpr uint32_t STAGE_BYTES = 2 * BOX_BYTES;
 constexpr uint32_t Q_BYTES = BM * HD * 4;                // raw Q rows of one item: two 128 x 32 boxes
-// row maxima exchanged between the two warps of a lane quarter ([block parity][half][row]) and
-// the row sums at the end of an item ([half][row])
-constexpr uint32_t XCHG_BYTES = (2 * 2 * BM + 2 * BM) * 4;
+// row maxima exchanged between the two softmax warps of a lane quarter ([block parity][half][row]),
+// their row sums at the end of an item ([half][row]), and what they hand to the fold warps: the
+// rescale factor of every block ([block parity][row]) and the row sum of every item ([item parity][row])
+constexpr uint32_t XCHG_BYTES = (2 * 2 * BM + 2 * BM + 2 * BM + 2 * BM) * 4;
 constexpr uint32_t SMEM_BYTES = (KSTAGES + VSTAGES) * STAGE_BYTES + Q_BYTES + XCHG_BYTES + 1024 + 1024;
 constexpr int TMEM_COLS = 512;
 // TMEM: Q_hi, Q_lo (fp16 pairs), two 128-column S/P buffers (S: Q_hi.K_hi (+ Q_lo.K_hi) in
@@ -225,6 +229,8 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint8_t *qbuf = vst + VSTAGES * STAGE_BYTES;                  // raw Q rows of the next item
     float *xmax = reinterpret_cast<float *>(qbuf + Q_BYTES);       // [2][2][BM]
     float *xsum = xmax + 2 * 2 * BM;                               // [2][BM]
+    float *xalpha = xsum + 2 * BM;                                 // [2][BM]
+    float *xl = xalpha + 2 * BM;                                   // [2][BM]
     uint64_t *k_full = reinterpret_cast<uint64_t *>(qbuf + Q_BYTES + XCHG_BYTES);
     uint64_t *k_empty = k_full + KSTAGES;
     uint64_t *v_full = k_empty + KSTAGES;
@@ -239,9 +245,13 @@ __global__ void __launch_bounds__(NTHREADS, 1)
     uint64_t *drain = o_empty + 1;
     uint64_t *max_bar = drain + 1;            // [4 quarters][2 block parities], 64 arrivals
     uint64_t *sum_bar = max_bar + 8;          // [4 quarters], 64 arrivals
-    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(sum_bar + 4);
+    uint64_t *a_full = sum_bar + 4;           // [4 quarters][2 block parities]: alpha of a block written
+    uint64_t *a_empty = a_full + 8;           // ... and read by the quarter's fold warp
+    uint64_t *l_full = a_empty + 8;           // [4 quarters][2 item parities]: an item's row sums written
+    uint64_t *l_empty = l_full + 8;           // ... and read
+    uint32_t *tmem_holder = reinterpret_cast<uint32_t *>(l_empty + 8);
     volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_holder + 1);
-    volatile int *rows_stored = abort_flag + 1;   // softmax-warp item stores done (8 per item)
+    volatile int *rows_stored = abort_flag + 1;   // fold-warp item stores done (4 per item)
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -262,10 +272,16 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         mbar_init(q_empty, SOFTMAX_WARPS);
         mbar_init(q_ready, SOFTMAX_WARPS);
         mbar_init(o_full, 1);
-        mbar_init(o_empty, SOFTMAX_WARPS);
+        mbar_init(o_empty, FOLD_WARPS);
         mbar_init(drain, 1);
         for (int b = 0; b < 8; ++b) mbar_init(&max_bar[b], 64);
         for (int b = 0; b < 4; ++b) mbar_init(&sum_bar[b], 64);
+        for (int b = 0; b < 8; ++b) {
+            mbar_init(&a_full[b], 1);
+            mbar_init(&a_empty[b], 1);
+            mbar_init(&l_full[b], 1);
+            mbar_init(&l_empty[b], 1);
+        }
         *abort_flag = 0;
         if constexpr (NTHREADS > THREADS) *rows_stored = 0;
         fence_mbarrier_init();
@@ -401,7 +417,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
         if constexpr (NTHREADS > THREADS) {
             int need = 0;
             for (int64_t it = blockIdx.x; it < a.items; it += gridDim.x) {
-                need += SOFTMAX_WARPS;
+                need += FOLD_WARPS;
                 int go = 1;
                 if (lane == 0 && *rows_stored < need) {
                     const uint64_t t0 = globaltimer();
@@ -441,10 +457,90 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 }
             }
         }
-    } else {
-        // ---------------- softmax / accumulate / store (warps 2-9) ----------------
+    } else if (warp >= FOLD_WARP0 && warp < FOLD_WARP0 + FOLD_WARPS) {
+        // ---------------- fold / store (warps 11-14, one per TMEM lane quarter) ----------------
+        // acc = acc * alpha + O_blk * vs for every block, alpha handed over by the quarter's softmax
+        // warps through shared memory; at the end of an item O = acc / l.
         const int quarter = warp & 3;
-        const int half = (warp - 2) >> 2;    // this warp's 32 keys of a block and 32 dimensions of O
+        const int rloc = quarter * 32 + lane;
+        const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
+        uint32_t g = 0, k = 0;
+        bool ok = true;
+        float acc[HD];
+        const bool o_vec = ((reinterpret_cast<uintptr_t>(a.o) | (uintptr_t)(a.soh * 4) | (uintptr_t)(a.som * 4)) & 15) == 0;
+        for (int64_t it = blockIdx.x; ok && it < a.items; it += gridDim.x, ++k) {
+            const Item w = item_of(a, it);
+            const int64_t row = w.q0 + rloc;
+            const int8_t *evh = a.ev + w.head * a.kv_blocks;
+            int ev_n = __ldg(evh);
+#pragma unroll
+            for (int d = 0; d < HD; ++d) acc[d] = 0.0f;
+            for (int j = 0; j < w.nblocks; ++j, ++g) {
+                const int ev = ev_n;
+                if (j + 1 < w.nblocks) ev_n = __ldg(evh + j + 1);
+                const float vs = pow2i(-(ev + 14));   // P (2^14) and V block scales out
+                if (*abort_flag || !warp_wait(&a_full[quarter * 2 + (g & 1)], (g >> 1) & 1)) {
+                    ok = false;
+                    break;
+                }
+                const float alpha = xalpha[(g & 1) * BM + rloc];
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&a_empty[quarter * 2 + (g & 1)]);
+                if (*abort_flag || !warp_wait(o_full, g & 1)) {
+                    ok = false;
+                    break;
+                }
+                tc_fence_after();
+#pragma unroll
+                for (int c = 0; c < HD; c += 16) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x16(lane_base + COL_O + c, *reinterpret_cast<uint32_t(*)[16]>(r));
+                    tmem_ld_32x32b_x16(lane_base + COL_O + HD + c, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
+                    tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        acc[c + e] = fmaf(acc[c + e], alpha, (__uint_as_float(r[e]) + __uint_as_float(r[16 + e])) * vs);
+                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(o_empty);
+            }
+            if (!ok) break;
+            // the item's row sums from the softmax warps
+            if (*abort_flag || !warp_wait(&l_full[quarter * 2 + (k & 1)], (k >> 1) & 1)) {
+                ok = false;
+                break;
+            }
+            const float l_i = xl[(k & 1) * BM + rloc];
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&l_empty[quarter * 2 + (k & 1)]);
+            if (row < a.row_end) {
+                const float inv = 1.0f / l_i;
+                float *orow = a.o + w.head * a.soh + row * a.som;
+                if (o_vec) {   // 16-byte stores
+#pragma unroll
+                    for (int d = 0; d < HD; d += 4)
+                        *reinterpret_cast<float4 *>(orow + d) =
+                            make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
+                } else {
+#pragma unroll
+                    for (int d = 0; d < HD; ++d) orow[d] = acc[d] * inv;
+                }
+            }
+            if constexpr (NTHREADS > THREADS) {   // the item's rows are in this rank's output: hand them to the gather warp
+                __threadfence();
+                __syncwarp();
+                if (lane == 0) atomicAdd(const_cast<int *>(rows_stored), 1);
+            }
+        }
+        if (!ok) {
+            if (lane == 0) record_status(STATUS_TIMEOUT_EPILOGUE);
+            *abort_flag = 1;
+        }
+    } else {
+        // ---------------- softmax (warps 2-9): S -> P, row maxima and sums ----------------
+        const int quarter = warp & 3;
+        const int half = (warp - 2) >> 2;    // this warp's 32 keys of a block and 32 columns of Q
         const int rloc = quarter * 32 + lane;
         const uint32_t lane_base = tmem + ((uint32_t)(quarter * 32) << 16);
         uint32_t g = 0, nq = 0, k = 0;
@@ -495,54 +591,26 @@ __global__ void __launch_bounds__(NTHREADS, 1)
             ++nq;
             return true;
         };
-        constexpr int HH = HD / 2;
-        float acc[HH];
-        // acc = acc * alpha + this warp's 32 dimensions of O_blk of global block gg, unscaled by vs
-        auto fold = [&](uint32_t gg, float alpha, float vs) -> bool {
-            if (*abort_flag || !warp_wait(o_full, gg & 1)) return false;
-            tc_fence_after();
-            uint32_t r[2 * HH];
-#pragma unroll
-            for (int c = 0; c < HH; c += 16) {
-                tmem_ld_32x32b_x16(lane_base + COL_O + HH * half + c, *reinterpret_cast<uint32_t(*)[16]>(r + c));
-                tmem_ld_32x32b_x16(lane_base + COL_O + HD + HH * half + c, *reinterpret_cast<uint32_t(*)[16]>(r + HH + c));
-            }
-            tmem_ld_wait();
-#pragma unroll
-            for (int c = 0; c < HH; ++c)
-                acc[c] = fmaf(acc[c], alpha, (__uint_as_float(r[c]) + __uint_as_float(r[HH + c])) * vs);
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(o_empty);
-            return true;
-        };
-        const bool o_vec = ((reinterpret_cast<uintptr_t>(a.o) | (uintptr_t)(a.soh * 4) | (uintptr_t)(a.som * 4)) & 15) == 0;
         if ((int64_t)blockIdx.x < a.items) ok = q_to_tmem();
         for (int64_t it = blockIdx.x; ok && it < a.items; it += gridDim.x, ++k) {
             const Item w = item_of(a, it);
             const int64_t row = w.q0 + rloc;
             const bool next = it + gridDim.x < a.items;   // its Q follows this item's last P
-            float m_i = -INFINITY, l_i = 0.0f, alpha_prev = 1.0f, vs_prev = 1.0f;
+            float m_i = -INFINITY, l_i = 0.0f;
             // the score multiplier without the block's K scale, and the blocks' exponents, each
             // loaded one block ahead of its use
             const float fq = a.qk_scale * pow2i(-eq_next);
-            const int8_t *ekh = a.ek + w.head * a.kv_blocks, *evh = a.ev + w.head * a.kv_blocks;
-            int ek_n = __ldg(ekh), ev_n = __ldg(evh);
-#pragma unroll
-            for (int d = 0; d < HH; ++d) acc[d] = 0.0f;
+            const int8_t *ekh = a.ek + w.head * a.kv_blocks;
+            int ek_n = __ldg(ekh);
             for (int j = 0; j < w.nblocks; ++j, ++g) {
                 if (*abort_flag || !warp_wait(&s_full[g & 1], (g >> 1) & 1)) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
-                const int ek = ek_n, ev = ev_n;
-                if (j + 1 < w.nblocks) {
-                    ek_n = __ldg(ekh + j + 1);
-                    ev_n = __ldg(evh + j + 1);
-                }
+                const int ek = ek_n;
+                if (j + 1 < w.nblocks) ek_n = __ldg(ekh + j + 1);
                 const float f = fq * pow2i(-ek);                  // score scale of this block
-                const float vs = pow2i(-(ev + 14));               // P (2^14) and V block scales out
                 constexpr int KH = BN / 2;
                 const int64_t k0 = (int64_t)j * BN + KH * half;   // this warp's first key
                 const uint32_t scol = COL_S0 + (g & 1) * 2 * BN, pcol = scol + BN;
@@ -576,7 +644,7 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     m2 = fmaxf(m2, sc[c + 2]);
                     m3 = fmaxf(m3, sc[c + 3]);
                 }
-                // the row maximum over both halves (scale > 0, so max(s) * scale = max(s * scale))
+                // the row maximum over both halves (f > 0, so max(s) * f = max(s * f))
                 const float m_mine = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3));
                 float *xm = xmax + (g & 1) * 2 * BM;
                 xm[half * BM + rloc] = m_mine;
@@ -612,43 +680,36 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&p_full[g & 1]);
+                // the block's rescale factor to the quarter's fold warp (both halves hold the same)
+                if (half == 0) {
+                    if (!warp_wait(&a_empty[quarter * 2 + (g & 1)], ((g >> 1) & 1) ^ 1)) {
+                        ok = false;
+                        break;
+                    }
+                    xalpha[(g & 1) * BM + rloc] = alpha;
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&a_full[quarter * 2 + (g & 1)]);
+                }
                 // after the item's last scores: the next item's Q (this item's S MMAs are all done)
                 if (j == w.nblocks - 1 && next && !(ok = q_to_tmem())) break;
-                // fold the previous block's P.V while this block's runs on the tensor core
-                if (j > 0 && !fold(g - 1, alpha_prev, vs_prev)) {
-                    ok = false;
-                    break;
-                }
-                alpha_prev = alpha;
-                vs_prev = vs;
             }
-            if (ok && !fold(g - 1, alpha_prev, vs_prev)) ok = false;
             if (!ok) break;
-            // the row sum: this warp's keys plus the other warp's
+            // the row sum: this warp's keys plus the other warp's, to the fold warp
             xsum[half * BM + rloc] = l_i;
             mbar_arrive(&sum_bar[quarter]);
             if (!warp_wait(&sum_bar[quarter], k & 1)) {
                 ok = false;
                 break;
             }
-            l_i += xsum[(half ^ 1) * BM + rloc];
-            if (row < a.row_end) {
-                const float inv = 1.0f / l_i;
-                float *orow = a.o + w.head * a.soh + row * a.som + HH * half;
-                if (o_vec) {   // 16-byte stores: a warp's store covers 32 rows x 16 bytes instead of 32 x 4
-#pragma unroll
-                    for (int d = 0; d < HH; d += 4)
-                        *reinterpret_cast<float4 *>(orow + d) =
-                            make_float4(acc[d] * inv, acc[d + 1] * inv, acc[d + 2] * inv, acc[d + 3] * inv);
-                } else {
-#pragma unroll
-                    for (int d = 0; d < HH; ++d) orow[d] = acc[d] * inv;
+            if (half == 0) {
+                const float l_all = l_i + xsum[BM + rloc];
+                if (!warp_wait(&l_empty[quarter * 2 + (k & 1)], ((k >> 1) & 1) ^ 1)) {
+                    ok = false;
+                    break;
                 }
-            }
-            if constexpr (NTHREADS > THREADS) {   // the item's rows are in this rank's output: hand them to the gather warp
-                __threadfence();
+                xl[(k & 1) * BM + rloc] = l_all;
                 __syncwarp();
-                if (lane == 0) atomicAdd(const_cast<int *>(rows_stored), 1);
+                if (lane == 0) mbar_arrive(&l_full[quarter * 2 + (k & 1)]);
             }
         }
         if (!ok) {

@@ -582,9 +582,20 @@ __global__ void __launch_bounds__(THREADS, 1)
 // the even CTA's barrier.  Waits are bounded as in the one-CTA kernel; the two
 // cluster barriers (after set-up, before TMEM is freed) are reached unconditionally.
 
-constexpr int STAGES2 = 6;
-constexpr uint32_t A2_TILE_BYTES = BM * BK * 2;   // 8 KB: this CTA's 128 rows x 32 fp16
-__host__ __device__ constexpr uint32_t b2_tile_bytes(int bnp) { return (uint32_t)(bnp / 2) * BK * 2; }
+// BK2: fp16 k-values per stage of the pair kernel (32: 64-byte rows, 64-byte swizzle; 64:
+// 128-byte rows, 128-byte swizzle); STAGES2 stages fill the shared memory.
+#ifndef PITON_GEMM2_BK
+#define PITON_GEMM2_BK 32
+#endif
+#ifndef PITON_GEMM2_STAGES
+#define PITON_GEMM2_STAGES 6
+#endif
+constexpr int BK2 = PITON_GEMM2_BK, STAGES2 = PITON_GEMM2_STAGES;
+static_assert(BK2 == 32 || BK2 == 64, "pair k-block: 32 or 64 fp16");
+constexpr int KC_BLOCKS2 = KC / BK2;
+constexpr uint64_t LAYOUT2 = BK2 == 64 ? LAYOUT_SWIZZLE_128B : LAYOUT_SWIZZLE_64B;
+constexpr uint32_t A2_TILE_BYTES = BM * BK2 * 2;   // this CTA's 128 rows x BK2 fp16
+__host__ __device__ constexpr uint32_t b2_tile_bytes(int bnp) { return (uint32_t)(bnp / 2) * BK2 * 2; }
 __host__ __device__ constexpr uint32_t stage2_bytes(int bnp) { return 2 * A2_TILE_BYTES + 2 * b2_tile_bytes(bnp); }
 __host__ __device__ constexpr uint32_t smem2_bytes(int bnp) { return STAGES2 * stage2_bytes(bnp) + 1024 + 1024; }
 
@@ -701,7 +712,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     uint8_t *st = smem + s * STAGE;
                     const uint32_t bar = cluster_addr_rank0(&full[s]);
                     if (leader) mbar_arrive_expect_tx(&full[s], 2 * STAGE);   // both CTAs' bytes
-                    const int kx = kb * BK;
+                    const int kx = kb * BK2;
                     tma_load_2d_pair(st, &tm_ah, bar, kx, arow);
                     tma_load_2d_pair(st + A2_TILE_BYTES, &tm_al, bar, kx, arow);
                     tma_load_2d_pair(st + 2 * A2_TILE_BYTES, &tm_bh, bar, kx, brow);
@@ -722,7 +733,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint32_t it = 0, chunk = 0;
             bool ok = true;
             for (int t = pair; ok && t < args.num_tiles && !*abort_flag; t += npairs) {
-                for (int kb0 = 0; ok && kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk) {
+                for (int kb0 = 0; ok && kb0 < kb_total; kb0 += KC_BLOCKS2, ++chunk) {
                     const int acc = chunk & 1;
                     const uint32_t use = chunk >> 1;
                     if (!mbar_wait(&tempty[acc], (use & 1) ^ 1)) {
@@ -731,7 +742,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                     }
                     tc_fence_after();
                     const uint32_t d_tmem = tmem_base + acc * BNP;
-                    const int kb1 = min(kb0 + KC_BLOCKS, kb_total);
+                    const int kb1 = min(kb0 + KC_BLOCKS2, kb_total);
                     for (int kb = kb0; kb < kb1; ++kb, ++it) {
                         const uint32_t s = it % STAGES2, round = it / STAGES2;
                         if (!mbar_wait(&full[s], round & 1)) {
@@ -743,12 +754,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                         const uint32_t a_hi = base, a_lo = base + A2_TILE_BYTES;
                         const uint32_t b_hi = base + 2 * A2_TILE_BYTES, b_lo = b_hi + B_TILE;
 #pragma unroll
-                        for (int ks = 0; ks < BK / 16; ++ks) {
+                        for (int ks = 0; ks < BK2 / 16; ++ks) {
                             const uint32_t off = ks * 32;   // 16 fp16 k-values
-                            const uint64_t dah = smem_desc_kmajor(a_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dal = smem_desc_kmajor(a_lo + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dbh = smem_desc_kmajor(b_hi + off, 64, LAYOUT_SWIZZLE_64B);
-                            const uint64_t dbl = smem_desc_kmajor(b_lo + off, 64, LAYOUT_SWIZZLE_64B);
+                            const uint64_t dah = smem_desc_kmajor(a_hi + off, BK2 * 2, LAYOUT2);
+                            const uint64_t dal = smem_desc_kmajor(a_lo + off, BK2 * 2, LAYOUT2);
+                            const uint64_t dbh = smem_desc_kmajor(b_hi + off, BK2 * 2, LAYOUT2);
+                            const uint64_t dbl = smem_desc_kmajor(b_lo + off, BK2 * 2, LAYOUT2);
                             const uint32_t first = (kb == kb0 && ks == 0) ? 0u : 1u;
                             mma_f16_pair(d_tmem, dah, dbh, IDESC, first);   // A_hi B_hi
                             mma_f16_pair(d_tmem, dah, dbl, IDESC, 1u);      // A_hi B_lo
@@ -777,7 +788,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint32_t chunk = 0;
         bool ok = true;
         const int et = threadIdx.x - 64;
-        const int n_chunks = (kb_total + KC_BLOCKS - 1) / KC_BLOCKS;
+        const int n_chunks = (kb_total + KC_BLOCKS2 - 1) / KC_BLOCKS2;
         const int rows_per_chunk = (BM + n_chunks - 1) / n_chunks;
         const uint32_t tempty_pair[2] = {cluster_addr_rank0(&tempty[0]), cluster_addr_rank0(&tempty[1])};
         int pend_tn = -1;
@@ -789,7 +800,7 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t row_base = (int64_t)tm * 2 * BM + (int64_t)rank * BM;
             const int64_t row = row_base + quarter * 32 + lane;
             const int64_t col0 = (int64_t)tn * BNP + half * HALF;
-            for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS, ++chunk, ++ci) {
+            for (int kb0 = 0, ci = 0; kb0 < kb_total; kb0 += KC_BLOCKS2, ++chunk, ++ci) {
                 const int acc = chunk & 1;
                 const uint32_t use = chunk >> 1;
                 bool got = !*abort_flag && mbar_wait(&tfull[acc], use & 1);
@@ -921,16 +932,19 @@ EncodeTiled encode_fn() {
     return fn;
 }
 
-// Row-major [rows, ldh] fp16, box [box_rows, BK] (64 bytes per row), 64-byte swizzle.
-int make_map16(CUtensorMap *map, const __half *base, int64_t rows, int64_t ldh, int box_rows) {
+// Row-major [rows, ldh] fp16, box [box_rows, box_k]: box_k 32 (64-byte rows, 64-byte swizzle)
+// or 64 (128-byte rows, 128-byte swizzle).
+int make_map16(CUtensorMap *map, const __half *base, int64_t rows, int64_t ldh, int box_rows, int box_k = BK) {
     EncodeTiled enc = encode_fn();
     if (!enc) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled unavailable");
     cuuint64_t dims[2] = {(cuuint64_t)ldh, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)(ldh * 2)};
-    cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+    cuuint32_t box[2] = {(cuuint32_t)box_k, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
     CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half *>(base), dims, strides, box, estr,
-                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_64B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE,
+                     box_k == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B,
+                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     if (r != CUDA_SUCCESS) return set_error(PITON_B200_ECUDA, "cuTensorMapEncodeTiled (fp16) failed (%d)", (int)r);
     return PITON_B200_OK;
@@ -1054,15 +1068,16 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     const bool pairs = use_pairs(s.M, s.N);
     const int bn = pairs ? pair_tile_width(s.M, s.N) : tile_width(s.M, s.N);
     const int b_box = pairs ? bn / 2 : bn;   // rows of B^T one CTA loads
+    const int bk = pairs ? BK2 : BK;         // k-values per stage
     CUtensorMap m_ah, m_al, m_bh, m_bl;
     int rc;
-    if ((rc = make_map16(&m_ah, A.hi, s.M, ldh, BM)) || (rc = make_map16(&m_al, A.lo, s.M, ldh, BM)) ||
-        (rc = make_map16(&m_bh, B.hi, s.N, ldh, b_box)) || (rc = make_map16(&m_bl, B.lo, s.N, ldh, b_box)))
+    if ((rc = make_map16(&m_ah, A.hi, s.M, ldh, BM, bk)) || (rc = make_map16(&m_al, A.lo, s.M, ldh, BM, bk)) ||
+        (rc = make_map16(&m_bh, B.hi, s.N, ldh, b_box, bk)) || (rc = make_map16(&m_bl, B.lo, s.N, ldh, b_box, bk)))
         return rc;
     GemmArgs g;
     g.c = s.c;
     g.M = s.M; g.N = s.N; g.K = s.K; g.scm = s.scm; g.scn = s.scn;
-    g.k_blocks = (int)cdiv(s.K, BK);
+    g.k_blocks = (int)cdiv(s.K, (int64_t)bk);
     g.world = s.world;
     g.rank = s.rank;
     g.row_offset = s.row_offset;
