@@ -147,10 +147,19 @@ __global__ void __launch_bounds__(256) split16_tile_kernel(const float *__restri
     const int c = blockIdx.x;
     const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)c * KC;
     if (lanes_along_rows) {
+        // 16 loads in flight per thread before they go to shared memory
         const int64_t r = r0 + lane;
-        for (int kk = warp; kk < KC; kk += 8) {
-            const int64_t k = k0 + kk;
-            tile[lane][kk] = (r < rows && k < K) ? src[r * s_row + k * s_col] : 0.0f;
+        const bool rin = r < rows;
+#pragma unroll
+        for (int i0 = 0; i0 < KC / 8; i0 += 16) {
+            float v[16];
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+                const int64_t k = k0 + warp + 8 * (i0 + i);
+                v[i] = (rin && k < K) ? __ldcs(src + r * s_row + k * s_col) : 0.0f;
+            }
+#pragma unroll
+            for (int i = 0; i < 16; ++i) tile[lane][warp + 8 * (i0 + i)] = v[i];
         }
     } else {
         for (int rr = warp; rr < 32; rr += 8) {
@@ -582,13 +591,14 @@ __global__ void __launch_bounds__(THREADS, 1)
 // the even CTA's barrier.  Waits are bounded as in the one-CTA kernel; the two
 // cluster barriers (after set-up, before TMEM is freed) are reached unconditionally.
 
-// BK2: fp16 k-values per stage of the pair kernel (32: 64-byte rows, 64-byte swizzle; 64:
-// 128-byte rows, 128-byte swizzle); STAGES2 stages fill the shared memory.
+// BK2: fp16 k-values per stage of the pair kernel (64: 128-byte rows, 128-byte swizzle; 32:
+// 64-byte rows, 64-byte swizzle); STAGES2 stages fill the shared memory.  At 8192^3 64 x 3
+// stages measured 411.5 TFLOP/s per step against 395.6 for 32 x 6 and 392 for 32 x 7.
 #ifndef PITON_GEMM2_BK
-#define PITON_GEMM2_BK 32
+#define PITON_GEMM2_BK 64
 #endif
 #ifndef PITON_GEMM2_STAGES
-#define PITON_GEMM2_STAGES 6
+#define PITON_GEMM2_STAGES 3
 #endif
 constexpr int BK2 = PITON_GEMM2_BK, STAGES2 = PITON_GEMM2_STAGES;
 static_assert(BK2 == 32 || BK2 == 64, "pair k-block: 32 or 64 fp16");
@@ -640,7 +650,9 @@ __device__ __forceinline__ void mma_commit_pair(uint64_t *bar) {
         : "memory");
 }
 
-template <int BNP>
+// GATHER: the output goes to the ranks' buffers (peer stores or a multicast address); the
+// single-GPU instantiation carries none of that code.
+template <int BNP, bool GATHER>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_f16x3_2sm_kernel(const __grid_constant__ CUtensorMap tm_ah, const __grid_constant__ CUtensorMap tm_al,
                           const __grid_constant__ CUtensorMap tm_bh, const __grid_constant__ CUtensorMap tm_bl,
@@ -837,12 +849,12 @@ __global__ void __launch_bounds__(THREADS, 1)
                 tc_fence_before();
                 __syncwarp();
                 if (lane == 0) mbar_arrive_cluster(tempty_pair[acc]);   // accumulator free (even CTA's barrier)
-                if (args.world > 1 && pend_row >= 0)
+                if (GATHER && args.world > 1 && pend_row >= 0)
                     copy_rows_to_peers<BNP>(args, pend_row, pend_tn, min(ci * rows_per_chunk, BM),
                                             min((ci + 1) * rows_per_chunk, BM), et);
             }
             if (!ok) break;
-            if (row < args.M && args.mc_c) {
+            if (GATHER && row < args.M && args.mc_c) {
                 // multicast all-gather: one store per element, replicated to every rank by the switch
                 float *mrow = args.mc_c + (args.row_offset + row) * args.ldc_peer;
 #pragma unroll
@@ -859,7 +871,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 float *crow;
                 bool vec;
                 int64_t scn;
-                if (args.world > 0) {
+                if (GATHER && args.world > 0) {
                     crow = args.peer_c[args.rank] + (args.row_offset + row) * args.ldc_peer;
                     vec = true;
                     scn = 1;
@@ -886,7 +898,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (col0 + j < args.N) crow[(col0 + j) * scn] = sum[j];
                 }
             }
-            if (args.world > 1 && !args.mc_c) {
+            if (GATHER && args.world > 1 && !args.mc_c) {
                 __threadfence_block();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(epi_bar);
@@ -902,8 +914,8 @@ __global__ void __launch_bounds__(THREADS, 1)
             }
             ++tiles_done;
         }
-        if (ok && args.world > 1 && pend_row >= 0) copy_rows_to_peers<BNP>(args, pend_row, pend_tn, 0, BM, et);
-        if (args.mc_c) __threadfence_system();
+        if (GATHER && ok && args.world > 1 && pend_row >= 0) copy_rows_to_peers<BNP>(args, pend_row, pend_tn, 0, BM, et);
+        if (GATHER && args.mc_c) __threadfence_system();
     }
     tc_fence_before();
     __syncthreads();
@@ -964,14 +976,14 @@ int pair_tile_width(int64_t M, int64_t N) {
     return cost224 < cost256 ? 224 : 256;
 }
 
-template <int BNP>
+template <int BNP, bool GATHER>
 int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtensorMap &b_hi, const CUtensorMap &b_lo,
                  GemmArgs g, cudaStream_t stream) {
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (dev < 64 && !attr[dev]) {
-        PITON_CUDA(cudaFuncSetAttribute(gemm_f16x3_2sm_kernel<BNP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        PITON_CUDA(cudaFuncSetAttribute(gemm_f16x3_2sm_kernel<BNP, GATHER>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                         smem2_bytes(BNP)));
         attr[dev] = true;
     }
@@ -988,7 +1000,7 @@ int launch_pairs(const CUtensorMap &a_hi, const CUtensorMap &a_lo, const CUtenso
     at[0].val.clusterDim.z = 1;
     cfg.attrs = at;
     cfg.numAttrs = 1;
-    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16x3_2sm_kernel<BNP>, a_hi, a_lo, b_hi, b_lo, g));
+    PITON_CUDA(cudaLaunchKernelEx(&cfg, gemm_f16x3_2sm_kernel<BNP, GATHER>, a_hi, a_lo, b_hi, b_lo, g));
     return PITON_B200_OK;
 }
 
@@ -1096,8 +1108,13 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
         g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
         g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
         g.num_tiles = g.tiles_m * g.tiles_n;
-        rc = bn == 224 ? launch_pairs<224>(m_ah, m_al, m_bh, m_bl, g, stream)
-                       : launch_pairs<256>(m_ah, m_al, m_bh, m_bl, g, stream);
+        const bool gather = g.world > 0 || g.mc_c != nullptr;
+        if (gather)
+            rc = bn == 224 ? launch_pairs<224, true>(m_ah, m_al, m_bh, m_bl, g, stream)
+                           : launch_pairs<256, true>(m_ah, m_al, m_bh, m_bl, g, stream);
+        else
+            rc = bn == 224 ? launch_pairs<224, false>(m_ah, m_al, m_bh, m_bl, g, stream)
+                           : launch_pairs<256, false>(m_ah, m_al, m_bh, m_bl, g, stream);
         if (rc) return rc;
         nonfinite_fixup_kernel<<<(unsigned)cdiv(s.M + s.N, 8), 256, 0, stream>>>(g, (int)chunks_of(s.K));
         return check_launch("gemm_f16x3_2sm", s.split_b ? 4 : 3);
