@@ -166,6 +166,89 @@ __global__ void __launch_bounds__(256) attn_split16_kernel(const float *__restri
     if (t == 0) ex[h * blocks + blk] = (int8_t)e;
 }
 
+// The same split for rows with unit stride along d and 16-byte aligned rows (the common
+// contiguous layout): thread t holds key t / 4, dimensions 16 (t % 4) .. + 15, loaded as four
+// float4 before any is used, so a CTA has its whole 16 KB block in flight at once.  K is
+// written straight from registers (32-byte runs per half); V goes through shared memory
+// for the transpose.
+template <bool TRANSPOSE>
+__global__ void __launch_bounds__(256) attn_split16_vec_kernel(const float *__restrict__ src, int64_t n_ctx,
+                                                               int64_t s_h, int64_t s_r, __half *__restrict__ hi,
+                                                               __half *__restrict__ lo, int64_t ld,
+                                                               int8_t *__restrict__ ex, int64_t blocks) {
+    __shared__ float tile[TRANSPOSE ? 64 : 1][65];   // [key][d]
+    __shared__ float wmax[8];
+    const int64_t blk = blockIdx.x, h = blockIdx.y, key0 = blk * 64;
+    const int t = threadIdx.x, lane = t & 31, warp = t >> 5;
+    const int key = t >> 2, d0 = (t & 3) * 16;
+    const bool live = key0 + key < n_ctx;
+    float v[16];
+    if (live) {
+        const float4 *p = reinterpret_cast<const float4 *>(src + h * s_h + (key0 + key) * s_r + d0);
+        float4 f[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) f[j] = __ldcs(p + j);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            v[4 * j] = f[j].x; v[4 * j + 1] = f[j].y; v[4 * j + 2] = f[j].z; v[4 * j + 3] = f[j].w;
+        }
+    } else {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) v[j] = 0.0f;
+    }
+    float m = 0.0f;
+#pragma unroll
+    for (int j = 0; j < 16; ++j) m = fmaxf(m, finite_abs(v[j]));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if (lane == 0) wmax[warp] = m;
+    if (TRANSPOSE) {
+#pragma unroll
+        for (int j = 0; j < 16; ++j) tile[key][d0 + j] = v[j];
+    }
+    __syncthreads();
+    m = wmax[0];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) m = fmaxf(m, wmax[w]);
+    const int e = block_exponent(m);
+    const float sc = pow2i(e);
+    if (!TRANSPOSE) {
+        if (live) {
+            __align__(16) __half hh[16], ll[16];
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+                float vh, vl;
+                split_f16(v[j] * sc, vh, vl);
+                hh[j] = __float2half_rn(vh);
+                ll[j] = __float2half_rn(vl);
+            }
+            const int64_t off = (h * n_ctx + key0 + key) * HD + d0;
+            uint4 *ph = reinterpret_cast<uint4 *>(hi + off), *pl = reinterpret_cast<uint4 *>(lo + off);
+            ph[0] = reinterpret_cast<const uint4 *>(hh)[0];
+            ph[1] = reinterpret_cast<const uint4 *>(hh)[1];
+            pl[0] = reinterpret_cast<const uint4 *>(ll)[0];
+            pl[1] = reinterpret_cast<const uint4 *>(ll)[1];
+        }
+    } else {
+        // 512 runs of 8 consecutive keys of one dimension (16-byte stores), two per thread
+        for (int c = t; c < 512; c += 256) {
+            const int a8 = c >> 3, b8 = (c & 7) * 8;   // d a8, keys b8 ..
+            __align__(16) __half hh[8], ll[8];
+#pragma unroll
+            for (int q = 0; q < 8; ++q) {
+                float vh, vl;
+                split_f16(tile[b8 + q][a8] * sc, vh, vl);
+                hh[q] = __float2half_rn(vh);
+                ll[q] = __float2half_rn(vl);
+            }
+            const int64_t off = (h * HD + a8) * ld + key0 + b8;
+            *reinterpret_cast<uint4 *>(hi + off) = *reinterpret_cast<const uint4 *>(hh);
+            *reinterpret_cast<uint4 *>(lo + off) = *reinterpret_cast<const uint4 *>(ll);
+        }
+    }
+    if (t == 0) ex[h * blocks + blk] = (int8_t)e;
+}
+
 struct TcAttnArgs {
     float *o;
     int64_t soh, som;
@@ -822,8 +905,18 @@ int attention_tc(const AttnParams &p, void *workspace, cudaStream_t stream) {
     const int64_t blocks = kv_blocks_of(p.n_ctx), ldv = v_ld(p.n_ctx);
     // K [n_ctx, D] per head (strides skn, skk) -> [heads * n_ctx, D]; V [n_ctx, D] (svn, 1) -> V^T
     dim3 g((unsigned)blocks, (unsigned)p.heads);
-    attn_split16_kernel<false><<<g, 256, 0, stream>>>(p.k, p.n_ctx, p.skh, p.skn, p.skk, k_hi, k_lo, HD, ek, blocks);
-    attn_split16_kernel<true><<<g, 256, 0, stream>>>(p.v, p.n_ctx, p.svh, p.svn, 1, v_hi, v_lo, ldv, ev, blocks);
+    auto rows16 = [](const float *base, int64_t s_h, int64_t s_r) {   // 16-byte aligned unit-stride rows
+        return (reinterpret_cast<uintptr_t>(base) & 15) == 0 && s_h % 4 == 0 && s_r % 4 == 0;
+    };
+    if (p.skk == 1 && rows16(p.k, p.skh, p.skn))
+        attn_split16_vec_kernel<false><<<g, 256, 0, stream>>>(p.k, p.n_ctx, p.skh, p.skn, k_hi, k_lo, HD, ek, blocks);
+    else
+        attn_split16_kernel<false><<<g, 256, 0, stream>>>(p.k, p.n_ctx, p.skh, p.skn, p.skk, k_hi, k_lo, HD, ek,
+                                                          blocks);
+    if (rows16(p.v, p.svh, p.svn))
+        attn_split16_vec_kernel<true><<<g, 256, 0, stream>>>(p.v, p.n_ctx, p.svh, p.svn, v_hi, v_lo, ldv, ev, blocks);
+    else
+        attn_split16_kernel<true><<<g, 256, 0, stream>>>(p.v, p.n_ctx, p.svh, p.svn, 1, v_hi, v_lo, ldv, ev, blocks);
     int launches = 3;
     const float *q = p.q;
     int64_t sqm = p.sqm, sqh = p.sqh;
