@@ -136,7 +136,8 @@ __global__ void __launch_bounds__(256) split16_rows_kernel(const float *__restri
 
 // Any strides (row-major B transposed into K-major rows, transposed or strided A): a CTA
 // stages a 32-row x 256-k tile in shared memory, reading with the lanes along whichever of
-// rows and k has the unit (smaller) stride so that the loads coalesce, then each warp splits
+// rows and k has the unit (smaller) stride so that the loads coalesce (lanes_along_rows 1 or
+// 0; 2: unit row stride and 16-byte aligned columns, float4 loads), then each warp splits
 // four rows: a half2 of consecutive k-values per lane, 128-byte stores per warp.
 __global__ void __launch_bounds__(256) split16_tile_kernel(const float *__restrict__ src, int64_t rows, int64_t K,
                                                            int64_t s_row, int64_t s_col, __half *__restrict__ hi,
@@ -146,7 +147,33 @@ __global__ void __launch_bounds__(256) split16_tile_kernel(const float *__restri
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int c = blockIdx.x;
     const int64_t r0 = (int64_t)blockIdx.y * 32, k0 = (int64_t)c * KC;
-    if (lanes_along_rows) {
+    if (lanes_along_rows == 2) {
+        // unit stride along rows, 16-byte aligned columns (row-major B): float4 of 4 rows,
+        // 8 per thread in flight; lanes cover 4 k x 8 row quads, conflict-free into the padded tile
+        const int n0 = 4 * (threadIdx.x & 7), kr = threadIdx.x >> 3;
+        const int64_t r = r0 + n0;
+        float4 f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int64_t k = k0 + kr + 32 * i;
+            if (k < K && r + 3 < rows) {
+                f[i] = __ldcs(reinterpret_cast<const float4 *>(src + r + k * s_col));
+            } else {
+                float e[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) e[j] = (k < K && r + j < rows) ? src[r + j + k * s_col] : 0.0f;
+                f[i] = make_float4(e[0], e[1], e[2], e[3]);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int kk = kr + 32 * i;
+            tile[n0][kk] = f[i].x;
+            tile[n0 + 1][kk] = f[i].y;
+            tile[n0 + 2][kk] = f[i].z;
+            tile[n0 + 3][kk] = f[i].w;
+        }
+    } else if (lanes_along_rows) {
         // 16 loads in flight per thread before they go to shared memory
         const int64_t r = r0 + lane;
         const bool rin = r < rows;
@@ -1059,8 +1086,9 @@ void split16(const float *src, int64_t rows, int64_t K, int64_t s_row, int64_t s
                                                                             lde, (int)chunks, vec);
     } else {
         dim3 g((unsigned)chunks, (unsigned)cdiv(rows, 32));
+        const bool vec_rows = s_row == 1 && s_col % 4 == 0 && (reinterpret_cast<uintptr_t>(src) & 15) == 0;
         split16_tile_kernel<<<g, 256, 0, stream>>>(src, rows, K, s_row, s_col, d.hi, d.lo, d.ex, ldh, lde,
-                                                   llabs(s_row) < llabs(s_col));
+                                                   vec_rows ? 2 : (int)(llabs(s_row) < llabs(s_col)));
     }
 }
 
