@@ -30,6 +30,14 @@ namespace tg {
 constexpr int V = 65, D = 128, L = 4, H = 4, HD = 32, F = 4 * D, CTX = 128;
 constexpr int SEQ = 2, THREADS = 256;
 constexpr int LAYER_FLOATS = 2 * D + D * 3 * D + 3 * D + D * D + D + 2 * D + D * F + F + F * D + D;
+// offsets of a layer's tensors in its packed block
+constexpr int O_LN1 = 0, O_WQKV = 2 * D, O_BQKV = O_WQKV + D * 3 * D, O_WO = O_BQKV + 3 * D, O_BO = O_WO + D * D,
+              O_LN2 = O_BO + D, O_WFC = O_LN2 + 2 * D, O_BFC = O_WFC + D * F, O_WPR = O_BFC + F,
+              O_BPR = O_WPR + F * D;
+static_assert(O_BPR + D == LAYER_FLOATS, "layer layout");
+// a layer's gains and biases as the step kernel keeps them in shared memory
+constexpr int P_LN1 = 0, P_BQKV = 2 * D, P_BO = P_BQKV + 3 * D, P_LN2 = P_BO + D, P_BFC = P_LN2 + 2 * D,
+              P_BPR = P_BFC + F, P_LAYER = P_BPR + D;
 constexpr int64_t TOTAL_FLOATS = (int64_t)V * D + (int64_t)CTX * D + (int64_t)L * LAYER_FLOATS + 2 * D;
 
 struct StepArgs {
@@ -46,12 +54,13 @@ struct StepArgs {
 // out[s][n] = act(sum_k in[s][k] W[k][n] + b[n]) for the CTA's SEQ rows.  A
 // thread owns 4 adjacent columns (16-byte weight loads) of one k-group; the
 // k range is split into G groups so that every thread has work, and the
-// partial sums meet in `scratch` (SEQ * THREADS * 4 floats).  Eight k-steps
-// are unrolled so 8 x 16 bytes of weights are in flight per thread: the
-// weights come from L2 and this loop is latency-bound otherwise.
+// partial sums meet in `scratch` (SEQ * THREADS * 4 floats).  The k-loop is
+// unrolled so that many 16-byte weight loads are in flight per thread: the
+// weights come from L2 and this loop is latency-bound otherwise.  b is in
+// shared memory.
 template <int K, int N, bool GELU>
-__device__ __forceinline__ void linear(const float *in, float *out, const float *__restrict__ W,
-                                       const float *__restrict__ b, float *scratch, bool residual) {
+__device__ __forceinline__ void linear(const float *in, float *out, const float *__restrict__ W, const float *b,
+                                       float *scratch, bool residual) {
     constexpr int NQ = N / 4;                             // column quads
     constexpr int G = THREADS / NQ > 0 ? THREADS / NQ : 1;  // k-groups
     constexpr int KG = K / G;
@@ -93,7 +102,7 @@ __device__ __forceinline__ void linear(const float *in, float *out, const float 
             float4 p = sc4[s * THREADS + gg * NQ + qq];
             v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
         }
-        float4 bb = __ldg(reinterpret_cast<const float4 *>(b) + qq);
+        float4 bb = reinterpret_cast<const float4 *>(b)[qq];   // shared memory
         float r[4] = {v.x + bb.x, v.y + bb.y, v.z + bb.z, v.w + bb.w};
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
@@ -105,9 +114,9 @@ __device__ __forceinline__ void linear(const float *in, float *out, const float 
     __syncthreads();
 }
 
-// y[s] = LayerNorm(x[s]) * g + b, one warp per sequence (biased variance, eps 1e-5).
-__device__ __forceinline__ void layernorm(const float *x, float *y, const float *__restrict__ g,
-                                          const float *__restrict__ b) {
+// y[s] = LayerNorm(x[s]) * g + b, one warp per sequence (biased variance, eps 1e-5); g and b in
+// shared memory.
+__device__ __forceinline__ void layernorm(const float *x, float *y, const float *g, const float *b) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     if (warp < SEQ) {
         const float *xs = x + warp * D;
@@ -131,7 +140,7 @@ __device__ __forceinline__ void layernorm(const float *x, float *y, const float 
 #pragma unroll
         for (int i = 0; i < D / 32; ++i) {
             int c = lane + 32 * i;
-            y[warp * D + c] = v[i] * r * __ldg(g + c) + __ldg(b + c);
+            y[warp * D + c] = v[i] * r * g[c] + b[c];
         }
     }
     __syncthreads();
@@ -139,13 +148,33 @@ __device__ __forceinline__ void layernorm(const float *x, float *y, const float 
 
 __global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
     __shared__ __align__(16) float x[SEQ * D], h[SEQ * D], qkv[SEQ * 3 * D], att[SEQ * D], f[SEQ * F];
-    __shared__ float probs[SEQ * H][CTX];
     __shared__ __align__(16) float scratch[SEQ * THREADS * 4];
+    // the attention's probabilities share the linear layers' split-k scratch (never live together)
+    static_assert(SEQ * H * CTX <= SEQ * THREADS * 4, "probabilities fit the scratch");
+    float (*probs)[CTX] = reinterpret_cast<float (*)[CTX]>(scratch);
     __shared__ float lg[SEQ][V + 3];
+    __shared__ __align__(16) float prm[L * P_LAYER + 2 * D];   // every layer's gains and biases, lnf
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t b0 = (int64_t)blockIdx.x * SEQ;
     const int pos = a.pos;
     const float *wte = a.w, *wpe = a.w + V * D;
+
+    // the gains and biases of all layers into shared memory, requested together with the
+    // embeddings below (one L2 round trip instead of one per LayerNorm and linear layer)
+    {
+        const float *lw0 = a.w + V * D + CTX * D;
+        for (int i = tid; i < (L * P_LAYER + 2 * D) / 4; i += THREADS) {
+            const int l = (4 * i) / P_LAYER, q = 4 * i - l * P_LAYER;
+            const float *lw = lw0 + (int64_t)l * LAYER_FLOATS;
+            const float *src = l == L                ? lw + q                      // lnf_g, lnf_b
+                               : q < P_BQKV          ? lw + O_LN1 + q
+                               : q < P_BO            ? lw + O_BQKV + (q - P_BQKV)
+                               : q < P_BFC           ? lw + O_BO + (q - P_BO)      // b_o, ln2_g, ln2_b
+                               : q < P_BPR           ? lw + O_BFC + (q - P_BFC)
+                                                     : lw + O_BPR + (q - P_BPR);
+            *reinterpret_cast<float4 *>(prm + 4 * i) = __ldg(reinterpret_cast<const float4 *>(src));
+        }
+    }
 
     // token + position embedding
     for (int i = tid; i < SEQ * D; i += THREADS) {
@@ -163,9 +192,10 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
 
     const float *lw = a.w + V * D + CTX * D;
     for (int l = 0; l < L; ++l, lw += LAYER_FLOATS) {
-        const float *ln1_g = lw, *ln1_b = ln1_g + D, *w_qkv = ln1_b + D, *b_qkv = w_qkv + D * 3 * D;
-        const float *w_o = b_qkv + 3 * D, *b_o = w_o + D * D, *ln2_g = b_o + D, *ln2_b = ln2_g + D;
-        const float *w_fc = ln2_b + D, *b_fc = w_fc + D * F, *w_pr = b_fc + F, *b_pr = w_pr + F * D;
+        const float *pl = prm + l * P_LAYER;
+        const float *ln1_g = pl + P_LN1, *ln1_b = ln1_g + D, *b_qkv = pl + P_BQKV, *b_o = pl + P_BO;
+        const float *ln2_g = pl + P_LN2, *ln2_b = ln2_g + D, *b_fc = pl + P_BFC, *b_pr = pl + P_BPR;
+        const float *w_qkv = lw + O_WQKV, *w_o = lw + O_WO, *w_fc = lw + O_WFC, *w_pr = lw + O_WPR;
         float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
         float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
 
@@ -236,26 +266,57 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
         linear<D, F, true>(h, f, w_fc, b_fc, scratch, false);         // f = gelu(h @ Wfc + bfc)
         linear<F, D, false>(f, x, w_pr, b_pr, scratch, true);          // x += f @ Wpr + bpr
     }
-    const float *lnf_g = lw, *lnf_b = lnf_g + D;
+    const float *lnf_g = prm + L * P_LAYER, *lnf_b = lnf_g + D;
     layernorm(x, h, lnf_g, lnf_b);
-    // tied head: logits[s][v] = h[s] . wte[v]; warp per (s, v) pair, lanes over D
-    for (int pv = warp; pv < SEQ * V; pv += THREADS / 32) {
-        int s = pv / V, vv = pv % V;
-        float acc = 0.0f;
+    // tied head: logits[s][v] = h[s] . wte[v]; a warp per (s, v) pair, lanes over D, the
+    // pairs' embedding rows requested together (one L2 round trip for all of a warp's pairs)
+    {
+        constexpr int PV = (SEQ * V + THREADS / 32 - 1) / (THREADS / 32);   // pairs per warp
+        float ew[PV][D / 32];
 #pragma unroll
-        for (int i = 0; i < D / 32; ++i) acc = fmaf(h[s * D + lane + 32 * i], __ldg(wte + vv * D + lane + 32 * i), acc);
+        for (int i = 0; i < PV; ++i) {
+            const int pv = warp + i * (THREADS / 32);
+            const int vv = pv < SEQ * V ? pv % V : 0;
 #pragma unroll
-        for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-        if (lane == 0) lg[s][vv] = acc;
+            for (int c = 0; c < D / 32; ++c) ew[i][c] = __ldg(wte + vv * D + lane + 32 * c);
+        }
+#pragma unroll
+        for (int i = 0; i < PV; ++i) {
+            const int pv = warp + i * (THREADS / 32);
+            if (pv < SEQ * V) {
+                const int s = pv / V, vv = pv % V;
+                float acc = 0.0f;
+#pragma unroll
+                for (int c = 0; c < D / 32; ++c) acc = fmaf(h[s * D + lane + 32 * c], ew[i][c], acc);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                if (lane == 0) lg[s][vv] = acc;
+            }
+        }
     }
     __syncthreads();
-    if (tid < SEQ && pos + 1 >= a.prompt_len && pos + 1 < a.end) {
-        int64_t b = b0 + tid;
+    // greedy token: warp s takes sequence s's argmax, lanes over the vocabulary, first maximum
+    // on ties (as numpy.argmax)
+    if (warp < SEQ && pos + 1 >= a.prompt_len && pos + 1 < a.end) {
+        const int64_t b = b0 + warp;
         if (b < a.batch) {
-            int best = 0;
-            for (int vv = 1; vv < V; ++vv)
-                if (lg[tid][vv] > lg[tid][best]) best = vv;     // first maximum, as numpy.argmax
-            a.tokens[b * CTX + pos + 1] = best;
+            float bv = -INFINITY;
+            int bi = V;
+            for (int vv = lane; vv < V; vv += 32)   // each lane's entries in increasing order
+                if (bi == V || lg[warp][vv] > bv) {
+                    bv = lg[warp][vv];
+                    bi = vv;
+                }
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                if (ov > bv || (ov == bv && oi < bi)) {
+                    bv = ov;
+                    bi = oi;
+                }
+            }
+            if (lane == 0) a.tokens[b * CTX + pos + 1] = bi;
         }
     }
     if (a.logits) {
