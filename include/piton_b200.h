@@ -273,7 +273,8 @@ PITON_B200_API int piton_b200_layernorm_f32(const piton_layernorm_args *args, vo
    op: 0 copy (examples/primitive_kernels.py:12-17 copy_kernel), 1 mul (examples/elementwise.py:5-9 mul_kernel),
    2 fma x*alpha + y with two roundings (primitive_kernels.py:20-27 fma_kernel), 3 scaled ReLU x > 0 ? x*alpha : 0
    (examples/kernels.py:79-85), 4 exp2, 5 log2, 6 1/x, 7 rsqrt, 8 exp, 9 sqrt (examples/sfu_tests.py sfu_kernel
-   OP 0-5), 10 natural log (primitive_kernels.py log_kernel).  QPU rounding: ops 0-3. */
+   OP 0-5), 10 natural log (primitive_kernels.py log_kernel), 11 sigmoid 1 / (1 + exp(-x)), each step
+   rounded as tl.sigmoid composes it (piton/language/core.py:787-790).  QPU rounding: ops 0-3. */
 typedef struct {
     uint64_t x, y, out;   /* float*; y only for mul and fma */
     int64_t n_elements, block_size, grid_x;

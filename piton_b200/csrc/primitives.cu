@@ -27,7 +27,7 @@ namespace piton {
 
 enum ElemOp : int {
     OP_COPY = 0, OP_MUL = 1, OP_FMA = 2, OP_SCALED_RELU = 3, OP_EXP2 = 4, OP_LOG2 = 5, OP_RECIP = 6,
-    OP_RSQRT = 7, OP_EXP = 8, OP_SQRT = 9, OP_LOG = 10,
+    OP_RSQRT = 7, OP_EXP = 8, OP_SQRT = 9, OP_LOG = 10, OP_SIGMOID = 11,
 };
 
 template <int OP, bool QPU>
@@ -42,6 +42,7 @@ __device__ __forceinline__ float elem(float x, float y, float alpha) {
     else if constexpr (OP == OP_RSQRT) return rsqrtf(x);
     else if constexpr (OP == OP_EXP) return expf(x);
     else if constexpr (OP == OP_SQRT) return __fsqrt_rn(x);
+    else if constexpr (OP == OP_SIGMOID) return __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));   // tl.sigmoid
     else return logf(x);
 }
 
@@ -227,7 +228,7 @@ using namespace piton;
 extern "C" int piton_b200_elementwise_f32(const piton_elementwise_args *a, void *stream) {
     PITON_REQUIRE(a != nullptr, "args is NULL");
     PITON_REQUIRE(a->n_elements >= 0 && a->block_size > 0 && a->grid_x >= 0, "bad shape");
-    PITON_REQUIRE(a->op >= OP_COPY && a->op <= OP_LOG, "unknown op %d", a->op);
+    PITON_REQUIRE(a->op >= OP_COPY && a->op <= OP_SIGMOID, "unknown op %d", a->op);
     PITON_REQUIRE((a->flags & ~PITON_B200_QPU_ROUNDING) == 0, "unknown flags 0x%x", a->flags);
     PITON_REQUIRE(!(a->flags & PITON_B200_QPU_ROUNDING) || a->op <= OP_SCALED_RELU,
                   "QPU rounding applies to copy, mul, fma and scaled_relu");
@@ -250,6 +251,7 @@ extern "C" int piton_b200_elementwise_f32(const piton_elementwise_args *a, void 
         case OP_RSQRT: launch_elem<OP_RSQRT>(&b, n, s); break;
         case OP_EXP: launch_elem<OP_EXP>(&b, n, s); break;
         case OP_SQRT: launch_elem<OP_SQRT>(&b, n, s); break;
+        case OP_SIGMOID: launch_elem<OP_SIGMOID>(&b, n, s); break;
         default: launch_elem<OP_LOG>(&b, n, s); break;
     }
     return check_launch("elementwise");

@@ -98,6 +98,12 @@ def log_kernel(x_ptr, out_ptr, n, BLOCK: tl.constexpr):
 
 
 @jit
+def sigmoid_kernel(x_ptr, out_ptr, n, BLOCK: tl.constexpr):
+    """out[i] = tl.sigmoid(x[i]) = 1 / (1 + exp(-x[i])), the language builtin applied element-wise
+    (piton/language/core.py:787-790); the reference has no example kernel for it."""
+
+
+@jit
 def idiv_kernel(x_ptr, y_ptr, q_ptr, r_ptr, n, BLOCK: tl.constexpr):
     """Exact 32-bit x // y and x % y, C truncation (int32 or uint32 arrays).
     (examples/primitive_kernels.py:30-38)"""

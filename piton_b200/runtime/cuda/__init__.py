@@ -408,7 +408,7 @@ __all__ = ["run_on_b200", "register", "registered", "Buffer", "Launch", "extent"
 # ---- element-wise, integer, reduction, transpose and Life operators --------------------------
 
 _ELEM_OPS = {"copy": 0, "mul": 1, "fma": 2, "scaled_relu": 3, "exp2": 4, "log2": 5, "recip": 6, "rsqrt": 7,
-             "exp": 8, "sqrt": 9, "log": 10}
+             "exp": 8, "sqrt": 9, "log": 10, "sigmoid": 11}
 
 
 def _elementwise(L: Launch, grid, op: str, x: str, y, out: str, alpha: float = 0.0):
@@ -457,6 +457,11 @@ def _sfu(L, grid):
 @register("log_kernel", ("x_ptr", "out_ptr", "n", "BLOCK"))
 def _log(L, grid):
     return _elementwise(L, grid, "log", "x_ptr", None, "out_ptr")
+
+
+@register("sigmoid_kernel", ("x_ptr", "out_ptr", "n", "BLOCK"))
+def _sigmoid(L, grid):
+    return _elementwise(L, grid, "sigmoid", "x_ptr", None, "out_ptr")
 
 
 @register("idiv_kernel", ("x_ptr", "y_ptr", "q_ptr", "r_ptr", "n", "BLOCK"))

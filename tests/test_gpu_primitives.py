@@ -152,6 +152,22 @@ def test_sfu_ops_accuracy(cuda, op, fn, lo, hi, ulps):
     np.testing.assert_allclose(lg, np.log(xp.astype(np.float64)), rtol=0, atol=4e-7 * np.log(1e3) + 1e-7)
 
 
+def test_sigmoid(cuda):
+    """tl.sigmoid (piton/language/core.py:787-790) element-wise: within the elementwise rel 1e-5 of
+    float64 over [-30, 30] with a ragged tail, the limits at +-inf, and nan through."""
+    rng = np.random.default_rng(11)
+    n = 100003
+    x = rng.uniform(-30, 30, n).astype(np.float32)
+    x[:6] = [np.inf, -np.inf, 0.0, -0.0, np.nan, 88.0]
+    out = np.full(n + 5, 7.0, np.float32)
+    K.sigmoid_kernel[(triton.cdiv(n, 256),)](x, out, n, BLOCK=256, device="b200")
+    exact = 1.0 / (1.0 + np.exp(-x.astype(np.float64)))
+    fin = np.isfinite(x)
+    np.testing.assert_allclose(out[:n][fin], exact[fin], rtol=1e-5, atol=0)
+    assert out[0] == 1.0 and out[1] == 0.0 and np.isnan(out[4])
+    assert np.all(out[n:] == 7.0)   # nothing past n is written
+
+
 def test_row_sum_and_row_max(cuda):
     rng = np.random.default_rng(42)
     m, n = 64, 96
