@@ -98,7 +98,8 @@ typedef struct {
     int64_t in_row_stride, out_row_stride, n_cols;
     int64_t block_size;   /* BLOCK_SIZE constexpr: columns >= BLOCK_SIZE are neither read nor written */
     int64_t grid_x;       /* rows = programs launched */
-    uint32_t flags;
+    uint32_t flags;       /* PITON_B200_QPU_ROUNDING: the QPU float model, bit for bit (ALU exp, Newton
+                             reciprocal, 16-lane sum); otherwise IEEE expf and division */
     uint32_t _pad;
 } piton_softmax_args;
 PITON_B200_API int piton_b200_softmax_f32(const piton_softmax_args *args, void *stream);

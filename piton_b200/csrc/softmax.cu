@@ -201,16 +201,69 @@ static bool dispatch_reg(const piton_softmax_args *a, int64_t n, cudaStream_t s,
 
 using namespace piton;
 
+// QPU rounding mode: the reference's softmax_kernel program on the QPU float model, bit for bit
+// (examples/kernels.py:60-76 as lowered by piton/backend/lower.py).  A row's BLOCK columns sit
+// 16 to a vector register: the maximum is an fmax fold over the columns in order (-inf for the
+// masked ones), then exp(x - max) with the ALU exp, the sum accumulates the registers lane by
+// lane in order and finishes with the rotate-and-add butterfly of lower.py:4043-4064
+// (lane i += lane i - s, s = 8, 4, 2, 1; lane 0 holds the sum), and each output is e / sum with
+// the Newton reciprocal.  16 threads per row stand for the 16 lanes; 16 rows per CTA.
+__global__ void __launch_bounds__(256) softmax_qpu_kernel(float *__restrict__ out, const float *__restrict__ in,
+                                                          int64_t sin, int64_t sout, int64_t n_cols, int64_t block,
+                                                          int64_t rows) {
+    const int l = threadIdx.x & 15;
+    const int64_t row = (int64_t)blockIdx.x * 16 + (threadIdx.x >> 4);
+    const bool live = row < rows;
+    const int64_t n = n_cols < block ? n_cols : block;
+    const float *x = in + (live ? row : 0) * sin;
+    // the fold's result: the column of the largest key, the last one among equal keys
+    long long key = qpu_fkey(-INFINITY);
+    int64_t idx = -1;
+    for (int64_t j = l; j < block; j += 16) {
+        const long long kj = qpu_fkey(live && j < n ? x[j] : -INFINITY);
+        if (kj >= key) {
+            key = kj;
+            idx = j;
+        }
+    }
+#pragma unroll
+    for (int o = 8; o >= 1; o >>= 1) {
+        const long long ok = __shfl_xor_sync(0xffffffffu, key, o, 16);
+        const int64_t oi = __shfl_xor_sync(0xffffffffu, idx, o, 16);
+        if (ok > key || (ok == key && oi > idx)) {
+            key = ok;
+            idx = oi;
+        }
+    }
+    const float m = (live && idx >= 0 && idx < n) ? x[idx] : -INFINITY;
+    float acc = 0.0f;   // lanes past BLOCK hold +0
+    for (int64_t j = l; j < block; j += 16) {
+        const float e = qpu_exp(qpu_fsub(live && j < n ? x[j] : -INFINITY, m), false);
+        acc = j == l ? e : qpu_fadd(acc, e);
+    }
+#pragma unroll
+    for (int sft = 8; sft >= 1; sft >>= 1) acc = qpu_fadd(acc, __shfl_sync(0xffffffffu, acc, (l - sft) & 15, 16));
+    const float sum = __shfl_sync(0xffffffffu, acc, 0, 16);
+    if (live)
+        for (int64_t j = l; j < n; j += 16) out[row * sout + j] = qpu_fdiv(qpu_exp(qpu_fsub(x[j], m), false), sum);
+}
+
 extern "C" int piton_b200_softmax_f32(const piton_softmax_args *a, void *stream) {
     PITON_REQUIRE(a != nullptr, "args is NULL");
     PITON_REQUIRE(a->grid_x >= 0 && a->n_cols >= 0 && a->block_size > 0, "bad shape: rows %lld cols %lld BLOCK %lld",
                   (long long)a->grid_x, (long long)a->n_cols, (long long)a->block_size);
-    PITON_REQUIRE(a->flags == 0, "unknown flags 0x%x", a->flags);
+    PITON_REQUIRE((a->flags & ~PITON_B200_QPU_ROUNDING) == 0, "unknown flags 0x%x", a->flags);
     PITON_REQUIRE(a->grid_x < (1ll << 31), "too many rows");
     int64_t n = a->n_cols < a->block_size ? a->n_cols : a->block_size;
     if (n == 0 || a->grid_x == 0) return PITON_B200_OK;
     PITON_REQUIRE(a->in && a->out, "NULL pointer");
     cudaStream_t s = as_stream(stream);
+    if (a->flags & PITON_B200_QPU_ROUNDING) {
+        softmax_qpu_kernel<<<(unsigned)cdiv(a->grid_x, (int64_t)16), 256, 0, s>>>(
+            reinterpret_cast<float *>(a->out), reinterpret_cast<const float *>(a->in), a->in_row_stride,
+            a->out_row_stride, a->n_cols, a->block_size, a->grid_x);
+        return check_launch("softmax_qpu");
+    }
     bool vec = ((a->in | a->out) & 15u) == 0 && a->in_row_stride % 4 == 0 && a->out_row_stride % 4 == 0 && n % 4 == 0;
     bool done = vec ? dispatch_reg<4>(a, n, s) : dispatch_reg<1>(a, n, s);
     if (!done)

@@ -238,7 +238,7 @@ def _flags(launch, allowed_qpu=True, simt_ok=False):
     """Flags word of an entry point: QPU rounding (launch option), and the CUDA-core
     path forced where an operator has both (PITON_B200_FORCE_SIMT=1, for comparisons)."""
     if launch.qpu and not allowed_qpu:
-        raise NotImplementedError("qpu_rounding is implemented for add, matmul and dense only")
+        raise NotImplementedError("qpu_rounding is implemented for add, softmax, matmul and dense only")
     f = _lib.QPU_ROUNDING if launch.qpu else 0
     if simt_ok and os.environ.get("PITON_B200_FORCE_SIMT", "0") not in ("", "0"):
         f |= _lib.FORCE_SIMT
@@ -270,7 +270,7 @@ def _softmax(L: Launch, grid):
     out, inp = L.ptr("output_ptr", written=True, covers=rows * n if sout == n else -1), L.ptr("input_ptr")
     inp.require(*extent((rows, sin), (n, 1)))
     out.require(*extent((rows, sout), (n, 1)))
-    a = _lib.SoftmaxArgs(out.addr, inp.addr, sin, sout, ncols, blk, rows, _flags(L, False), 0)
+    a = _lib.SoftmaxArgs(out.addr, inp.addr, sin, sout, ncols, blk, rows, _flags(L), 0)
     L.call("piton_b200_softmax_f32", a, "softmax_kernel")
     return {"bytes": 8 * rows * n, "flops": 4 * rows * n, "path": "softmax"}
 

@@ -3,13 +3,14 @@
 Tolerance: relative error <= 1e-5 per element against the oracle (which
 reproduces the emulator bit for bit) and against float64, as the hot-path
 contract states for softmax; the reference's own test uses rtol 2e-5,
-atol 1e-6 against numpy (tests/test_kernels.py:16-22).
+atol 1e-6 against numpy (tests/test_kernels.py:16-22).  With qpu_rounding=True
+the kernel runs the QPU float model and must match the emulator bit for bit.
 """
 
 import numpy as np
 import pytest
 
-from conftest import golden_ids, goldens
+from conftest import golden_ids, goldens, sha256
 from oracle import oracle as O
 from piton_b200 import workloads as W
 from piton_b200.kernels import softmax_kernel
@@ -47,6 +48,38 @@ def test_matches_emulator_golden(cuda, g):
     ref = O.qpu_softmax(x, m["block"])
     assert rel_err(y, ref) <= RTOL
     assert np.all(y[np.isneginf(x)] == 0)
+
+
+@pytest.mark.parametrize("g", SOFTMAX, ids=golden_ids(SOFTMAX))
+def test_qpu_rounding_bit_exact_with_emulator(cuda, g):
+    """qpu_rounding=True: the reference's program on the QPU float model, every output word equal
+    to the emulator's (the fixture holds the SHA-256 of its output)."""
+    m = g.meta
+    x = W.softmax_input(1823 if m["n"] == 781 else m["m"], m["n"], m["seed"])[:m["m"]]
+    y = np.zeros_like(x)
+    softmax_kernel[(x.shape[0],)](y, x, x.shape[1], x.shape[1], x.shape[1], BLOCK_SIZE=m["block"],
+                                  device="b200", qpu_rounding=True)
+    assert sha256(y) == m["sha_out"]
+
+
+@pytest.mark.parametrize("rows,cols,block", [(7, 5, 8), (9, 16, 16), (33, 100, 128), (5, 300, 128),
+                                             (3, 2000, 2048)])
+def test_qpu_rounding_matches_oracle(cuda, rows, cols, block):
+    """Ragged rows, BLOCK below 16 and below the row, all--inf and single-finite rows, signed
+    zeros and large values: bit for bit with the oracle's restatement."""
+    rng = np.random.default_rng(rows * cols)
+    x = (rng.standard_normal((rows, cols)) * 8).astype(np.float32)
+    x[0, :] = -np.inf
+    x[1, :] = -np.inf
+    x[1, cols // 2] = 3.0
+    x[2, ::3] = -0.0
+    x[-1, 0] = 80.0
+    y = np.full((rows, cols), 9.0, np.float32)
+    softmax_kernel[(rows,)](y, x, cols, cols, cols, BLOCK_SIZE=block, device="b200", qpu_rounding=True)
+    ref = O.qpu_softmax(x, block)
+    n = min(cols, block)
+    np.testing.assert_array_equal(y[:, :n].view(np.uint32), ref[:, :n].view(np.uint32))
+    assert np.all(y[:, n:] == 9.0)
 
 
 def test_config_1823x781_vs_float64(cuda):
