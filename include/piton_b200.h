@@ -239,7 +239,8 @@ typedef struct {
     int32_t causal, even_n;
     uint64_t workspace;   /* device scratch for the tensor-core path, >= piton_b200_attention_workspace_size() */
     uint64_t workspace_bytes;
-    uint32_t flags;       /* PITON_B200_FORCE_SIMT */
+    uint32_t flags;       /* PITON_B200_FORCE_SIMT; PITON_B200_QPU_ROUNDING: the reference program on the QPU
+                             float model, bit for bit (BLOCK_N <= 128, a warp per query row) */
     uint32_t _pad;
 } piton_attention_args;
 /* Bytes of workspace the call needs (0 when it takes the CUDA-core path: HEAD_DIM != 64, n_ctx < 64). */
@@ -252,7 +253,7 @@ PITON_B200_API int piton_b200_attention_f32(const piton_attention_args *args, vo
    [row_offset, row_offset + args->grid_y) of the full output (args->out is ignored; q, k, v
    hold this rank's heads), and every finished 128-row block of a head is stored into each
    rank's full output peer_c[r] (head h at peer_c[r] + h * stride_oh, rows stride_om apart,
-   the same strides on every rank, multiples of 4 elements): into the own one by the softmax
+   the same strides on every rank, multiples of 4 elements): into the own one by the fold
    warps, into the others by a gather warp that trails them (NVLink peer stores, overlapped
    with the next blocks' math).  Tensor-core path only (ENOTSUP otherwise); ldc is not used and
    a nonzero multicast_c is rejected with ENOTSUP.  Every rank must pass a barrier after its

@@ -238,7 +238,7 @@ def _flags(launch, allowed_qpu=True, simt_ok=False):
     """Flags word of an entry point: QPU rounding (launch option), and the CUDA-core
     path forced where an operator has both (PITON_B200_FORCE_SIMT=1, for comparisons)."""
     if launch.qpu and not allowed_qpu:
-        raise NotImplementedError("qpu_rounding is implemented for add, softmax, matmul and dense only")
+        raise NotImplementedError("qpu_rounding is implemented for add, softmax, matmul, dense and attention only")
     f = _lib.QPU_ROUNDING if launch.qpu else 0
     if simt_ok and os.environ.get("PITON_B200_FORCE_SIMT", "0") not in ("", "0"):
         f |= _lib.FORCE_SIMT
@@ -299,7 +299,7 @@ def _matmul(L: Launch, grid):
     a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_matmul_f32", a, "matmul_kernel")
     return {"bytes": 4 * (M * K + K * N + M * N), "flops": 2 * M * N * K,
-            "path": "tcgen05_f16x3" if ws else "cuda_core"}
+            "path": "qpu_rounding" if L.qpu else ("tcgen05_f16x3" if ws else "cuda_core")}
 
 
 def _matmul_on_host_buffers(L: Launch, M, N, K, s, bm, bn, bk, g, grid) -> bool:
@@ -374,13 +374,13 @@ def _attention(L: Launch, grid):
     a = _lib.AttentionArgs(Q.addr, K.addr, V.addr, O.addr, L.float("sm_scale"), st["stride_qh"], st["stride_qm"],
                            st["stride_kh"], st["stride_kn"], st["stride_kk"], st["stride_vh"], st["stride_vn"],
                            st["stride_oh"], st["stride_om"], n_ctx, d, bm, bn, grid[0], heads, int(causal),
-                           int(even), 0, 0, _flags(L, False, simt_ok=True), 0)
+                           int(even), 0, 0, _flags(L, True, simt_ok=True), 0)
     ws = lib().piton_b200_attention_workspace_size(C.byref(a))
     a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_attention_f32", a, "attn_fwd_kernel")
     flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
     return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops,
-            "path": "tcgen05_f16x3" if ws else "cuda_core"}
+            "path": "qpu_rounding" if L.qpu else ("tcgen05_f16x3" if ws else "cuda_core")}
 
 
 @register("layernorm_kernel", ("x_ptr", "out_ptr", "n", "eps", "BLOCK"))

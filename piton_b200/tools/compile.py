@@ -41,8 +41,8 @@ C_TYPES = {"*fp32": "uint64_t", "*i32": "uint64_t", "*u32": "uint64_t", "*u8": "
            "i1": "int32_t"}
 
 # operators that accept PITON_B200_QPU_ROUNDING / PITON_B200_FORCE_SIMT
-QPU_OK = {"add_kernel", "matmul_kernel", "dense_layer_kernel", "copy_kernel", "mul_kernel", "fma_kernel",
-          "scaled_relu_kernel"}
+QPU_OK = {"add_kernel", "softmax_kernel", "matmul_kernel", "dense_layer_kernel", "attn_fwd_kernel", "copy_kernel",
+          "mul_kernel", "fma_kernel", "scaled_relu_kernel"}
 SIMT_OK = {"matmul_kernel", "dense_layer_kernel", "attn_fwd_kernel"}
 
 
@@ -270,6 +270,7 @@ OPERATORS = {
     "scaled_relu_kernel": _elementwise(3, alpha="alpha"),
     "sfu_kernel": _op_sfu,
     "log_kernel": _elementwise(10),
+    "sigmoid_kernel": _elementwise(11),
     "idiv_kernel": _op_idiv,
     "row_sum_kernel": _row_reduce(0),
     "row_max_kernel": _row_reduce(1),

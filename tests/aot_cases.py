@@ -29,6 +29,14 @@ CASES = [
      "Q=*fp32,K=*fp32,V=*fp32,Out=*fp32,sm_scale=fp32,stride_qh=i32,stride_kh=i32,stride_vh=i32,stride_oh=i32",
      "stride_qm=64,stride_kn=64,stride_kk=1,stride_vn=64,stride_om=64,N_CTX=256,HEAD_DIM=64,BLOCK_M=2,"
      "BLOCK_N=16,CAUSAL=1,EVEN_N=1", {}),
+    ("aot_softmax_qpu", "softmax_kernel",
+     "output_ptr=*fp32,input_ptr=*fp32,input_row_stride=i32,output_row_stride=i32,n_cols=i32", "BLOCK_SIZE=1024",
+     {"qpu_rounding": True}),
+    ("aot_attn_qpu", "attn_fwd_kernel",
+     "Q=*fp32,K=*fp32,V=*fp32,Out=*fp32,sm_scale=fp32,stride_qh=i32,stride_kh=i32,stride_vh=i32,stride_oh=i32",
+     "stride_qm=64,stride_kn=64,stride_kk=1,stride_vn=64,stride_om=64,N_CTX=256,HEAD_DIM=64,BLOCK_M=2,"
+     "BLOCK_N=16,CAUSAL=1,EVEN_N=1", {"qpu_rounding": True}),
+    ("aot_sigmoid", "sigmoid_kernel", "x_ptr=*fp32,out_ptr=*fp32,n=i32", "BLOCK=256", {}),
     ("aot_layernorm", "layernorm_kernel", "x_ptr=*fp32,out_ptr=*fp32,n=i32,eps=fp32", "BLOCK=128", {}),
     ("aot_copy", "copy_kernel", "x_ptr=*fp32,out_ptr=*fp32,n=i32", "BLOCK=256", {}),
     ("aot_mul", "mul_kernel", "x_ptr=*fp32,y_ptr=*fp32,out_ptr=*fp32,n=i32", "BLOCK=256", {}),

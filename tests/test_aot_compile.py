@@ -85,8 +85,8 @@ def test_ctypes_mirror_matches_the_emitted_struct():
      "not parameters"),
     ("add_kernel", "x_ptr=*fp32,y_ptr=*fp32,n_elements=i32", "BLOCK_SIZE=256,output_ptr=0", {}, "pointer"),
     ("add_kernel", "x_ptr=*fp32,y_ptr=*fp32,output_ptr=*fp32,n_elements=f16", "BLOCK_SIZE=256", {}, "type"),
-    ("softmax_kernel", "output_ptr=*fp32,input_ptr=*fp32,input_row_stride=i32,output_row_stride=i32,n_cols=i32",
-     "BLOCK_SIZE=1024", {"qpu_rounding": True}, "qpu-rounding"),
+    ("layernorm_kernel", "x_ptr=*fp32,out_ptr=*fp32,n=i32,eps=fp32", "BLOCK=128", {"qpu_rounding": True},
+     "qpu-rounding"),
     ("add_kernel", "x_ptr=*fp32,y_ptr=*fp32,output_ptr=*fp32,n_elements=i32", "BLOCK_SIZE=256",
      {"force_simt": True}, "force-simt"),
     ("idiv_kernel", "x_ptr=*i32,y_ptr=*u32,q_ptr=*i32,r_ptr=*i32,n=i32", "BLOCK=256", {}, "must all be"),

@@ -145,6 +145,32 @@ def test_attention_same_bits_as_the_launch(cuda, launchers):
     np.testing.assert_array_equal(bits(to.cpu().numpy()), bits(want))
 
 
+def test_qpu_softmax_attention_and_sigmoid_launchers(cuda, launchers):
+    """The QPU-rounding softmax and attention launchers give the oracle's (the emulator's) bits;
+    the sigmoid launcher the kernel[grid] launch's."""
+    torch = cuda
+    x = W.softmax_input(64, 781, 1)
+    tx, to = dev(torch, x), torch.zeros(64, 781, device="cuda")
+    assert launchers("aot_softmax_qpu", (64,), output_ptr=to.data_ptr(), input_ptr=tx.data_ptr(),
+                     input_row_stride=781, output_row_stride=781, n_cols=781) < UINT32_MAX
+    np.testing.assert_array_equal(bits(to.cpu().numpy()), bits(O.qpu_softmax(x, 1024)))
+    heads, S, D = 2, 256, 64
+    q, k, v = W.attention_inputs(heads, S, D, 3)
+    tq, tk, tv, ta = dev(torch, q), dev(torch, k), dev(torch, v), torch.zeros(heads, S, D, device="cuda")
+    assert launchers("aot_attn_qpu", (triton.cdiv(S, 2), heads), Q=tq.data_ptr(), K=tk.data_ptr(),
+                     V=tv.data_ptr(), Out=ta.data_ptr(), sm_scale=0.125, stride_qh=S * D, stride_kh=S * D,
+                     stride_vh=S * D, stride_oh=S * D) < UINT32_MAX
+    np.testing.assert_array_equal(bits(ta.cpu().numpy()), bits(O.qpu_attention(q, k, v, True, sm_scale=0.125)))
+    n = 1000
+    xs = np.linspace(-12, 12, n, dtype=np.float32)
+    want = np.zeros(n, np.float32)
+    K.sigmoid_kernel[(triton.cdiv(n, 256),)](xs, want, n, BLOCK=256, device="b200")
+    ts, tso = dev(torch, xs), torch.zeros(n, device="cuda")
+    assert launchers("aot_sigmoid", (triton.cdiv(n, 256),), x_ptr=ts.data_ptr(), out_ptr=tso.data_ptr(),
+                     n=n) < UINT32_MAX
+    np.testing.assert_array_equal(bits(tso.cpu().numpy()), bits(want))
+
+
 def test_integer_and_life_launchers_are_exact(cuda, launchers):
     torch = cuda
     rng = np.random.default_rng(9)

@@ -9,7 +9,7 @@ launcher, transposed K, hard attention, causal rows independent of future keys.
 import numpy as np
 import pytest
 
-from conftest import golden_ids, goldens
+from conftest import golden_ids, goldens, sha256
 from oracle import oracle as O
 from piton_b200 import workloads as W
 from piton_b200.kernels import attn_fwd_kernel
@@ -26,7 +26,7 @@ def qkv(n, d, seed=0, gain=1.0, heads=None):
     return (q * np.float32(gain)).astype(np.float32), k, v
 
 
-def run(q, k, v, causal, block_m=2, block_n=16, k_layout="nd", out=None, even_n=None):
+def run(q, k, v, causal, block_m=2, block_n=16, k_layout="nd", out=None, even_n=None, qpu=False):
     squeeze = q.ndim == 2
     if squeeze:
         q, k, v = q[None], k[None], v[None]
@@ -38,7 +38,8 @@ def run(q, k, v, causal, block_m=2, block_n=16, k_layout="nd", out=None, even_n=
     grid = (-(-n // block_m), h)
     attn_fwd_kernel[grid](q, kk, v, o, float(1 / np.sqrt(d)), n * d, d, n * d, s_kn, s_kk, n * d, d,
                           o.shape[-2] * d if o.ndim == 3 else 0, d, n, HEAD_DIM=d, BLOCK_M=block_m,
-                          BLOCK_N=block_n, CAUSAL=bool(causal), EVEN_N=bool(even), device="b200")
+                          BLOCK_N=block_n, CAUSAL=bool(causal), EVEN_N=bool(even), device="b200",
+                          **({"qpu_rounding": True} if qpu else {}))
     return o[0] if squeeze else o
 
 
@@ -59,6 +60,30 @@ def test_matches_emulator_golden(cuda, g):
     out = run(q, k, v, m["causal"], m["block"][0], m["block"][1])
     ref = O.qpu_attention(q, k, v, m["causal"], m["block"][0], m["block"][1])
     np.testing.assert_allclose(out, ref, rtol=0, atol=ATOL)
+
+
+@pytest.mark.parametrize("g", ATTN, ids=golden_ids(ATTN))
+def test_qpu_rounding_bit_exact_with_emulator(cuda, g):
+    """qpu_rounding=True: the reference program on the QPU float model, every output word equal to
+    the emulator's (the fixture holds the SHA-256 of its whole output)."""
+    m = g.meta
+    q, k, v = W.attention_inputs(m["heads"], m["n"], m["d"], m["seed"])
+    out = run(q, k, v, m["causal"], m["block"][0], m["block"][1], qpu=True)
+    assert sha256(out) == m["sha_out"]
+
+
+@pytest.mark.parametrize("n,d,block_m,block_n,causal,even", [
+    (37, 16, 2, 16, True, False), (37, 16, 4, 16, False, False), (64, 32, 2, 32, False, True),
+    (100, 64, 8, 64, True, False), (130, 128, 2, 128, False, False), (48, 16, 3, 8, True, True)])
+def test_qpu_rounding_matches_oracle(cuda, n, d, block_m, block_n, causal, even):
+    """Ragged contexts, BLOCK_N from 8 to 128, BLOCK_M not a divisor, EVEN_N both ways: bit for bit
+    with the oracle's restatement (which matches the emulator goldens)."""
+    q, k, v = qkv(n, d, seed=n * d + block_n)
+    if even and n % block_n:
+        pytest.skip("EVEN_N promises N_CTX % BLOCK_N == 0")
+    out = run(q, k, v, causal, block_m, block_n, even_n=even, qpu=True)
+    ref = O.qpu_attention(q, k, v, causal, block_m, block_n, even_n=even)
+    np.testing.assert_array_equal(out.view(np.uint32), ref.view(np.uint32))
 
 
 def test_config_b4_h4_s256_d64(cuda):
