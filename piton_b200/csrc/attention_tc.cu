@@ -574,15 +574,25 @@ __global__ void __launch_bounds__(NTHREADS, 1)
                     break;
                 }
                 tc_fence_after();
+                // once the rows' maxima have settled (alpha exactly 1 in all 32 rows) the rescale
+                // drops out and the block's scale goes into one fused multiply-add
+                const bool settled = __all_sync(0xffffffffu, alpha == 1.0f);
 #pragma unroll
                 for (int c = 0; c < HD; c += 16) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x16(lane_base + COL_O + c, *reinterpret_cast<uint32_t(*)[16]>(r));
                     tmem_ld_32x32b_x16(lane_base + COL_O + HD + c, *reinterpret_cast<uint32_t(*)[16]>(r + 16));
                     tmem_ld_wait();
+                    if (settled) {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e)
-                        acc[c + e] = fmaf(acc[c + e], alpha, (__uint_as_float(r[e]) + __uint_as_float(r[16 + e])) * vs);
+                        for (int e = 0; e < 16; ++e)
+                            acc[c + e] = fmaf(__uint_as_float(r[e]) + __uint_as_float(r[16 + e]), vs, acc[c + e]);
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 16; ++e)
+                            acc[c + e] =
+                                fmaf(acc[c + e], alpha, (__uint_as_float(r[e]) + __uint_as_float(r[16 + e])) * vs);
+                    }
                 }
                 tc_fence_before();
                 __syncwarp();
