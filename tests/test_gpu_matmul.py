@@ -205,6 +205,25 @@ def test_tensor_core_k_edges(cuda, K):
     assert bool((C[M:] == 3.0).all())
 
 
+def test_tensor_core_b_padded_rows_ragged_columns(cuda):
+    """Row-major B viewed out of wider padded rows (row stride a multiple of 4 elements, 16-byte
+    aligned, N = 258 not a multiple of 4): the B split loads four columns per float4 and the
+    last, partial quad element by element."""
+    torch = cuda
+    M, N, K = 512, 258, 300
+    A = torch.rand(M, K, device="cuda") * 2 - 1
+    B = (torch.rand(K, 260, device="cuda") * 2 - 1)[:, :N]
+    C = torch.zeros(M, N, device="cuda")
+    st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+        A, B, C, M, N, K, A.stride(0), A.stride(1), B.stride(0), B.stride(1), C.stride(0), C.stride(1),
+        BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8, GROUP_SIZE_M=8, device="b200").last_stats
+    assert st["path"] == "tcgen05_f16x3"
+    assert device_status() == 0
+    ref = A.double() @ B.double()
+    err = float((C.double() - ref).abs().max() / ref.abs().max())
+    assert err <= fp32_bound(K), err
+
+
 @pytest.mark.parametrize("K", [257, 1004])
 def test_tensor_core_transposed_operands_odd_k(cuda, K):
     """A and B given as transposes (unit stride along M and along K): A goes through the
