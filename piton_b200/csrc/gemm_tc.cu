@@ -1133,7 +1133,9 @@ int tc_gemm(const TcGemmShape &s, void *workspace, cudaStream_t stream) {
     g.sam = s.sam; g.sak = s.sak; g.sbk = s.sbk; g.sbn = s.sbn;
     if (pairs) {
         g.tiles_m = (int)cdiv(s.M, (int64_t)(2 * BM));
-        g.group = GROUP_M / 2;   // 8 tile rows of 256 = 2048 rows of A per group
+        // 8 tile rows of 256 = 2048 rows of A per group: at 8192^3 the fewest DRAM bytes (2.33 GB
+        // read, against 3.11 / 2.58 / 2.50 GB for groups of 4 / 6 / 12) at the same speed
+        g.group = GROUP_M / 2;
         g.tiles_n = (int)cdiv(s.N, (int64_t)bn);
         g.num_tiles = g.tiles_m * g.tiles_n;
         const bool gather = g.world > 0 || g.mc_c != nullptr;
