@@ -205,6 +205,30 @@ def test_tensor_core_k_edges(cuda, K):
     assert bool((C[M:] == 3.0).all())
 
 
+@pytest.mark.parametrize("K", [16, 17, 255, 257, 1001, 4099])
+def test_tensor_core_pairs_streamed_split_k_edges(cuda, K):
+    """Row-major operands on the CTA-pair kernel: the split runs ahead of the GEMM chunk by chunk
+    and the GEMM's loads wait on each chunk's ready count.  K off the 256-wide chunk and the 8-wide
+    fp16 row (zero tails), A's rows read from a wider padded buffer, N = 520 (last 16-column item
+    partial), two calls in a row on the same buffers (the ready counts start from zero each call)."""
+    torch = cuda
+    M, N = 512, 520
+    g = torch.Generator(device="cuda").manual_seed(K)
+    lda = (K + 3) // 4 * 4 + 4                                # a multiple of 4: 16-byte rows
+    A = (torch.rand(M, lda, device="cuda", generator=g) * 2 - 1)[:, :K]
+    B = torch.rand(K, N, device="cuda", generator=g) * 2 - 1
+    ref = A.double() @ B.double()
+    for _ in range(2):
+        C = torch.full((M, N), 9.0, device="cuda")
+        st = Launcher(matmul_kernel, (triton.cdiv(M, 8) * triton.cdiv(N, 64),))(
+            A, B, C, M, N, K, A.stride(0), A.stride(1), N, 1, N, 1, BLOCK_SIZE_M=8, BLOCK_SIZE_N=64, BLOCK_SIZE_K=8,
+            GROUP_SIZE_M=8, device="b200").last_stats
+        assert st["path"] == "tcgen05_f16x3"
+        assert device_status() == 0
+        err = float((C.double() - ref).abs().max() / ref.abs().max())
+        assert err <= fp32_bound(K), (K, err)
+
+
 def test_tensor_core_b_padded_rows_ragged_columns(cuda):
     """Row-major B viewed out of wider padded rows (row stride a multiple of 4 elements, 16-byte
     aligned, N = 258 not a multiple of 4): the B split loads four columns per float4 and the
