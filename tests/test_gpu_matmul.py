@@ -206,11 +206,11 @@ def test_tensor_core_k_edges(cuda, K):
 
 
 @pytest.mark.parametrize("K", [16, 17, 255, 257, 1001, 4099])
-def test_tensor_core_pairs_streamed_split_k_edges(cuda, K):
-    """Row-major operands on the CTA-pair kernel: the split runs ahead of the GEMM chunk by chunk
-    and the GEMM's loads wait on each chunk's ready count.  K off the 256-wide chunk and the 8-wide
-    fp16 row (zero tails), A's rows read from a wider padded buffer, N = 520 (last 16-column item
-    partial), two calls in a row on the same buffers (the ready counts start from zero each call)."""
+def test_tensor_core_pairs_k_edges_padded_rows(cuda, K):
+    """Row-major operands on the CTA-pair kernel (M >= 512) with K off the 256-wide chunk and the
+    8-wide fp16 row (the split's zero tails), A's rows read from a wider padded buffer, N = 520 (a
+    partial last tile), and two calls in a row on the same buffers (the workspace's earlier
+    contents never reach C)."""
     torch = cuda
     M, N = 512, 520
     g = torch.Generator(device="cuda").manual_seed(K)
