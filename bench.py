@@ -1040,7 +1040,8 @@ def main():
                    "workload": "greedy decode of 64 tokens after 16-token prompts; batches up to the "
                                "number of 16-CTA clusters that fit (9 on 148 SMs) run as one cluster launch "
                                "per decode with the weights in shared memory, batches that fill the SMs with "
-                               "2 sequences per CTA as 79 launches of one position each, the ones between as "
+                               "2 sequences per CTA as one launch per decode (each CTA feeds its sequences' "
+                               "positions in turn), the ones between as "
                                "one launch of 4-CTA clusters (a CTA per head); value: replayed from a CUDA "
                                "graph, eager_value: launched directly"}
             if r["weak"]:

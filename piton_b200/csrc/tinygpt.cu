@@ -3,14 +3,14 @@
 // pre-LayerNorm blocks of 4-head causal attention (head dim 32) and a 4x GELU
 // MLP, learned positions, tied input/output embeddings, context 128.
 //
-// One launch per token position.  A CTA owns SEQ sequences; for its new token
-// it runs every layer with the activations in shared memory, appends the
-// token's keys and values to the caller's KV cache, attends over the cached
-// positions (one warp per sequence x head), and at the end writes the greedy
-// next token (argmax of the 65 tied-embedding logits, first maximum) into
-// the token buffer, which the next launch reads: the whole generation runs
-// on the stream without host round trips.  Weights (3.2 MB) stay L2-resident
-// and are read through L1.
+// Step kernel (batches that fill the SMs): one launch per decode.  A CTA owns SEQ
+// sequences and feeds their positions one after another; for each it runs every
+// layer with the activations in shared memory, appends the token's keys and
+// values to the caller's KV cache, attends over the cached positions (one warp
+// per sequence x head), and writes the greedy next token (argmax of the 65
+// tied-embedding logits, first maximum) into the token buffer, which its next
+// position reads: no CTA waits on another and the generation needs no host
+// round trips.  Weights (3.2 MB) stay L2-resident and are read through L1.
 //
 // Packed weight layout (fp32, row-major, input-by-output matrices):
 //   wte[V,D] wpe[CTX,D]
@@ -29,6 +29,7 @@ namespace tg {
 
 constexpr int V = 65, D = 128, L = 4, H = 4, HD = 32, F = 4 * D, CTX = 128;
 constexpr int SEQ = 2, THREADS = 256;
+constexpr int PRE_W = 2;   // weight quads per thread requested ahead of a linear layer (step kernel; 2 measured best of 1-16)
 constexpr int LAYER_FLOATS = 2 * D + D * 3 * D + 3 * D + D * D + D + 2 * D + D * F + F + F * D + D;
 // offsets of a layer's tensors in its packed block
 constexpr int O_LN1 = 0, O_WQKV = 2 * D, O_BQKV = O_WQKV + D * 3 * D, O_WO = O_BQKV + 3 * D, O_BO = O_WO + D * D,
@@ -46,7 +47,7 @@ struct StepArgs {
     int32_t *tokens;
     float *logits;
     int64_t batch;
-    int pos;          // position of the token fed at this step
+    int steps;        // positions fed, 0 .. steps - 1, all in one launch
     int prompt_len;   // the next token is written when prompt_len - 1 <= pos and pos + 1 < end
     int end;          // prompt_len + new_tokens
 };
@@ -58,13 +59,35 @@ struct StepArgs {
 // unrolled so that many 16-byte weight loads are in flight per thread: the
 // weights come from L2 and this loop is latency-bound otherwise.  b is in
 // shared memory.
-template <int K, int N, bool GELU>
-__device__ __forceinline__ void linear(const float *in, float *out, const float *__restrict__ W, const float *b,
-                                       float *scratch, bool residual) {
-    constexpr int NQ = N / 4;                             // column quads
-    constexpr int G = THREADS / NQ > 0 ? THREADS / NQ : 1;  // k-groups
-    constexpr int KG = K / G;
+//
+// PRE > 0: the first PRE weight quads of the thread's k-range were requested earlier by
+// linear_prefetch (before the phase that precedes this layer) and arrive in `pre`.
+template <int K, int N> struct LinearTiling {
+    static constexpr int NQ = N / 4;                              // column quads
+    static constexpr int G = THREADS / NQ > 0 ? THREADS / NQ : 1;  // k-groups
+    static constexpr int KG = K / G;
     static_assert(N % 4 == 0 && K % G == 0 && NQ * G <= THREADS && G >= 2, "linear tiling");
+};
+
+// The first PRE weight quads of this thread's k-range of linear<K, N>: the weights do not depend
+// on the activations, so they are requested before the phase that precedes the layer (a
+// LayerNorm, the attention) and their L2 latency runs under it instead of opening the layer.
+template <int K, int N, int PRE>
+__device__ __forceinline__ void linear_prefetch(const float *__restrict__ W, float4 (&pre)[PRE]) {
+    using T = LinearTiling<K, N>;
+    static_assert(PRE <= T::KG, "prefetch within the k-range");
+    const int q = threadIdx.x % T::NQ, g = threadIdx.x / T::NQ;
+    if (g < T::G) {
+        const float4 *w4 = reinterpret_cast<const float4 *>(W) + q;
+#pragma unroll
+        for (int i = 0; i < PRE; ++i) pre[i] = __ldg(w4 + (int64_t)(g * T::KG + i) * T::NQ);
+    }
+}
+
+template <int K, int N, bool GELU, int PRE = 0>
+__device__ __forceinline__ void linear(const float *in, float *out, const float *__restrict__ W, const float *b,
+                                       float *scratch, bool residual, const float4 (&pre)[PRE > 0 ? PRE : 1]) {
+    constexpr int NQ = LinearTiling<K, N>::NQ, G = LinearTiling<K, N>::G, KG = LinearTiling<K, N>::KG;
     const int tid = threadIdx.x;
     const int q = tid % NQ, g = tid / NQ;
     float4 acc[SEQ];
@@ -72,8 +95,21 @@ __device__ __forceinline__ void linear(const float *in, float *out, const float 
     for (int s = 0; s < SEQ; ++s) acc[s] = make_float4(0.f, 0.f, 0.f, 0.f);
     if (g < G) {
         const float4 *w4 = reinterpret_cast<const float4 *>(W) + q;
+#pragma unroll
+        for (int i = 0; i < PRE; ++i) {
+            const float4 w = pre[i];
+            const int k = g * KG + i;
+#pragma unroll
+            for (int s = 0; s < SEQ; ++s) {
+                float xv = in[s * K + k];
+                acc[s].x = fmaf(xv, w.x, acc[s].x);
+                acc[s].y = fmaf(xv, w.y, acc[s].y);
+                acc[s].z = fmaf(xv, w.z, acc[s].z);
+                acc[s].w = fmaf(xv, w.w, acc[s].w);
+            }
+        }
 #pragma unroll 32
-        for (int k = g * KG; k < (g + 1) * KG; ++k) {
+        for (int k = g * KG + PRE; k < (g + 1) * KG; ++k) {
             float4 w = __ldg(w4 + (int64_t)k * NQ);
 #pragma unroll
             for (int s = 0; s < SEQ; ++s) {
@@ -156,7 +192,6 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
     __shared__ __align__(16) float prm[L * P_LAYER + 2 * D];   // every layer's gains and biases, lnf
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int64_t b0 = (int64_t)blockIdx.x * SEQ;
-    const int pos = a.pos;
     const float *wte = a.w, *wpe = a.w + V * D;
 
     // the gains and biases of all layers into shared memory, requested together with the
@@ -176,155 +211,164 @@ __global__ void __launch_bounds__(THREADS, 1) tinygpt_step_kernel(StepArgs a) {
         }
     }
 
-    // token + position embedding
-    for (int i = tid; i < SEQ * D; i += THREADS) {
-        int s = i / D, c = i % D;
-        int64_t b = b0 + s;
-        float v = 0.0f;
-        if (b < a.batch) {
-            int tok = a.tokens[b * CTX + pos];
-            tok = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
-            v = __ldg(wte + tok * D + c) + __ldg(wpe + pos * D + c);
-        }
-        x[i] = v;
-    }
-    __syncthreads();
-
-    const float *lw = a.w + V * D + CTX * D;
-    for (int l = 0; l < L; ++l, lw += LAYER_FLOATS) {
-        const float *pl = prm + l * P_LAYER;
-        const float *ln1_g = pl + P_LN1, *ln1_b = ln1_g + D, *b_qkv = pl + P_BQKV, *b_o = pl + P_BO;
-        const float *ln2_g = pl + P_LN2, *ln2_b = ln2_g + D, *b_fc = pl + P_BFC, *b_pr = pl + P_BPR;
-        const float *w_qkv = lw + O_WQKV, *w_o = lw + O_WO, *w_fc = lw + O_WFC, *w_pr = lw + O_WPR;
-        float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
-        float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
-
-        layernorm(x, h, ln1_g, ln1_b);
-        linear<D, 3 * D, false>(h, qkv, w_qkv, b_qkv, scratch, false);
-        // append this position's keys and values
+    // one position after another; the CTA's sequences depend on no other CTA, so the whole
+    // decode is one launch (the gains and biases above are loaded once)
+    for (int pos = 0; pos < a.steps; ++pos) {
+        // token + position embedding
         for (int i = tid; i < SEQ * D; i += THREADS) {
             int s = i / D, c = i % D;
             int64_t b = b0 + s;
+            float v = 0.0f;
             if (b < a.batch) {
-                kc[(b * CTX + pos) * D + c] = qkv[s * 3 * D + D + c];
-                vc[(b * CTX + pos) * D + c] = qkv[s * 3 * D + 2 * D + c];
+                int tok = a.tokens[b * CTX + pos];
+                tok = tok < 0 ? 0 : (tok >= V ? V - 1 : tok);
+                v = __ldg(wte + tok * D + c) + __ldg(wpe + pos * D + c);
             }
+            x[i] = v;
         }
         __syncthreads();
-        // causal attention over positions 0..pos: warp = (sequence, head)
-        {
-            const int s = warp / H, hh = warp % H;
-            const int64_t b = b0 + s;
-            if (b < a.batch) {
-                const float *q = qkv + s * 3 * D + hh * HD;
-                const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
-                float sc[CTX / 32];
-                float mx = -INFINITY;
-#pragma unroll
-                for (int j = 0; j < CTX / 32; ++j) {
-                    int t = lane + 32 * j;
-                    float dot = -INFINITY;
-                    if (t <= pos) {
-                        const float *kr = kc + (b * CTX + t) * D + hh * HD;
-                        float acc = 0.0f;
-#pragma unroll
-                        for (int d = 0; d < HD; d += 4) {
-                            float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
-                            acc = fmaf(q[d], k4.x, acc);
-                            acc = fmaf(q[d + 1], k4.y, acc);
-                            acc = fmaf(q[d + 2], k4.z, acc);
-                            acc = fmaf(q[d + 3], k4.w, acc);
+
+        const float *lw = a.w + V * D + CTX * D;
+        for (int l = 0; l < L; ++l, lw += LAYER_FLOATS) {
+            const float *pl = prm + l * P_LAYER;
+            const float *ln1_g = pl + P_LN1, *ln1_b = ln1_g + D, *b_qkv = pl + P_BQKV, *b_o = pl + P_BO;
+            const float *ln2_g = pl + P_LN2, *ln2_b = ln2_g + D, *b_fc = pl + P_BFC, *b_pr = pl + P_BPR;
+            const float *w_qkv = lw + O_WQKV, *w_o = lw + O_WO, *w_fc = lw + O_WFC, *w_pr = lw + O_WPR;
+            float *kc = a.kv + ((int64_t)l * 2 + 0) * a.batch * CTX * D;
+            float *vc = a.kv + ((int64_t)l * 2 + 1) * a.batch * CTX * D;
+
+            float4 pre_qkv[PRE_W], pre_o[PRE_W], pre_fc[PRE_W], no_pre[1];
+            linear_prefetch<D, 3 * D>(w_qkv, pre_qkv);
+            layernorm(x, h, ln1_g, ln1_b);
+            linear<D, 3 * D, false, PRE_W>(h, qkv, w_qkv, b_qkv, scratch, false, pre_qkv);
+            linear_prefetch<D, D>(w_o, pre_o);   // under the key / value append and the attention
+            // append this position's keys and values
+            for (int i = tid; i < SEQ * D; i += THREADS) {
+                int s = i / D, c = i % D;
+                int64_t b = b0 + s;
+                if (b < a.batch) {
+                    kc[(b * CTX + pos) * D + c] = qkv[s * 3 * D + D + c];
+                    vc[(b * CTX + pos) * D + c] = qkv[s * 3 * D + 2 * D + c];
+                }
+            }
+            __syncthreads();
+            // causal attention over positions 0..pos: warp = (sequence, head)
+            {
+                const int s = warp / H, hh = warp % H;
+                const int64_t b = b0 + s;
+                if (b < a.batch) {
+                    const float *q = qkv + s * 3 * D + hh * HD;
+                    const float scale = 0.17677669529663688f;   // 1 / sqrt(32)
+                    float sc[CTX / 32];
+                    float mx = -INFINITY;
+    #pragma unroll
+                    for (int j = 0; j < CTX / 32; ++j) {
+                        int t = lane + 32 * j;
+                        float dot = -INFINITY;
+                        if (t <= pos) {
+                            const float *kr = kc + (b * CTX + t) * D + hh * HD;
+                            float acc = 0.0f;
+    #pragma unroll
+                            for (int d = 0; d < HD; d += 4) {
+                                float4 k4 = *reinterpret_cast<const float4 *>(kr + d);
+                                acc = fmaf(q[d], k4.x, acc);
+                                acc = fmaf(q[d + 1], k4.y, acc);
+                                acc = fmaf(q[d + 2], k4.z, acc);
+                                acc = fmaf(q[d + 3], k4.w, acc);
+                            }
+                            dot = acc * scale;
                         }
-                        dot = acc * scale;
+                        sc[j] = dot;
+                        mx = fmaxf(mx, dot);
                     }
-                    sc[j] = dot;
-                    mx = fmaxf(mx, dot);
+    #pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+                    float sum = 0.0f;
+    #pragma unroll
+                    for (int j = 0; j < CTX / 32; ++j) {
+                        int t = lane + 32 * j;
+                        float p = t <= pos ? expf(sc[j] - mx) : 0.0f;
+                        probs[warp][t] = p;
+                        sum += p;
+                    }
+    #pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+                    __syncwarp();
+                    float o_acc = 0.0f;
+                    for (int t = 0; t <= pos; ++t) o_acc = fmaf(probs[warp][t], vc[(b * CTX + t) * D + hh * HD + lane], o_acc);
+                    att[s * D + hh * HD + lane] = o_acc / sum;
+                } else {
+                    att[s * D + hh * HD + lane] = 0.0f;
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-                float sum = 0.0f;
-#pragma unroll
-                for (int j = 0; j < CTX / 32; ++j) {
-                    int t = lane + 32 * j;
-                    float p = t <= pos ? expf(sc[j] - mx) : 0.0f;
-                    probs[warp][t] = p;
-                    sum += p;
+            }
+            __syncthreads();
+            linear<D, D, false, PRE_W>(att, x, w_o, b_o, scratch, true, pre_o);          // x += attn @ Wo + bo
+            linear_prefetch<D, F>(w_fc, pre_fc);
+            layernorm(x, h, ln2_g, ln2_b);
+            linear<D, F, true, PRE_W>(h, f, w_fc, b_fc, scratch, false, pre_fc);         // f = gelu(h @ Wfc + bfc)
+            linear<F, D, false>(f, x, w_pr, b_pr, scratch, true, no_pre);   // x += f @ Wpr + bpr
+        }
+        const float *lnf_g = prm + L * P_LAYER, *lnf_b = lnf_g + D;
+        layernorm(x, h, lnf_g, lnf_b);
+        // tied head: logits[s][v] = h[s] . wte[v]; a warp per (s, v) pair, lanes over D, the
+        // pairs' embedding rows requested together (one L2 round trip for all of a warp's pairs)
+        {
+            constexpr int PV = (SEQ * V + THREADS / 32 - 1) / (THREADS / 32);   // pairs per warp
+            float ew[PV][D / 32];
+    #pragma unroll
+            for (int i = 0; i < PV; ++i) {
+                const int pv = warp + i * (THREADS / 32);
+                const int vv = pv < SEQ * V ? pv % V : 0;
+    #pragma unroll
+                for (int c = 0; c < D / 32; ++c) ew[i][c] = __ldg(wte + vv * D + lane + 32 * c);
+            }
+    #pragma unroll
+            for (int i = 0; i < PV; ++i) {
+                const int pv = warp + i * (THREADS / 32);
+                if (pv < SEQ * V) {
+                    const int s = pv / V, vv = pv % V;
+                    float acc = 0.0f;
+    #pragma unroll
+                    for (int c = 0; c < D / 32; ++c) acc = fmaf(h[s * D + lane + 32 * c], ew[i][c], acc);
+    #pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+                    if (lane == 0) lg[s][vv] = acc;
                 }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
-                __syncwarp();
-                float o_acc = 0.0f;
-                for (int t = 0; t <= pos; ++t) o_acc = fmaf(probs[warp][t], vc[(b * CTX + t) * D + hh * HD + lane], o_acc);
-                att[s * D + hh * HD + lane] = o_acc / sum;
-            } else {
-                att[s * D + hh * HD + lane] = 0.0f;
             }
         }
         __syncthreads();
-        linear<D, D, false>(att, x, w_o, b_o, scratch, true);          // x += attn @ Wo + bo
-        layernorm(x, h, ln2_g, ln2_b);
-        linear<D, F, true>(h, f, w_fc, b_fc, scratch, false);         // f = gelu(h @ Wfc + bfc)
-        linear<F, D, false>(f, x, w_pr, b_pr, scratch, true);          // x += f @ Wpr + bpr
-    }
-    const float *lnf_g = prm + L * P_LAYER, *lnf_b = lnf_g + D;
-    layernorm(x, h, lnf_g, lnf_b);
-    // tied head: logits[s][v] = h[s] . wte[v]; a warp per (s, v) pair, lanes over D, the
-    // pairs' embedding rows requested together (one L2 round trip for all of a warp's pairs)
-    {
-        constexpr int PV = (SEQ * V + THREADS / 32 - 1) / (THREADS / 32);   // pairs per warp
-        float ew[PV][D / 32];
-#pragma unroll
-        for (int i = 0; i < PV; ++i) {
-            const int pv = warp + i * (THREADS / 32);
-            const int vv = pv < SEQ * V ? pv % V : 0;
-#pragma unroll
-            for (int c = 0; c < D / 32; ++c) ew[i][c] = __ldg(wte + vv * D + lane + 32 * c);
-        }
-#pragma unroll
-        for (int i = 0; i < PV; ++i) {
-            const int pv = warp + i * (THREADS / 32);
-            if (pv < SEQ * V) {
-                const int s = pv / V, vv = pv % V;
-                float acc = 0.0f;
-#pragma unroll
-                for (int c = 0; c < D / 32; ++c) acc = fmaf(h[s * D + lane + 32 * c], ew[i][c], acc);
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-                if (lane == 0) lg[s][vv] = acc;
+        // greedy token: warp s takes sequence s's argmax, lanes over the vocabulary, first maximum
+        // on ties (as numpy.argmax)
+        if (warp < SEQ && pos + 1 >= a.prompt_len && pos + 1 < a.end) {
+            const int64_t b = b0 + warp;
+            if (b < a.batch) {
+                float bv = -INFINITY;
+                int bi = V;
+                for (int vv = lane; vv < V; vv += 32)   // each lane's entries in increasing order
+                    if (bi == V || lg[warp][vv] > bv) {
+                        bv = lg[warp][vv];
+                        bi = vv;
+                    }
+    #pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > bv || (ov == bv && oi < bi)) {
+                        bv = ov;
+                        bi = oi;
+                    }
+                }
+                if (lane == 0) a.tokens[b * CTX + pos + 1] = bi;
             }
         }
-    }
-    __syncthreads();
-    // greedy token: warp s takes sequence s's argmax, lanes over the vocabulary, first maximum
-    // on ties (as numpy.argmax)
-    if (warp < SEQ && pos + 1 >= a.prompt_len && pos + 1 < a.end) {
-        const int64_t b = b0 + warp;
-        if (b < a.batch) {
-            float bv = -INFINITY;
-            int bi = V;
-            for (int vv = lane; vv < V; vv += 32)   // each lane's entries in increasing order
-                if (bi == V || lg[warp][vv] > bv) {
-                    bv = lg[warp][vv];
-                    bi = vv;
-                }
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) {
-                const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-                if (ov > bv || (ov == bv && oi < bi)) {
-                    bv = ov;
-                    bi = oi;
-                }
+        if (a.logits && pos == a.steps - 1) {
+            for (int i = tid; i < SEQ * V; i += THREADS) {
+                int s = i / V, vv = i % V;
+                int64_t b = b0 + s;
+                if (b < a.batch) a.logits[b * V + vv] = lg[s][vv];
             }
-            if (lane == 0) a.tokens[b * CTX + pos + 1] = bi;
         }
-    }
-    if (a.logits) {
-        for (int i = tid; i < SEQ * V; i += THREADS) {
-            int s = i / V, vv = i % V;
-            int64_t b = b0 + s;
-            if (b < a.batch) a.logits[b * V + vv] = lg[s][vv];
-        }
+        __syncthreads();   // the next token and the KV-cache rows written, shared buffers free
     }
 }
 
@@ -1195,11 +1239,10 @@ int forced_kernel() {
 }  // namespace
 
 // ---------------------------------------------------------------------------
-// CUDA-graph cache: a decode is ~80 launches of one small kernel, so the host
-// launch path costs a few microseconds a token.  With PITON_B200_CUDA_GRAPH the
-// sequence is captured once per argument set (stream capture on an internal
-// stream, thread-local mode), instantiated, and replayed with one
-// cudaGraphLaunch on the caller's stream.
+// CUDA-graph cache: with PITON_B200_CUDA_GRAPH a decode's launch is captured
+// once per argument set (stream capture on an internal stream, thread-local
+// mode), instantiated, and replayed with one cudaGraphLaunch on the caller's
+// stream, so a repeated decode skips the host launch path and its argument set-up.
 // ---------------------------------------------------------------------------
 #include <mutex>
 
@@ -1305,7 +1348,7 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
         group = (int)std::min<int64_t>(GS, std::max<int64_t>(1, cdiv(a->batch, hcap)));
         hclusters = (int)std::min<int64_t>(hcap, cdiv(a->batch, group));
     }
-    const int launches = (use_cluster || use_heads) ? 1 : steps;
+    const int launches = 1;
     auto enqueue = [&](cudaStream_t q) {
         if (use_heads) {
             HeadsArgs h;
@@ -1334,11 +1377,9 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
             launch_cluster(c, (int)a->batch, q);
             return;
         }
-        for (int p = 0; p < steps; ++p) {
-            s.pos = p;
-            s.logits = p == steps - 1 ? reinterpret_cast<float *>(a->logits) : nullptr;
-            tinygpt_step_kernel<<<grid, THREADS, 0, q>>>(s);
-        }
+        s.steps = steps;
+        s.logits = reinterpret_cast<float *>(a->logits);
+        tinygpt_step_kernel<<<grid, THREADS, 0, q>>>(s);
     };
     if (!(a->flags & PITON_B200_CUDA_GRAPH)) {
         enqueue(st);
