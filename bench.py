@@ -1039,11 +1039,9 @@ def main():
                    "eager_value": r["tokens"] / r["t_eager"], "batch": r["batch"],
                    "workload": "greedy decode of 64 tokens after 16-token prompts; batches up to the "
                                "number of 16-CTA clusters that fit (9 on 148 SMs) run as one cluster launch "
-                               "per decode with the weights in shared memory, batches that fill the SMs with "
-                               "2 sequences per CTA as one launch per decode (each CTA feeds its sequences' "
-                               "positions in turn), the ones between as "
-                               "one launch of 4-CTA clusters (a CTA per head); value: replayed from a CUDA "
-                               "graph, eager_value: launched directly"}
+                               "per decode with the weights in shared memory, larger batches with 2 sequences "
+                               "per CTA as one launch per decode (each CTA feeds its sequences' positions in "
+                               "turn); value: replayed from a CUDA graph, eager_value: launched directly"}
             if r["weak"]:
                 ent["scaling"] = "weak"
                 ent["workload"] += f"; at N = {D.world} every GPU decodes its own single sequence (batch 1 " \
@@ -1056,8 +1054,7 @@ def main():
                 per_seq = sum(kv * (p + 1) + kv for p in range(pos))
                 byts = pos * wbytes + r["per_rank"] * per_seq
                 ent["roofline"] = roofline("hbm", byts / r["t_step"] / 1e9, hbm, "GB/s",
-                                           kernel="tinygpt_step_kernel" if r["per_rank"] >= 222 else
-                                           "tinygpt_heads_kernel",
+                                           kernel="tinygpt_step_kernel",
                                            algorithmic_bytes_per_decode=byts,
                                            note="KV cache (134 MB at batch 256) and weights mostly L2-resident")
             else:

@@ -1224,9 +1224,8 @@ void launch_heads(const tg::HeadsArgs &h, int clusters, cudaStream_t q) {
 }
 
 // PITON_B200_TINYGPT_KERNEL=cluster|heads|step picks a decode kernel for comparisons; by default
-// batches up to the number of 16-CTA clusters that fit use the cluster kernel, batches whose
-// 2-sequence CTAs fill three quarters of the SMs the per-position step kernel, the ones between
-// the heads kernel (and the step kernel when neither cluster launch is possible).
+// batches up to the number of 16-CTA clusters that fit use the cluster kernel and larger ones (or
+// every batch when no cluster launch is possible) the step kernel.
 int forced_kernel() {
     const char *e = getenv("PITON_B200_TINYGPT_KERNEL");
     if (!e || !*e) return 0;
@@ -1322,18 +1321,17 @@ extern "C" int piton_b200_tinygpt_generate(const piton_tinygpt_args *a, void *st
     if (a->new_tokens == 0 && a->logits) steps = (int)a->prompt_len;
     const unsigned grid = (unsigned)cdiv(a->batch, SEQ);
     cudaStream_t st = as_stream(stream);
-    // small batches: one 16-CTA cluster per sequence, weights resident in shared memory, one launch;
-    // larger ones: one 4-CTA cluster (a CTA per head) per group of up to 8 sequences, one launch
+    // small batches: one 16-CTA cluster per sequence, weights resident in shared memory; larger
+    // ones: the step kernel (2 sequences per CTA); each is one launch per decode.  The 4-CTA-cluster
+    // heads kernel runs only when asked for (PITON_B200_TINYGPT_KERNEL=heads): measured against the
+    // step kernel at batches 16-256 it is as fast at 16 and slower above (2.22 against 2.45 M
+    // tokens/s at 128, 3.01 against 3.67 M at 192), with the same tokens
     const int forced = forced_kernel();
     PITON_REQUIRE(forced >= 0, "PITON_B200_TINYGPT_KERNEL must be cluster, heads or step");
     const int clusters = cluster_capacity();
     const int hcap = heads_capacity();
     bool use_cluster = clusters > 0 && a->batch <= clusters;
-    // the per-position step kernel (2 sequences per CTA, every CTA reading all the weights) wins
-    // once its CTAs fill three quarters of the SMs (measured: 3.79 M against 3.63 M tokens/s at
-    // batch 256); below that the heads kernel spreads even a few sequences over 4 SMs each
-    const bool step_fills = cdiv(a->batch, SEQ) * 4 >= (int64_t)num_sms() * 3;
-    bool use_heads = !use_cluster && hcap > 0 && !step_fills;
+    bool use_heads = false;
     if (forced == 1) {
         PITON_REQUIRE(clusters > 0 && a->batch <= clusters, "the cluster kernel takes at most %d sequences", clusters);
         use_cluster = true, use_heads = false;
