@@ -369,8 +369,8 @@ def bench_softmax(torch, D, args, lib_calls):
         launch = softmax_kernel[(mloc,)]
         sec, st = timed_e2e(torch, D, lambda: launch(yh, xh, SM_N, SM_N, SM_N, BLOCK_SIZE=SM_N,
                                                      device="b200").last_stats, max(2, args.steps // 10))
-        lib_calls["launches"] += max(2, args.steps // 10) + 1
-        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        lib_calls["launches"] += (max(2, args.steps // 10) + 1) * st.get("launches", 1)
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"], "op_path": st.get("path")}
         del xh, yh
     return {"bytes": 8.0 * SM_M * SM_N, "t_step": t_step, "t_kernel": t_kernel, "err": err,
             "local_bytes": 8.0 * mloc * SM_N, "e2e": e2e}
@@ -472,8 +472,8 @@ def bench_attention(torch, D, args, lib_calls):
         sec, st = timed_e2e(torch, D, lambda: launch(hq, hk, hv, ho, sm, sd, AT_D, sd, AT_D, 1, sd, AT_D, sd, AT_D, AT_S,
                                                      HEAD_DIM=AT_D, BLOCK_M=2, BLOCK_N=16, CAUSAL=True, EVEN_N=True,
                                                      device="b200").last_stats, 2)
-        lib_calls["launches"] += 3 * per_call
-        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        lib_calls["launches"] += 3 * st.get("launches", 1) * per_call
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"], "op_path": st.get("path")}
         del hq, hk, hv, ho
     return {"flops": flops, "bytes": 16.0 * BH * AT_S * AT_D, "t_step": t_step, "t_kernel": t_kernel, "err": err,
             "local_flops": flops * hloc / BH, "tc": ws > 0, "fused": fused, "e2e": e2e, "heads_local": hloc}
@@ -548,8 +548,8 @@ def bench_add(torch, D, args, lib_calls):
         launch = add_kernel[((nloc + 1023) // 1024,)]
         k = max(2, args.steps // 10)
         sec, st = timed_e2e(torch, D, lambda: launch(xh, yh, oh, nloc, BLOCK_SIZE=1024, device="b200").last_stats, k)
-        lib_calls["launches"] += k + 1
-        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"]}
+        lib_calls["launches"] += (k + 1) * st.get("launches", 1)
+        e2e = {"sec": sec, "h2d": st["h2d_bytes"], "d2h": st["d2h_bytes"], "op_path": st.get("path")}
         del xh, yh, oh
     return {"bytes": 12.0 * ADD_N, "t_step": t_step, "t_kernel": t_kernel, "err": err, "local_bytes": 12.0 * nloc,
             "e2e": e2e}
@@ -958,7 +958,9 @@ def main():
             return None
         return {"value": units / e["sec"] / scale, "unit": unit, "h2d_bytes_per_step": e["h2d"],
                 "d2h_bytes_per_step": e["d2h"], "ms_per_step": 1e3 * e["sec"],
-                "path": "the public call with pinned host buffers (copy in, launch, copy back every step)"
+                "path": "the public call with pinned host buffers (copy in, launch, copy back every step"
+                        + ("; the copies overlapped with the launches chunk by chunk)"
+                           if "host_pipelined" in (e.get("op_path") or "") else ")")
                         + ("; per rank: its own shard in and out, max over ranks" if D.world > 1 else "")}
 
     sec = {}

@@ -21,6 +21,7 @@ A kernel (or constexpr combination) without a B200 implementation raises
 from __future__ import annotations
 
 import ctypes as C
+import math
 import os
 
 import numpy as np
@@ -142,6 +143,7 @@ class Launch:
         self.ev0 = None if self.capturing else torch.cuda.Event(enable_timing=True)
         self.ev1 = None if self.capturing else torch.cuda.Event(enable_timing=True)
         self.called = False
+        self.launches = 0                    # entry-point calls (several on the pipelined host-buffer paths)
         self.host_h2d = self.host_d2h = 0   # bytes an entry point copied itself (host-buffer paths)
 
     def call(self, fname: str, args, what: str):
@@ -153,6 +155,14 @@ class Launch:
         if self.ev1 is not None:
             self.ev1.record(self.stream)
         self.called = True
+        self.launches += 1
+        check(rc, what)
+
+    def call_untimed(self, fname: str, args, what: str):
+        """One C-ABI entry point on the launch's stream, inside a region the caller times."""
+        rc = getattr(lib(), fname)(C.byref(args), self.stream_ptr)
+        self.called = True
+        self.launches += 1
         check(rc, what)
 
     def ptr(self, name, written: bool = False, covers: int = -1) -> Buffer:
@@ -231,6 +241,7 @@ def run_on_b200(jitfn, grid, constants, values, device=None, qpu=False):
         if launch.called and launch.ev0 is not None:
             stats["time_us"] = launch.ev0.elapsed_time(launch.ev1) * 1e3
         stats["h2d_bytes"], stats["d2h_bytes"] = h2d, d2h
+        stats["launches"] = launch.launches
     return stats
 
 
@@ -246,6 +257,98 @@ def _flags(launch, allowed_qpu=True, simt_ok=False):
 
 
 # ---------------------------------------------------------------------------------------
+# host buffers: copies in, launches and copies back overlapped chunk by chunk
+# ---------------------------------------------------------------------------------------
+
+PIPE_MIN_BYTES = 64 << 20   # below this a transfer is short next to the per-chunk launch costs
+PIPE_CHUNKS = 8
+_COPY_STREAMS = {}
+
+
+def _copy_streams(device):
+    torch = _torch()
+    key = device.index if device.index is not None else torch.cuda.current_device()
+    st = _COPY_STREAMS.get(key)
+    if st is None:
+        st = (torch.cuda.Stream(device), torch.cuda.Stream(device))
+        _COPY_STREAMS[key] = st
+    return st
+
+
+def _pipelined_on_host(L: Launch, ins, outs, units: int, align: int, launch_chunk) -> bool:
+    """An operator whose inputs and outputs split along one leading dimension (rows of a
+    softmax, elements of an add, heads of an attention), given as page-locked numpy arrays:
+    chunk i's launch runs on the launch's stream while chunk i + 1 is copied in on one copy
+    stream and chunk i - 1 is copied back on another, instead of all copies in, the launch,
+    all copies back one after the other (the generic path, ``Buffer``).  ``ins`` / ``outs``
+    are (argument name, array, elements per unit); ``launch_chunk(u0, u1, in_addrs,
+    out_addrs)`` enqueues the operator for units [u0, u1) on the device copies (chunk
+    boundaries are multiples of ``align`` units).  Elements of an output past ``units`` are
+    neither copied in nor back, so they keep their host values, as the generic path leaves
+    them.  Returns False, having done nothing, when the arguments do not qualify: under
+    graph capture, fewer than PIPE_MIN_BYTES, arrays that are not C-contiguous page-locked
+    float32 numpy arrays holding the units, or an output sharing memory with an input."""
+    torch = _torch()
+    if L.capturing or units <= 0:
+        return False
+    every = ins + outs
+    arrs = [a for _, a, _ in every]
+    if not all(type(a) is np.ndarray and a.dtype == np.float32 and a.flags.c_contiguous and a.size > 0
+               for a in arrs):
+        return False
+    if any(a.size < units * e for _, a, e in every) or sum(4 * units * e for _, _, e in every) < PIPE_MIN_BYTES:
+        return False
+    if not all(a.flags.writeable for _, a, _ in outs):
+        return False
+    if any(np.may_share_memory(o, i) for _, o, _ in outs for _, i, _ in ins):
+        return False
+    host_in = [torch.from_numpy(a.reshape(-1)) for _, a, _ in ins]
+    host_out = [torch.from_numpy(a.reshape(-1)) for _, a, _ in outs]
+    if not all(t.is_pinned() for t in host_in + host_out):
+        return False
+    h2d, d2h = _copy_streams(L.device)
+    dev_in = [torch.empty(units * e, dtype=torch.float32, device=L.device) for _, _, e in ins]
+    dev_out = [torch.empty(units * e, dtype=torch.float32, device=L.device) for _, _, e in outs]
+    step = -(-units // PIPE_CHUNKS)
+    step = -(-step // align) * align
+    bounds = [(u, min(units, u + step)) for u in range(0, units, step)]
+    start = torch.cuda.Event()
+    start.record(L.stream)          # the copies follow whatever the stream already holds
+    h2d.wait_event(start)
+    d2h.wait_event(start)
+    arrived = []
+    with torch.cuda.stream(h2d):
+        for u0, u1 in bounds:
+            for t, h, (_, _, e) in zip(dev_in, host_in, ins):
+                t[u0 * e:u1 * e].copy_(h[u0 * e:u1 * e], non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record(h2d)
+            arrived.append(ev)
+    if L.ev0 is not None:
+        L.ev0.record(L.stream)
+    for (u0, u1), ev in zip(bounds, arrived):
+        L.stream.wait_event(ev)
+        launch_chunk(u0, u1, [t.data_ptr() + 4 * u0 * e for t, (_, _, e) in zip(dev_in, ins)],
+                     [t.data_ptr() + 4 * u0 * e for t, (_, _, e) in zip(dev_out, outs)])
+        done = torch.cuda.Event()
+        done.record(L.stream)
+        d2h.wait_event(done)
+        with torch.cuda.stream(d2h):
+            for t, h, (_, _, e) in zip(dev_out, host_out, outs):
+                h[u0 * e:u1 * e].copy_(t[u0 * e:u1 * e], non_blocking=True)
+    if L.ev1 is not None:
+        L.ev1.record(L.stream)
+    L.stream.wait_stream(d2h)       # finish() synchronises the stream: every copy back is done
+    for t in dev_in:
+        t.record_stream(h2d)
+    for t in dev_out:
+        t.record_stream(d2h)
+    L.host_h2d += sum(4 * units * e for _, _, e in ins)
+    L.host_d2h += sum(4 * units * e for _, _, e in outs)
+    return True
+
+
+# ---------------------------------------------------------------------------------------
 # operators
 # ---------------------------------------------------------------------------------------
 
@@ -253,6 +356,17 @@ def _flags(launch, allowed_qpu=True, simt_ok=False):
 def _add(L: Launch, grid):
     n, blk = L.int("n_elements"), L.int("BLOCK_SIZE")
     n_eff = max(0, min(n, grid[0] * blk))
+    flags = _flags(L)
+
+    def chunk(u0, u1, ins, outs):
+        L.call_untimed("piton_b200_add_f32",
+                       _lib.AddArgs(ins[0], ins[1], outs[0], u1 - u0, blk, -(-(u1 - u0) // blk), flags, 0), "add_kernel")
+
+    # whole programs per chunk (BLOCK_SIZE elements each), 16-byte aligned chunk starts
+    if blk > 0 and _pipelined_on_host(L, [("x_ptr", L.args["x_ptr"], 1), ("y_ptr", L.args["y_ptr"], 1)],
+                                      [("output_ptr", L.args["output_ptr"], 1)], n_eff, blk * (4 // math.gcd(blk, 4)),
+                                      chunk):
+        return {"bytes": 12 * n_eff, "flops": n_eff, "path": "add_vec4_host_pipelined"}
     x, y, out = L.ptr("x_ptr"), L.ptr("y_ptr"), L.ptr("output_ptr", written=True, covers=n_eff)
     for b in (x, y, out):
         b.require(0, n_eff - 1)
@@ -267,6 +381,16 @@ def _softmax(L: Launch, grid):
     rows, ncols, blk = grid[0], L.int("n_cols"), L.int("BLOCK_SIZE")
     sin, sout = L.int("input_row_stride"), L.int("output_row_stride")
     n = max(0, min(ncols, blk))
+    flags = _flags(L)
+
+    def chunk(u0, u1, ins, outs):
+        L.call_untimed("piton_b200_softmax_f32",
+                       _lib.SoftmaxArgs(outs[0], ins[0], sin, sout, ncols, blk, u1 - u0, flags, 0), "softmax_kernel")
+
+    # dense rows (row strides = n_cols, every column inside BLOCK_SIZE): chunks of whole rows
+    if sin == sout == n == ncols and _pipelined_on_host(L, [("input_ptr", L.args["input_ptr"], n)],
+                                                        [("output_ptr", L.args["output_ptr"], n)], rows, 1, chunk):
+        return {"bytes": 8 * rows * n, "flops": 4 * rows * n, "path": "softmax_host_pipelined"}
     out, inp = L.ptr("output_ptr", written=True, covers=rows * n if sout == n else -1), L.ptr("input_ptr")
     inp.require(*extent((rows, sin), (n, 1)))
     out.require(*extent((rows, sout), (n, 1)))
@@ -364,6 +488,24 @@ def _attention(L: Launch, grid):
     heads = grid[1]
     rows = max(0, min(n_ctx, grid[0] * bm))
     keys = n_ctx if (causal or not even) else (n_ctx // bn) * bn
+    hd = n_ctx * d
+    flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
+    flags = _flags(L, True, simt_ok=True)
+
+    def chunk(h0, h1, ins, outs):
+        a = _lib.AttentionArgs(ins[0], ins[1], ins[2], outs[0], L.float("sm_scale"), hd, d, hd, d, 1, hd, d, hd, d,
+                               n_ctx, d, bm, bn, grid[0], h1 - h0, int(causal), int(even), 0, 0, flags, 0)
+        ws = lib().piton_b200_attention_workspace_size(C.byref(a))
+        a.workspace, a.workspace_bytes = L.workspace(ws), ws
+        L.call_untimed("piton_b200_attention_f32", a, "attn_fwd_kernel")
+
+    # dense [heads, N_CTX, HEAD_DIM] operands and every query row written: chunks of whole heads
+    dense = all(st[k] == hd for k in ("stride_qh", "stride_kh", "stride_vh", "stride_oh")) and \
+        all(st[k] == d for k in ("stride_qm", "stride_kn", "stride_vn", "stride_om")) and st["stride_kk"] == 1
+    if dense and rows == n_ctx and _pipelined_on_host(L, [("Q", L.args["Q"], hd), ("K", L.args["K"], hd),
+                                                          ("V", L.args["V"], hd)], [("Out", L.args["Out"], hd)],
+                                                      heads, 1, chunk):
+        return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops, "path": "attention_host_pipelined"}
     Q, K, V, O = L.ptr("Q"), L.ptr("K"), L.ptr("V"), L.ptr("Out", written=True)
     if rows > 0 and heads > 0:
         Q.require(*extent((heads, st["stride_qh"]), (rows, st["stride_qm"]), (d, 1)))
@@ -378,7 +520,6 @@ def _attention(L: Launch, grid):
     ws = lib().piton_b200_attention_workspace_size(C.byref(a))
     a.workspace, a.workspace_bytes = L.workspace(ws), ws
     L.call("piton_b200_attention_f32", a, "attn_fwd_kernel")
-    flops = 4.0 * n_ctx * n_ctx * d * heads * (0.5 if causal else 1.0)
     return {"bytes": 4 * 4 * heads * n_ctx * d, "flops": flops,
             "path": "qpu_rounding" if L.qpu else ("tcgen05_f16x3" if ws else "cuda_core")}
 
