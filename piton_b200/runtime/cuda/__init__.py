@@ -309,6 +309,12 @@ def _pipelined_on_host(L: Launch, ins, outs, units: int, align: int, launch_chun
     h2d, d2h = _copy_streams(L.device)
     dev_in = [torch.empty(units * e, dtype=torch.float32, device=L.device) for _, _, e in ins]
     dev_out = [torch.empty(units * e, dtype=torch.float32, device=L.device) for _, _, e in outs]
+    # the device copies are used on the copy streams too: the allocator must not hand their
+    # memory out again before the work queued there is done (also when a launch below fails)
+    for t in dev_in:
+        t.record_stream(h2d)
+    for t in dev_out:
+        t.record_stream(d2h)
     step = -(-units // PIPE_CHUNKS)
     step = -(-step // align) * align
     bounds = [(u, min(units, u + step)) for u in range(0, units, step)]
@@ -339,10 +345,6 @@ def _pipelined_on_host(L: Launch, ins, outs, units: int, align: int, launch_chun
     if L.ev1 is not None:
         L.ev1.record(L.stream)
     L.stream.wait_stream(d2h)       # finish() synchronises the stream: every copy back is done
-    for t in dev_in:
-        t.record_stream(h2d)
-    for t in dev_out:
-        t.record_stream(d2h)
     L.host_h2d += sum(4 * units * e for _, _, e in ins)
     L.host_d2h += sum(4 * units * e for _, _, e in outs)
     return True
