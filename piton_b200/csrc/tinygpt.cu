@@ -3,7 +3,7 @@
 // pre-LayerNorm blocks of 4-head causal attention (head dim 32) and a 4x GELU
 // MLP, learned positions, tied input/output embeddings, context 128.
 //
-// Step kernel (batches that fill the SMs): one launch per decode.  A CTA owns SEQ
+// Step kernel (batches above the cluster kernel's): one launch per decode.  A CTA owns SEQ
 // sequences and feeds their positions one after another; for each it runs every
 // layer with the activations in shared memory, appends the token's keys and
 // values to the caller's KV cache, attends over the cached positions (one warp
